@@ -1,0 +1,189 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference implementation.
+
+Run in a container where the reference sources are present (the fixtures are committed; the GPU
+box never runs this):
+
+    KVB_REFERENCE=/path/to/KV-Project python tests/golden/make_golden.py
+
+It imports the reference modules read-only (``STRATA_KV.py``, ``QUASAR_KV.py``), calls their own
+functions on seeded inputs and stores inputs and outputs as small ``.npz`` files beside this
+script.  ``tests/test_oracle_golden.py`` checks the numpy oracle against every array here.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import tempfile
+from dataclasses import replace
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def load_reference():
+    ref = os.environ.get("KVB_REFERENCE", "/root/reference")
+    scratch = tempfile.mkdtemp(prefix="kvb_golden_")
+    os.environ.setdefault("KV_PROJECT_ROOT", scratch)
+    os.environ.setdefault("KV_STRATA_OUTPUT_DIR", os.path.join(scratch, "out"))
+    sys.dont_write_bytecode = True
+    sys.path.insert(0, ref)
+    import STRATA_KV as S            # noqa: E402  (reference module, read-only)
+    import QUASAR_KV as Q            # noqa: E402
+    return S, Q
+
+
+def np32(t):
+    return t.detach().cpu().float().numpy()
+
+
+def main():
+    S, Q = load_reference()
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(1234)
+    out = {}
+
+    # ---- storage rounding ------------------------------------------------------------------
+    edge = torch.tensor([0.0, -0.0, 1.0, 65504.0, 65520.0, 1e6, -1e6, 6.1e-5, 3e-8, 1e-9, -2.5e-6, 0.1, 1 / 3.0])
+    out["as_stored_in"] = np32(edge)
+    out["as_stored_out"] = np32(S.as_stored(edge))
+
+    # ---- KIVI group quantiser --------------------------------------------------------------
+    kcases = [  # (B, H, T, d, bits, group, along_tokens, n_sink, bf16)
+        (1, 2, 70, 64, 4, 32, True, 4, False),
+        (1, 2, 70, 64, 2, 32, False, 4, False),
+        (2, 2, 33, 64, 8, 64, False, 0, True),
+        (1, 3, 64, 32, 2, 16, True, 0, True),
+        (1, 2, 19, 48, 4, 32, False, 0, False),     # group does not divide d -> whole row
+        (1, 2, 40, 128, 4, 128, True, 0, True),     # one partial group (40 < 128)
+        (2, 2, 50, 128, 2, 64, False, 0, True),
+        (2, 2, 50, 128, 4, 64, False, 0, True),
+    ]
+    for i, (B, H, T, d, bits, group, along, sink, bf) in enumerate(kcases):
+        x = torch.randn(B, H, T, d, generator=g) * (1.0 + 3.0 * torch.rand(1, 1, 1, d, generator=g))
+        x[..., 3] *= 8.0
+        if bf:
+            x = x.to(torch.bfloat16).float()
+        r = S.kivi_quant(x, bits, group, along, sink)
+        out[f"kivi{i}_case"] = np.array([B, H, T, d, bits, group, int(along), sink, int(bf)], np.int64)
+        out[f"kivi{i}_x"] = np32(x)
+        for k in ("xhat", "lo", "scale"):
+            out[f"kivi{i}_{k}"] = np32(r[k])
+        out[f"kivi{i}_codes"] = r["codes"].numpy()
+
+    # ---- STRATA codes, packing, rotation ---------------------------------------------------
+    for b in (2, 3, 4, 8):
+        out[f"uniform_step_{b}"] = np.array(S.uniform_step(b), np.float64)
+    R = S.rotation_matrix(32, "strata")
+    out["rot32_strata"] = np32(R)
+    out["rot24_t"] = np32(S.rotation_matrix(24, "t"))
+    x = torch.randn(60, 32, generator=g) * torch.linspace(0.2, 3.0, 32)
+    x[:, 7] *= 20
+    out["sq_x"] = np32(x @ R.T)
+    for b in (2, 4, 8):
+        c, s, yh = S.strata_quantize(x @ R.T, b)
+        out[f"sq{b}_codes"], out[f"sq{b}_s"], out[f"sq{b}_yhat"] = c.numpy(), np32(s), np32(yh)
+        out[f"planar{b}"] = S.pack_planar(c, b).numpy()
+        out[f"codes_msb{b}"] = S.pack_codes(c, b).numpy()
+    out["absmax_x"] = np32(x)
+    for b in (4, 8):
+        c, s = S.absmax_quant(x, b)
+        out[f"absmax{b}_codes"], out[f"absmax{b}_s"] = np32(c), np32(s)
+    rc = torch.randint(0, 4, (5, 16), generator=g)
+    out["rows2_in"], out["rows2_out"] = rc.numpy().astype(np.uint8), Q.pack_rows(rc, 2).numpy()
+    rc4 = torch.randint(0, 16, (5, 16), generator=g)
+    out["rows4_in"], out["rows4_out"] = rc4.numpy().astype(np.uint8), Q.pack_rows(rc4, 4).numpy()
+    np.savez_compressed(HERE / "codecs.npz", **out)
+
+    # ---- SnapKV scores and selection -------------------------------------------------------
+    sel = {}
+    cfg = S.Config(SNAPKV_WINDOW=16, SNAPKV_KERNEL=5, SMOKE=True)
+    B, Hkv, rep, H, d = 2, 2, 2, 96, 16
+    q = torch.randn(B, Hkv * rep, H, d, generator=g)
+    k = torch.randn(B, Hkv, H, d, generator=g)
+    sc = S.snapkv_scores(q, k, H, d ** -0.5, cfg)
+    sel.update(q=np32(q), k=np32(k), scores=np32(sc), H=np.array(H), window=np.array(16), kernel=np.array(5))
+    body = sc[..., :H - 16]
+    sel["top20"] = body.topk(20, dim=-1).indices.sort(-1).values.numpy()
+    # the full SnapKV + KIVI hybrid entries of one layer (selection, gather, codes of kept tokens)
+    m = S.SnapKVQuantMethod(cfg, 0.25, 4, "mtlp4", H, d)
+    m.begin()
+    m.freeze_at, m.capture_extra = H, 1
+    Kc, Vc, hide, tok = m.entries(0, q, k, torch.randn(B, Hkv, H, d, generator=g), d ** -0.5, torch.arange(H))
+    sel["mtlp_n_q"] = np.array(tok["k"].shape[2])
+    sel["mtlp_v"] = np32(Vc)
+    sel["mtlp_hide"] = hide.numpy()
+    for side in ("k", "v"):
+        for x_ in ("codes", "lo", "scale"):
+            t_ = m.stored[0][side][x_]
+            sel[f"mtlp_{side}_{x_}"] = t_.numpy() if x_ == "codes" else np32(t_)
+    np.savez_compressed(HERE / "select.npz", **sel)
+
+    # ---- dequantise-then-attend ------------------------------------------------------------
+    att = {}
+    B, Hkv, rep, Tq, Tk, d, nt = 1, 2, 2, 3, 40, 16, 12
+    q = torch.randn(B, Hkv * rep, Tq, d, generator=g)
+    K = torch.randn(B, Hkv, Tk, d, generator=g)
+    V = torch.randn(B, Hkv, Tk, d, generator=g)
+    hide = torch.full((B, Hkv, Tk), S.BIG, dtype=torch.long)
+    hide[0, 0, 5:15] = 38
+    hide[0, 1, 20:30] = 36
+    tok = {"k": torch.randn(B, Hkv, nt, d, generator=g), "v": torch.randn(B, Hkv, nt, d, generator=g),
+           "b": torch.zeros(B, Hkv, nt), "tau": torch.tensor([30] * 6 + [41] * 6)}
+    tok["b"][0, 1, -2:] = float("-inf")
+    qpos = torch.tensor([39, 40, 41])
+    o = S.chunked_attention(q, d ** -0.5, qpos, K, V, torch.arange(Tk), hide, tok, 2)
+    att.update(q=np32(q), K=np32(K), V=np32(V), hide=hide.numpy(), tk=np32(tok["k"]), tv=np32(tok["v"]),
+               tb=np32(tok["b"]), ttau=tok["tau"].numpy(), qpos=qpos.numpy(), out=np32(o))
+    np.savez_compressed(HERE / "attention.npz", **att)
+
+    # ---- STRATA packed strata + compressed-domain decode -----------------------------------
+    st = {}
+    Hkv, rep, dd, H = 2, 2, 32, 600
+    fr = S._fake_runner(dd, Hkv, rep, dev=torch.device("cpu"))
+    tc = replace(S.Config(SMOKE=True), STRATA_SEGMENT=64, STRATA_QUERIES=8, STRATA_LOCAL=16)
+    spec = torch.exp(-torch.arange(dd) / 6.0)
+    Kx = torch.randn(1, Hkv, H, dd, generator=g) * spec.sqrt() * 3 + 1.0
+    Vx = torch.randn(1, Hkv, H, dd, generator=g)
+    Qx = torch.randn(1, Hkv * rep, H, dd, generator=g) * spec.sqrt() * 3
+    meth = S.StrataMethod(tc, 0.15, "t", fr)
+    meth.begin()
+    meth.freeze_at, meth.capture_extra = H, 4
+    pos = torch.arange(H)
+    K2, V2, hide, tok = meth.entries(0, Qx, Kx, Vx, dd ** -0.5, pos)
+    meth.capture(0, K2, V2, pos, hide, tok)
+    qn = torch.randn(1, Hkv * rep, 1, dd, generator=g) * spec.sqrt() * 3
+    kn, vn = torch.randn(1, Hkv, 1, dd, generator=g), torch.randn(1, Hkv, 1, dd, generator=g)
+    st_h = meth.states[0]
+    st_h.append(kn, vn, torch.tensor([H]))
+    o_h = st_h.attend(qn, dd ** -0.5, torch.tensor([H]), 64)
+    st_n = meth.native_state(0, Kx, Vx, 4, torch.float32)
+    st_n.append(kn, vn, torch.tensor([H]))
+    o_n = st_n.attend(qn, dd ** -0.5, torch.tensor([H]))
+    p = st_n.p
+    st.update(q=np32(qn), Ke=np32(st_n.K[:, :, :st_n.n]), Ve=np32(st_n.V[:, :, :st_n.n]), n0=np.array(st_n.n0),
+              H=np.array(H), R=np32(st_n.R), mu_k=np32(p["mu_k"]), mu_v=np32(p["mu_v"]), out_native=np32(o_n),
+              out_harness=np32(o_h), n_tiers=np.array(len(p["tiers"])), counts=p["counts"].numpy())
+    for i, t in enumerate(p["tiers"]):
+        st[f"t{i}_bits"] = np.array(t["bits"])
+        for x_ in ("kc", "vc"):
+            st[f"t{i}_{x_}"] = t[x_].numpy()
+        for x_ in ("ks", "vs"):
+            st[f"t{i}_{x_}"] = np32(t[x_])
+        qg = qn.reshape(Hkv, rep, dd)
+        qr = (qg.float() @ st_n.R.float().T) * dd ** -0.5
+        qb = (qg @ p["mu_k"][..., None])[..., 0].float() * dd ** -0.5
+        m_, l_, a_, _ = S.StrataState.tier_reference(qr, qb, t)
+        st[f"t{i}_m"], st[f"t{i}_l"], st[f"t{i}_acc"] = np32(m_[:, 0]), np32(l_[:, 0]), np32(a_[:, 0])
+    st["qr"], st["qb"] = np32(qr), np32(qb)
+    np.savez_compressed(HERE / "strata.npz", **st)
+
+    sizes = {f: (HERE / f).stat().st_size for f in ("codecs.npz", "select.npz", "attention.npz", "strata.npz")}
+    print("wrote", sizes)
+
+
+if __name__ == "__main__":
+    main()
