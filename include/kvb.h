@@ -1,0 +1,170 @@
+/*
+ * kvb.h - C ABI of the B200 (sm_100a) packed-KV decode path.
+ *
+ * Drop-in native replacement for the decode-time hot path of TahirSher/KV-Project's KV-cache
+ * compression methods (STRATA_KV.py, QUASAR_KV.py, HEDGE_KV.py, TILT_KV.py, LCTC_KV.py, KV_LDT).
+ * Every entry point takes plain device pointers, 64-bit sizes and a cudaStream_t passed as void*.
+ * No call allocates device memory or synchronises the stream, except kvb_device_status (which
+ * reads the device status word).  Errors come back as a kvb_status; kvb_last_error() returns a
+ * thread-local description of the last failure.
+ *
+ * Numerics contract (checked by tests/ against the reference on identical seeded inputs):
+ *   - codes, fp16 scales / zero points and selected index sets are bit-exact;
+ *   - attention outputs agree with the reference's float32 dequantise-then-attend result
+ *     (chunked_attention, STRATA_KV.py:641) within max-abs 2e-3.
+ */
+#ifndef KVB_H
+#define KVB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int kvb_status;
+#define KVB_OK 0
+#define KVB_EINVAL 1          /* bad shape, dtype, stride, alignment or size */
+#define KVB_ECUDA 2           /* a CUDA runtime call failed (message in kvb_last_error) */
+#define KVB_ETIMEDOUT 3       /* a bounded device wait gave up (device status word set) */
+#define KVB_EUNSUPPORTED 4    /* valid request outside the instantiated kernel set */
+
+/* element types */
+#define KVB_F32 0
+#define KVB_F16 1
+#define KVB_BF16 2
+#define KVB_F64 3
+
+/* how a stored vector is coded */
+#define KVB_CODE_ASYM 0       /* KIVI: per group fp16 (lo, scale) pair, x ~ code * scale + lo */
+#define KVB_CODE_MIDRISE 1    /* STRATA: one fp16 scale s per vector, x ~ (code - (2^b - 1) / 2) * s */
+
+/* grouping of the key code (values are always grouped per token) */
+#define KVB_K_PER_TOKEN 0     /* groups of `group` channels inside each token (or one scale per token) */
+#define KVB_K_PER_CHANNEL 1   /* per channel over groups of `group` consecutive stored tokens */
+
+const char* kvb_last_error(void);
+int kvb_version(void);
+
+/* Device status word (bit 0: a bounded wait timed out; bit 1: a bounds check failed).  Synchronises
+ * `stream`, copies the word to *out and clears it when `clear` is non-zero. */
+kvb_status kvb_device_status(unsigned* out, int clear, void* stream);
+
+/* ------------------------------------------------------------------------------------------ *
+ * K1: quantise + planar-pack.  Replaces kivi_quant (STRATA_KV.py:826-856), strata_quantize +
+ * pack_planar (STRATA_KV.py:1158-1182) and the per-stratum gather of StrataMethod.pack
+ * (STRATA_KV.py:1611-1627) / SnapKVQuantMethod.entries (STRATA_KV.py:1024-1027).
+ *
+ * Rows: for each (b, h), stored row j (0 <= j < n) is source row idx[b, h, j] when idx is given,
+ * else source row first_row + j.  x: (B, H, T, d) of dtype x_dtype with element strides
+ * (sb, sh, st) and unit channel stride.  bits in {2, 4, 8}; d % 32 == 0 and d <= 256.
+ * Outputs (all dense, row capacity n_alloc >= n per (b, h); n_alloc % 16 == 0):
+ *   codes (B, H, n_alloc, d * bits / 8) planar bytes (byte i holds channel p * d / P + i in bits
+ *         [p * bits, (p + 1) * bits), P = 8 / bits);
+ *   meta  ASYM per token:    (B, H, n_alloc, d / group, 2) fp16 (lo, scale) pairs;
+ *         ASYM per channel:  (B, H, n_alloc / group, d, 2) fp16 (lo, scale) pairs, group in
+ *                            {16, 32, 64, 128}; a partial last group uses its valid rows only
+ *                            (the reference's repeat-last-row padding leaves min / max unchanged);
+ *         MIDRISE:           (B, H, n_alloc) fp16 scales (group must equal d);
+ *   xhat  optional (nullable) float32 (B, H, n, d): what a reader dequantises.
+ * `step` is the MIDRISE step in RMS units (uniform_step(bits)[0], STRATA_KV.py:1133). */
+kvb_status kvb_quant_pack(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t d,
+                          int64_t sb, int64_t sh, int64_t st,
+                          const int64_t* idx, int64_t first_row, int64_t n, int64_t n_alloc,
+                          int bits, int group, int k_mode, int code_kind, float step,
+                          uint8_t* codes, void* meta, float* xhat, void* stream);
+
+/* ------------------------------------------------------------------------------------------ *
+ * K2: rank split + compaction (budgeted eviction / strata assignment).  Replaces the topk + sort
+ * of SnapKVQuantMethod.entries (STRATA_KV.py:1022-1023) and the importance ordering that feeds the
+ * strata (STRATA_KV.py:1560-1571).  For each of `rows` rows of `n` keys (f32 or f64, row stride
+ * key_stride elements), elements are ranked by key descending, ties by LOWER index first; class c
+ * takes ranks [sum(counts[:c]), sum(counts[:c+1])) and the last class takes the rest
+ * (n_classes <= 4, n_classes - 1 counts given).  out[c] (nullable) receives, per row, the class's
+ * indices in ASCENDING order, row stride out_stride[c].  NaN keys are rejected by the wrapper. */
+kvb_status kvb_rank_split(const void* keys, int key_dtype, int64_t rows, int64_t n, int64_t key_stride,
+                          int n_classes, const int64_t* counts, int64_t* const* out,
+                          const int64_t* out_stride, void* stream);
+
+/* Per-token key energy sum_c k_c^2 in float64 (exact for bf16 / fp16 keys, so rankings are
+ * order-independent): k (B, H, T, d) strides (sb, sh, st) -> out (B, H, T) float64. */
+kvb_status kvb_key_energy(const void* k, int dtype, int64_t B, int64_t H, int64_t T, int64_t d,
+                          int64_t sb, int64_t sh, int64_t st, double* out, void* stream);
+
+/* Accumulated attention of `nq` queries per query head over all T keys (SnapKV-style scores,
+ * snapkv_scores STRATA_KV.py:932-953 with decode-time queries): for each (b, kv head h),
+ * score[j] = mean over the rep query heads and nq queries of softmax_j(scaling * q . k_j), for
+ * j < n_cand; q (B, Hq, nq, d), k (B, Hkv, T, d) in dtype (f16 / bf16), dense, d in {64, 128},
+ * rep * nq <= 256; out (B, Hkv, n_cand) float32.  `pool` in {0, 1, 3, 5, ...}: avg_pool1d over
+ * the candidates (zero padding counted) before the head mean.  workspace: 256-byte aligned,
+ * >= kvb_scores_workspace_size(B, Hkv, n_cand) bytes. */
+size_t kvb_scores_workspace_size(int64_t B, int64_t Hkv, int64_t n_cand);
+kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                            int64_t nq, int64_t T, int64_t d, float scaling, int64_t n_cand, int pool,
+                            float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------ *
+ * K3: fused split-K flash decode over a packed, head-synchronous cache.  Replaces StrataState.attend
+ * + strata_tier_kernel (STRATA_KV.py:1762-1796, :1450-1469), LayerState.attend / chunked_attention
+ * (STRATA_KV.py:716, :641) over KIVI codes, and QuasarState.attend (QUASAR_KV.py:1942-1967, one
+ * stage) over spectral coefficients. */
+typedef struct kvb_stratum {
+    int kbits, vbits;         /* code widths of keys and values: 2, 4 or 8 each */
+    int64_t n;                /* stored tokens per (b, h) */
+    int64_t n_alloc;          /* row capacity per (b, h), multiple of 16 */
+    const uint8_t* kc;        /* (B, Hkv, n_alloc, d_code * kbits / 8) planar */
+    const uint8_t* vc;        /* (B, Hkv, n_alloc, d_code * vbits / 8) planar */
+    const void* kmeta;        /* as kvb_quant_pack's meta for the key code */
+    const void* vmeta;        /* as kvb_quant_pack's meta for the value code (per token) */
+} kvb_stratum;
+
+typedef struct kvb_cache {
+    int B, Hkv;
+    int d;                    /* model head dim (exact rows, queries, output) */
+    int d_code;               /* coded dimension (== d, or r for the spectral code) */
+    int code_kind;            /* KVB_CODE_ASYM / KVB_CODE_MIDRISE */
+    int k_mode;               /* KVB_K_PER_TOKEN / KVB_K_PER_CHANNEL */
+    int k_group;              /* channels per key group (per token) or tokens per group (per channel) */
+    int v_group;              /* channels per value group */
+    int n_strata;             /* 0..4 */
+    kvb_stratum strata[4];
+    /* exact rows (model dtype, (B, Hkv, cap, d) dense): rows [0, n0) always readable, rows
+     * [n0, n_exact) sit at positions pos0 + (i - n0) (causal w.r.t. each query's position) */
+    const void* k_exact;
+    const void* v_exact;
+    int exact_dtype;
+    int64_t exact_cap, n_exact, n0, pos0;
+    /* optional query map and output lift (code space != model space), float32:
+     *   qmap (Hkv, d, d_code): q_code = q @ qmap[h]   (rotation R^T, or spectral basis B_r)
+     *   lift (Hkv, d_code, d): out_code @ lift[h]     (R, or B_r^T)
+     *   mu_k, mu_v (Hkv, d):   mean key / value (logit bias scaling q . mu_k; value (sum p) mu_v) */
+    const float* qmap;
+    const float* lift;
+    const float* mu_k;
+    const float* mu_v;
+} kvb_cache;
+
+/* Number of split-K pieces and the plan / workspace sizes for a cache shape. */
+size_t kvb_decode_workspace_size(const kvb_cache* c, int Hq, int Tq, int n_ctas);
+/* q (B, Hq, Tq, d) dtype q_dtype dense; qpos (Tq) host array of query positions (used only for
+ * appended exact rows); out (B, Tq, Hq, d) in out_dtype.  n_ctas: persistent CTAs (0 = one per
+ * SM).  workspace: device buffer of kvb_decode_workspace_size bytes, 256-byte aligned. */
+kvb_status kvb_decode(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                      const int64_t* qpos, void* out, int out_dtype, int n_ctas,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* As kvb_decode, and records the cudaEvent_t handles ev_begin / ev_end (nullable) on `stream`
+ * immediately before and after the main split-K kernel, so a caller can time that kernel alone. */
+kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                             const int64_t* qpos, void* out, int out_dtype, int n_ctas,
+                             void* workspace, size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end);
+
+/* Build the split-K plan (pure host computation, no CUDA calls): piece table for n_ctas CTAs.
+ * Exposed for tests; kvb_decode builds and uploads it inside its workspace. */
+int64_t kvb_decode_plan(const kvb_cache* c, int n_ctas, int32_t* plan_out, int64_t plan_capacity);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVB_H */

@@ -1,0 +1,614 @@
+// kvb_api.cu - the C ABI of include/kvb.h (host code) and the kernel instantiations.
+//
+// One translation unit: every kernel header is included here, so the device status word and all
+// kernels live in one module of libkvb.so.  Host functions validate shapes, dtypes, strides and
+// alignment, build launch parameters and enqueue kernels on the caller's stream; they never
+// allocate device memory and never synchronise (kvb_device_status excepted).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <type_traits>
+#include <vector>
+
+#include "../../include/kvb.h"
+#include "kvb_common.cuh"
+#include "kvb_quant.cuh"
+#include "kvb_select.cuh"
+#include "kvb_decode.cuh"
+#include "kvb_scores.cuh"
+
+#define KVB_VERSION 100
+
+namespace {
+
+thread_local std::string g_last_error;
+
+kvb_status fail(kvb_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+kvb_status fail(kvb_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return s;
+}
+
+kvb_status cuda_check(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return KVB_OK;
+    return fail(KVB_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+kvb_status launch_check(const char* what) { return cuda_check(cudaGetLastError(), what); }
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int elem_size(int dt) { return dt == KVB_F32 ? 4 : dt == KVB_F64 ? 8 : 2; }
+
+}  // namespace
+
+extern "C" {
+
+const char* kvb_last_error(void) { return g_last_error.c_str(); }
+int kvb_version(void) { return KVB_VERSION; }
+
+kvb_status kvb_device_status(unsigned* out, int clear, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned v = 0;
+    kvb_status st = cuda_check(cudaMemcpyFromSymbolAsync(&v, kvb::g_status, sizeof(v), 0, cudaMemcpyDeviceToHost, s),
+                               "read status");
+    if (st) return st;
+    if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
+    if (out) *out = v;
+    if (clear) {
+        const unsigned z = 0;
+        if ((st = cuda_check(cudaMemcpyToSymbolAsync(kvb::g_status, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s),
+                             "clear status")))
+            return st;
+        if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
+    }
+    return KVB_OK;
+}
+
+// =============================================================================================
+// K1
+// =============================================================================================
+kvb_status kvb_quant_pack(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t d, int64_t sb,
+                          int64_t sh, int64_t st, const int64_t* idx, int64_t first_row, int64_t n, int64_t n_alloc,
+                          int bits, int group, int k_mode, int code_kind, float step, uint8_t* codes, void* meta,
+                          float* xhat, void* stream) {
+    if (!x || !codes || !meta) return fail(KVB_EINVAL, "quant_pack: null pointer");
+    if (x_dtype != KVB_F32 && x_dtype != KVB_F16 && x_dtype != KVB_BF16) return fail(KVB_EINVAL, "quant_pack: dtype");
+    if (bits != 2 && bits != 4 && bits != 8) return fail(KVB_EINVAL, "quant_pack: bits must be 2, 4 or 8");
+    if (d % 32 || d < 32 || d > 256) return fail(KVB_EINVAL, "quant_pack: d must be a multiple of 32 in [32, 256]");
+    if (B <= 0 || H <= 0 || n < 0 || n_alloc < n || n_alloc % 16) return fail(KVB_EINVAL, "quant_pack: sizes");
+    if (!idx && (first_row < 0 || first_row + n > T)) return fail(KVB_EINVAL, "quant_pack: row range");
+    if (!aligned(codes, 16) || !aligned(meta, 4)) return fail(KVB_EINVAL, "quant_pack: output alignment");
+    if ((d * bits / 8) % 4) return fail(KVB_EINVAL, "quant_pack: packed row must be a multiple of 4 bytes");
+    if (B * H > 65535) return fail(KVB_EINVAL, "quant_pack: B * H > 65535");
+    kvb::QuantTokenParams p{x, B, H, T, d, sb, sh, st, idx, first_row, n, n_alloc,
+                            bits, group, code_kind == KVB_CODE_MIDRISE ? 1 : 0, step, codes, meta, xhat};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (k_mode == KVB_K_PER_CHANNEL) {
+        if (code_kind != KVB_CODE_ASYM) return fail(KVB_EINVAL, "quant_pack: per-channel mode is asymmetric only");
+        if (group != 16 && group != 32 && group != 64 && group != 128)
+            return fail(KVB_EINVAL, "quant_pack: per-channel group must be 16, 32, 64 or 128");
+        if (n_alloc % group) return fail(KVB_EINVAL, "quant_pack: n_alloc must be a multiple of group");
+        if (d != 128 && d != 64 && d != 32) return fail(KVB_EUNSUPPORTED, "quant_pack: per-channel d");
+        if (n_alloc == 0) return KVB_OK;
+        dim3 grid(unsigned(n_alloc / group), unsigned(B * H));
+        const size_t sm = size_t(group) * d + size_t(group) * d * bits / 8;
+#define KVB_QC(T_, D_) kvb::quant_channel_kernel<T_, D_><<<grid, D_, sm, s>>>(p)
+#define KVB_QCD(T_) \
+    if (d == 128) KVB_QC(T_, 128); else if (d == 64) KVB_QC(T_, 64); else KVB_QC(T_, 32)
+        if (x_dtype == KVB_F32) { KVB_QCD(float); }
+        else if (x_dtype == KVB_F16) { KVB_QCD(__half); }
+        else { KVB_QCD(__nv_bfloat16); }
+#undef KVB_QCD
+#undef KVB_QC
+        return launch_check("quant_channel_kernel");
+    }
+    if (code_kind == KVB_CODE_MIDRISE && group != d) return fail(KVB_EINVAL, "quant_pack: midrise needs group == d");
+    if (code_kind == KVB_CODE_ASYM && (d % group == 0) && d / group > 8)
+        return fail(KVB_EINVAL, "quant_pack: at most 8 groups per token");
+    if (n_alloc == 0) return KVB_OK;
+    dim3 grid(unsigned((n_alloc + kvb::QROWS - 1) / kvb::QROWS), unsigned(B * H));
+#define KVB_QT(T_, N_) kvb::quant_token_kernel<T_, N_><<<grid, 128, 0, s>>>(p)
+#define KVB_QTD(T_)                                                                                    \
+    switch (d / 32) {                                                                                  \
+        case 1: KVB_QT(T_, 1); break;                                                                  \
+        case 2: KVB_QT(T_, 2); break;                                                                  \
+        case 3: KVB_QT(T_, 3); break;                                                                  \
+        case 4: KVB_QT(T_, 4); break;                                                                  \
+        case 5: KVB_QT(T_, 5); break;                                                                  \
+        case 6: KVB_QT(T_, 6); break;                                                                  \
+        case 7: KVB_QT(T_, 7); break;                                                                  \
+        default: KVB_QT(T_, 8); break;                                                                 \
+    }
+    if (x_dtype == KVB_F32) { KVB_QTD(float); }
+    else if (x_dtype == KVB_F16) { KVB_QTD(__half); }
+    else { KVB_QTD(__nv_bfloat16); }
+#undef KVB_QTD
+#undef KVB_QT
+    return launch_check("quant_token_kernel");
+}
+
+// =============================================================================================
+// K2
+// =============================================================================================
+kvb_status kvb_rank_split(const void* keys, int key_dtype, int64_t rows, int64_t n, int64_t key_stride, int n_classes,
+                          const int64_t* counts, int64_t* const* out, const int64_t* out_stride, void* stream) {
+    if (!keys || !counts || !out || !out_stride) return fail(KVB_EINVAL, "rank_split: null pointer");
+    if (key_dtype != KVB_F32 && key_dtype != KVB_F64) return fail(KVB_EINVAL, "rank_split: keys must be f32 or f64");
+    if (n_classes < 2 || n_classes > kvb::SEL_MAX_CLASSES) return fail(KVB_EINVAL, "rank_split: 2..4 classes");
+    if (rows <= 0 || n <= 0 || rows > 2147483647) return fail(KVB_EINVAL, "rank_split: sizes");
+    kvb::RankSplitParams p{};
+    p.keys = keys;
+    p.rows = rows;
+    p.n = n;
+    p.key_stride = key_stride;
+    p.n_classes = n_classes;
+    for (int c = 0; c < n_classes - 1; ++c) {
+        if (counts[c] < 0) return fail(KVB_EINVAL, "rank_split: negative count");
+        p.counts[c] = counts[c];
+    }
+    for (int c = 0; c < n_classes; ++c) {
+        p.out[c] = out[c];
+        p.out_stride[c] = out_stride[c];
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (key_dtype == KVB_F32) kvb::rank_split_kernel<float><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p);
+    else kvb::rank_split_kernel<double><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p);
+    return launch_check("rank_split_kernel");
+}
+
+kvb_status kvb_key_energy(const void* k, int dtype, int64_t B, int64_t H, int64_t T, int64_t d, int64_t sb, int64_t sh,
+                          int64_t st, double* out, void* stream) {
+    if (!k || !out) return fail(KVB_EINVAL, "key_energy: null pointer");
+    if (B <= 0 || H <= 0 || T <= 0 || d <= 0) return fail(KVB_EINVAL, "key_energy: sizes");
+    const int64_t rows = B * H * T;
+    const unsigned blocks = unsigned((rows * 32 + 255) / 256);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == KVB_F32)
+        kvb::key_energy_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(k), B, H, T, d, sb, sh, st, out);
+    else if (dtype == KVB_F16)
+        kvb::key_energy_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(k), B, H, T, d, sb, sh, st, out);
+    else if (dtype == KVB_BF16)
+        kvb::key_energy_kernel<__nv_bfloat16>
+            <<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(k), B, H, T, d, sb, sh, st, out);
+    else
+        return fail(KVB_EINVAL, "key_energy: dtype");
+    return launch_check("key_energy_kernel");
+}
+
+size_t kvb_scores_workspace_size(int64_t B, int64_t Hkv, int64_t n_cand) {
+    const size_t heads = size_t(B) * Hkv;
+    const size_t part = heads * kvb::SC_SPLIT * kvb::SC_ROWS * 2 * 4;
+    const size_t lse = heads * kvb::SC_ROWS * 4;
+    const size_t tmp = heads * size_t(n_cand) * 4;
+    auto a = [](size_t x) { return (x + 255) / 256 * 256; };
+    return a(part) + a(lse) + a(tmp);
+}
+
+kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t nq,
+                            int64_t T, int64_t d, float scaling, int64_t n_cand, int pool, float* out, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+    if (!q || !k || !out || !workspace) return fail(KVB_EINVAL, "query_scores: null pointer");
+    if (dtype != KVB_F16 && dtype != KVB_BF16) return fail(KVB_EINVAL, "query_scores: dtype must be f16 or bf16");
+    if (B <= 0 || Hkv <= 0 || Hq % Hkv || nq <= 0 || T <= 0 || n_cand <= 0 || n_cand > T)
+        return fail(KVB_EINVAL, "query_scores: sizes");
+    if ((Hq / Hkv) * nq > kvb::SC_ROWS) return fail(KVB_EUNSUPPORTED, "query_scores: rep * nq > 256");
+    if (d != 64 && d != 128) return fail(KVB_EUNSUPPORTED, "query_scores: d must be 64 or 128");
+    if (pool < 0 || (pool > 1 && pool % 2 == 0)) return fail(KVB_EINVAL, "query_scores: pool must be odd");
+    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(workspace, 256)) return fail(KVB_EINVAL, "query_scores: alignment");
+    if (workspace_bytes < kvb_scores_workspace_size(B, Hkv, n_cand)) return fail(KVB_EINVAL, "query_scores: workspace");
+    const size_t heads = size_t(B) * Hkv;
+    auto a = [](size_t x) { return (x + 255) / 256 * 256; };
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    kvb::ScoreParams p{};
+    p.q = q;
+    p.k = k;
+    p.B = B;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.nq = nq;
+    p.T = T;
+    p.d = d;
+    p.n_cand = n_cand;
+    p.rep = int(Hq / Hkv);
+    p.rows = int(p.rep * nq);
+    p.lam = scaling * kvb::LOG2E;
+    p.part = reinterpret_cast<float*>(ws);
+    p.lse = reinterpret_cast<float*>(ws + a(heads * kvb::SC_SPLIT * kvb::SC_ROWS * 2 * 4));
+    float* tmp = reinterpret_cast<float*>(ws + a(heads * kvb::SC_SPLIT * kvb::SC_ROWS * 2 * 4) + a(heads * kvb::SC_ROWS * 4));
+    p.out = pool > 1 ? tmp : out;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    dim3 grid(kvb::SC_SPLIT, unsigned(heads));
+    for (int pass = 1; pass <= 2; ++pass) {
+        p.pass = pass;
+        if (dtype == KVB_BF16) {
+            if (d == 128) kvb::scores_kernel<__nv_bfloat16, 128><<<grid, 256, 0, s>>>(p);
+            else kvb::scores_kernel<__nv_bfloat16, 64><<<grid, 256, 0, s>>>(p);
+        } else {
+            if (d == 128) kvb::scores_kernel<__half, 128><<<grid, 256, 0, s>>>(p);
+            else kvb::scores_kernel<__half, 64><<<grid, 256, 0, s>>>(p);
+        }
+        kvb_status st = launch_check("scores_kernel");
+        if (st) return st;
+        if (pass == 1) {
+            kvb::scores_lse_kernel<<<unsigned(heads), kvb::SC_ROWS, 0, s>>>(p);
+            if ((st = launch_check("scores_lse_kernel"))) return st;
+        }
+    }
+    if (pool > 1) {
+        const int64_t nthreads = int64_t(heads) * n_cand;
+        kvb::scores_pool_kernel<<<unsigned((nthreads + 255) / 256), 256, 0, s>>>(tmp, out, int64_t(heads), n_cand, pool);
+        return launch_check("scores_pool_kernel");
+    }
+    return KVB_OK;
+}
+
+}  // extern "C"
+
+// =============================================================================================
+// K3 host side: validation, plan, dispatch
+// =============================================================================================
+namespace {
+
+struct DecodeShape {
+    int D, R, GK, GV, kmode, code;
+};
+
+int tokens_per_chunk(int D, int kbits, int vbits) {
+    const int rb = D * kbits / 8 + D * vbits / 8;
+    int tok = 32768 / rb;
+    int p2 = 128;
+    while (p2 * 2 <= tok && p2 < 512) p2 *= 2;
+    return p2;
+}
+
+kvb_status validate_cache(const kvb_cache* c, DecodeShape& sh, int Hq, int Tq) {
+    if (!c) return fail(KVB_EINVAL, "decode: null cache");
+    if (c->B <= 0 || c->Hkv <= 0 || Hq <= 0 || Hq % c->Hkv || Tq <= 0 || Tq > 16)
+        return fail(KVB_EINVAL, "decode: heads / Tq (need Hq %% Hkv == 0, 1 <= Tq <= 16)");
+    const int rep = Hq / c->Hkv;
+    const int Ra = rep * Tq;
+    if (Ra > 8) return fail(KVB_EUNSUPPORTED, "decode: rep * Tq = %d > 8 query rows per KV head", Ra);
+    sh.R = Ra <= 4 ? 4 : 8;
+    sh.D = c->d_code;
+    sh.kmode = c->k_mode;
+    sh.code = c->code_kind;
+    if (c->n_strata < 0 || c->n_strata > 4) return fail(KVB_EINVAL, "decode: n_strata");
+    if (c->d % 32 || c->d > 256 || c->d <= 0) return fail(KVB_EINVAL, "decode: d");
+    if (c->code_kind == KVB_CODE_MIDRISE) {
+        sh.GK = sh.GV = 1;
+        if (c->k_mode != KVB_K_PER_TOKEN) return fail(KVB_EINVAL, "decode: midrise code is per token");
+    } else {
+        if (c->v_group <= 0 || c->d_code % c->v_group) return fail(KVB_EINVAL, "decode: v_group");
+        sh.GV = c->d_code / c->v_group;
+        if (c->k_mode == KVB_K_PER_TOKEN) {
+            if (c->k_group <= 0 || c->d_code % c->k_group) return fail(KVB_EINVAL, "decode: k_group");
+            sh.GK = c->d_code / c->k_group;
+        } else {
+            sh.GK = 1;
+            if (c->k_group != 16 && c->k_group != 32 && c->k_group != 64 && c->k_group != 128)
+                return fail(KVB_EINVAL, "decode: per-channel k_group must be 16, 32, 64 or 128");
+        }
+    }
+    if (c->lift == nullptr && c->d_code != c->d) return fail(KVB_EINVAL, "decode: d_code != d needs a lift matrix");
+    for (int i = 0; i < c->n_strata; ++i) {
+        const kvb_stratum& s = c->strata[i];
+        const bool okb = (s.kbits == s.vbits && (s.kbits == 2 || s.kbits == 4 || s.kbits == 8)) ||
+                         (s.kbits == 4 && s.vbits == 2);
+        if (!okb) return fail(KVB_EUNSUPPORTED, "decode: stratum %d widths (%d, %d)", i, s.kbits, s.vbits);
+        if (sh.D * s.kbits < 128 || sh.D * s.vbits < 128)
+            return fail(KVB_EUNSUPPORTED, "decode: d_code * bits must be >= 128");
+        if (s.n < 0 || s.n_alloc < ((s.n + 15) / 16) * 16 || s.n_alloc % 16)
+            return fail(KVB_EINVAL, "decode: stratum %d n / n_alloc", i);
+        if (c->k_mode == KVB_K_PER_CHANNEL && s.n_alloc % c->k_group)
+            return fail(KVB_EINVAL, "decode: n_alloc must be a multiple of k_group");
+        if (s.n > 0 && (!s.kc || !s.vc || !s.kmeta || !s.vmeta)) return fail(KVB_EINVAL, "decode: null stratum pointer");
+        if (!aligned(s.kc, 16) || !aligned(s.vc, 16) || !aligned(s.kmeta, 16) || !aligned(s.vmeta, 16))
+            return fail(KVB_EINVAL, "decode: stratum %d pointers must be 16-byte aligned", i);
+    }
+    if (c->n_exact < 0 || c->n_exact > c->exact_cap || c->n0 < 0 || c->n0 > c->n_exact)
+        return fail(KVB_EINVAL, "decode: exact rows");
+    if (c->n_exact > 0 && (!c->k_exact || !c->v_exact)) return fail(KVB_EINVAL, "decode: null exact rows");
+    if (c->n_exact > 0 && c->exact_dtype != KVB_F16 && c->exact_dtype != KVB_BF16 && c->exact_dtype != KVB_F32)
+        return fail(KVB_EINVAL, "decode: exact dtype");
+    return KVB_OK;
+}
+
+struct Plan {
+    int n_ctas = 0, n_pieces = 0, n_heads = 0;
+    std::vector<int> cta_begin, head_begin;
+    std::vector<int> piece;   // 4 per piece
+    std::vector<int> tok;     // tokens per chunk per stratum
+};
+
+kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
+    const int heads = c->B * c->Hkv;
+    P.n_ctas = n_ctas;
+    P.n_heads = heads;
+    P.tok.assign(4, 0);
+    std::vector<int64_t> nch(c->n_strata), wfull(c->n_strata), wlast(c->n_strata);
+    int64_t chunks_per_head = 0, w_head = 0;
+    for (int s = 0; s < c->n_strata; ++s) {
+        const kvb_stratum& st = c->strata[s];
+        P.tok[s] = tokens_per_chunk(c->d_code, st.kbits, st.vbits);
+        nch[s] = (st.n + P.tok[s] - 1) / P.tok[s];
+        const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + 8;
+        wfull[s] = int64_t(P.tok[s]) * bpt;
+        wlast[s] = (st.n - (nch[s] - 1) * P.tok[s]) * bpt;
+        chunks_per_head += nch[s];
+        w_head += nch[s] ? (nch[s] - 1) * wfull[s] + wlast[s] : 0;
+    }
+    const double W = double(w_head) * heads;
+    P.cta_begin.assign(n_ctas + 1, 0);
+    P.head_begin.assign(heads + 1, 0);
+    P.piece.clear();
+    int cur_cta = 0;
+    int last_key_cta = -1, last_head = -1, last_s = -1;
+    double cum = 0.0;
+    for (int h = 0; h < heads; ++h) {
+        P.head_begin[h] = int(P.piece.size() / 4);
+        for (int s = 0; s < c->n_strata; ++s) {
+            for (int64_t k = 0; k < nch[s]; ++k) {
+                const double w = double(k + 1 == nch[s] ? wlast[s] : wfull[s]);
+                int cta = W > 0 ? int((cum + 0.5 * w) * n_ctas / W) : 0;
+                cta = std::min(std::max(cta, cur_cta), n_ctas - 1);
+                cum += w;
+                if (cta != last_key_cta || h != last_head || s != last_s) {
+                    while (cur_cta < cta) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
+                    P.piece.push_back(h);
+                    P.piece.push_back(s);
+                    P.piece.push_back(int(k));
+                    P.piece.push_back(int(k + 1));
+                    last_key_cta = cta;
+                    last_head = h;
+                    last_s = s;
+                } else {
+                    P.piece.back() = int(k + 1);
+                }
+            }
+        }
+    }
+    while (cur_cta < n_ctas) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
+    P.head_begin[heads] = int(P.piece.size() / 4);
+    P.n_pieces = int(P.piece.size() / 4);
+    return KVB_OK;
+}
+
+int resolve_ctas(int n_ctas) {
+    if (n_ctas > 0) return std::min(n_ctas, kvb::DEC_MAX_CTAS);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return std::min(sms, kvb::DEC_MAX_CTAS);
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct WsLayout {
+    size_t qp, part, total;
+    int qp_stride;
+};
+
+WsLayout ws_layout(const kvb_cache* c, const DecodeShape& sh, int n_pieces) {
+    WsLayout L;
+    L.qp_stride = kvb::qp_size(sh.R, sh.D);
+    L.qp = 256;
+    L.part = align256(L.qp + size_t(c->B) * c->Hkv * L.qp_stride * 4);
+    L.total = align256(L.part + size_t(n_pieces) * (2 * sh.R + sh.R * sh.D) * 4);
+    return L;
+}
+
+// ---- instantiation table ----
+template <int D, int R, int GK, int GV, int KM, int CK>
+kvb_status launch_main(const kvb::DecodeParams& p, int n_ctas, size_t smem, cudaStream_t s) {
+    auto fn = kvb::decode_main<D, R, GK, GV, KM, CK>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return cuda_check(e, "decode_main smem attribute");
+    fn<<<n_ctas, kvb::DEC_THREADS, smem, s>>>(p);
+    return launch_check("decode_main");
+}
+
+template <int D, int R, int GK, int GV, int KM, int CK>
+int stage_bytes_for(const kvb_cache* c, const Plan& P) {
+    int mx = 0;
+    for (int s = 0; s < c->n_strata; ++s) {
+        const kvb::StageLay L =
+            kvb::stage_lay<D, R, GK, GV, KM, CK>(c->strata[s].kbits, c->strata[s].vbits, P.tok[s], c->k_group);
+        mx = std::max(mx, L.end);
+    }
+    return (mx + 127) / 128 * 128;
+}
+
+template <int D, int R, int GK, int GV, int KM, int CK>
+kvb_status run_main(const kvb_cache* c, const Plan& P, kvb::DecodeParams& p, cudaStream_t s) {
+    const int sb = std::max(128, stage_bytes_for<D, R, GK, GV, KM, CK>(c, P));
+    const int red = (2 * kvb::DEC_CWARPS * R + kvb::DEC_CWARPS * R * D) * 4;
+    const int fixed = 128 + (red + 127) / 128 * 128;
+    const int ns = std::min(kvb::DEC_MAX_STAGES, (kvb::DEC_SMEM_BUDGET - fixed) / sb);
+    if (ns < 2) return fail(KVB_EUNSUPPORTED, "decode: stage of %d bytes does not fit twice in shared memory", sb);
+    p.stage_bytes = sb;
+    p.nstage = ns;
+    return launch_main<D, R, GK, GV, KM, CK>(p, P.n_ctas, size_t(fixed) + size_t(ns) * sb, s);
+}
+
+kvb_status dispatch_main(const DecodeShape& sh, const kvb_cache* c, const Plan& P, kvb::DecodeParams& p,
+                         cudaStream_t s) {
+    using namespace kvb;
+#define KVB_CASE(D_, R_, GK_, GV_, KM_, CK_)                                                           \
+    if (sh.D == D_ && sh.R == R_ && sh.GK == GK_ && sh.GV == GV_ && sh.kmode == KM_ && sh.code == CK_) \
+        return run_main<D_, R_, GK_, GV_, KM_, CK_>(c, P, p, s);
+    // KIVI per-token keys (mixed-precision strata, config 1)
+    KVB_CASE(128, 4, 2, 2, KM_TOKEN, KV_ASYM)
+    KVB_CASE(128, 8, 2, 2, KM_TOKEN, KV_ASYM)
+    KVB_CASE(128, 4, 1, 1, KM_TOKEN, KV_ASYM)
+    KVB_CASE(128, 8, 1, 1, KM_TOKEN, KV_ASYM)
+    // KIVI per-channel keys (configs 0, 2, 4)
+    KVB_CASE(128, 4, 1, 4, KM_CHANNEL, KV_ASYM)
+    KVB_CASE(128, 4, 1, 2, KM_CHANNEL, KV_ASYM)
+    KVB_CASE(128, 4, 1, 1, KM_CHANNEL, KV_ASYM)
+    KVB_CASE(128, 8, 1, 1, KM_CHANNEL, KV_ASYM)
+    KVB_CASE(128, 8, 1, 2, KM_CHANNEL, KV_ASYM)
+    // STRATA / spectral mid-rise codes
+    KVB_CASE(128, 4, 1, 1, KM_TOKEN, KV_MIDRISE)
+    KVB_CASE(128, 8, 1, 1, KM_TOKEN, KV_MIDRISE)
+    KVB_CASE(64, 4, 1, 1, KM_TOKEN, KV_MIDRISE)
+    KVB_CASE(32, 4, 1, 1, KM_TOKEN, KV_MIDRISE)
+    KVB_CASE(32, 8, 1, 1, KM_TOKEN, KV_MIDRISE)
+#undef KVB_CASE
+    return fail(KVB_EUNSUPPORTED, "decode: no kernel for d_code=%d rows=%d key groups=%d value groups=%d mode=%d code=%d",
+                sh.D, sh.R, sh.GK, sh.GV, sh.kmode, sh.code);
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t kvb_decode_plan(const kvb_cache* c, int n_ctas, int32_t* plan_out, int64_t plan_capacity) {
+    if (!c || n_ctas <= 0) return -1;
+    Plan P;
+    build_plan(c, std::min(n_ctas, kvb::DEC_MAX_CTAS), P);
+    const int64_t need = 3 + (P.n_ctas + 1) + 4 * int64_t(P.n_pieces) + (P.n_heads + 1);
+    if (plan_out && plan_capacity >= need) {
+        int64_t o = 0;
+        plan_out[o++] = P.n_ctas;
+        plan_out[o++] = P.n_pieces;
+        plan_out[o++] = P.n_heads;
+        for (int v : P.cta_begin) plan_out[o++] = v;
+        for (int v : P.piece) plan_out[o++] = v;
+        for (int v : P.head_begin) plan_out[o++] = v;
+    }
+    return need;
+}
+
+size_t kvb_decode_workspace_size(const kvb_cache* c, int Hq, int Tq, int n_ctas) {
+    DecodeShape sh{};
+    if (validate_cache(c, sh, Hq, Tq)) return 0;
+    Plan P;
+    build_plan(c, resolve_ctas(n_ctas), P);
+    return ws_layout(c, sh, P.n_pieces).total;
+}
+
+kvb_status kvb_decode(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                      const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    return kvb_decode_events(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, n_ctas, workspace, workspace_bytes,
+                             stream, nullptr, nullptr);
+}
+
+kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                             const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* workspace,
+                             size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end) {
+    DecodeShape sh{};
+    kvb_status st = validate_cache(c, sh, Hq, Tq);
+    if (st) return st;
+    if (!q || !out || !workspace) return fail(KVB_EINVAL, "decode: null q / out / workspace");
+    if (q_dtype != KVB_F32 && q_dtype != KVB_F16 && q_dtype != KVB_BF16) return fail(KVB_EINVAL, "decode: q dtype");
+    if (out_dtype != KVB_F32 && out_dtype != KVB_F16 && out_dtype != KVB_BF16) return fail(KVB_EINVAL, "decode: out dtype");
+    if (c->n_exact > c->n0 && !qpos) return fail(KVB_EINVAL, "decode: qpos needed for appended exact rows");
+    if (c->n_exact > 0 && c->exact_dtype != q_dtype) return fail(KVB_EINVAL, "decode: exact rows must have q's dtype");
+    if (!aligned(workspace, 256)) return fail(KVB_EINVAL, "decode: workspace must be 256-byte aligned");
+    const int nct = resolve_ctas(n_ctas);
+    Plan P;
+    build_plan(c, nct, P);
+    if (P.n_pieces > kvb::DEC_MAX_PIECES) return fail(KVB_EUNSUPPORTED, "decode: %d pieces > %d", P.n_pieces, kvb::DEC_MAX_PIECES);
+    if (P.n_heads > kvb::MERGE_MAX_HEADS) return fail(KVB_EUNSUPPORTED, "decode: too many heads");
+    const WsLayout W = ws_layout(c, sh, P.n_pieces);
+    if (workspace_bytes < W.total) return fail(KVB_EINVAL, "decode: workspace %zu < %zu bytes", workspace_bytes, W.total);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* qp = reinterpret_cast<float*>(ws + W.qp);
+    float* part = reinterpret_cast<float*>(ws + W.part);
+    const int rep = Hq / c->Hkv;
+
+    // 1. prologue
+    kvb::PrologueParams pp{q, q_dtype, c->B, c->Hkv, Hq, Tq, rep, rep * Tq, c->d, c->d_code,
+                           c->code_kind == KVB_CODE_MIDRISE ? c->d_code
+                                                            : (c->k_mode == KVB_K_PER_TOKEN ? c->k_group : c->d_code),
+                           scaling, c->qmap, c->mu_k, qp, W.qp_stride};
+    const size_t psm = size_t(sh.R) * (c->d + c->d_code) * 4;
+    const unsigned heads = unsigned(c->B * c->Hkv);
+#define KVB_PRO(T_)                                                                        \
+    if (sh.R == 4) kvb::decode_prologue<T_, 4><<<heads, 128, psm, s>>>(pp);               \
+    else kvb::decode_prologue<T_, 8><<<heads, 128, psm, s>>>(pp);
+    if (q_dtype == KVB_F32) { KVB_PRO(float) }
+    else if (q_dtype == KVB_F16) { KVB_PRO(__half) }
+    else { KVB_PRO(__nv_bfloat16) }
+#undef KVB_PRO
+    if ((st = launch_check("decode_prologue"))) return st;
+
+    // 2. main
+    if (P.n_pieces > 0) {
+        static thread_local kvb::DecodeParams dp;
+        std::memset(&dp, 0, sizeof(dp));
+        dp.B = c->B;
+        dp.Hkv = c->Hkv;
+        dp.R_act = rep * Tq;
+        dp.k_group = c->k_group;
+        dp.n_strata = c->n_strata;
+        dp.qp_stride = W.qp_stride;
+        for (int i = 0; i < c->n_strata; ++i) {
+            const kvb_stratum& sd = c->strata[i];
+            dp.st[i] = kvb::StratumDev{sd.kbits, sd.vbits, P.tok[i], 0, sd.n, sd.n_alloc, sd.kc, sd.vc, sd.kmeta, sd.vmeta};
+        }
+        dp.qp = qp;
+        dp.part = part;
+        dp.n_pieces = P.n_pieces;
+        for (int i = 0; i <= P.n_ctas; ++i) dp.cta_begin[i] = P.cta_begin[i];
+        for (int i = 0; i < P.n_pieces; ++i)
+            dp.piece[i] = make_int4(P.piece[4 * i], P.piece[4 * i + 1], P.piece[4 * i + 2], P.piece[4 * i + 3]);
+        if (ev_begin && (st = cuda_check(cudaEventRecord(static_cast<cudaEvent_t>(ev_begin), s), "record event")))
+            return st;
+        if ((st = dispatch_main(sh, c, P, dp, s))) return st;
+        if (ev_end && (st = cuda_check(cudaEventRecord(static_cast<cudaEvent_t>(ev_end), s), "record event")))
+            return st;
+    }
+
+    // 3. merge
+    static thread_local kvb::MergeParams mp;
+    std::memset(&mp, 0, sizeof(mp));
+    mp.B = c->B;
+    mp.Hkv = c->Hkv;
+    mp.Hq = Hq;
+    mp.Tq = Tq;
+    mp.rep = rep;
+    mp.R_act = rep * Tq;
+    mp.R = sh.R;
+    mp.d = c->d;
+    mp.d_code = c->d_code;
+    mp.out_dtype = out_dtype == KVB_F32 ? 0 : out_dtype == KVB_F16 ? 1 : 2;
+    mp.q_dtype = q_dtype;
+    mp.exact_dtype = c->exact_dtype;
+    mp.scaling = scaling;
+    mp.part = part;
+    mp.q = q;
+    mp.k_exact = c->k_exact;
+    mp.v_exact = c->v_exact;
+    mp.exact_cap = c->exact_cap;
+    mp.n_exact = c->n_exact;
+    mp.n0 = c->n0;
+    mp.pos0 = c->pos0;
+    for (int t = 0; t < Tq; ++t) mp.qpos[t] = qpos ? qpos[t] : 0;
+    mp.lift = c->lift;
+    mp.mu_v = c->mu_v;
+    mp.out = out;
+    for (int h = 0; h <= P.n_heads; ++h) mp.head_begin[h] = P.head_begin[h];
+    const int Ra = rep * Tq;
+    const size_t msm = size_t(Ra) * (2 * c->d + c->d_code) * 4 + 3 * Ra * 4 + 256 * 4;
+#define KVB_MERGE(T_)                                                                       \
+    kvb::decode_merge<T_, T_><<<heads, 256, msm, s>>>(mp);
+    if (q_dtype == KVB_F32) { KVB_MERGE(float) }
+    else if (q_dtype == KVB_F16) { KVB_MERGE(__half) }
+    else { KVB_MERGE(__nv_bfloat16) }
+#undef KVB_MERGE
+    return launch_check("decode_merge");
+}
+
+}  // extern "C"

@@ -1,0 +1,181 @@
+// kvb_select.cuh - K2: importance energy, radix rank split and index compaction.
+//
+// rank_split: one CTA (1024 threads) per row.  For every class boundary R_k (cumulative counts)
+// an MSB-first radix select (8-bit digits over an order-preserving unsigned image of the key)
+// finds the key tau_k of rank R_k - 1 and how many keys equal to tau_k still belong above the
+// boundary.  A final pass in index order classifies every element (key > tau_k, or key == tau_k
+// and among the first `need_k` equal keys by index) and compacts each class's indices in
+// ascending order with warp ballots + a block scan.  Ties therefore go to the LOWER index, the
+// rule the oracle uses (a stable descending sort); the reference's torch.topk leaves it open
+// (STRATA_KV.py:1023).
+#pragma once
+#include "kvb_common.cuh"
+
+namespace kvb {
+
+constexpr int SEL_THREADS = 1024;
+constexpr int SEL_MAX_CLASSES = 4;
+
+// Order-preserving unsigned image of a key (larger key -> larger image); -0.0 maps like +0.0.
+__device__ __forceinline__ uint64_t order_key(float v) {
+    if (v == 0.f) v = 0.f;
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return u;
+}
+__device__ __forceinline__ uint64_t order_key(double v) {
+    if (v == 0.0) v = 0.0;
+    uint64_t u = static_cast<uint64_t>(__double_as_longlong(v));
+    return (u & 0x8000000000000000ull) ? ~u : (u | 0x8000000000000000ull);
+}
+
+struct RankSplitParams {
+    const void* keys;
+    int64_t rows, n, key_stride;
+    int n_classes;
+    int64_t counts[SEL_MAX_CLASSES];
+    int64_t* out[SEL_MAX_CLASSES];
+    int64_t out_stride[SEL_MAX_CLASSES];
+};
+
+// Block-wide exclusive scan of up to 8 flag vectors at once (one bit per vector in `bits`).
+// Returns per-vector exclusive prefixes in pre[] and totals in tot[].
+template <int NV>
+__device__ __forceinline__ void block_scan_flags(uint32_t bits, int* pre, int* tot, int* s_cnt) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t lt = (1u << lane) - 1u;
+    int in_warp[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+        const uint32_t b = __ballot_sync(0xffffffffu, (bits >> v) & 1u);
+        in_warp[v] = __popc(b & lt);
+        if (lane == 0) s_cnt[v * 32 + warp] = __popc(b);
+    }
+    __syncthreads();
+    if (warp < NV) {
+        const int c = s_cnt[warp * 32 + lane];
+        int x = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        s_cnt[warp * 32 + lane] = x - c;                        // exclusive warp offsets
+        if (lane == 31) s_cnt[NV * 32 + warp] = x;              // total
+    }
+    __syncthreads();
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+        pre[v] = s_cnt[v * 32 + warp] + in_warp[v];
+        tot[v] = s_cnt[NV * 32 + v];
+    }
+    __syncthreads();
+}
+
+template <typename K>
+__global__ void __launch_bounds__(SEL_THREADS) rank_split_kernel(const RankSplitParams p) {
+    __shared__ int s_hist[256];
+    __shared__ int s_cnt[9 * 32 + 8];
+    __shared__ uint64_t s_tau[SEL_MAX_CLASSES];
+    __shared__ int64_t s_need[SEL_MAX_CLASSES];
+    __shared__ int s_digit;
+    __shared__ int64_t s_rem;
+    const int64_t row = blockIdx.x;
+    const K* keys = static_cast<const K*>(p.keys) + row * p.key_stride;
+    const int nb = p.n_classes - 1;                  // boundaries
+    constexpr int NBITS = sizeof(K) * 8;
+
+    // ---- radix select of every boundary ----
+    int64_t cum = 0;
+    for (int k = 0; k < nb; ++k) {
+        cum += p.counts[k];
+        if (cum <= 0 || cum > p.n) {                 // boundary outside the row: everything on one side
+            if (threadIdx.x == 0) {
+                s_tau[k] = cum <= 0 ? ~0ull : 0ull;
+                s_need[k] = cum <= 0 ? 0 : p.n;      // all keys "equal-or-above" when cum >= n
+            }
+            __syncthreads();
+            continue;
+        }
+        uint64_t prefix = 0, mask = 0;
+        int64_t rem = cum;                           // rank (1-based, descending) still to locate
+        for (int shift = NBITS - 8; shift >= 0; shift -= 8) {
+            for (int i = threadIdx.x; i < 256; i += blockDim.x) s_hist[i] = 0;
+            __syncthreads();
+            for (int64_t i = threadIdx.x; i < p.n; i += blockDim.x) {
+                const uint64_t u = order_key(keys[i]);
+                if ((u & mask) == prefix) atomicAdd(&s_hist[(u >> shift) & 255], 1);
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                int64_t acc = 0;
+                int dsel = 0;
+                for (int dg = 255; dg >= 0; --dg) {
+                    if (acc + s_hist[dg] >= rem) { dsel = dg; break; }
+                    acc += s_hist[dg];
+                }
+                s_digit = dsel;
+                s_rem = rem - acc;
+            }
+            __syncthreads();
+            prefix |= uint64_t(s_digit) << shift;
+            mask |= uint64_t(255) << shift;
+            rem = s_rem;
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) {
+            s_tau[k] = prefix;
+            s_need[k] = rem;                         // equal keys (lowest indices) inside the boundary
+        }
+        __syncthreads();
+    }
+
+    // ---- classify in index order and compact ----
+    int64_t eq_seen[SEL_MAX_CLASSES] = {0, 0, 0, 0};
+    int64_t cls_off[SEL_MAX_CLASSES] = {0, 0, 0, 0};
+    for (int64_t base = 0; base < p.n; base += blockDim.x) {
+        const int64_t i = base + threadIdx.x;
+        const bool valid = i < p.n;
+        const uint64_t u = valid ? order_key(keys[valid ? i : 0]) : 0;
+        uint32_t eqbits = 0;
+        for (int k = 0; k < nb; ++k)
+            if (valid && u == s_tau[k]) eqbits |= 1u << k;
+        int pre[SEL_MAX_CLASSES], tot[SEL_MAX_CLASSES];
+        block_scan_flags<SEL_MAX_CLASSES>(eqbits, pre, tot, s_cnt);
+        int cls = 0;
+        for (int k = 0; k < nb; ++k) {
+            bool in;
+            if (s_tau[k] == ~0ull && s_need[k] == 0) in = false;               // empty upper part
+            else if (s_tau[k] == 0ull && s_need[k] == p.n) in = true;          // everything inside
+            else in = u > s_tau[k] || (u == s_tau[k] && eq_seen[k] + pre[k] < s_need[k]);
+            if (!in) ++cls;
+        }
+        for (int k = 0; k < nb; ++k) eq_seen[k] += tot[k];
+        uint32_t cbits = valid ? (1u << cls) : 0u;
+        int cpre[SEL_MAX_CLASSES], ctot[SEL_MAX_CLASSES];
+        block_scan_flags<SEL_MAX_CLASSES>(cbits, cpre, ctot, s_cnt);
+        if (valid && p.out[cls]) p.out[cls][row * p.out_stride[cls] + cls_off[cls] + cpre[cls]] = i;
+        for (int c = 0; c < SEL_MAX_CLASSES; ++c) cls_off[c] += ctot[c];
+    }
+}
+
+// Per-token sum of squares in float64.  One warp per token row.
+template <typename T>
+__global__ void key_energy_kernel(const T* k, int64_t B, int64_t H, int64_t T_, int64_t d, int64_t sb, int64_t sh,
+                                  int64_t st, double* out) {
+    const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= B * H * T_) return;
+    const int64_t b = row / (H * T_), h = (row / T_) % H, t = row % T_;
+    const T* x = k + b * sb + h * sh + t * st;
+    double s = 0.0;
+    for (int64_t c = lane; c < d; c += 32) {
+        const double v = double(to_f32(x[c]));
+        s += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) out[row] = s;
+}
+
+}  // namespace kvb

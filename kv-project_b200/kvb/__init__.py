@@ -1,0 +1,15 @@
+"""kvb - B200-native (sm_100a) packed-KV decode path.
+
+Drop-in native replacement for the decode-time hot path shared by the KV-cache compression
+methods of TahirSher/KV-Project: quantise + pack (K1), importance scores + budgeted eviction /
+strata assignment (K2), fused split-K flash decoding over packed codes (K3) and the spectral code
+(K4).  All compute runs in ``libkvb.so`` (hand-written CUDA for sm_100a behind the C ABI of
+``include/kvb.h``); this package only moves tensors and builds descriptors.
+"""
+
+from . import _lib, ops, cache, workloads          # noqa: F401
+from .ops import (PackedCache, quant_pack, key_energy, rank_split, query_scores, decode, decode_plan,  # noqa: F401
+                  device_status, UNIFORM_STEP)
+
+__all__ = ["ops", "cache", "workloads", "PackedCache", "quant_pack", "key_energy", "rank_split",
+           "query_scores", "decode", "decode_plan", "device_status", "UNIFORM_STEP"]

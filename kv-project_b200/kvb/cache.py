@@ -1,0 +1,73 @@
+"""Cache builders: from model-dtype K / V to packed, head-synchronous caches (all on the GPU).
+
+  build_mixed     config 1: per-token importance = key energy, head-synchronous 8 / 4 / 2-bit
+                  strata (10 % / 30 % / 60 %), KIVI per-token groups for keys and values
+                  (kivi_quant(..., along_tokens=False) per stratum, STRATA_KV.py:826).
+  build_kivi      configs 0 / 4: KIVI keys per channel over token groups, values per token
+                  (KIVIMethod.entries, STRATA_KV.py:797-803).
+  build_eviction  config 2: SnapKV-style scores of decode queries, top-`budget` heavy hitters +
+                  recent window, KIVI codes of the kept tokens (SnapKVQuantMethod.entries,
+                  STRATA_KV.py:1010-1033).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+def strata_counts(T: int, tenths8: int = 1, tenths4: int = 3):
+    n8 = (T * tenths8) // 10
+    n4 = (T * tenths4) // 10
+    return n8, n4, T - n8 - n4
+
+
+def build_mixed(K: torch.Tensor, V: torch.Tensor, group: int = 64, tenths=(1, 3)):
+    B, H, T, d = K.shape
+    n8, n4, _ = strata_counts(T, *tenths)
+    imp = ops.key_energy(K)
+    i8, i4, i2 = ops.rank_split(imp, [n8, n4])
+    cache = ops.PackedCache(B, H, d, k_group=group, v_group=group)
+    sets = {}
+    for bits, idx in ((8, i8), (4, i4), (2, i2)):
+        if idx is None:
+            continue
+        kq = ops.quant_pack(K, bits, group, idx=idx)
+        vq = ops.quant_pack(V, bits, group, idx=idx)
+        cache.add_stratum(kq, vq)
+        sets[bits] = idx
+    return cache, sets
+
+
+def build_kivi(K: torch.Tensor, V: torch.Tensor, kbits: int, vbits: int, kgroup: int, vgroup: int,
+               n_sink: int = 0):
+    """Keys per channel over `kgroup` tokens, values per token over `vgroup` channels; rows before
+    n_sink become exact rows of the cache."""
+    B, H, T, d = K.shape
+    n = T - n_sink
+    kq = ops.quant_pack(K, kbits, kgroup, per_channel=True, first_row=n_sink, n=n)
+    vq = ops.quant_pack(V, vbits, vgroup, first_row=n_sink, n=n, n_alloc=kq["n_alloc"])
+    cache = ops.PackedCache(B, H, d, per_channel=True, k_group=kgroup, v_group=vgroup)
+    cache.add_stratum(kq, vq)
+    if n_sink:
+        cache.set_exact(K[:, :, :n_sink], V[:, :, :n_sink])
+    return cache
+
+
+def build_eviction(q_obs: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scaling: float, budget: int,
+                   window: int, bits: int = 4, group: int = 64, pool: int = 0):
+    """Heavy hitters by accumulated decode-query attention over [0, T - window), plus the window;
+    kept tokens (position order) stored with KIVI codes: keys per channel over `group` kept tokens,
+    values per token over `group` channels.  Returns (cache, kept idx (B, H, budget + window))."""
+    B, H, T, d = K.shape
+    n_cand = T - window
+    sc = ops.query_scores(q_obs, K, scaling, n_cand, pool)
+    top = ops.rank_split(sc, [min(budget, n_cand)], want=[0])[0]
+    win = torch.arange(n_cand, T, device=K.device, dtype=torch.int64).expand(B, H, window)
+    kept = torch.cat([top, win], -1).contiguous()
+    kq = ops.quant_pack(K, bits, group, per_channel=True, idx=kept)
+    vq = ops.quant_pack(V, bits, group, idx=kept, n_alloc=kq["n_alloc"])
+    cache = ops.PackedCache(B, H, d, per_channel=True, k_group=group, v_group=group)
+    cache.add_stratum(kq, vq)
+    return cache, kept, sc

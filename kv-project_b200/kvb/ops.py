@@ -1,0 +1,295 @@
+"""Tensor-level wrappers over the C ABI (include/kvb.h).
+
+PyTorch provides device memory and the current stream; every computation runs in libkvb.so.
+Each wrapper checks shapes / dtypes / devices, passes raw pointers and raises on a non-zero
+status.  No wrapper falls back to another implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float32: L.KVB_F32, torch.float16: L.KVB_F16, torch.bfloat16: L.KVB_BF16, torch.float64: L.KVB_F64}
+
+# MSE-optimal mid-rise steps of N(0, 1) (uniform_step, STRATA_KV.py:1133), by golden-section search
+UNIFORM_STEP = {2: 0.9956803260610909, 3: 0.5860196721213176, 4: 0.33520647283490446, 8: 0.030762719123913013}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise ValueError(f"kvb: unsupported dtype {t.dtype}") from None
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("kvb: tensors must live on a CUDA device")
+
+
+def round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+# ------------------------------------------------------------------------------------------------
+# K1: quantise + pack
+# ------------------------------------------------------------------------------------------------
+def quant_pack(x: torch.Tensor, bits: int, group: int, *, per_channel: bool = False, midrise: bool = False,
+               idx: torch.Tensor = None, first_row: int = 0, n: int = None, n_alloc: int = None,
+               want_xhat: bool = False, step: float = None) -> dict:
+    """Quantise rows of x (B, H, T, d) and planar-pack them.
+
+    Rows: idx (B, H, n) int64 gathers source rows; otherwise rows first_row .. first_row + n - 1.
+    per_channel: KIVI keys (min / max per channel over `group` stored rows); else per-token groups
+    of `group` channels (KIVI values / the mixed strata), or, with midrise, the STRATA code.
+    Returns codes (B, H, n_alloc, d * bits / 8) uint8, meta (fp16 pairs / scales as documented in
+    kvb.h), n, n_alloc, optional xhat (B, H, n, d) float32."""
+    _cuda(x, idx)
+    if x.dim() != 4 or x.stride(-1) != 1:
+        raise ValueError("quant_pack: x must be (B, H, T, d) with unit channel stride")
+    B, H, T, d = x.shape
+    if idx is not None:
+        if idx.dtype != torch.int64 or idx.shape[:2] != (B, H):
+            raise ValueError("quant_pack: idx must be int64 (B, H, n)")
+        idx = idx.contiguous()
+        n = idx.shape[2]
+    elif n is None:
+        n = T - first_row
+    align = max(16, group if per_channel else 16)
+    n_alloc = round_up(max(n, 1), align) if n_alloc is None else n_alloc
+    rb = d * bits // 8
+    codes = torch.empty((B, H, n_alloc, rb), dtype=torch.uint8, device=x.device)
+    if midrise:
+        meta = torch.empty((B, H, n_alloc), dtype=torch.float16, device=x.device)
+    elif per_channel:
+        meta = torch.empty((B, H, n_alloc // group, d, 2), dtype=torch.float16, device=x.device)
+    else:
+        width = group if d % group == 0 else d
+        meta = torch.empty((B, H, n_alloc, d // width, 2), dtype=torch.float16, device=x.device)
+    xhat = torch.empty((B, H, n, d), dtype=torch.float32, device=x.device) if want_xhat else None
+    st = UNIFORM_STEP[bits] if (midrise and step is None) else (step or 0.0)
+    L.check(L.lib().kvb_quant_pack(
+        _ptr(x), dtype_code(x), B, H, T, d, x.stride(0), x.stride(1), x.stride(2),
+        _ptr(idx), first_row, n, n_alloc, bits, group if not midrise else d,
+        L.KVB_K_PER_CHANNEL if per_channel else L.KVB_K_PER_TOKEN,
+        L.KVB_CODE_MIDRISE if midrise else L.KVB_CODE_ASYM, C.c_float(st),
+        _ptr(codes), _ptr(meta), _ptr(xhat), C.c_void_p(_stream(x.device))), "kvb_quant_pack")
+    return {"codes": codes, "meta": meta, "xhat": xhat, "n": n, "n_alloc": n_alloc, "bits": bits, "group": group}
+
+
+# ------------------------------------------------------------------------------------------------
+# K2: importance, rank split, scores
+# ------------------------------------------------------------------------------------------------
+def key_energy(k: torch.Tensor) -> torch.Tensor:
+    """sum_c k_c^2 per token in float64, (B, H, T)."""
+    _cuda(k)
+    B, H, T, d = k.shape
+    if k.stride(-1) != 1:
+        raise ValueError("key_energy: unit channel stride required")
+    out = torch.empty((B, H, T), dtype=torch.float64, device=k.device)
+    L.check(L.lib().kvb_key_energy(_ptr(k), dtype_code(k), B, H, T, d, k.stride(0), k.stride(1), k.stride(2),
+                                   _ptr(out), C.c_void_p(_stream(k.device))), "kvb_key_energy")
+    return out
+
+
+def rank_split(keys: torch.Tensor, counts, want=None):
+    """keys (..., n) float32 / float64.  Class c gets ranks [sum(counts[:c]), sum(counts[:c+1])) by
+    key descending (ties: lower index first); the last class gets the rest.  Returns one int64
+    tensor (..., count_c) per class (ascending indices); classes not in `want` are None."""
+    _cuda(keys)
+    if keys.dtype not in (torch.float32, torch.float64):
+        raise ValueError("rank_split: keys must be float32 or float64")
+    if torch.isnan(keys).any():
+        raise ValueError("rank_split: NaN keys")
+    lead, n = keys.shape[:-1], keys.shape[-1]
+    k2 = keys.reshape(-1, n)
+    if k2.stride(-1) != 1:
+        k2 = k2.contiguous()
+    rows = k2.shape[0]
+    counts = [int(c) for c in counts]
+    if any(c < 0 for c in counts) or sum(counts) > n:
+        raise ValueError("rank_split: counts must be >= 0 and sum to <= n")
+    sizes = counts + [n - sum(counts)]
+    ncls = len(sizes)
+    want = set(range(ncls)) if want is None else set(want)
+    outs = [torch.empty((rows, s), dtype=torch.int64, device=keys.device) if (c in want and s > 0) else None
+            for c, s in enumerate(sizes)]
+    cnt = (C.c_int64 * 4)(*(counts + [0] * (4 - len(counts))))
+    ptrs = (C.c_void_p * 4)(*[(o.data_ptr() if o is not None else None) for o in outs] + [None] * (4 - ncls))
+    strides = (C.c_int64 * 4)(*[(o.stride(0) if o is not None else 0) for o in outs] + [0] * (4 - ncls))
+    L.check(L.lib().kvb_rank_split(_ptr(k2), dtype_code(k2), rows, n, k2.stride(0), ncls, cnt, ptrs, strides,
+                                   C.c_void_p(_stream(keys.device))), "kvb_rank_split")
+    return [None if o is None else o.reshape(*lead, o.shape[-1]) for o in outs]
+
+
+def query_scores(q: torch.Tensor, k: torch.Tensor, scaling: float, n_cand: int, pool: int = 0) -> torch.Tensor:
+    """Accumulated attention of decode queries (B, Hq, nq, d) over keys (B, Hkv, T, d):
+    (B, Hkv, n_cand) float32 = mean over the group's query heads and queries of softmax(q K^T s)."""
+    _cuda(q, k)
+    if q.dtype != k.dtype or q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("query_scores: q and k must share dtype f16 / bf16")
+    q, k = q.contiguous(), k.contiguous()
+    B, Hq, nq, d = q.shape
+    Hkv, T = k.shape[1], k.shape[2]
+    lib = L.lib()
+    wsb = lib.kvb_scores_workspace_size(B, Hkv, n_cand)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=q.device)
+    out = torch.empty((B, Hkv, n_cand), dtype=torch.float32, device=q.device)
+    L.check(lib.kvb_query_scores(_ptr(q), _ptr(k), dtype_code(q), B, Hq, Hkv, nq, T, d, C.c_float(scaling),
+                                 n_cand, pool, _ptr(out), _ptr(ws), wsb, C.c_void_p(_stream(q.device))),
+            "kvb_query_scores")
+    return out
+
+
+def device_status(clear: bool = True, device=None) -> int:
+    v = C.c_uint(0)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    L.check(L.lib().kvb_device_status(C.byref(v), int(clear), C.c_void_p(_stream(dev))), "kvb_device_status")
+    return v.value
+
+
+# ------------------------------------------------------------------------------------------------
+# K3: decode over a packed cache
+# ------------------------------------------------------------------------------------------------
+class PackedCache:
+    """A head-synchronous packed cache of one layer: up to 4 strata of codes (+ optional exact rows,
+    query map / lift for rotated or spectral codes).  Holds the device tensors and builds the
+    kvb_cache descriptor."""
+
+    def __init__(self, B, Hkv, d, *, d_code=None, midrise=False, per_channel=False, k_group=None, v_group=None):
+        self.B, self.Hkv, self.d = B, Hkv, d
+        self.d_code = d if d_code is None else d_code
+        self.midrise, self.per_channel = midrise, per_channel
+        self.k_group = self.d_code if midrise else k_group
+        self.v_group = self.d_code if midrise else v_group
+        self.strata = []
+        self.k_exact = self.v_exact = None
+        self.n_exact = self.n0 = self.pos0 = 0
+        self.qmap = self.lift = self.mu_k = self.mu_v = None
+        self._ws = {}
+
+    def add_stratum(self, kq: dict, vq: dict):
+        if kq["n"] != vq["n"] or kq["n_alloc"] != vq["n_alloc"]:
+            raise ValueError("key and value codes of a stratum must hold the same tokens")
+        self.strata.append({"kbits": kq["bits"], "vbits": vq["bits"], "n": kq["n"], "n_alloc": kq["n_alloc"],
+                            "kc": kq["codes"], "vc": vq["codes"], "km": kq["meta"], "vm": vq["meta"]})
+        return self
+
+    def set_exact(self, K, V, n_exact=None, n0=None, pos0=0):
+        self.k_exact, self.v_exact = K.contiguous(), V.contiguous()
+        self.n_exact = K.shape[2] if n_exact is None else n_exact
+        self.n0 = self.n_exact if n0 is None else n0
+        self.pos0 = pos0
+        return self
+
+    def struct(self) -> L.Cache:
+        c = L.Cache()
+        c.B, c.Hkv, c.d, c.d_code = self.B, self.Hkv, self.d, self.d_code
+        c.code_kind = L.KVB_CODE_MIDRISE if self.midrise else L.KVB_CODE_ASYM
+        c.k_mode = L.KVB_K_PER_CHANNEL if self.per_channel else L.KVB_K_PER_TOKEN
+        c.k_group = int(self.k_group or self.d_code)
+        c.v_group = int(self.v_group or self.d_code)
+        c.n_strata = len(self.strata)
+        for i, s in enumerate(self.strata):
+            c.strata[i].kbits, c.strata[i].vbits = s["kbits"], s["vbits"]
+            c.strata[i].n, c.strata[i].n_alloc = s["n"], s["n_alloc"]
+            c.strata[i].kc, c.strata[i].vc = s["kc"].data_ptr(), s["vc"].data_ptr()
+            c.strata[i].kmeta, c.strata[i].vmeta = s["km"].data_ptr(), s["vm"].data_ptr()
+        if self.k_exact is not None and self.n_exact > 0:
+            c.k_exact, c.v_exact = self.k_exact.data_ptr(), self.v_exact.data_ptr()
+            c.exact_dtype = dtype_code(self.k_exact)
+            c.exact_cap = self.k_exact.shape[2]
+            c.n_exact, c.n0, c.pos0 = self.n_exact, self.n0, self.pos0
+        for name in ("qmap", "lift", "mu_k", "mu_v"):
+            t = getattr(self, name)
+            setattr(c, name, None if t is None else t.data_ptr())
+        return c
+
+    def stored_bytes(self) -> int:
+        """Bytes of every stored tensor a decode step reads (codes + metadata + exact rows)."""
+        tot = 0
+        for s in self.strata:
+            n = s["n"]
+            tot += n * (s["kc"].shape[-1] + s["vc"].shape[-1]) * self.B * self.Hkv
+            for m in ("km", "vm"):
+                t = s[m]
+                if t.dim() == 5 and m == "km" and self.per_channel:
+                    tot += self.B * self.Hkv * (-(-n // self.k_group)) * t.shape[3] * 4
+                else:
+                    tot += t[:, :, :n].numel() * t.element_size()
+        if self.n_exact:
+            tot += 2 * self.B * self.Hkv * self.n_exact * self.d * self.k_exact.element_size()
+        return tot
+
+    def workspace(self, Hq, Tq, n_ctas=0):
+        key = (Hq, Tq, n_ctas)
+        if key not in self._ws:
+            c = self.struct()
+            size = L.lib().kvb_decode_workspace_size(C.byref(c), Hq, Tq, n_ctas)
+            if size == 0:
+                L.check(L.KVB_EINVAL, "kvb_decode_workspace_size")
+            dev = self.strata[0]["kc"].device if self.strata else self.k_exact.device
+            self._ws[key] = torch.empty(size, dtype=torch.uint8, device=dev)
+        return self._ws[key]
+
+
+def decode(cache: PackedCache, q: torch.Tensor, scaling: float, qpos=None, out=None, out_dtype=None,
+           n_ctas: int = 0, events=None) -> torch.Tensor:
+    """Decode attention of q (B, Hq, Tq, d) over the packed cache -> (B, Tq, Hq, d).
+    events: optional (begin, end) torch.cuda.Event pair (already created, e.g. recorded once)
+    recorded around the main split-K kernel on the current stream."""
+    _cuda(q)
+    q = q.contiguous()
+    B, Hq, Tq, d = q.shape
+    if B != cache.B or d != cache.d:
+        raise ValueError("decode: q shape does not match the cache")
+    odt = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty((B, Tq, Hq, d), dtype=odt, device=q.device)
+    ws = cache.workspace(Hq, Tq, n_ctas)
+    c = cache.struct()
+    qp = None
+    if qpos is not None:
+        qp = (C.c_int64 * Tq)(*[int(v) for v in qpos])
+    if events is None:
+        L.check(L.lib().kvb_decode(C.byref(c), _ptr(q), dtype_code(q), Hq, Tq, C.c_float(scaling), qp, _ptr(out),
+                                   dtype_code(out), n_ctas, _ptr(ws), ws.numel(), C.c_void_p(_stream(q.device))),
+                "kvb_decode")
+    else:
+        e0, e1 = (C.c_void_p(e.cuda_event) for e in events)
+        L.check(L.lib().kvb_decode_events(C.byref(c), _ptr(q), dtype_code(q), Hq, Tq, C.c_float(scaling), qp,
+                                          _ptr(out), dtype_code(out), n_ctas, _ptr(ws), ws.numel(),
+                                          C.c_void_p(_stream(q.device)), e0, e1), "kvb_decode_events")
+    return out
+
+
+def decode_plan(cache: PackedCache, n_ctas: int):
+    """The split-K plan (host computation): dict with cta_begin, pieces (head, stratum, lo, hi), head_begin."""
+    c = cache.struct()
+    lib = L.lib()
+    need = lib.kvb_decode_plan(C.byref(c), n_ctas, None, 0)
+    buf = (C.c_int32 * need)()
+    lib.kvb_decode_plan(C.byref(c), n_ctas, buf, need)
+    v = list(buf)
+    nc, npc, nh = v[0], v[1], v[2]
+    o = 3
+    cta_begin = v[o:o + nc + 1]
+    o += nc + 1
+    pieces = [tuple(v[o + 4 * i:o + 4 * i + 4]) for i in range(npc)]
+    o += 4 * npc
+    head_begin = v[o:o + nh + 1]
+    return {"n_ctas": nc, "cta_begin": cta_begin, "pieces": pieces, "head_begin": head_begin}
