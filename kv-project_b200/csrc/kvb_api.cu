@@ -263,12 +263,13 @@ struct DecodeShape {
     int D, R, GK, GV, kmode, code;
 };
 
+// Tokens per chunk (one pipeline stage): a multiple of 12 tiles x 16 tokens (every one of the 12
+// warps gets the same number of tiles), about 48 KB of codes, at most 768 tokens.
 int tokens_per_chunk(int D, int kbits, int vbits) {
     const int rb = D * kbits / 8 + D * vbits / 8;
-    int tok = 32768 / rb;
-    int p2 = 128;
-    while (p2 * 2 <= tok && p2 < 512) p2 *= 2;
-    return p2;
+    const int unit = kvb::DEC_CWARPS * 16;
+    const int m = std::max(1, 49152 / (unit * rb));
+    return std::min(unit * m, 4 * unit);
 }
 
 kvb_status validate_cache(const kvb_cache* c, DecodeShape& sh, int Hq, int Tq) {
@@ -564,10 +565,19 @@ kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int
         for (int i = 0; i <= P.n_ctas; ++i) dp.cta_begin[i] = P.cta_begin[i];
         for (int i = 0; i < P.n_pieces; ++i)
             dp.piece[i] = make_int4(P.piece[4 * i], P.piece[4 * i + 1], P.piece[4 * i + 2], P.piece[4 * i + 3]);
-        if (ev_begin && (st = cuda_check(cudaEventRecord(static_cast<cudaEvent_t>(ev_begin), s), "record event")))
+        // inside a stream capture the events become external event nodes, so they also fire on replay
+        unsigned ev_flags = cudaEventRecordDefault;
+        if (ev_begin || ev_end) {
+            cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+            if ((st = cuda_check(cudaStreamIsCapturing(s, &cs), "capture status"))) return st;
+            if (cs == cudaStreamCaptureStatusActive) ev_flags = cudaEventRecordExternal;
+        }
+        if (ev_begin && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_begin), s, ev_flags),
+                                         "record event")))
             return st;
         if ((st = dispatch_main(sh, c, P, dp, s))) return st;
-        if (ev_end && (st = cuda_check(cudaEventRecord(static_cast<cudaEvent_t>(ev_end), s), "record event")))
+        if (ev_end && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_end), s, ev_flags),
+                                       "record event")))
             return st;
     }
 

@@ -49,6 +49,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// Order this thread's earlier generic-proxy shared-memory accesses before later async-proxy
+// (bulk copy) accesses to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -131,6 +137,14 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t v) {
 // 1024 + c * 2^m.  The decode kernel keeps m >= 4 for the 2- and 4-bit codes (so the 1024 offset
 // costs few bits of fp32 accumulation precision) and folds 2^m and the offset into the query.
 constexpr uint32_t kMagic = 0x64006400u;
+
+// (x & mask) | kMagic as one LOP3 (LUT 0xEA = (a & b) | c).
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t and_or_magic(uint32_t x) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(x), "n"(MASK), "r"(kMagic));
+    return d;
+}
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);

@@ -64,7 +64,7 @@ def _plan(c, n_ctas):
     return cta_begin, pieces, head_begin
 
 
-TOK = {(8, 8): 128, (4, 4): 256, (2, 2): 512, (4, 2): 256}
+TOK = {(8, 8): 192, (4, 4): 384, (2, 2): 768, (4, 2): 384}
 
 
 @pytest.mark.parametrize("B,H,T,n_ctas", [(8, 8, 32768, 148), (1, 8, 4096, 148), (2, 2, 300, 148), (8, 8, 32768, 7)])

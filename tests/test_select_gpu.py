@@ -39,8 +39,9 @@ def test_topk_float32(cuda_dev, n, k):
     gen = torch.Generator().manual_seed(n + k)
     s = torch.rand(3, n, generator=gen)
     s[:, ::7] = 0.5                                                       # ties
-    s[0, 1] = -0.0
-    s[1, 2] = -1e-30
+    if n > 2:
+        s[0, 1] = -0.0
+        s[1, 2] = -1e-30
     top = kvb.rank_split(s.to(cuda_dev), [k], want=[0])[0]
     ref = O.topk_kept(s.numpy(), k)
     if k == 0:
