@@ -265,12 +265,7 @@ struct DecodeShape {
 
 // Tokens per chunk (one pipeline stage): a multiple of 12 tiles x 16 tokens (every one of the 12
 // warps gets the same number of tiles), about 48 KB of codes, at most 768 tokens.
-int tokens_per_chunk(int D, int kbits, int vbits) {
-    const int rb = D * kbits / 8 + D * vbits / 8;
-    const int unit = kvb::DEC_CWARPS * 16;
-    const int m = std::max(1, 49152 / (unit * rb));
-    return std::min(unit * m, 4 * unit);
-}
+int tokens_per_chunk(int D, int kbits, int vbits) { return kvb::chunk_tokens(D, kbits, vbits); }
 
 kvb_status validate_cache(const kvb_cache* c, DecodeShape& sh, int Hq, int Tq) {
     if (!c) return fail(KVB_EINVAL, "decode: null cache");

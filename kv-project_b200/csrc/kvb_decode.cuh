@@ -292,6 +292,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
             const StageLay L = stage_lay<D, R, GK, GV, KMODE, CODE>(KB, VB, sd.tok, p.k_group);
             typename TL::Ctx X;
             TL::build_ctx(X, qp, lane);
+            const typename TL::Off O = TL::lane_off(L, lane);
+            constexpr int TOK = chunk_tokens(D, KB, VB);
+            constexpr int PW = TOK / 16 / DEC_CWARPS;            // tiles per warp in a full chunk
             WarpState<C> S;
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
@@ -317,16 +320,27 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
                     const int64_t tok0 = int64_t(ch) * sd.tok;
                     const int ntok = int(imin64(sd.tok, sd.n - tok0));
                     const int ntiles = (ntok + 15) >> 4;
-                    const uint8_t* st = stages + size_t(s) * p.stage_bytes;
-                    for (int tl = warp; tl < ntiles; tl += 2 * DEC_CWARPS) {
-                        const int tl1 = tl + DEC_CWARPS < ntiles ? tl + DEC_CWARPS : -1;
-                        const uint8_t* cf0 = nullptr;
-                        const uint8_t* cf1 = nullptr;
-                        if constexpr (KMODE == KM_CHANNEL) {
-                            cf0 = st + L.km + ((tl * 16) / p.k_group) * C::FRAG_BYTES;
-                            cf1 = st + L.km + ((imax64(tl1, 0) * 16) / p.k_group) * C::FRAG_BYTES;
+                    const uint8_t* st = stages + s * p.stage_bytes;
+                    auto cfp = [&](int tl) -> const uint8_t* {
+                        if constexpr (KMODE == KM_CHANNEL) return st + L.km + ((tl * 16) / p.k_group) * C::FRAG_BYTES;
+                        else return nullptr;
+                    };
+                    if (ntok == TOK && sd.tok == TOK) {
+                        // whole chunk: fixed tile count per warp, no masking
+                        if constexpr (PW == 1) {
+                            TL::template run<true, 1>(S, X, st, O, warp, -1, ntok, lane, cfp(warp), nullptr);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < PW; i += 2) {
+                                const int t0 = warp + DEC_CWARPS * i, t1 = t0 + DEC_CWARPS;
+                                TL::template run<true, 2>(S, X, st, O, t0, t1, ntok, lane, cfp(t0), cfp(t1));
+                            }
                         }
-                        TL::run2(S, X, st, L, tl, tl1, ntok, lane, cf0, cf1);
+                    } else {
+                        for (int tl = warp; tl < ntiles; tl += 2 * DEC_CWARPS) {
+                            const int tl1 = tl + DEC_CWARPS < ntiles ? tl + DEC_CWARPS : -1;
+                            TL::template run<false, 2>(S, X, st, O, tl, tl1, ntok, lane, cfp(tl), cfp(imax64(tl1, 0)));
+                        }
                     }
                 }
                 // release the stage; the last of the 12 warps refills it (acq_rel counter in smem,

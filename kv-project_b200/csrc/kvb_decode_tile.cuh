@@ -106,6 +106,15 @@ struct DecCfg {
     static constexpr int FRAG_BYTES = ((NB * KS * 32 * 8 + 8 * 4 + R * 4) + 15) / 16 * 16;
 };
 
+// Tokens per chunk (one pipeline stage): a multiple of 12 tiles x 16 tokens (every warp gets the
+// same number of tiles), about 48 KB of codes, at most 768 tokens.  Shared by host and device.
+__host__ __device__ constexpr int chunk_tokens(int D, int kbits, int vbits) {
+    const int rb = D * kbits / 8 + D * vbits / 8;
+    const int unit = DEC_CWARPS * 16;
+    const int m = 49152 / (unit * rb) > 1 ? 49152 / (unit * rb) : 1;
+    return unit * m < 4 * unit ? unit * m : 4 * unit;
+}
+
 // Shared-memory layout of one stage for a stratum.
 struct StageLay {
     int kc, vc, km, vm, end;
@@ -227,11 +236,34 @@ struct Tile {
         }
     }
 
-    // Logits (log2 domain) of my two tokens of one tile, rows r0 + e.
-    __device__ static void logits(float (&s2)[2][2], const Ctx& X, const uint8_t* stage, const StageLay& L,
-                                  int base, int lane, const uint8_t* cf) {
+    // Byte offsets (from the stage base) of this lane's rows in tile 0; tile i adds 16 i rows.
+    static constexpr int KMB = CODE == KV_MIDRISE ? 2 : GK * 4;   // key meta bytes per token (per-token mode)
+    static constexpr int VMB = CODE == KV_MIDRISE ? 2 : GV * 4;   // value meta bytes per token
+    struct Off {
+        int kA;                  // key codes of row tA (logical token g), this lane's quarter t
+        int vA;                  // value codes of row t, this lane's slice g
+        int kmA[NKT];            // key meta of row tA for my group of each key n-tile
+        int vmA[NVT];            // value meta of row tA for my group of each value n-tile
+    };
+    __device__ static Off lane_off(const StageLay& L, int lane) {
         const int g = lane >> 2, t = lane & 3;
-        const int tA = (g >> 1) + 4 * (g & 1), tB = tA + 8;          // physical rows of logical g, g + 8
+        const int tA = (g >> 1) + 4 * (g & 1);
+        Off O;
+        O.kA = L.kc + tA * LK::RB + t * (LK::RB / 4);
+        O.vA = L.vc + t * LV::RB + LV::U * g;
+#pragma unroll
+        for (int j = 0; j < NKT; ++j)
+            O.kmA[j] = L.km + tA * KMB + (CODE == KV_MIDRISE ? 0 : C::KC::grp(8 * j + 2 * t) * 4);
+#pragma unroll
+        for (int jv = 0; jv < NVT; ++jv)
+            O.vmA[jv] = L.vm + tA * VMB + (CODE == KV_MIDRISE ? 0 : C::VC::grp(8 * jv + 2 * t) * 4);
+        return O;
+    }
+
+    // Logits (log2 domain) of my two tokens of one tile, rows r0 + e.
+    __device__ static void logits(float (&s2)[2][2], const Ctx& X, const uint8_t* stage, const Off& O, int tile,
+                                  int lane, const uint8_t* cf) {
+        const int t = lane & 3;
         float acc[NKT][NCH][4];
 #pragma unroll
         for (int j = 0; j < NKT; ++j)
@@ -240,9 +272,10 @@ struct Tile {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[j][c][e] = 0.f;
         {
+            const uint8_t* ka = stage + O.kA + tile * (16 * LK::RB);
             uint32_t wa[LK::KW], wb[LK::KW];
-            lds_words<LK::KW>(stage + L.kc + (base + tA) * LK::RB + t * (LK::RB / 4), wa);
-            lds_words<LK::KW>(stage + L.kc + (base + tB) * LK::RB + t * (LK::RB / 4), wb);
+            lds_words<LK::KW>(ka, wa);
+            lds_words<LK::KW>(ka + 8 * LK::RB, wb);
             uint32_t ha[D / 8], hb[D / 8];
 #pragma unroll
             for (int w = 0; w < LK::KW; ++w) {
@@ -290,17 +323,16 @@ struct Tile {
         } else {
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                const int row = base + (hh ? tB : tA);
                 float part[2] = {0.f, 0.f};
 #pragma unroll
                 for (int j = 0; j < NKT; ++j) {
+                    const uint8_t* mp = stage + O.kmA[j] + tile * (16 * KMB) + hh * (8 * KMB);
                     float sc, lo;
                     if constexpr (CODE == KV_MIDRISE) {
-                        sc = __half2float(reinterpret_cast<const __half*>(stage + L.km)[row]);
+                        sc = __half2float(*reinterpret_cast<const __half*>(mp));
                         lo = -0.5f * float((1 << KB) - 1) * sc;
                     } else {
-                        const int gs = C::KC::grp(8 * j + 2 * t);
-                        const float2 f = unpack_half2(reinterpret_cast<const uint32_t*>(stage + L.km)[row * GK + gs]);
+                        const float2 f = unpack_half2(*reinterpret_cast<const uint32_t*>(mp));
                         lo = f.x;
                         sc = f.y;
                     }
@@ -324,27 +356,29 @@ struct Tile {
     }
 
     // Values of one tile: P' fragments from my probabilities, value codes as A, MMA into S.acc.
+    // MASK: zero the scale / zero point of padding rows (a partial chunk may read rows past n).
+    template <bool MASK>
     __device__ static void values(WarpState<C>& S, const float (&pr)[2][2], const bool (&vld)[2],
-                                  const uint8_t* stage, const StageLay& L, int base, int lane) {
+                                  const uint8_t* stage, const Off& O, int tile, int lane) {
         const int g = lane >> 2, t = lane & 3;
-        const int tA = (g >> 1) + 4 * (g & 1), tB = tA + 8;
         uint32_t bv[NVT][2];
 #pragma unroll
         for (int jv = 0; jv < NVT; ++jv) {
-            const int gs = C::VC::grp(8 * jv + 2 * t);
             float sc[2], lo[2];
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                const int row = base + (hh ? tB : tA);
+                const uint8_t* mp = stage + O.vmA[jv] + tile * (16 * VMB) + hh * (8 * VMB);
                 if constexpr (CODE == KV_MIDRISE) {
-                    sc[hh] = __half2float(reinterpret_cast<const __half*>(stage + L.vm)[row]);
+                    sc[hh] = __half2float(*reinterpret_cast<const __half*>(mp));
                     lo[hh] = -0.5f * float((1 << VB) - 1) * sc[hh];
                 } else {
-                    const float2 f = unpack_half2(reinterpret_cast<const uint32_t*>(stage + L.vm)[row * GV + gs]);
+                    const float2 f = unpack_half2(*reinterpret_cast<const uint32_t*>(mp));
                     lo[hh] = f.x;
                     sc[hh] = f.y;
                 }
-                if (!vld[hh]) { sc[hh] = 0.f; lo[hh] = 0.f; }         // padding rows may hold any bits
+                if constexpr (MASK) {
+                    if (!vld[hh]) { sc[hh] = 0.f; lo[hh] = 0.f; }
+                }
             }
             const uint32_t ra = pack_half2(pr[0][0] * sc[0], pr[0][1] * sc[0]);
             const uint32_t rb = pack_half2(pr[1][0] * sc[1], pr[1][1] * sc[1]);
@@ -360,7 +394,7 @@ struct Tile {
         uint32_t va[2][D / 8];
 #pragma unroll
         for (int pair = 0; pair < 2; ++pair) {
-            const uint8_t* r0p = stage + L.vc + (base + t + 8 * pair) * LV::RB + LV::U * g;
+            const uint8_t* r0p = stage + O.vA + tile * (16 * LV::RB) + pair * (8 * LV::RB);
             const uint8_t* r1p = r0p + 4 * LV::RB;
             uint32_t cw[LV::NCW];
             if constexpr (LV::U == 2) {
@@ -388,30 +422,40 @@ struct Tile {
         }
     }
 
-    // Two tiles (tl1 < 0: only one).  cf0 / cf1: per-channel key fragments of each tile's group.
-    __device__ static void run2(WarpState<C>& S, const Ctx& X, const uint8_t* stage, const StageLay& L, int tl0,
-                                int tl1, int ntok, int lane, const uint8_t* cf0, const uint8_t* cf1) {
+    // NT (1 or 2) tiles tl0, tl1.  FULL: every token of the tiles is valid (whole chunk), no masks.
+    // Otherwise tl1 < 0 means tile 1 is absent and tokens >= ntok are masked.  cf0 / cf1: per-channel
+    // key fragments of each tile's token group.
+    template <bool FULL, int NT>
+    __device__ static void run(WarpState<C>& S, const Ctx& X, const uint8_t* stage, const Off& O, int tl0,
+                               int tl1, int ntok, int lane, const uint8_t* cf0, const uint8_t* cf1) {
         const int g = lane >> 2;
         const int tA = (g >> 1) + 4 * (g & 1);
-        const int base0 = tl0 * 16, base1 = tl1 * 16;
-        const bool two = tl1 >= 0;
+        const bool two = NT == 2 && (FULL || tl1 >= 0);
         bool vld[2][2];
-        vld[0][0] = base0 + tA < ntok;
-        vld[0][1] = base0 + tA + 8 < ntok;
-        vld[1][0] = two && base1 + tA < ntok;
-        vld[1][1] = two && base1 + tA + 8 < ntok;
+        if constexpr (FULL) {
+            vld[0][0] = vld[0][1] = vld[1][0] = vld[1][1] = true;
+        } else {
+            vld[0][0] = tl0 * 16 + tA < ntok;
+            vld[0][1] = tl0 * 16 + tA + 8 < ntok;
+            vld[1][0] = two && tl1 * 16 + tA < ntok;
+            vld[1][1] = two && tl1 * 16 + tA + 8 < ntok;
+        }
         float s2[2][2][2];
-        logits(s2[0], X, stage, L, base0, lane, cf0);
-        if (two) logits(s2[1], X, stage, L, base1, lane, cf1);
+        logits(s2[0], X, stage, O, tl0, lane, cf0);
+        if constexpr (NT == 2) {
+            if (two) logits(s2[1], X, stage, O, tl1, lane, cf1);
+        }
+        if constexpr (NT == 1 || !FULL) {
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
+            for (int u = 0; u < 2; ++u)
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh)
+                for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-                for (int e = 0; e < 2; ++e)
-                    if (!vld[u][hh]) s2[u][hh][e] = -INFINITY;
+                    for (int e = 0; e < 2; ++e)
+                        if (!vld[u][hh] || (NT == 1 && u == 1)) s2[u][hh][e] = -INFINITY;
+        }
 
-        // online softmax over both tiles, rows r0 + e.  Lazy reference max: the warp-wide max is
+        // online softmax over the tiles, rows r0 + e.  Lazy reference max: the warp-wide max is
         // taken (and the state rescaled) only when some logit exceeds the running reference by more
         // than 8 (log2 units); otherwise p = 2^(s - m) <= 256, harmless for fp32 sums and fp16 P'.
         float pr[2][2][2];
@@ -459,8 +503,10 @@ struct Tile {
                 for (int hh = 0; hh < 2; ++hh) pr[u][hh][e] = none ? 0.f : ex2(s2[u][hh][e] - S.m[e]);
             S.l[e] += (pr[0][0][e] + pr[0][1][e]) + (pr[1][0][e] + pr[1][1][e]);
         }
-        values(S, pr[0], vld[0], stage, L, base0, lane);
-        if (two) values(S, pr[1], vld[1], stage, L, base1, lane);
+        values<!FULL>(S, pr[0], vld[0], stage, O, tl0, lane);
+        if constexpr (NT == 2) {
+            if (two) values<!FULL>(S, pr[1], vld[1], stage, O, tl1, lane);
+        }
     }
 
     // End of a piece: exact merge of the 8 warps' states, one partial to global memory.
