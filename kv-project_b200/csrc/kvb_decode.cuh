@@ -315,7 +315,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
             for (int ch = pc.z; ch < pc.w; ++ch) {
                 const int s = it % p.nstage;
                 const uint32_t ph = (it / p.nstage) & 1;
-                if (ok && !mbar_wait(&full[s], ph)) ok = false;
+                // after a timeout, keep polling briefly (a fill may still land) but skip the compute
+                if (!mbar_wait(&full[s], ph, ok ? 2000000000ull : 1000000ull)) ok = false;
                 if (ok) {
                     const int64_t tok0 = int64_t(ch) * sd.tok;
                     const int ntok = int(imin64(sd.tok, sd.n - tok0));
@@ -378,6 +379,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
             if (sd.kbits == 4 && sd.vbits == 2) { body(I4{}, I2{}); done = true; }
         }
         if (!done) raise_status(KVB_DEV_BOUNDS);
+    }
+    // Every issued fill has been waited for above; if a wait gave up, give late copies a bounded
+    // chance to land before the CTA's shared memory is released.
+    if (threadIdx.x == 0 && it > 0) {
+        const uint32_t first = it > uint32_t(p.nstage) ? it - p.nstage : 0;
+        for (uint32_t k = first; k < it; ++k) mbar_wait(&full[k % p.nstage], (k / p.nstage) & 1, 10000000ull);
     }
 }
 
