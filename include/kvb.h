@@ -160,6 +160,23 @@ kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int
                              const int64_t* qpos, void* out, int out_dtype, int n_ctas,
                              void* workspace, size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end);
 
+/* Decode attention for callers that cannot allocate device memory.  No counterpart in the reference
+ * (which allocates with PyTorch freely); added for hosts that hand an operator only its input and
+ * output buffers: serving engines whose memory planner reserves all device memory up front, code that
+ * runs while another framework is capturing a CUDA graph (where cudaMalloc / cudaFree are not
+ * allowed), and plugin interfaces without an allocator.
+ * Same arguments and result as kvb_decode, minus the workspace: the split-K scratch lives in a
+ * file-scope __device__ array of KVB_NOALLOC_SCRATCH_BYTES (8 MiB) that every device loading the
+ * library keeps until process exit.  Requests needing more scratch return KVB_EINVAL (the message
+ * gives the size needed; use kvb_decode with your own workspace for those).  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress, with that device current); make
+ * that first call before any stream capture.  All calls share the one array and nothing in it needs
+ * to start at zero, but calls that overlap on the GPU (concurrent streams, or several host threads)
+ * race on it: serialise them.  The current device must be the device of `stream`. */
+#define KVB_NOALLOC_SCRATCH_BYTES (8u << 20)
+kvb_status kvb_decode_noalloc(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                              const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* stream);
+
 /* Build the split-K plan (pure host computation, no CUDA calls): piece table for n_ctas CTAs.
  * Exposed for tests; kvb_decode builds and uploads it inside its workspace. */
 int64_t kvb_decode_plan(const kvb_cache* c, int n_ctas, int32_t* plan_out, int64_t plan_capacity);

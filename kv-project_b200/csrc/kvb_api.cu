@@ -617,3 +617,57 @@ kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int
 }
 
 }  // extern "C"
+
+// =============================================================================================
+// Allocation-free decode.  For callers that may not allocate device memory at all (serving engines
+// whose planner owns every byte, code running inside another framework's CUDA-graph capture,
+// allocator-less plugin interfaces), the split-K scratch is a file-scope __device__ array instead
+// of a caller workspace.  Host code may not pass `g_noalloc_scratch` itself to a kernel: on the host
+// that name is only a stand-in symbol, not a device address.  Its real address is looked up once per
+// device (cudaGetSymbolAddress with that device current) and cached here.
+// =============================================================================================
+#include <mutex>
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KVB_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+kvb_status noalloc_scratch(void** out) {
+    int dev = 0;
+    kvb_status st = cuda_check(cudaGetDevice(&dev), "decode_noalloc: current device");
+    if (st) return st;
+    if (dev < 0 || dev >= kMaxDevices) return fail(KVB_EUNSUPPORTED, "decode_noalloc: device ordinal %d", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        if ((st = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "decode_noalloc: scratch address")))
+            return st;
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return KVB_OK;
+}
+
+}  // namespace
+
+extern "C" kvb_status kvb_decode_noalloc(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                                         const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* stream) {
+    DecodeShape sh{};
+    kvb_status st = validate_cache(c, sh, Hq, Tq);
+    if (st) return st;
+    const size_t need = kvb_decode_workspace_size(c, Hq, Tq, n_ctas);
+    if (need == 0) return fail(KVB_EINVAL, "decode_noalloc: invalid request");
+    if (need > size_t(KVB_NOALLOC_SCRATCH_BYTES))
+        return fail(KVB_EINVAL,
+                    "decode_noalloc: this request needs %zu bytes of scratch, the built-in array holds %u; "
+                    "call kvb_decode with a workspace instead",
+                    need, unsigned(KVB_NOALLOC_SCRATCH_BYTES));
+    void* scratch = nullptr;
+    if ((st = noalloc_scratch(&scratch))) return st;
+    return kvb_decode_events(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, n_ctas, scratch,
+                             size_t(KVB_NOALLOC_SCRATCH_BYTES), stream, nullptr, nullptr);
+}

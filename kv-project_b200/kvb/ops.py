@@ -277,6 +277,26 @@ def decode(cache: PackedCache, q: torch.Tensor, scaling: float, qpos=None, out=N
     return out
 
 
+def decode_noalloc(cache: PackedCache, q: torch.Tensor, scaling: float, out: torch.Tensor, qpos=None,
+                   n_ctas: int = 0) -> torch.Tensor:
+    """Decode attention for callers that cannot allocate device memory (an engine that owns every
+    byte of the GPU, a CUDA-graph capture run by another framework, an allocator-less plugin host):
+    `out` (B, Tq, Hq, d) is supplied by the caller and the split-K scratch is the library's built-in
+    8 MiB device array, so neither this wrapper nor the library allocates.  Calls share that array:
+    do not run two of them concurrently.  Raises ValueError when a request needs more scratch than
+    the array holds (use `decode` with a workspace for those)."""
+    _cuda(q, out)
+    q = q.contiguous()
+    B, Hq, Tq, d = q.shape
+    if B != cache.B or d != cache.d or tuple(out.shape) != (B, Tq, Hq, d) or not out.is_contiguous():
+        raise ValueError("decode_noalloc: q / out shapes do not match the cache")
+    c = cache.struct()
+    qp = None if qpos is None else (C.c_int64 * Tq)(*[int(v) for v in qpos])
+    L.check(L.lib().kvb_decode_noalloc(C.byref(c), _ptr(q), dtype_code(q), Hq, Tq, C.c_float(scaling), qp, _ptr(out),
+                                       dtype_code(out), n_ctas, C.c_void_p(_stream(q.device))), "kvb_decode_noalloc")
+    return out
+
+
 def decode_plan(cache: PackedCache, n_ctas: int):
     """The split-K plan (host computation): dict with cta_begin, pieces (head, stratum, lo, hi), head_begin."""
     c = cache.struct()
