@@ -105,6 +105,19 @@ kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, 
                             float* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------ *
+ * K4: spectral code.  Replaces the basis projection of spectral_side (QUASAR_KV.py:1354-1382, with a
+ * fixed per-head orthonormal basis) followed by the per-token mid-rise code of strata_quantize
+ * (STRATA_KV.py:1158-1168) on the leading r = 32 coefficients, on tcgen05 tensor cores.
+ * x: (B, H, T, 128) fp16, dense, 16-byte aligned.  basis_t: (2, H, 32, 128) fp16 = the transposed
+ * leading basis columns split into a high part and a low part (basis = hi + lo to ~22 bits).
+ * Outputs per kvb_quant_pack's mid-rise layout: codes (B, H, n_alloc, 32 * bits / 8) planar, scales
+ * (B, H, n_alloc) fp16; coef (nullable) (B, H, T, 32) float32 coefficients.  `step`: the mid-rise
+ * step in RMS units (uniform_step(bits)[0]).  n_ctas: persistent CTAs (0 = one per SM). */
+kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, const void* basis_t, int bits,
+                               float step, uint8_t* codes, void* scales, int64_t n_alloc, float* coef, int n_ctas,
+                               void* stream);
+
+/* ------------------------------------------------------------------------------------------ *
  * K3: fused split-K flash decode over a packed, head-synchronous cache.  Replaces StrataState.attend
  * + strata_tier_kernel (STRATA_KV.py:1762-1796, :1450-1469), LayerState.attend / chunked_attention
  * (STRATA_KV.py:716, :641) over KIVI codes, and QuasarState.attend (QUASAR_KV.py:1942-1967, one

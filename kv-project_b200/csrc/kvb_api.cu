@@ -20,6 +20,7 @@
 #include "kvb_select.cuh"
 #include "kvb_decode.cuh"
 #include "kvb_scores.cuh"
+#include "kvb_spectral.cuh"
 
 #define KVB_VERSION 100
 
@@ -253,6 +254,76 @@ kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, 
 }
 
 }  // extern "C"
+
+// =============================================================================================
+// K4: spectral projection + code (tcgen05)
+// =============================================================================================
+namespace {
+int resolve_ctas(int n_ctas);
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2D fp16 tensor map: inner dimension 128 elements (256-byte rows), box 64 x box_rows, 128-byte swizzle.
+kvb_status make_map_fp16(CUtensorMap* m, const void* base, int64_t rows, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return fail(KVB_ECUDA, "spectral: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {128, cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {256};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KVB_ECUDA, "spectral: cuTensorMapEncodeTiled failed (%d)", int(r));
+    return KVB_OK;
+}
+}  // namespace
+
+extern "C" kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, const void* basis_t, int bits,
+                                          float step, uint8_t* codes, void* scales, int64_t n_alloc, float* coef,
+                                          int n_ctas, void* stream) {
+    if (!x || !basis_t || !codes || !scales) return fail(KVB_EINVAL, "spectral_encode: null pointer");
+    if (B <= 0 || H <= 0 || T <= 0 || n_alloc < T || n_alloc % 16) return fail(KVB_EINVAL, "spectral_encode: sizes");
+    if (bits != 2 && bits != 4 && bits != 8) return fail(KVB_EINVAL, "spectral_encode: bits must be 2, 4 or 8");
+    if (!aligned(x, 16) || !aligned(basis_t, 16) || !aligned(codes, 16) || !aligned(scales, 2) || !aligned(coef, 16))
+        return fail(KVB_EINVAL, "spectral_encode: alignment");
+    if (B * H * T >= (int64_t(1) << 31)) return fail(KVB_EUNSUPPORTED, "spectral_encode: more than 2^31 rows");
+    kvb::SpectralParams p{};
+    kvb_status st = make_map_fp16(&p.tmap_x, x, B * H * T, kvb::SP_TILE);
+    if (st) return st;
+    if ((st = make_map_fp16(&p.tmap_b, basis_t, 2 * H * kvb::SP_R, kvb::SP_R))) return st;
+    p.H = H;
+    p.T = T;
+    p.n_alloc = n_alloc;
+    p.tiles_per_head = (T + kvb::SP_TILE - 1) / kvb::SP_TILE;
+    p.ntiles = p.tiles_per_head * B * H;
+    p.bits = bits;
+    p.step = step;
+    p.codes = codes;
+    p.scales = static_cast<__half*>(scales);
+    p.coef = coef;
+    int grid = resolve_ctas(n_ctas);
+    if (int64_t(grid) > p.ntiles) grid = int(p.ntiles);
+    const size_t smem = 1024 + size_t(kvb::SP_STAGES) * kvb::SP_A_BYTES + 2 * size_t(kvb::SP_B_BYTES) + 256;
+    cudaError_t e = cudaFuncSetAttribute(kvb::spectral_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem));
+    if (e != cudaSuccess) return cuda_check(e, "spectral smem attribute");
+    kvb::spectral_encode_kernel<<<grid, kvb::SP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(p);
+    return launch_check("spectral_encode_kernel");
+}
 
 // =============================================================================================
 // K3 host side: validation, plan, dispatch

@@ -55,6 +55,23 @@ def build_kivi(K: torch.Tensor, V: torch.Tensor, kbits: int, vbits: int, kgroup:
     return cache
 
 
+def build_spectral(K: torch.Tensor, V: torch.Tensor, basis: torch.Tensor, bits: int = 4, r: int = 32):
+    """Config 3: per KV head an orthonormal (d, d) basis; keys and values are stored as their leading
+    r coefficients, coded per token with the mid-rise code (tcgen05 projection + code epilogue);
+    decode runs in the coefficient domain (query mapped by B_r, output lifted by B_r^T).
+    basis: (H, d, d) float.  Returns the PackedCache."""
+    B, H, T, d = K.shape
+    br = basis[:, :, :r].to(device=K.device, dtype=torch.float32).contiguous()          # (H, d, r)
+    hilo = ops.split_basis(br)
+    kq = ops.spectral_encode(K.to(torch.float16), hilo, bits)
+    vq = ops.spectral_encode(V.to(torch.float16), hilo, bits)
+    cache = ops.PackedCache(B, H, d, d_code=r, midrise=True)
+    cache.add_stratum(kq, vq)
+    cache.qmap = br
+    cache.lift = br.transpose(1, 2).contiguous()
+    return cache
+
+
 def build_eviction(q_obs: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scaling: float, budget: int,
                    window: int, bits: int = 4, group: int = 64, pool: int = 0):
     """Heavy hitters by accumulated decode-query attention over [0, T - window), plus the window;

@@ -313,3 +313,44 @@ def decode_plan(cache: PackedCache, n_ctas: int):
     o += 4 * npc
     head_begin = v[o:o + nh + 1]
     return {"n_ctas": nc, "cta_begin": cta_begin, "pieces": pieces, "head_begin": head_begin}
+
+
+# ------------------------------------------------------------------------------------------------
+# K4: spectral code
+# ------------------------------------------------------------------------------------------------
+SPECTRAL_R = 32
+
+
+def split_basis(basis_r: torch.Tensor) -> torch.Tensor:
+    """basis_r (H, d, r) float -> (2, H, r, d) fp16: transposed basis split as hi + lo (exact to ~22
+    bits), the operand layout kvb_spectral_encode expects."""
+    bt = basis_r.transpose(1, 2).contiguous().float()
+    hi = bt.to(torch.float16)
+    lo = (bt - hi.float()).to(torch.float16)
+    return torch.stack([hi, lo]).contiguous()
+
+
+def spectral_encode(x: torch.Tensor, basis_hilo: torch.Tensor, bits: int = 4, want_coef: bool = False,
+                    n_alloc: int = None, n_ctas: int = 0) -> dict:
+    """Project x (B, H, T, 128) fp16 onto each head's leading 32 basis columns on the tensor cores and
+    code each token's coefficients with the mid-rise code.  Returns a stratum dict (codes, meta =
+    fp16 scales, n, n_alloc, bits) and optionally the float32 coefficients."""
+    _cuda(x, basis_hilo)
+    if x.dtype != torch.float16 or x.dim() != 4 or x.shape[-1] != 128:
+        raise ValueError("spectral_encode: x must be fp16 (B, H, T, 128)")
+    x = x.contiguous()
+    B, H, T, d = x.shape
+    if basis_hilo.dtype != torch.float16 or tuple(basis_hilo.shape) != (2, H, SPECTRAL_R, d):
+        raise ValueError("spectral_encode: basis must be fp16 (2, H, 32, 128) (see split_basis)")
+    basis_hilo = basis_hilo.contiguous()
+    n_alloc = round_up(T, 16) if n_alloc is None else n_alloc
+    codes = torch.empty((B, H, n_alloc, SPECTRAL_R * bits // 8), dtype=torch.uint8, device=x.device)
+    scales = torch.zeros((B, H, n_alloc), dtype=torch.float16, device=x.device)
+    if n_alloc > T:
+        codes[:, :, T:].zero_()
+    coef = torch.empty((B, H, T, SPECTRAL_R), dtype=torch.float32, device=x.device) if want_coef else None
+    L.check(L.lib().kvb_spectral_encode(_ptr(x), B, H, T, _ptr(basis_hilo), bits, C.c_float(UNIFORM_STEP[bits]),
+                                        _ptr(codes), _ptr(scales), n_alloc, _ptr(coef), n_ctas,
+                                        C.c_void_p(_stream(x.device))), "kvb_spectral_encode")
+    return {"codes": codes, "meta": scales, "n": T, "n_alloc": n_alloc, "bits": bits, "group": SPECTRAL_R,
+            "coef": coef}
