@@ -1,7 +1,7 @@
 #!/usr/bin/env python
-"""Packed-KV decode attention benchmark (the BASELINE metric on config 1).
+"""Packed-KV decode attention benchmark (the BASELINE metric; default: config 1).
 
-Workload: Llama-3-8B attention shape, 32 layers, B = 8 per GPU,
+Default workload: Llama-3-8B attention shape, 32 layers, B = 8 per GPU,
 32 query / 8 KV heads, head_dim 128, context 32768, bf16 activations; per (b, kv head) every token
 is coded at 8 / 4 / 2 bits (10 % / 30 % / 60 % by key L2 norm, head-synchronous strata), KIVI
 asymmetric per-token groups of 64 channels with fp16 zero point and scale.  Inputs are seeded
@@ -13,9 +13,22 @@ call per layer: prologue + split-K main kernel + merge).  value = packed bytes r
 ranks) / max-over-ranks step time, in GB/s; the packed cache is 7.95 GB per GPU per step, far larger
 than L2, so no flush is needed between steps.
 
-  python bench.py [--gpus N --steps K --warmup W]          # kvb (CUDA) arm
-  python bench.py --impl reference                          # reference CPU path (oracle port) arm
-Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N  (weak scaling: each rank decodes its own B = 8)
+Other workloads (--workload), each printing the same JSON line for its own config:
+  c0          config 0: B 1, 4096 tokens, K 4-bit per channel (128 tokens), V 2-bit per token (32 ch)
+  c2          config 2: B 4, 32768 tokens, 2048 heavy hitters + 128 window kept, 4-bit group 64
+  c3          config 3: B 16, 16384 tokens, 32 spectral coefficients, 4-bit mid-rise per token
+  c4          config 4: 70B shape, B 32 sharded over ranks (strong scaling), 131072 tokens, 4-bit g128;
+              the layers that fit in HBM are resident and timed (config.layers)
+  c4s         config 4 with batch 4: the 131072-token context split over ranks (strong scaling), one
+              NCCL all-gather of (output, lse) parts + kvb_lse_merge per layer
+  c1-pack     compress side of config 1 (key energy, rank split, 6 quantise+pack calls per layer)
+  c2-evict    compress side of config 2 (accumulated scores of 64 queries, top-k, 2 packs per layer)
+  c3-project  compress side of config 3 (tcgen05 basis projection + mid-rise code of K and V)
+
+  python bench.py [--gpus N --steps K --warmup W] [--workload W]   # kvb (CUDA) arm
+  python bench.py --impl reference [--workload W]                   # reference CPU path (oracle port)
+Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N  (c0-c3: weak scaling, each rank its own
+batch; c4: the batch of 32 is split over the ranks)
 """
 
 from __future__ import annotations
@@ -35,6 +48,12 @@ sys.path.insert(0, str(ROOT / "kv-project_b200"))
 
 METRIC = "packed-KV decode attn µs/step and HBM GB/s (% of peak) at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+DECODE = ("c1", "c0", "c2", "c3", "c4", "c4s")
+COMPRESS = ("c1-pack", "c2-evict", "c3-project")
+
+# DRAM bytes (read + write) of one decode_main launch from an ncu capture of this bench's workload
+# (`ncu --set full -k regex:decode_main`, see profiles/); None where no capture was taken.
+TRAFFIC = {"c1": 248.84e6 + 5.64e6}
 
 
 def args_():
@@ -43,9 +62,10 @@ def args_():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["kvb", "reference"], default="kvb")
-    p.add_argument("--layers", type=int, default=32)
-    p.add_argument("--batch", type=int, default=8)
-    p.add_argument("--context", type=int, default=32768)
+    p.add_argument("--workload", choices=DECODE + COMPRESS, default="c1")
+    p.add_argument("--layers", type=int, default=None, help="layers per rank (default: the config's)")
+    p.add_argument("--batch", type=int, default=None, help="batch per rank (default: the config's)")
+    p.add_argument("--context", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -104,40 +124,100 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------------
+# workload shapes
+# ------------------------------------------------------------------------------------------------
+def shape(a, world):
+    """(layers, batch per rank, context, Hq, Hkv, dtype name, description) of a workload."""
+    w = a.workload.split("-")[0]
+    base = {"c0": (1, 1, 4096, 32, 8, "f16"), "c1": (32, 8, 32768, 32, 8, "bf16"),
+            "c2": (32, 4, 32768, 32, 8, "bf16"), "c3": (1, 16, 16384, 32, 8, "f16"),
+            "c4": (80, 32, 131072, 64, 8, "bf16"), "c4s": (80, 4, 131072, 64, 8, "bf16")}[w]
+    L, B, T, Hq, Hkv, dt = base
+    if w == "c4":                                   # strong scaling: the batch of 32 is split over ranks
+        if B % world:
+            raise SystemExit(f"config 4: batch 32 does not split over {world} ranks")
+        B //= world
+        per_layer = B * Hkv * T * 136               # 4-bit K + V codes (128 B) + per-channel / per-token fp16 pairs
+        L = min(L, int(110e9 // per_layer))         # layers resident on one GPU (all 80 from 4 GPUs up)
+    if a.workload in COMPRESS:
+        L = min(L, 4)                               # distinct layer inputs cycled through (each > L2)
+    L = a.layers or L
+    B = a.batch or B
+    T = a.context or T
+    return L, B, T, Hq, Hkv, dt
+
+
+DESC = {
+    "c0": "config0-gqa-decode-kivi-k4ch-v2tok",
+    "c1": "config1-mixed-8/4/2bit-decode",
+    "c2": "config2-evict-2048+128-kivi4-decode",
+    "c3": "config3-spectral-r32-4bit-decode",
+    "c4": "config4-70b-131k-kivi4-decode",
+    "c4s": "config4-70b-131k-kivi4-decode-seqsplit-b4",
+    "c1-pack": "config1-compress-mixed-strata",
+    "c2-evict": "config2-compress-scores-topk-pack",
+    "c3-project": "config3-compress-tcgen05-projection",
+}
+
+
+def build_decode(a, rank, dev):
+    """Per-layer packed caches of a decode workload on this rank + queries / outputs."""
+    import torch
+    import kvb
+    from kvb import workloads as W
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    L, B, T, Hq, Hkv, dt = shape(a, world)
+    dtype = torch.bfloat16 if dt == "bf16" else torch.float16
+    d = 128
+    w = a.workload
+    caches = []
+    for layer in range(L):
+        seed = 43 + 1000 * rank + layer
+        if w == "c4s":
+            seed = 43 + layer                        # the same model on every rank; ranks hold slices
+        if w == "c1":
+            K, V = W.lognormal_kv(B, Hkv, T, d, dtype, device=dev, seed=43 + 1000 * rank, layer=layer)
+            cache, _ = kvb.cache.build_mixed(K, V)
+        elif w == "c0":
+            K, V = W.outlier_kv(B, Hkv, T, d, dtype, device=dev, seed=42 + 1000 * rank)
+            cache = kvb.cache.build_kivi(K, V, 4, 2, 128, 32)
+        elif w == "c2":
+            g = W.gen(dev, seed)
+            K = torch.randn(B, Hkv, T, d, generator=g, device=dev).to(dtype)
+            V = torch.randn(B, Hkv, T, d, generator=g, device=dev).to(dtype)
+            q_obs = torch.randn(B, Hq, 64, d, generator=g, device=dev).to(dtype)
+            cache, _, _ = kvb.cache.build_eviction(q_obs, K, V, d ** -0.5, 2048, 128, bits=4, group=64)
+            del q_obs
+        elif w == "c3":
+            bases = W.qr_bases(Hkv, d, seed=45)
+            K, V = W.spectral_kv(B, Hkv, T, d, bases, dtype, device=dev, seed=45 + 1000 * rank)
+            cache = kvb.cache.build_spectral(K, V, bases)
+        elif w == "c4s":                             # this rank's token range of every (b, kv head)
+            from kvb.seqsplit import token_ranges
+            lo, hi = token_ranges(T, world, 128)[rank]
+            K, V = W.outlier_kv(B, Hkv, hi - lo, d, dtype, device=dev, seed=seed * 64 + 7)
+            cache = kvb.cache.build_kivi(K, V, 4, 4, 128, 128)
+        else:                                        # c4: generated in batch chunks (fp32 temporaries)
+            K = torch.empty((B, Hkv, T, d), dtype=dtype, device=dev)
+            V = torch.empty_like(K)
+            for b0 in range(0, B, 4):
+                kb, vb = W.outlier_kv(min(4, B - b0), Hkv, T, d, dtype, device=dev, seed=seed * 64 + b0)
+                K[b0:b0 + 4], V[b0:b0 + 4] = kb, vb
+                del kb, vb
+            cache = kvb.cache.build_kivi(K, V, 4, 4, 128, 128)
+        caches.append(cache)
+        del K, V
+    torch.cuda.synchronize()
+    q = W.queries(L * B, Hq, 1, d, dtype, device=dev, seed=42 + rank).view(L, B, Hq, 1, d)
+    out = torch.empty((L, B, 1, Hq, d), dtype=dtype, device=dev)
+    return caches, q, out, (L, B, T, Hq, Hkv, dt)
+
+
+# ------------------------------------------------------------------------------------------------
 # reference arm: the reference's CPU decode path (dequantise-then-attend), oracle port
 # ------------------------------------------------------------------------------------------------
-def cpu_reference_sample(batch_rows=1, context=32768, min_seconds=10.0, seed=42):
-    """Times chunked_attention (STRATA_KV.py:641, numpy port in oracle/) over one layer's
-    dequantised mixed cache for `batch_rows` of the 8 batch rows (8 KV heads each).  Returns
-    (seconds per sample, packed bytes the sample represents, threads, description)."""
-    import numpy as np
+def _threads():
     import torch
-    import oracle as O
-    from kvb import workloads as W
-    torch.manual_seed(seed)
-    K, V = W.lognormal_kv(batch_rows, 8, context, 128, torch.bfloat16, seed=seed + 1, layer=0)
-    q = W.queries(batch_rows, 32, 1, 128, torch.bfloat16, seed=seed)
-    Kf, Vf = K.float().numpy(), V.float().numpy()
-    sets = O.mixed_strata(O.l2_importance(Kf))
-    Kh, Vh = np.empty_like(Kf), np.empty_like(Vf)
-    for b, idx in sets.items():
-        gk = np.take_along_axis(Kf, idx[..., None].repeat(128, -1), 2)
-        gv = np.take_along_axis(Vf, idx[..., None].repeat(128, -1), 2)
-        np.put_along_axis(Kh, idx[..., None].repeat(128, -1), O.kivi_quant(gk, b, 64, False, 0)["xhat"], 2)
-        np.put_along_axis(Vh, idx[..., None].repeat(128, -1), O.kivi_quant(gv, b, 64, False, 0)["xhat"], 2)
-    qn = q.float().numpy()
-    pos = np.arange(context)
-    hide = np.full(context, O.attention.BIG)
-    O.chunked_attention(qn, 128 ** -0.5, np.array([context]), Kh, Vh, pos, hide, None, 256)   # warm
-    t0 = time.perf_counter()
-    reps = 0
-    while reps < 200 and (reps < 3 or time.perf_counter() - t0 < min_seconds):
-        O.chunked_attention(qn, 128 ** -0.5, np.array([context]), Kh, Vh, pos, hide, None, 256)
-        reps += 1
-    dt = (time.perf_counter() - t0) / reps
-    n8, n4, n2 = O.strata_counts(context)
-    per_head = n8 * (256 + 16) + n4 * (128 + 16) + n2 * (64 + 16)
-    packed = per_head * 8 * batch_rows
     threads = torch.get_num_threads()
     try:
         import threadpoolctl
@@ -145,28 +225,95 @@ def cpu_reference_sample(batch_rows=1, context=32768, min_seconds=10.0, seed=42)
         threads = max([i.get("num_threads", 1) for i in info] + [1])
     except Exception:
         pass
-    desc = (f"chunked_attention (numpy port, fp32) over 1 layer x {batch_rows} batch row(s) x 8 KV heads x "
-            f"{context} dequantised tokens, mean of {reps}")
-    return dt, packed, threads, desc
+    return threads
+
+
+def cpu_reference_sample(workload="c1", context=None, min_seconds=10.0, seed=42):
+    """Times the reference's CPU decode (chunked_attention STRATA_KV.py:641, or the coefficient-
+    domain attend QUASAR_KV.py:1942 for config 3; numpy ports in oracle/) over one batch row of one
+    layer of the workload's cache, dequantised.  Returns (seconds per sample, packed bytes the
+    sample represents, threads, description)."""
+    import numpy as np
+    import torch
+    import oracle as O
+    from kvb import workloads as W
+    workload = "c4" if workload == "c4s" else workload      # same per-row cache as config 4
+    T = context or {"c0": 4096, "c1": 32768, "c2": 32768, "c3": 16384, "c4": 32768}[workload]
+    Hq = 64 if workload == "c4" else 32
+    Hkv, d = 8, 128
+    dt = torch.float16 if workload in ("c0", "c3") else torch.bfloat16
+    q = W.queries(1, Hq, 1, d, dt, seed=seed).float().numpy()
+    pos, hide = np.arange(T), np.full(T, O.attention.BIG)
+    if workload == "c1":
+        K, V = W.lognormal_kv(1, Hkv, T, d, dt, seed=seed + 1, layer=0)
+        Kf, Vf = K.float().numpy(), V.float().numpy()
+        sets = O.mixed_strata(O.l2_importance(Kf))
+        Kh, Vh = np.empty_like(Kf), np.empty_like(Vf)
+        for b, idx in sets.items():
+            gk = np.take_along_axis(Kf, idx[..., None].repeat(d, -1), 2)
+            gv = np.take_along_axis(Vf, idx[..., None].repeat(d, -1), 2)
+            np.put_along_axis(Kh, idx[..., None].repeat(d, -1), O.kivi_quant(gk, b, 64, False, 0)["xhat"], 2)
+            np.put_along_axis(Vh, idx[..., None].repeat(d, -1), O.kivi_quant(gv, b, 64, False, 0)["xhat"], 2)
+        n8, n4, n2 = O.strata_counts(T)
+        packed = Hkv * (n8 * (256 + 16) + n4 * (128 + 16) + n2 * (64 + 16))
+        what = "mixed 8/4/2-bit KIVI strata"
+    elif workload in ("c0", "c4"):
+        K, V = W.outlier_kv(1, Hkv, T, d, dt, seed=seed)
+        kb, vb, vg = (4, 2, 32) if workload == "c0" else (4, 4, 128)
+        Kh = O.kivi_quant(K.float().numpy(), kb, 128, True, 0)["xhat"]
+        Vh = O.kivi_quant(V.float().numpy(), vb, vg, False, 0)["xhat"]
+        packed = Hkv * T * (d * (kb + vb) // 8) + Hkv * (T // 128) * d * 4 + Hkv * T * (d // vg) * 4
+        what = f"KIVI K {kb}-bit per channel (128 tokens), V {vb}-bit per token ({vg} channels)"
+    elif workload == "c2":
+        n = 2048 + 128
+        g = torch.Generator().manual_seed(seed)
+        K = torch.randn(1, Hkv, n, d, generator=g).to(dt)
+        V = torch.randn(1, Hkv, n, d, generator=g).to(dt)
+        Kh = O.kivi_quant(K.float().numpy(), 4, 64, True, 0)["xhat"]
+        Vh = O.kivi_quant(V.float().numpy(), 4, 64, False, 0)["xhat"]
+        T, pos, hide = n, np.arange(n), np.full(n, O.attention.BIG)
+        packed = Hkv * n * 128 + Hkv * (n // 64) * d * 4 + Hkv * n * 2 * 4
+        what = "KIVI 4-bit g64 over the 2176 kept tokens"
+    else:                                            # c3: coefficient-domain decode
+        bases = W.qr_bases(Hkv, d, seed=45)
+        K, V = W.spectral_kv(1, Hkv, T, d, bases, dt, seed=45)
+        br = bases[:, :, :32].float().numpy()
+        _, kc, ks, _ = O.spectral_encode(K.float().numpy(), br, 4)
+        _, vc, vs, _ = O.spectral_encode(V.float().numpy(), br, 4)
+        run = lambda: O.spectral_attend(q, d ** -0.5, br, kc, ks, vc, vs, 4)   # noqa: E731
+        packed = Hkv * T * 36
+        what = "spectral 32 coefficients 4-bit, coefficient-domain attend"
+    if workload != "c3":
+        run = lambda: O.chunked_attention(q, d ** -0.5, np.array([T]), Kh, Vh, pos, hide, None, 256)  # noqa: E731
+    run()                                            # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 200 and (reps < 3 or time.perf_counter() - t0 < min_seconds):
+        run()
+        reps += 1
+    dt_s = (time.perf_counter() - t0) / reps
+    desc = (f"{'spectral_attend' if workload == 'c3' else 'chunked_attention'} (numpy port, fp32) over 1 layer x "
+            f"1 batch row x {Hkv} KV heads x {T} dequantised tokens ({what}), mean of {reps}")
+    return dt_s, packed, _threads(), desc
 
 
 def reference_arm(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    dt, packed, threads, desc = cpu_reference_sample(context=a.context)
-    layer_bytes = packed * a.batch                    # the sample is 1 of `batch` rows of one layer
-    step_bytes = layer_bytes * a.layers
-    gbs = packed / dt / 1e9
-    us_step = step_bytes / (gbs * 1e9) * 1e6
+    w = a.workload.split("-")[0]
+    dt_s, packed, threads, desc = cpu_reference_sample(w, context=a.context)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    L, B, T, Hq, Hkv, _ = shape(argparse.Namespace(**{**vars(a), "workload": w}), world)
+    gbs = packed / dt_s / 1e9
+    step_bytes = packed * B * L                       # the sample is 1 of B rows of one layer
     line = {"metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "impl": "reference",
             "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": round(us_step / 1000, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config1-mixed-8/4/2bit-decode", "layers": a.layers, "batch_per_gpu": a.batch,
-                       "context": a.context, "Hq": 32, "Hkv": 8, "d": 128},
-            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": desc},
+            "ms_per_step": round(step_bytes / (gbs * 1e9) * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong" if w in ("c4", "c4s") else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": DESC[w], "layers": L, "batch_per_gpu": B, "context": T, "Hq": Hq, "Hkv": Hkv,
+                       "d": 128},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -174,15 +321,9 @@ def reference_arm(a):
 # ------------------------------------------------------------------------------------------------
 # kvb arm
 # ------------------------------------------------------------------------------------------------
-def main():
-    a = args_()
-    if a.impl == "reference":
-        return reference_arm(a)
+def setup_dist():
     import torch
     import torch.distributed as dist
-    import kvb
-    from kvb import workloads as W
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -191,24 +332,52 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    return world, rank, local, dev
 
-    L, B, T, Hq, Hkv, d = a.layers, a.batch, a.context, 32, 8, 128
-    scaling = d ** -0.5
-    caches = []
-    for layer in range(L):
-        K, V = W.lognormal_kv(B, Hkv, T, d, torch.bfloat16, device=dev, seed=43 + 1000 * rank, layer=layer)
-        cache, _ = kvb.cache.build_mixed(K, V)
-        caches.append(cache)
-        del K, V
+
+def max_over_ranks(ms, world, dev):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
     torch.cuda.synchronize()
-    q = W.queries(L * B, Hq, 1, d, torch.bfloat16, device=dev, seed=42 + rank).view(L, B, Hq, 1, d)
-    out = torch.empty((L, B, 1, Hq, d), dtype=torch.bfloat16, device=dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def decode_arm(a):
+    import torch
+    import torch.distributed as dist
+    import kvb
+    world, rank, local, dev = setup_dist()
+    caches, q, out, (L, B, T, Hq, Hkv, dt) = build_decode(a, rank, dev)
+    d = 128
+    scaling = d ** -0.5
     bytes_layer = [c.stored_bytes() for c in caches]
-    bytes_step = sum(bytes_layer) + q.numel() * 2 + out.numel() * 2
+    esz = q.element_size()
+    bytes_step = sum(bytes_layer) + q.numel() * esz + out.numel() * esz
+
+    split = a.workload == "c4s" and world > 1
+    dec = kvb.seqsplit.SeqSplitDecoder() if split else None
+
+    def attend(layer, qq, events=None):
+        if split:
+            dec.attend(caches[layer], qq[layer], scaling, out=out[layer])
+        else:
+            kvb.decode(caches[layer], qq[layer], scaling, out=out[layer], events=events)
 
     def step():
         for layer in range(L):
-            kvb.decode(caches[layer], q[layer], scaling, out=out[layer])
+            attend(layer, q)
 
     step()
     torch.cuda.synchronize()
@@ -224,10 +393,7 @@ def main():
         step()
     for _ in range(max(3, a.warmup)):
         graph.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         e0.record()
@@ -235,13 +401,8 @@ def main():
             graph.replay()
         e1.record()
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / a.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps, world, dev)
+    barrier(world)
 
     # ---- main split-K kernel alone: events recorded by the library around it, inside a graph ----
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
@@ -252,7 +413,11 @@ def main():
 
     def step_ev():
         for layer in range(L):
-            kvb.decode(caches[layer], q[layer], scaling, out=out[layer], events=evs[layer])
+            if split:
+                # the main kernel's events come from a plain decode of this rank's slice (no exchange)
+                kvb.decode(caches[layer], q[layer], scaling, out=out[layer], events=evs[layer])
+            else:
+                attend(layer, q, evs[layer])
 
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.stream(s):
@@ -277,25 +442,19 @@ def main():
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
         for layer in range(L):
-            kvb.decode(caches[layer], q_dev[layer], scaling, out=out[layer])
+            attend(layer, q_dev)
         out_host.copy_(out, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    barrier(world)
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     x0.record()
     for _ in range(a.steps):
         e2e_step()
     x1.record()
     torch.cuda.synchronize()
-    e2e_ms = x0.elapsed_time(x1) / a.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(x0.elapsed_time(x1) / a.steps, world, dev)
     status = kvb.device_status()
     if status:
         raise RuntimeError(f"device status word {status} after the timed region")
@@ -304,36 +463,155 @@ def main():
         peak, peak_kind = peaks()
         gbs = world * bytes_step / (ms * 1e-3) / 1e9
         achieved = (sum(bytes_layer) / L) / (main_ms_avg * 1e-3) / 1e9
+        traffic = TRAFFIC.get(a.workload) if (a.layers, a.batch, a.context) == (None, None, None) else None
+        w = a.workload
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms, 4), "us_per_step": round(ms * 1000, 1),
-            "pct_of_peak": round(100 * gbs / world / peak, 1), "higher_is_better": True, "scaling": "weak",
+            "pct_of_peak": round(100 * gbs / world / peak, 1), "higher_is_better": True,
+            "scaling": "strong" if w in ("c4", "c4s") else "weak",
             "vs_baseline": None, "dtype": "u8 codes / fp16 MMA / fp32 softmax", "data": "synthetic",
-            "config": {"workload": "config1-mixed-8/4/2bit-decode", "layers": L, "batch_per_gpu": B,
-                       "global_batch": B * world, "context": T, "Hq": Hq, "Hkv": Hkv, "d": d,
-                       "strata": "10% 8-bit / 30% 4-bit / 60% 2-bit, KIVI per-token groups of 64",
-                       "l2": "inputs larger than L2 (248 MB packed per layer, 7.95 GB per step)",
-                       "parallelism": f"dp{world} (batch x kv-head shards, no collective)",
+            "config": {"workload": DESC[w], "layers": L, "batch_per_gpu": B, "global_batch": B * world,
+                       "context": T, "Hq": Hq, "Hkv": Hkv, "d": d, "act_dtype": dt,
+                       "l2": ("inputs larger than L2" if sum(bytes_layer) > 126e6 else
+                              "packed cache smaller than L2: timed warm (launch-bound config)"),
+                       "parallelism": {"c4": f"batch split over {world} ranks, no collective",
+                                       "c4s": f"context split over {world} ranks, NCCL all-gather + LSE merge "
+                                              f"per layer"}.get(w, f"dp{world} (batch x kv-head shards, "
+                                                                    f"no collective)"),
                        "bytes_per_step_per_gpu": bytes_step},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "kernel": "decode_main", "bytes_per_launch": sum(bytes_layer) // L,
-                         "us_per_launch": round(main_ms_avg * 1000, 2), "traffic": None},
+                         "us_per_launch": round(main_ms_avg * 1000, 2),
+                         "traffic": None if traffic is None else round(traffic)},
             "e2e": {"value": round(world * bytes_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": q.numel() * 2,
-                    "d2h_bytes_per_step": out.numel() * 2},
-            "gpu_launches": 3 * L * a.steps,
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": q.numel() * esz,
+                    "d2h_bytes_per_step": out.numel() * esz},
+            "gpu_launches": (3 + int(split)) * L * a.steps,
             "clocks": clk.summary(),
         }
+        if w == "c1":
+            line["config"]["strata"] = "10% 8-bit / 30% 4-bit / 60% 2-bit, KIVI per-token groups of 64"
         if world == 1 and not a.no_cpu_baseline:
-            dt, packed, threads, desc = cpu_reference_sample(context=T)
-            line["cpu_baseline"] = {"value": round(packed / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
+            dt_s, packed, threads, desc = cpu_reference_sample(w, context=a.context)
+            line["cpu_baseline"] = {"value": round(packed / dt_s / 1e9, 4), "unit": "GB/s", "cores": threads,
                                     "kind": "port", "sample": desc}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         del graph
+        torch.cuda.synchronize()
         dist.destroy_process_group()
+
+
+def compress_arm(a):
+    """Compress-side kernels of a config: one step = compressing one layer's K / V (layers cycled,
+    each layer's inputs larger than L2).  value = algorithmic bytes (inputs read + packed output
+    written) / step time."""
+    import torch
+    import torch.distributed as dist
+    import kvb
+    from kvb import workloads as W
+    world, rank, local, dev = setup_dist()
+    w = a.workload
+    L, B, T, Hq, Hkv, dt = shape(a, world)
+    dtype = torch.bfloat16 if dt == "bf16" else torch.float16
+    d = 128
+    layers, launches = [], 0
+    for layer in range(L):
+        seed = 50 + 1000 * rank + layer
+        if w == "c1-pack":
+            K, V = W.lognormal_kv(B, Hkv, T, d, dtype, device=dev, seed=seed, layer=layer)
+            layers.append((K, V))
+        elif w == "c2-evict":
+            g = W.gen(dev, seed)
+            K = torch.randn(B, Hkv, T, d, generator=g, device=dev).to(dtype)
+            V = torch.randn(B, Hkv, T, d, generator=g, device=dev).to(dtype)
+            qo = torch.randn(B, Hq, 64, d, generator=g, device=dev).to(dtype)
+            layers.append((K, V, qo))
+        else:
+            bases = W.qr_bases(Hkv, d, seed=45)
+            K, V = W.spectral_kv(B, Hkv, T, d, bases, dtype, device=dev, seed=seed)
+            hilo = kvb.ops.split_basis(bases[:, :, :32].float().to(dev))
+            layers.append((K, V, hilo))
+
+    res = {}
+
+    def step(i):
+        x = layers[i % L]
+        if w == "c1-pack":
+            res["c"], _ = kvb.cache.build_mixed(x[0], x[1])
+        elif w == "c2-evict":
+            res["c"] = kvb.cache.build_eviction(x[2], x[0], x[1], d ** -0.5, 2048, 128, bits=4, group=64)[0]
+        else:
+            res["k"] = kvb.ops.spectral_encode(x[0], x[2], 4)
+            res["v"] = kvb.ops.spectral_encode(x[1], x[2], 4)
+
+    step(0)
+    torch.cuda.synchronize()
+    if w == "c3-project":
+        out_bytes = sum(r["codes"].numel() + r["meta"].numel() * 2 for r in (res["k"], res["v"]))
+        in_bytes = 2 * layers[0][0].numel() * 2 + 2 * layers[0][2].numel() * 2
+        launches = 2
+        flops = 2 * 2 * B * Hkv * T * d * 32             # algorithmic: K and V, 2 FLOP per multiply-add
+    else:
+        c = res["c"]
+        out_bytes = c.stored_bytes()
+        if w == "c1-pack":
+            in_bytes = 2 * 2 * B * Hkv * T * d + B * Hkv * T * d * 2   # K, V read for packing + K for energy
+            launches = 2 + 6
+        else:
+            in_bytes = 2 * B * Hkv * T * d * 2 + 2 * 2 * B * Hkv * 2176 * d   # K (score pass) + kept K / V
+            launches = 3 + 1 + 2
+        flops = 0
+    for i in range(max(3, a.warmup)):
+        step(i)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for i in range(a.steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps, world, dev)
+    if kvb.device_status():
+        raise RuntimeError("device status word set after the timed region")
+    if rank == 0:
+        peak, peak_kind = peaks()
+        alg = in_bytes + out_bytes
+        gbs = alg / (ms * 1e-3) / 1e9
+        line = {
+            "metric": f"{DESC[w]} GB/s (inputs read + packed output written)", "value": round(world * gbs, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dt, "data": "synthetic",
+            "config": {"workload": DESC[w], "layers_cycled": L, "batch_per_gpu": B, "context": T, "Hq": Hq,
+                       "Hkv": Hkv, "d": d, "l2": "inputs larger than L2", "bytes_per_step": alg},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_source": peak_kind, "kernel": "whole compress step",
+                         "traffic": None},
+            "gpu_launches": launches * a.steps,
+            "clocks": clk.summary(),
+        }
+        if flops:
+            line["tensor_tflops"] = round(flops / (ms * 1e-3) / 1e12, 2)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    a = args_()
+    if a.impl == "reference":
+        if a.workload in COMPRESS:
+            print(json.dumps({"impl": "reference", "unavailable": "reference arm times the decode workloads only"}))
+            return
+        return reference_arm(a)
+    if a.workload in COMPRESS:
+        return compress_arm(a)
+    return decode_arm(a)
 
 
 if __name__ == "__main__":

@@ -173,6 +173,23 @@ kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int
                              const int64_t* qpos, void* out, int out_dtype, int n_ctas,
                              void* workspace, size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end);
 
+/* As kvb_decode, and also writes lse (B, Tq, Hq) float32: the natural-log sum of exp(scaled logit) over
+ * every token this call attended (-inf, with a zero output row, where none was readable).  Used by
+ * a sequence split: each rank decodes its own token range, the (out, lse) parts are exchanged, and
+ * kvb_lse_merge combines them.  Replaces the per-stratum (m, l, acc) partials of strata_tier_kernel
+ * (STRATA_KV.py:1450-1469) at the granularity of a whole rank. */
+kvb_status kvb_decode_lse(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                          const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Merge of n_parts attention parts over disjoint token sets: part k's rows at parts + k * part_stride
+ * ((rows, d) float32, each row normalised) with lse at lse + k * lse_stride ((rows) float32, natural
+ * log).  out (rows, d) in out_dtype = sum_k exp(lse_k - M) o_k / sum_k exp(lse_k - M) (the exact LSE
+ * merge of StrataState.attend, STRATA_KV.py:1784-1792, across parts).  Parts with lse -inf are
+ * skipped; a row with no part gets zeros. */
+kvb_status kvb_lse_merge(const float* parts, int64_t part_stride, const float* lse, int64_t lse_stride, int n_parts,
+                         int64_t rows, int d, void* out, int out_dtype, void* stream);
+
 /* Decode attention for callers that cannot allocate device memory.  No counterpart in the reference
  * (which allocates with PyTorch freely); added for hosts that hand an operator only its input and
  * output buffers: serving engines whose memory planner reserves all device memory up front, code that

@@ -336,7 +336,9 @@ struct DecodeShape {
 
 // Tokens per chunk (one pipeline stage): a multiple of 12 tiles x 16 tokens (every one of the 12
 // warps gets the same number of tiles), about 48 KB of codes, at most 768 tokens.
-int tokens_per_chunk(int D, int kbits, int vbits) { return kvb::chunk_tokens(D, kbits, vbits); }
+int tokens_per_chunk(int D, int kbits, int vbits, int k_mode) {
+    return kvb::chunk_tokens(D, kbits, vbits, k_mode == KVB_K_PER_CHANNEL);
+}
 
 kvb_status validate_cache(const kvb_cache* c, DecodeShape& sh, int Hq, int Tq) {
     if (!c) return fail(KVB_EINVAL, "decode: null cache");
@@ -378,6 +380,10 @@ kvb_status validate_cache(const kvb_cache* c, DecodeShape& sh, int Hq, int Tq) {
             return fail(KVB_EINVAL, "decode: stratum %d n / n_alloc", i);
         if (c->k_mode == KVB_K_PER_CHANNEL && s.n_alloc % c->k_group)
             return fail(KVB_EINVAL, "decode: n_alloc must be a multiple of k_group");
+        if (c->k_mode == KVB_K_PER_CHANNEL && tokens_per_chunk(sh.D, s.kbits, s.vbits, c->k_mode) % c->k_group)
+            return fail(KVB_EUNSUPPORTED, "decode: per-channel key groups of %d tokens with %d/%d-bit codes "
+                        "(chunks of %d tokens must hold whole groups)", c->k_group, s.kbits, s.vbits,
+                        tokens_per_chunk(sh.D, s.kbits, s.vbits, c->k_mode));
         if (s.n > 0 && (!s.kc || !s.vc || !s.kmeta || !s.vmeta)) return fail(KVB_EINVAL, "decode: null stratum pointer");
         if (!aligned(s.kc, 16) || !aligned(s.vc, 16) || !aligned(s.kmeta, 16) || !aligned(s.vmeta, 16))
             return fail(KVB_EINVAL, "decode: stratum %d pointers must be 16-byte aligned", i);
@@ -406,7 +412,7 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
     int64_t chunks_per_head = 0, w_head = 0;
     for (int s = 0; s < c->n_strata; ++s) {
         const kvb_stratum& st = c->strata[s];
-        P.tok[s] = tokens_per_chunk(c->d_code, st.kbits, st.vbits);
+        P.tok[s] = tokens_per_chunk(c->d_code, st.kbits, st.vbits, c->k_mode);
         nch[s] = (st.n + P.tok[s] - 1) / P.tok[s];
         const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + 8;
         wfull[s] = int64_t(P.tok[s]) * bpt;
@@ -563,16 +569,58 @@ size_t kvb_decode_workspace_size(const kvb_cache* c, int Hq, int Tq, int n_ctas)
     return ws_layout(c, sh, P.n_pieces).total;
 }
 
+}  // extern "C"
+
+namespace {
+kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                       const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas, void* workspace,
+                       size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end);
+}  // namespace
+
+extern "C" {
+
 kvb_status kvb_decode(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                       const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* workspace,
                       size_t workspace_bytes, void* stream) {
-    return kvb_decode_events(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, n_ctas, workspace, workspace_bytes,
-                             stream, nullptr, nullptr);
+    return decode_impl(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, nullptr, n_ctas, workspace,
+                       workspace_bytes, stream, nullptr, nullptr);
 }
 
 kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                              const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* workspace,
                              size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end) {
+    return decode_impl(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, nullptr, n_ctas, workspace,
+                       workspace_bytes, stream, ev_begin, ev_end);
+}
+
+kvb_status kvb_decode_lse(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                          const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    if (!lse) return fail(KVB_EINVAL, "decode_lse: null lse");
+    if (!aligned(lse, 4)) return fail(KVB_EINVAL, "decode_lse: lse alignment");
+    return decode_impl(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, lse, n_ctas, workspace,
+                       workspace_bytes, stream, nullptr, nullptr);
+}
+
+kvb_status kvb_lse_merge(const float* parts, int64_t part_stride, const float* lse, int64_t lse_stride, int n_parts,
+                         int64_t rows, int d, void* out, int out_dtype, void* stream) {
+    if (!parts || !lse || !out) return fail(KVB_EINVAL, "lse_merge: null pointer");
+    if (n_parts <= 0 || rows <= 0 || d <= 0 || d > 1024 || part_stride < rows * d || lse_stride < rows)
+        return fail(KVB_EINVAL, "lse_merge: sizes");
+    if (out_dtype != KVB_F32 && out_dtype != KVB_F16 && out_dtype != KVB_BF16) return fail(KVB_EINVAL, "lse_merge: out dtype");
+    if (rows > (int64_t(1) << 34)) return fail(KVB_EUNSUPPORTED, "lse_merge: too many rows");
+    kvb::LseMergeParams p{parts, lse, part_stride, lse_stride, rows, n_parts, d,
+                          out_dtype == KVB_F32 ? 0 : out_dtype == KVB_F16 ? 1 : 2, out};
+    kvb::lse_merge_kernel<<<unsigned((rows + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    return launch_check("lse_merge_kernel");
+}
+
+}  // extern "C"
+
+namespace {
+kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                       const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas, void* workspace,
+                       size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end) {
     DecodeShape sh{};
     kvb_status st = validate_cache(c, sh, Hq, Tq);
     if (st) return st;
@@ -675,6 +723,7 @@ kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int
     mp.lift = c->lift;
     mp.mu_v = c->mu_v;
     mp.out = out;
+    mp.lse = lse;
     for (int h = 0; h <= P.n_heads; ++h) mp.head_begin[h] = P.head_begin[h];
     const int Ra = rep * Tq;
     const size_t msm = size_t(Ra) * (2 * c->d + c->d_code) * 4 + 3 * Ra * 4 + 256 * 4;
@@ -686,8 +735,7 @@ kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int
 #undef KVB_MERGE
     return launch_check("decode_merge");
 }
-
-}  // extern "C"
+}  // namespace
 
 // =============================================================================================
 // Allocation-free decode.  For callers that may not allocate device memory at all (serving engines

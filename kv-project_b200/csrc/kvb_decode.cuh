@@ -140,19 +140,53 @@ __global__ void __launch_bounds__(128) decode_prologue(const PrologueParams p) {
 // ------------------------------------------------------------------------------------------
 // 2. main kernel
 // ------------------------------------------------------------------------------------------
-// Per-channel key fragments of one token group, computed by the producer warp into the stage.
-template <int D, int R, int GK, int GV, int KMODE, int CODE, int KB>
-__device__ void build_channel_frag(uint8_t* dst, const float* qp, const uint32_t* kmeta_group, int lane) {
+// Sum of R per-lane values over the warp, scattered: on return lane l holds the total of row
+// row_of(l) (rows from lane bits 4, 3(, 2)); log2(R) halving rounds then full xor rounds.
+template <int R>
+__device__ __forceinline__ float reduce_rows(float (&w)[R], int lane) {
+    constexpr int LOG = R == 8 ? 3 : R == 4 ? 2 : R == 2 ? 1 : 0;
+#pragma unroll
+    for (int round = 0; round < LOG; ++round) {
+        const int half = (R >> round) / 2;
+        const int m = 16 >> round;
+        const bool up = lane & m;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float mine = up ? w[i + half] : w[i];
+            const float other = up ? w[i] : w[i + half];
+            w[i] = mine + __shfl_xor_sync(0xffffffffu, other, m);
+        }
+    }
+    float v = w[0];
+#pragma unroll
+    for (int m = 16 >> LOG; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+template <int R>
+__device__ __forceinline__ int reduce_row_of(int lane) {
+    constexpr int LOG = R == 8 ? 3 : R == 4 ? 2 : R == 2 ? 1 : 0;
+    int r = 0;
+#pragma unroll
+    for (int round = 0; round < LOG; ++round) r = 2 * r + ((lane >> (4 - round)) & 1);
+    return r;
+}
+
+// One unit of the per-channel key fragments of a chunk: token group `grp` (its raw (lo, scale)
+// pairs at `kraw`), k-steps 2 KP and 2 KP + 1 = 32 channels.  Writes those k-steps' B fragments
+// (query x scale, split hi / lo in fp16), the unit's share of the 8 column sums and of the R row
+// biases sum_c q[r][c] lo[c].  Built by all warps together, one unit each (see decode_main).
+template <int D, int R, int GK, int GV, int KMODE, int CODE, int KB, int KP>
+__device__ __forceinline__ void build_channel_unit(uint8_t* frag, const uint32_t* kraw, const float* qc, int lane) {
     using C = DecCfg<D, R, GK, GV, KMODE, CODE>;
     using LK = Lay<D, KB>;
     constexpr int KS = C::KS, NB = C::NB;
     const int g = lane >> 2, t = lane & 3;
-    const float* qc = qp + qp_qc(R);
     const int r = C::KC::row(g);
-    uint2* fr = reinterpret_cast<uint2*>(dst);
+    uint2* fr = reinterpret_cast<uint2*>(frag);
     float cs = 0.f;
 #pragma unroll
-    for (int k = 0; k < KS; ++k) {
+    for (int kk = 0; kk < 2; ++kk) {
+        const int k = 2 * KP + kk;
         uint32_t regs[NB][2];
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
@@ -160,8 +194,8 @@ __device__ void build_channel_frag(uint8_t* dst, const float* qp, const uint32_t
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
                 const int ch = LK::kch(t, 2 * k + s, hh);
-                const float sc = unpack_half2(kmeta_group[ch]).y;
-                const float v = qc[r * D + ch] * sc / LK::kf(2 * k + s);
+                const float sc = unpack_half2(kraw[ch]).y;
+                const float v = __ldg(qc + r * D + ch) * sc * (1.f / LK::kf(2 * k + s));
                 const float hi = __half2float(__float2half_rn(v));
                 const float lo = __half2float(__float2half_rn(v - hi));
                 hv[hh][0] = hi;
@@ -172,19 +206,42 @@ __device__ void build_channel_frag(uint8_t* dst, const float* qp, const uint32_t
             regs[NB - 1][s] = pack_half2(hv[0][1], hv[1][1]);
         }
 #pragma unroll
-        for (int s = 0; s < NB; ++s) fr[(s * KS + k) * 32 + lane] = make_uint2(regs[s][0], regs[s][1]);
+        for (int part = 0; part < NB; ++part) fr[(part * KS + k) * 32 + lane] = make_uint2(regs[part][0], regs[part][1]);
     }
     cs += __shfl_xor_sync(0xffffffffu, cs, 1);
     cs += __shfl_xor_sync(0xffffffffu, cs, 2);
-    float* colsum = reinterpret_cast<float*>(dst + NB * KS * 32 * 8);
-    if (t == 0) colsum[g] = cs;
-    // bias[r] = sum_ch q[r][ch] * lo[ch]
+    float* colsum = reinterpret_cast<float*>(frag + NB * KS * 32 * 8);      // [8][4]
+    float* bias = colsum + 8 * 4;                                           // [R][4]
+    if (t == 0) colsum[g * 4 + KP] = cs;
+    // bias partial over this unit's 32 channels: lane l takes channel l of the unit
+    {
+        const int tt = lane & 3, idx = lane >> 2;
+        const int k = 2 * KP + (idx >> 2), s = (idx >> 1) & 1, hh = idx & 1;
+        const int ch = LK::kch(tt, 2 * k + s, hh);
+        const float lo = unpack_half2(kraw[ch]).x;
+        float w[R];
 #pragma unroll
-    for (int rr = 0; rr < R; ++rr) {
-        float b = 0.f;
-        for (int ch = lane; ch < D; ch += 32) b = fmaf(qc[rr * D + ch], unpack_half2(kmeta_group[ch]).x, b);
-        b = warp_sum(b);
-        if (lane == 0) colsum[8 + rr] = b;
+        for (int rr = 0; rr < R; ++rr) w[rr] = __ldg(qc + rr * D + ch) * lo;
+        const float b = reduce_rows<R>(w, lane);
+        if ((lane & (32 / R - 1)) == 0) bias[reduce_row_of<R>(lane) * 4 + KP] = b;
+    }
+}
+
+// Every warp builds its units (u = warp, warp + 12, ...) of the chunk's ng token groups x 4 units.
+template <int D, int R, int GK, int GV, int KMODE, int CODE, int KB>
+__device__ __forceinline__ void build_channel_frags(uint8_t* km, const uint8_t* kr, int ng, const float* qc, int warp,
+                                                    int lane) {
+    using C = DecCfg<D, R, GK, GV, KMODE, CODE>;
+    for (int u = warp; u < ng * 4; u += DEC_CWARPS) {
+        const int gi = u >> 2;
+        uint8_t* frag = km + gi * C::FRAG_BYTES;
+        const uint32_t* kraw = reinterpret_cast<const uint32_t*>(kr) + gi * D;
+        switch (u & 3) {
+            case 0: build_channel_unit<D, R, GK, GV, KMODE, CODE, KB, 0>(frag, kraw, qc, lane); break;
+            case 1: build_channel_unit<D, R, GK, GV, KMODE, CODE, KB, 1>(frag, kraw, qc, lane); break;
+            case 2: build_channel_unit<D, R, GK, GV, KMODE, CODE, KB, 2>(frag, kraw, qc, lane); break;
+            default: build_channel_unit<D, R, GK, GV, KMODE, CODE, KB, 3>(frag, kraw, qc, lane); break;
+        }
     }
 }
 
@@ -242,23 +299,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
                 kmb = (kmb + 15) & ~15;
                 vmb = (vmb + 15) & ~15;
                 bytes += kmb + vmb;
-                if constexpr (KMODE == KM_CHANNEL) {
-                    // fragments of every token group of the chunk (producer-side compute)
-                    const int ng = (rows + p.k_group - 1) / p.k_group;
-                    const uint32_t* kmg = static_cast<const uint32_t*>(sd.km) +
-                                          (int64_t(head) * (sd.n_alloc / p.k_group) + tok0 / p.k_group) * D;
-                    for (int gi = 0; gi < ng; ++gi) {
-                        uint8_t* dst = st + L.km + gi * C::FRAG_BYTES;
-                        if constexpr (D * 2 >= 128) {
-                            if (sd.kbits == 2) build_channel_frag<D, R, GK, GV, KMODE, CODE, 2>(dst, qp, kmg + gi * D, lane);
-                        }
-                        if constexpr (D * 4 >= 128) {
-                            if (sd.kbits == 4) build_channel_frag<D, R, GK, GV, KMODE, CODE, 4>(dst, qp, kmg + gi * D, lane);
-                        }
-                        if (sd.kbits == 8) build_channel_frag<D, R, GK, GV, KMODE, CODE, 8>(dst, qp, kmg + gi * D, lane);
-                    }
-                    __syncwarp();
-                }
+                // per-channel keys: the raw (lo, scale) pairs of the chunk's token groups; the query x
+                // scale fragments are built from them by all warps once the stage has landed
+                int krb = 0;
+                if constexpr (KMODE == KM_CHANNEL) krb = ((rows + p.k_group - 1) / p.k_group) * D * 4;
+                bytes += krb;
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&full[s], uint32_t(bytes));
                     bulk_g2s(st + L.kc, sd.kc + row0 * rbk, rows * rbk, &full[s]);
@@ -266,6 +311,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
                     if (KMODE == KM_TOKEN) {
                         const int per = CODE == KV_MIDRISE ? 2 : GK * 4;
                         bulk_g2s(st + L.km, static_cast<const uint8_t*>(sd.km) + row0 * per, kmb, &full[s]);
+                    } else {
+                        const uint8_t* kmg = static_cast<const uint8_t*>(sd.km) +
+                                             (int64_t(head) * (sd.n_alloc / p.k_group) + tok0 / p.k_group) * D * 4;
+                        bulk_g2s(st + L.kr, kmg, krb, &full[s]);
                     }
                     const int perv = CODE == KV_MIDRISE ? 2 : GV * 4;
                     bulk_g2s(st + L.vm, static_cast<const uint8_t*>(sd.vm) + row0 * perv, vmb, &full[s]);
@@ -293,7 +342,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
             typename TL::Ctx X;
             TL::build_ctx(X, qp, lane);
             const typename TL::Off O = TL::lane_off(L, lane);
-            constexpr int TOK = chunk_tokens(D, KB, VB);
+            constexpr int TOK = chunk_tokens(D, KB, VB, KMODE == KM_CHANNEL);
             constexpr int PW = TOK / 16 / DEC_CWARPS;            // tiles per warp in a full chunk
             WarpState<C> S;
 #pragma unroll
@@ -317,6 +366,18 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
                 const uint32_t ph = (it / p.nstage) & 1;
                 // after a timeout, keep polling briefly (a fill may still land) but skip the compute
                 if (!mbar_wait(&full[s], ph, ok ? 2000000000ull : 1000000ull)) ok = false;
+                if constexpr (KMODE == KM_CHANNEL) {
+                    // all warps build this chunk's per-channel fragments, then meet before using them
+                    if (ok) {
+                        const int64_t tok0 = int64_t(ch) * sd.tok;
+                        const int ntok = int(imin64(sd.tok, sd.n - tok0));
+                        const int ng = (ntok + p.k_group - 1) / p.k_group;
+                        uint8_t* st = stages + s * p.stage_bytes;
+                        build_channel_frags<D, R, GK, GV, KMODE, CODE, KB>(st + L.km, st + L.kr, ng, qp + qp_qc(R),
+                                                                           warp, lane);
+                    }
+                    __syncthreads();
+                }
                 if (ok) {
                     const int64_t tok0 = int64_t(ch) * sd.tok;
                     const int ntok = int(imin64(sd.tok, sd.n - tok0));
@@ -404,6 +465,7 @@ struct MergeParams {
     const float* lift;      // (Hkv, d_code, d) or null
     const float* mu_v;      // (Hkv, d) or null
     void* out;
+    float* lse;             // (B, Tq, Hq) natural-log sum of exp(scaled logits), or null
     int head_begin[MERGE_MAX_HEADS + 1];
 };
 
@@ -514,13 +576,68 @@ __global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ Merg
         }
     }
     __syncthreads();
+    // a row with no readable token (possible in one part of a sequence split) gets 0 and lse -inf
     for (int o = tid; o < Ra * d; o += blockDim.x) {
         const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
-        const float v = s_out[o] / s_rowL[r];
+        const float v = s_rowL[r] > 0.f ? s_out[o] / s_rowL[r] : 0.f;
         const size_t oi = ((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c;
         if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
         else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
         else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
+    }
+    if (p.lse && tid < Ra) {
+        const int i = tid / p.Tq, t = tid % p.Tq;
+        const float L = s_rowL[tid];
+        p.lse[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
+            L > 0.f ? (s_rowM[tid] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+    }
+}
+
+// Merge of P attention parts over disjoint token sets (a sequence split across ranks): row r of
+// part k is a normalised output o_k (d floats) with its natural-log mass lse_k; the merged row is
+// sum_k exp(lse_k - M) o_k / sum_k exp(lse_k - M), M = max_k lse_k (the LSE merge of
+// StrataState.attend STRATA_KV.py:1784-1792 applied across parts).  One warp per row.
+struct LseMergeParams {
+    const float* parts;     // part k, row r, channel c at parts[k * part_stride + r * d + c]
+    const float* lse;       // lse[k * lse_stride + r]
+    int64_t part_stride, lse_stride, rows;
+    int n_parts, d, out_dtype;
+    void* out;              // (rows, d)
+};
+
+__global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ LseMergeParams p) {
+    const int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= p.rows) return;
+    float M = -INFINITY;
+    for (int k = 0; k < p.n_parts; ++k) M = fmaxf(M, p.lse[k * p.lse_stride + r]);
+    float wsum = 0.f;
+    for (int c0 = 0; c0 < p.d; c0 += 128) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float ws = 0.f;
+        for (int k = 0; k < p.n_parts; ++k) {
+            const float l = p.lse[k * p.lse_stride + r];
+            if (l == -INFINITY) continue;
+            const float w = __expf(l - M);
+            ws += w;
+            const float* src = p.parts + k * p.part_stride + r * p.d + c0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int c = lane + 32 * e;
+                if (c0 + c < p.d) acc[e] = fmaf(w, src[c], acc[e]);
+            }
+        }
+        wsum = ws;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int c = c0 + lane + 32 * e;
+            if (c >= p.d) continue;
+            const float v = wsum > 0.f ? acc[e] / wsum : 0.f;
+            const size_t oi = size_t(r) * p.d + c;
+            if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
+            else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
+            else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
+        }
     }
 }
 

@@ -102,22 +102,27 @@ struct DecCfg {
     static constexpr int NB = (KMODE == KM_CHANNEL || CODE == KV_MIDRISE) ? 2 : 1;   // hi / lo query split
     static constexpr int KS = D / 16;
     static constexpr int MT = D / 16;
-    // per-channel fragments: NB x KS x 32 lanes x uint2, then 8 column sums, then R biases
-    static constexpr int FRAG_BYTES = ((NB * KS * 32 * 8 + 8 * 4 + R * 4) + 15) / 16 * 16;
+    // per-channel fragments of one token group: NB x KS x 32 lanes x uint2, then the column sums
+    // [8 columns][4 k-step pairs] and the row biases [R rows][4 k-step pairs] (partials of the four
+    // 32-channel units that built them; readers add the four)
+    static constexpr int FRAG_BYTES = ((NB * KS * 32 * 8 + 8 * 4 * 4 + R * 4 * 4) + 15) / 16 * 16;
 };
 
 // Tokens per chunk (one pipeline stage): a multiple of 12 tiles x 16 tokens (every warp gets the
-// same number of tiles), about 48 KB of codes, at most 768 tokens.  Shared by host and device.
-__host__ __device__ constexpr int chunk_tokens(int D, int kbits, int vbits) {
+// same number of tiles), about 48 KB of codes, at most 768 tokens; with per-channel keys at most
+// 384 (a multiple of every key group size, and room for the groups' query fragments).  Shared by
+// host and device.
+__host__ __device__ constexpr int chunk_tokens(int D, int kbits, int vbits, bool per_channel = false) {
     const int rb = D * kbits / 8 + D * vbits / 8;
     const int unit = DEC_CWARPS * 16;
     const int m = 49152 / (unit * rb) > 1 ? 49152 / (unit * rb) : 1;
-    return unit * m < 4 * unit ? unit * m : 4 * unit;
+    const int cap = per_channel ? 2 * unit : 4 * unit;
+    return unit * m < cap ? unit * m : cap;
 }
 
 // Shared-memory layout of one stage for a stratum.
 struct StageLay {
-    int kc, vc, km, vm, end;
+    int kc, vc, km, kr, vm, end;     // kr: raw per-channel (lo, scale) pairs of the chunk's key groups
 };
 template <int D, int R, int GK, int GV, int KMODE, int CODE>
 __host__ __device__ inline StageLay stage_lay(int kbits, int vbits, int tok, int kgroup) {
@@ -126,11 +131,16 @@ __host__ __device__ inline StageLay stage_lay(int kbits, int vbits, int tok, int
     L.kc = 0;
     L.vc = tok * D * kbits / 8;
     L.km = L.vc + tok * D * vbits / 8;
-    int kmb, vmb;
-    if (KMODE == KM_CHANNEL) kmb = (tok / kgroup) * C::FRAG_BYTES;
-    else kmb = CODE == KV_MIDRISE ? tok * 2 : tok * GK * 4;
+    int kmb, vmb, krb = 0;
+    if (KMODE == KM_CHANNEL) {
+        kmb = (tok / kgroup) * C::FRAG_BYTES;
+        krb = (tok / kgroup) * D * 4;
+    } else {
+        kmb = CODE == KV_MIDRISE ? tok * 2 : tok * GK * 4;
+    }
     vmb = CODE == KV_MIDRISE ? tok * 2 : tok * GV * 4;
-    L.vm = L.km + ((kmb + 15) / 16) * 16;
+    L.kr = L.km + ((kmb + 15) / 16) * 16;
+    L.vm = L.kr + ((krb + 15) / 16) * 16;
     L.end = L.vm + ((vmb + 15) / 16) * 16;
     return L;
 }
@@ -311,12 +321,13 @@ struct Tile {
                 dot[j][e] = v;
             }
         if constexpr (KMODE == KM_CHANNEL) {
-            const float* cs = reinterpret_cast<const float*>(cf + NB * KS * 32 * 8);
-            const float* bias = cs + 8;
+            const float4* cs = reinterpret_cast<const float4*>(cf + NB * KS * 32 * 8);   // [8 columns]
+            const float4* bias = cs + 8;                                                 // [R rows]
             const int r0 = (2 * t) % R;
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                const float k0 = bias[r0 + e] - 1024.f * cs[2 * t + e];
+                const float4 c4 = cs[2 * t + e], b4 = bias[r0 + e];
+                const float k0 = ((b4.x + b4.y) + (b4.z + b4.w)) - 1024.f * ((c4.x + c4.y) + (c4.z + c4.w));
                 s2[0][e] = X.lam * (dot[0][e] + k0) + X.qb[e];
                 s2[1][e] = X.lam * (dot[0][2 + e] + k0) + X.qb[e];
             }

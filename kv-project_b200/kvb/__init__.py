@@ -7,9 +7,11 @@ strata assignment (K2), fused split-K flash decoding over packed codes (K3) and 
 ``include/kvb.h``); this package only moves tensors and builds descriptors.
 """
 
-from . import _lib, ops, cache, workloads          # noqa: F401
+from . import _lib, ops, cache, workloads, state, seqsplit   # noqa: F401
 from .ops import (PackedCache, quant_pack, key_energy, rank_split, query_scores, decode, decode_plan,  # noqa: F401
                   device_status, UNIFORM_STEP)
+from .state import KvbStrataState, KvbCodedState, tier_as_kvb  # noqa: F401
 
-__all__ = ["ops", "cache", "workloads", "PackedCache", "quant_pack", "key_energy", "rank_split",
-           "query_scores", "decode", "decode_plan", "device_status", "UNIFORM_STEP"]
+__all__ = ["ops", "cache", "workloads", "state", "seqsplit", "PackedCache", "quant_pack", "key_energy", "rank_split",
+           "query_scores", "decode", "decode_plan", "device_status", "UNIFORM_STEP",
+           "KvbStrataState", "KvbCodedState", "tier_as_kvb"]

@@ -52,6 +52,9 @@ SIGNATURES = {
                           _p, C.c_size_t, _p]),
     "kvb_decode_events": (_i32, [C.POINTER(Cache), _p, _i32, _i32, _i32, _f32, C.POINTER(C.c_int64), _p, _i32,
                                  _i32, _p, C.c_size_t, _p, _p, _p]),
+    "kvb_decode_lse": (_i32, [C.POINTER(Cache), _p, _i32, _i32, _i32, _f32, C.POINTER(C.c_int64), _p, _i32, _p,
+                              _i32, _p, C.c_size_t, _p]),
+    "kvb_lse_merge": (_i32, [_p, _i64, _p, _i64, _i32, _i64, _i32, _p, _i32, _p]),
     "kvb_decode_plan": (C.c_int64, [C.POINTER(Cache), _i32, C.POINTER(C.c_int32), C.c_int64]),
     "kvb_decode_noalloc": (_i32, [C.POINTER(Cache), _p, _i32, _i32, _i32, _f32, C.POINTER(C.c_int64), _p, _i32,
                                   _i32, _p]),

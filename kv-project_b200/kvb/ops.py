@@ -277,6 +277,42 @@ def decode(cache: PackedCache, q: torch.Tensor, scaling: float, qpos=None, out=N
     return out
 
 
+def decode_lse(cache: PackedCache, q: torch.Tensor, scaling: float, out: torch.Tensor, lse: torch.Tensor,
+               qpos=None, n_ctas: int = 0):
+    """decode() that also writes lse (B, Tq, Hq) float32 (natural log of the attended mass); `out`
+    (B, Tq, Hq, d) and `lse` are caller-provided (views of one exchange buffer in a sequence split)."""
+    _cuda(q, out, lse)
+    q = q.contiguous()
+    B, Hq, Tq, d = q.shape
+    if (B != cache.B or d != cache.d or tuple(out.shape) != (B, Tq, Hq, d) or tuple(lse.shape) != (B, Tq, Hq)
+            or lse.dtype != torch.float32 or not out.is_contiguous() or not lse.is_contiguous()):
+        raise ValueError("decode_lse: q / out / lse shapes do not match the cache")
+    ws = cache.workspace(Hq, Tq, n_ctas)
+    c = cache.struct()
+    qp = None if qpos is None else (C.c_int64 * Tq)(*[int(v) for v in qpos])
+    L.check(L.lib().kvb_decode_lse(C.byref(c), _ptr(q), dtype_code(q), Hq, Tq, C.c_float(scaling), qp, _ptr(out),
+                                   dtype_code(out), _ptr(lse), n_ctas, _ptr(ws), ws.numel(),
+                                   C.c_void_p(_stream(q.device))), "kvb_decode_lse")
+    return out, lse
+
+
+def lse_merge(parts: torch.Tensor, lse: torch.Tensor, out: torch.Tensor = None, out_dtype=None) -> torch.Tensor:
+    """parts (P, rows..., d) float32, lse (P, rows...) float32 -> merged (rows..., d).  Strided views
+    are accepted along P (e.g. the two regions of a gathered exchange buffer)."""
+    _cuda(parts, lse)
+    P, d = parts.shape[0], parts.shape[-1]
+    rows = lse[0].numel()
+    if parts.dtype != torch.float32 or lse.dtype != torch.float32 or parts[0].numel() != rows * d:
+        raise ValueError("lse_merge: parts (P, ..., d) and lse (P, ...) float32 with matching rows")
+    if not (parts[0].is_contiguous() and lse[0].is_contiguous()):
+        raise ValueError("lse_merge: each part must be contiguous")
+    if out is None:
+        out = torch.empty(parts.shape[1:], dtype=out_dtype or torch.float32, device=parts.device)
+    L.check(L.lib().kvb_lse_merge(_ptr(parts), parts.stride(0), _ptr(lse), lse.stride(0), P, rows, d, _ptr(out),
+                                  dtype_code(out), C.c_void_p(_stream(parts.device))), "kvb_lse_merge")
+    return out
+
+
 def decode_noalloc(cache: PackedCache, q: torch.Tensor, scaling: float, out: torch.Tensor, qpos=None,
                    n_ctas: int = 0) -> torch.Tensor:
     """Decode attention for callers that cannot allocate device memory (an engine that owns every

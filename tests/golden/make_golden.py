@@ -181,7 +181,42 @@ def main():
     st["qr"], st["qb"] = np32(qr), np32(qb)
     np.savez_compressed(HERE / "strata.npz", **st)
 
-    sizes = {f: (HERE / f).stat().st_size for f in ("codecs.npz", "select.npz", "attention.npz", "strata.npz")}
+    # ---- StrataState at head dim 128: packed state + attend after appends (drop-in pin) ---------
+    ss = {}
+    Hkv, rep, dd, H = 2, 4, 128, 640
+    fr = S._fake_runner(dd, Hkv, rep, dev=torch.device("cpu"))
+    spec = torch.exp(-torch.arange(dd) / 24.0)
+    Kx = torch.randn(1, Hkv, H, dd, generator=g) * spec.sqrt() * 3 + 0.5
+    Vx = torch.randn(1, Hkv, H, dd, generator=g)
+    Qx = torch.randn(1, Hkv * rep, H, dd, generator=g) * spec.sqrt() * 3
+    meth = S.StrataMethod(tc, 0.12, "t", fr)
+    meth.begin()
+    meth.freeze_at, meth.capture_extra = H, 4
+    pos = torch.arange(H)
+    K2, V2, hide, tok = meth.entries(0, Qx, Kx, Vx, dd ** -0.5, pos)
+    meth.capture(0, K2, V2, pos, hide, tok)
+    sn = meth.native_state(0, Kx, Vx, 4, torch.float32)
+    ss.update(Ke=np32(sn.K[:, :, :sn.n0]), Ve=np32(sn.V[:, :, :sn.n0]), n0=np.array(sn.n0), H=np.array(H),
+              extra=np.array(4), R=np32(sn.R), mu_k=np32(sn.p["mu_k"]), mu_v=np32(sn.p["mu_v"]),
+              counts=sn.p["counts"].numpy(), n_c=np.array(sn.p["n_c"]), n_tiers=np.array(len(sn.p["tiers"])),
+              context_bytes=np.array(sn.context_bytes()))
+    for i, t in enumerate(sn.p["tiers"]):
+        ss[f"t{i}_bits"], ss[f"t{i}_n"] = np.array(t["bits"]), np.array(t["n"])
+        ss[f"t{i}_kc"], ss[f"t{i}_vc"] = t["kc"].numpy(), t["vc"].numpy()
+        ss[f"t{i}_ks"], ss[f"t{i}_vs"] = t["ks"].numpy(), t["vs"].numpy()           # fp16 as stored
+    # step 1: one appended token, one query at position H; step 2: a second token, two queries
+    kn, vn = torch.randn(1, Hkv, 2, dd, generator=g), torch.randn(1, Hkv, 2, dd, generator=g)
+    q1 = torch.randn(1, Hkv * rep, 1, dd, generator=g) * spec.sqrt() * 3
+    q2 = torch.randn(1, Hkv * rep, 2, dd, generator=g) * spec.sqrt() * 3
+    sn.append(kn[:, :, :1], vn[:, :, :1], torch.tensor([H]))
+    o1 = sn.attend(q1, dd ** -0.5, torch.tensor([H]))
+    sn.append(kn[:, :, 1:], vn[:, :, 1:], torch.tensor([H + 1]))
+    o2 = sn.attend(q2, dd ** -0.5, torch.tensor([H, H + 1]))
+    ss.update(kn=np32(kn), vn=np32(vn), q1=np32(q1), q2=np32(q2), out1=np32(o1), out2=np32(o2))
+    np.savez_compressed(HERE / "strata_state.npz", **ss)
+
+    sizes = {f: (HERE / f).stat().st_size
+             for f in ("codecs.npz", "select.npz", "attention.npz", "strata.npz", "strata_state.npz")}
     print("wrote", sizes)
 
 

@@ -1,0 +1,140 @@
+"""Sequence split of a layer over ranks (config 4, batch <= 4): token ranges, the exchange buffer and
+its all-gather (2 gloo ranks on CPU, oracle partials standing in for the GPU decode), and on the GPU
+the decode_lse parts of P slices merged by kvb_lse_merge against the full-context decode."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from kvref import np32
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_token_ranges():
+    from kvb.seqsplit import token_ranges
+    for T, world, align in [(131072, 8, 128), (4096, 3, 128), (1000, 4, 64), (100, 2, 128), (5, 1, 16)]:
+        rs = token_ranges(T, world, align)
+        assert len(rs) == world and rs[0][0] == 0 and rs[-1][1] == T
+        for (a, b), (c, _) in zip(rs, rs[1:]):
+            assert b == c and b % align == 0
+        sizes = [b - a for a, b in rs]
+        assert max(sizes) - min(sizes) <= align
+    with pytest.raises(ValueError):
+        token_ranges(0, 2)
+
+
+def _partial(q, scaling, K, V):
+    """Oracle part over a token range: normalised output (B, Tq, Hq, d) and natural-log mass (B, Tq, Hq)."""
+    B, Hq, Tq, d = q.shape
+    Hkv = K.shape[1]
+    rep = Hq // Hkv
+    qg = q.reshape(B, Hkv, rep * Tq, d)
+    s = np.einsum("bhrd,bhnd->bhrn", qg, K) * scaling
+    m = s.max(-1)
+    e = np.exp(s - m[..., None])
+    lse = m + np.log(e.sum(-1))
+    o = np.einsum("bhrn,bhnd->bhrd", e, V) / e.sum(-1)[..., None]
+    o = o.reshape(B, Hq, Tq, d).transpose(0, 2, 1, 3)
+    return np.ascontiguousarray(o, np.float32), np.ascontiguousarray(lse.reshape(B, Hq, Tq).transpose(0, 2, 1),
+                                                                     np.float32)
+
+
+def _rank_main(rank, world, port, ret):
+    import torch.distributed as dist
+    from kvb import seqsplit as SS
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(7)
+        B, Hkv, rep, Tq, T, d = 2, 2, 4, 2, 1000, 32
+        K = torch.randn(B, Hkv, T, d, generator=g).numpy()
+        V = torch.randn(B, Hkv, T, d, generator=g).numpy()
+        q = torch.randn(B, Hkv * rep, Tq, d, generator=g).numpy()
+        lo, hi = SS.token_ranges(T, world, 128)[rank]
+        buf = torch.empty(B * Tq * Hkv * rep * (d + 1))
+        o, lse = SS.exchange_views(buf, B, Tq, Hkv * rep, d)
+        po, pl = _partial(q, d ** -0.5, K[:, :, lo:hi], V[:, :, lo:hi])
+        o.copy_(torch.from_numpy(po))
+        lse.copy_(torch.from_numpy(pl))
+        gath = torch.empty(world, buf.numel())
+        SS.all_gather_into(gath, buf)
+        parts, lses = SS.gathered_views(gath, B, Tq, Hkv * rep, d)
+        M = lses.max(0).values
+        w = torch.exp(lses - M)
+        merged = (w[..., None] * parts).sum(0) / w.sum(0)[..., None]
+        full = O.chunked_attention(q, d ** -0.5, np.full(Tq, T), K, V, np.arange(T), np.full(T, 1 << 40), None, 256)
+        ret[rank] = float(np.abs(merged.numpy() - full).max())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_gloo_two_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as man:
+        ret = man.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_rank_main, args=(r, 2, port, ret)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        assert sorted(ret.keys()) == [0, 1]
+        assert max(ret.values()) <= 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("P", [2, 3])
+def test_seqsplit_parts_merge(cuda_dev, P):
+    """P token slices of a config-4-style KIVI cache (4-bit, groups of 128), each decoded with
+    decode_lse into one row of a gathered buffer, merged with kvb_lse_merge == the full decode."""
+    import kvb
+    from kvb import seqsplit as SS
+    B, Hkv, rep, Tq, T, d = 2, 2, 8, 1, 2000, 128
+    K, V = kvb.workloads.outlier_kv(B, Hkv, T, d, torch.bfloat16, seed=11)
+    K, V = K.to(cuda_dev), V.to(cuda_dev)
+    q = kvb.workloads.queries(B, Hkv * rep, Tq, d, torch.bfloat16, seed=11).to(cuda_dev)
+    Hq = Hkv * rep
+    n = B * Tq * Hq * (d + 1)
+    gath = torch.empty((P, n), dtype=torch.float32, device=cuda_dev)
+    for r, (lo, hi) in enumerate(SS.token_ranges(T, P, 128)):
+        cache = kvb.cache.build_kivi(K[:, :, lo:hi], V[:, :, lo:hi], 4, 4, 128, 128)
+        o, lse = SS.exchange_views(gath[r], B, Tq, Hq, d)
+        kvb.ops.decode_lse(cache, q, d ** -0.5, o, lse)
+    parts, lses = SS.gathered_views(gath, B, Tq, Hq, d)
+    merged = kvb.ops.lse_merge(parts, lses, out_dtype=torch.float32)
+    full = kvb.decode(kvb.cache.build_kivi(K, V, 4, 4, 128, 128), q, d ** -0.5, out_dtype=torch.float32)
+    assert (merged - full).abs().max().item() <= 1e-4
+    # and against the oracle (dequantise-then-attend over the whole context)
+    Kh = O.kivi_quant(np32(K), 4, 128, True, 0)["xhat"]
+    Vh = O.kivi_quant(np32(V), 4, 128, False, 0)["xhat"]
+    ref = O.chunked_attention(np32(q), d ** -0.5, np.array([T]), Kh, Vh, np.arange(T), np.full(T, 1 << 40), None, 256)
+    assert np.abs(np32(merged) - ref).max() <= 2e-3
+    # lse of a part is its natural-log mass: exp(lse) sums to the full mass
+    assert torch.isfinite(lses).all()
+
+
+@pytest.mark.gpu
+def test_lse_merge_empty_part(cuda_dev):
+    """A part with lse -inf (no readable token) is ignored; a row with no part gives zeros."""
+    import kvb
+    rows, d = 6, 128
+    parts = torch.randn(3, rows, d, device=cuda_dev)
+    lse = torch.randn(3, rows, device=cuda_dev)
+    lse[1] = -float("inf")
+    lse[:, 5] = -float("inf")
+    out = kvb.ops.lse_merge(parts, lse)
+    w = torch.exp(lse[[0, 2], :5] - lse[[0, 2], :5].max(0).values)
+    ref = (w[..., None] * parts[[0, 2], :5]).sum(0) / w.sum(0)[..., None]
+    assert (out[:5] - ref).abs().max().item() <= 1e-5
+    assert (out[5] == 0).all()
