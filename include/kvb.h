@@ -47,7 +47,8 @@ typedef int kvb_status;
 const char* kvb_last_error(void);
 int kvb_version(void);
 
-/* Device status word (bit 0: a bounded wait timed out; bit 1: a bounds check failed).  Synchronises
+/* Device status word (bit 0: a bounded wait timed out; bit 1: a bounds check failed; bit 2: a NaN
+ * key reached kvb_rank_split, whose ranking is then undefined).  Synchronises
  * `stream`, copies the word to *out and clears it when `clear` is non-zero. */
 kvb_status kvb_device_status(unsigned* out, int clear, void* stream);
 
@@ -108,14 +109,15 @@ kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, 
  * K4: spectral code.  Replaces the basis projection of spectral_side (QUASAR_KV.py:1354-1382, with a
  * fixed per-head orthonormal basis) followed by the per-token mid-rise code of strata_quantize
  * (STRATA_KV.py:1158-1168) on the leading r = 32 coefficients, on tcgen05 tensor cores.
- * x: (B, H, T, 128) fp16, dense, 16-byte aligned.  basis_t: (2, H, 32, 128) fp16 = the transposed
+ * x: (B, H, T, 128) fp16, unit channel stride, element strides sb / sh / st of batch, head and token
+ * (multiples of 8, i.e. 16 bytes: any layout a model's K / V projection produces), 16-byte aligned.  basis_t: (2, H, 32, 128) fp16 = the transposed
  * leading basis columns split into a high part and a low part (basis = hi + lo to ~22 bits).
  * Outputs per kvb_quant_pack's mid-rise layout: codes (B, H, n_alloc, 32 * bits / 8) planar, scales
  * (B, H, n_alloc) fp16; coef (nullable) (B, H, T, 32) float32 coefficients.  `step`: the mid-rise
  * step in RMS units (uniform_step(bits)[0]).  n_ctas: persistent CTAs (0 = one per SM). */
-kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, const void* basis_t, int bits,
-                               float step, uint8_t* codes, void* scales, int64_t n_alloc, float* coef, int n_ctas,
-                               void* stream);
+kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, int64_t sb, int64_t sh, int64_t st,
+                               const void* basis_t, int bits, float step, uint8_t* codes, void* scales,
+                               int64_t n_alloc, float* coef, int n_ctas, void* stream);
 
 /* ------------------------------------------------------------------------------------------ *
  * K3: fused split-K flash decode over a packed, head-synchronous cache.  Replaces StrataState.attend

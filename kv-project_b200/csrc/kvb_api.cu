@@ -94,6 +94,42 @@ kvb_status kvb_quant_pack(const void* x, int x_dtype, int64_t B, int64_t H, int6
     kvb::QuantTokenParams p{x, B, H, T, d, sb, sh, st, idx, first_row, n, n_alloc,
                             bits, group, code_kind == KVB_CODE_MIDRISE ? 1 : 0, step, codes, meta, xhat};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // d = 128, 16-bit rows on 16-byte boundaries: the 128-bit-load kernels
+    const bool fast = d == 128 && (x_dtype == KVB_F16 || x_dtype == KVB_BF16) && aligned(x, 16) && sb % 8 == 0 &&
+                      sh % 8 == 0 && st % 8 == 0 && aligned(meta, 16) && n_alloc > 0;
+    if (fast) {
+        kvb::QuantFastParams f{x, H, T, sb, sh, st, idx, first_row, n, n_alloc, step, codes, meta, xhat};
+        const bool f16 = x_dtype == KVB_F16;
+        if (k_mode == KVB_K_PER_CHANNEL && code_kind == KVB_CODE_ASYM && n_alloc % group == 0 &&
+            (group == 16 || group == 32 || group == 64 || group == 128)) {
+            dim3 grid(unsigned(n_alloc / group), unsigned(B * H));
+#define KVB_QC8(T_, B_, G_) kvb::quant_channel128_kernel<T_, B_, G_><<<grid, 256, 0, s>>>(f)
+#define KVB_QC8G(T_, B_)                                                  \
+    if (group == 16) KVB_QC8(T_, B_, 16); else if (group == 32) KVB_QC8(T_, B_, 32); \
+    else if (group == 64) KVB_QC8(T_, B_, 64); else KVB_QC8(T_, B_, 128)
+#define KVB_QC8B(T_) if (bits == 2) { KVB_QC8G(T_, 2); } else if (bits == 4) { KVB_QC8G(T_, 4); } else { KVB_QC8G(T_, 8); }
+            if (f16) { KVB_QC8B(__half) } else { KVB_QC8B(__nv_bfloat16) }
+#undef KVB_QC8B
+#undef KVB_QC8G
+#undef KVB_QC8
+            return launch_check("quant_channel128_kernel");
+        }
+        const int gsel = code_kind == KVB_CODE_MIDRISE ? (group == 128 ? 0 : -1)
+                                                       : (group == 32 || group == 64 || group == 128 ? group : -1);
+        if (k_mode == KVB_K_PER_TOKEN && gsel >= 0) {
+            dim3 grid(unsigned((n_alloc + 63) / 64), unsigned(B * H));
+#define KVB_QT8(T_, B_, G_) kvb::quant_token128_kernel<T_, B_, G_><<<grid, 256, 0, s>>>(f)
+#define KVB_QT8G(T_, B_)                                                 \
+    if (gsel == 0) KVB_QT8(T_, B_, 0); else if (gsel == 32) KVB_QT8(T_, B_, 32); \
+    else if (gsel == 64) KVB_QT8(T_, B_, 64); else KVB_QT8(T_, B_, 128)
+#define KVB_QT8B(T_) if (bits == 2) { KVB_QT8G(T_, 2); } else if (bits == 4) { KVB_QT8G(T_, 4); } else { KVB_QT8G(T_, 8); }
+            if (f16) { KVB_QT8B(__half) } else { KVB_QT8B(__nv_bfloat16) }
+#undef KVB_QT8B
+#undef KVB_QT8G
+#undef KVB_QT8
+            return launch_check("quant_token128_kernel");
+        }
+    }
     if (k_mode == KVB_K_PER_CHANNEL) {
         if (code_kind != KVB_CODE_ASYM) return fail(KVB_EINVAL, "quant_pack: per-channel mode is asymmetric only");
         if (group != 16 && group != 32 && group != 64 && group != 128)
@@ -174,6 +210,16 @@ kvb_status kvb_key_energy(const void* k, int dtype, int64_t B, int64_t H, int64_
     const int64_t rows = B * H * T;
     const unsigned blocks = unsigned((rows * 32 + 255) / 256);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (d == 128 && (dtype == KVB_F16 || dtype == KVB_BF16) && aligned(k, 16) && sb % 8 == 0 && sh % 8 == 0 &&
+        st % 8 == 0 && B * H <= 65535) {
+        dim3 grid(unsigned((T + 63) / 64), unsigned(B * H));
+        if (dtype == KVB_F16)
+            kvb::key_energy128_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(k), H, T, sb, sh, st, out);
+        else
+            kvb::key_energy128_kernel<__nv_bfloat16>
+                <<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(k), H, T, sb, sh, st, out);
+        return launch_check("key_energy128_kernel");
+    }
     if (dtype == KVB_F32)
         kvb::key_energy_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(k), B, H, T, d, sb, sh, st, out);
     else if (dtype == KVB_F16)
@@ -292,17 +338,37 @@ kvb_status make_map_fp16(CUtensorMap* m, const void* base, int64_t rows, uint32_
 }
 }  // namespace
 
-extern "C" kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, const void* basis_t, int bits,
-                                          float step, uint8_t* codes, void* scales, int64_t n_alloc, float* coef,
-                                          int n_ctas, void* stream) {
+// 4D fp16 tensor map of x (B, H, T, 128) with element strides sb, sh, st: dims (128, T, H, B), box
+// 64 x 128 x 1 x 1, 128-byte swizzle; rows past T read as zeros.
+kvb_status make_map_x4(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t T, int64_t sb, int64_t sh,
+                       int64_t st) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return fail(KVB_ECUDA, "spectral: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[4] = {128, cuuint64_t(T), cuuint64_t(H), cuuint64_t(B)};
+    const cuuint64_t strides[3] = {cuuint64_t(st) * 2, cuuint64_t(sh) * 2, cuuint64_t(sb) * 2};
+    const cuuint32_t box[4] = {64, kvb::SP_TILE, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KVB_ECUDA, "spectral: cuTensorMapEncodeTiled (x) failed (%d)", int(r));
+    return KVB_OK;
+}
+
+extern "C" kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, int64_t sb, int64_t sh,
+                                          int64_t st_, const void* basis_t, int bits, float step, uint8_t* codes,
+                                          void* scales, int64_t n_alloc, float* coef, int n_ctas, void* stream) {
     if (!x || !basis_t || !codes || !scales) return fail(KVB_EINVAL, "spectral_encode: null pointer");
     if (B <= 0 || H <= 0 || T <= 0 || n_alloc < T || n_alloc % 16) return fail(KVB_EINVAL, "spectral_encode: sizes");
     if (bits != 2 && bits != 4 && bits != 8) return fail(KVB_EINVAL, "spectral_encode: bits must be 2, 4 or 8");
     if (!aligned(x, 16) || !aligned(basis_t, 16) || !aligned(codes, 16) || !aligned(scales, 2) || !aligned(coef, 16))
         return fail(KVB_EINVAL, "spectral_encode: alignment");
-    if (B * H * T >= (int64_t(1) << 31)) return fail(KVB_EUNSUPPORTED, "spectral_encode: more than 2^31 rows");
+    if (sb % 8 || sh % 8 || st_ % 8 || st_ < 128 || sb <= 0 || sh <= 0)
+        return fail(KVB_EINVAL, "spectral_encode: row / head / batch strides must be multiples of 8 elements, rows >= 128");
+    if (B * H * ((T + 127) / 128) >= (int64_t(1) << 31) || T >= (int64_t(1) << 31))
+        return fail(KVB_EUNSUPPORTED, "spectral_encode: too many tiles");
     kvb::SpectralParams p{};
-    kvb_status st = make_map_fp16(&p.tmap_x, x, B * H * T, kvb::SP_TILE);
+    kvb_status st = make_map_x4(&p.tmap_x, x, B, H, T, sb, sh, st_);
     if (st) return st;
     if ((st = make_map_fp16(&p.tmap_b, basis_t, 2 * H * kvb::SP_R, kvb::SP_R))) return st;
     p.H = H;
@@ -318,11 +384,15 @@ extern "C" kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, i
     int grid = resolve_ctas(n_ctas);
     if (int64_t(grid) > p.ntiles) grid = int(p.ntiles);
     const size_t smem = 1024 + size_t(kvb::SP_STAGES) * kvb::SP_A_BYTES + 2 * size_t(kvb::SP_B_BYTES) + 256;
-    cudaError_t e = cudaFuncSetAttribute(kvb::spectral_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(smem));
-    if (e != cudaSuccess) return cuda_check(e, "spectral smem attribute");
-    kvb::spectral_encode_kernel<<<grid, kvb::SP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(p);
-    return launch_check("spectral_encode_kernel");
+    auto launch = [&](auto kern) -> kvb_status {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return cuda_check(e, "spectral smem attribute");
+        kern<<<grid, kvb::SP_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(p);
+        return launch_check("spectral_encode_kernel");
+    };
+    if (bits == 2) return launch(kvb::spectral_encode_kernel<2>);
+    if (bits == 4) return launch(kvb::spectral_encode_kernel<4>);
+    return launch(kvb::spectral_encode_kernel<8>);
 }
 
 // =============================================================================================

@@ -15,6 +15,7 @@
 
 #define KVB_DEV_TIMEOUT 1u
 #define KVB_DEV_BOUNDS 2u
+#define KVB_DEV_NAN 4u
 
 namespace kvb {
 

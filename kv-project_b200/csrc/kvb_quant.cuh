@@ -16,6 +16,8 @@
 // Output: packed rows are staged in shared memory and written with 16-byte stores; padding rows
 // [n, n_alloc) are zero-filled so a reader of whole 16-row tiles sees defined bytes.
 #pragma once
+#include <type_traits>
+
 #include "kvb_common.cuh"
 
 namespace kvb {
@@ -231,6 +233,271 @@ __global__ void __launch_bounds__(D) quant_channel_kernel(const QuantTokenParams
     }
     __syncthreads();
     block_copy_out(p.codes + (bh * p.n_alloc + j0) * RB, s_packed, gt * RB);
+}
+
+// =============================================================================================
+// Fast paths for d = 128 with 16-bit inputs whose rows are 16-byte aligned.  16 lanes per row, 8
+// channels per lane (one 128-bit load), so a warp reads two rows per instruction; group extrema by
+// xor shuffles inside the group's 4 / 8 / 16 lanes; division by the group scale through its
+// correctly rounded reciprocal plus Markstein's correction (div_rn_markstein: the exact IEEE
+// quotient, so codes stay bit-identical); planar packing by shuffling the other planes' codes in;
+// 128-bit stores of the packed rows.
+// =============================================================================================
+
+// a / b rounded to nearest even from y = RN(1 / b) (P. Markstein, IBM J. Res. Dev. 34(1), 1990):
+// q0 = RN(a y), r = a - q0 b exactly (FMA), RN(q0 + r y) = RN(a / b) for normal b and quotients
+// that neither overflow nor underflow (b >= 2^-24 here; |a / b| is bounded by the code range).
+__device__ __forceinline__ float div_rn_markstein(float a, float b, float y) {
+    const float q0 = __fmul_rn(a, y);
+    const float r = __fmaf_rn(-q0, b, a);
+    return __fmaf_rn(r, y, q0);
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* src, float (&v)[8]) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(src);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (std::is_same<T, __half>::value) {
+            const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+            v[2 * i] = __low2float(h);
+            v[2 * i + 1] = __high2float(h);
+        } else {
+            const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+            v[2 * i] = __low2float(h);
+            v[2 * i + 1] = __high2float(h);
+        }
+    }
+}
+
+// 8 codes (bytes) of this lane -> the planar-packed bytes it owns, as 2 words; lanes whose l16 is
+// below 16 / P own packed bytes 8 l16 .. 8 l16 + 7 (channels pl * 128 / P + k from lane l16 + 2 pl
+// * 8 / P... i.e. from lanes l16 + pl * 16 / P).  Lanes of the other planes return garbage.
+template <int BITS>
+__device__ __forceinline__ uint2 pack_planar_lane(uint32_t c0, uint32_t c1) {
+    constexpr int P = 8 / BITS;
+    uint32_t w0 = c0, w1 = c1;
+#pragma unroll
+    for (int pl = 1; pl < P; ++pl) {
+        const int m = pl * (16 / P);
+        const uint32_t o0 = __shfl_down_sync(0xffffffffu, c0, m, 16);
+        const uint32_t o1 = __shfl_down_sync(0xffffffffu, c1, m, 16);
+        w0 |= o0 << (pl * BITS);
+        w1 |= o1 << (pl * BITS);
+    }
+    return make_uint2(w0, w1);
+}
+
+// Stores the packed row (RB = 16 * BITS bytes) of one row from the lanes that own it: pairs of
+// lanes combine to 16 bytes, so the row goes out in RB / 16 128-bit stores.
+template <int BITS>
+__device__ __forceinline__ void store_packed(uint8_t* row, uint2 w, int l16) {
+    constexpr int P = 8 / BITS, OWN = 16 / P;          // lanes owning the packed row (8 bytes each)
+    const uint32_t n0 = __shfl_down_sync(0xffffffffu, w.x, 1, 16);
+    const uint32_t n1 = __shfl_down_sync(0xffffffffu, w.y, 1, 16);
+    if (l16 < OWN && (l16 & 1) == 0) *reinterpret_cast<uint4*>(row + 8 * l16) = make_uint4(w.x, w.y, n0, n1);
+}
+
+struct QuantFastParams {
+    const void* x;
+    int64_t H, T, sb, sh, st;
+    const int64_t* idx;
+    int64_t first_row, n, n_alloc;
+    float step;
+    uint8_t* codes;
+    void* meta;
+    float* xhat;
+};
+
+// GROUP: channels per (lo, scale) group (32, 64, 128) or 0 for the mid-rise code.  grid = (ceil(
+// n_alloc / 64), B * H), block 256: 8 warps x 2 rows x 4 passes = 64 rows per CTA.
+template <typename T, int BITS, int GROUP>
+__global__ void __launch_bounds__(256) quant_token128_kernel(const QuantFastParams p) {
+    constexpr int D = 128, TOP = (1 << BITS) - 1, RB = D * BITS / 8;
+    constexpr int LPG = GROUP ? GROUP / 8 : 16;         // lanes per group
+    constexpr int G = GROUP ? D / GROUP : 1;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int l16 = lane & 15, half = lane >> 4;
+    const int64_t bh = blockIdx.y;
+    const int64_t b = bh / p.H, h = bh % p.H;
+    const T* xb = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + 8 * l16;
+    const int64_t jbase = int64_t(blockIdx.x) * 64 + warp * 2 + half;
+    // issue all four passes' loads first (memory-level parallelism), then compute
+    float v[4][8];
+    bool valid[4];
+#pragma unroll
+    for (int ps = 0; ps < 4; ++ps) {
+        const int64_t j = jbase + 16 * ps;
+        int64_t src = 0;
+        valid[ps] = j < p.n;
+        if (valid[ps]) {
+            src = p.idx ? p.idx[bh * p.n + j] : p.first_row + j;
+            if (src < 0 || src >= p.T) {
+                raise_status(KVB_DEV_BOUNDS);
+                valid[ps] = false;
+            }
+        }
+        if (valid[ps]) {
+            load8<T>(xb + src * p.st, v[ps]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[ps][i] = 0.f;
+        }
+    }
+#pragma unroll
+    for (int ps = 0; ps < 4; ++ps) {
+        const int64_t j = jbase + 16 * ps;
+        if (j >= p.n_alloc) continue;                  // uniform per half-warp row; no shuffles skipped unevenly
+        float lo, sc;
+        if constexpr (GROUP == 0) {
+            double ss = 0.0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss += double(__fmul_rn(v[ps][i], v[ps][i]));
+#pragma unroll
+            for (int m = 8; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+            const float rms = __fsqrt_rn(float(ss / double(D)));
+            sc = fmaxf(as_stored(__fmul_rn(p.step, rms)), 5.9604644775390625e-8f);
+            lo = 0.f;
+        } else {
+            float mn = v[ps][0], mx = v[ps][0];
+#pragma unroll
+            for (int i = 1; i < 8; ++i) {
+                mn = fminf(mn, v[ps][i]);
+                mx = fmaxf(mx, v[ps][i]);
+            }
+#pragma unroll
+            for (int m = LPG / 2; m >= 1; m >>= 1) {
+                mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, m));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+            }
+            lo = as_stored(mn);
+            sc = fmaxf(as_stored(__fdiv_rn(__fsub_rn(mx, lo), float(TOP))), 5.9604644775390625e-8f);
+        }
+        const float y = __frcp_rn(sc);
+        uint32_t c[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float q;
+            if constexpr (GROUP == 0) q = rintf(__fadd_rn(div_rn_markstein(v[ps][i], sc, y), 0.5f * float(TOP)));
+            else q = rintf(div_rn_markstein(__fsub_rn(v[ps][i], lo), sc, y));
+            q = fminf(fmaxf(q, 0.f), float(TOP));
+            c[i] = valid[ps] ? uint32_t(q) : 0u;
+            if (p.xhat && valid[ps]) {
+                const float xh = GROUP == 0 ? __fmul_rn(__fsub_rn(q, 0.5f * float(TOP)), sc) : __fadd_rn(__fmul_rn(q, sc), lo);
+                p.xhat[(bh * p.n + j) * D + 8 * l16 + i] = xh;
+            }
+        }
+        const uint32_t c0 = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+        const uint32_t c1 = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
+        store_packed<BITS>(p.codes + (bh * p.n_alloc + j) * RB, pack_planar_lane<BITS>(c0, c1), l16);
+        if constexpr (GROUP == 0) {
+            if (l16 == 0) static_cast<__half*>(p.meta)[bh * p.n_alloc + j] = __float2half_rn(valid[ps] ? sc : 0.f);
+        } else {
+            if (l16 % LPG == 0)
+                static_cast<uint32_t*>(p.meta)[(bh * p.n_alloc + j) * G + l16 / LPG] =
+                    valid[ps] ? pack_half2(lo, sc) : 0u;
+        }
+    }
+}
+
+// Per-channel key groups of GT tokens, d = 128: one CTA per group, 256 threads = 16 row slots x 16
+// channel chunks of 8; each thread keeps its GT / 16 rows in registers.  grid = (n_alloc / GT, B * H).
+template <typename T, int BITS, int GT>
+__global__ void __launch_bounds__(256) quant_channel128_kernel(const QuantFastParams p) {
+    constexpr int D = 128, TOP = (1 << BITS) - 1, RB = D * BITS / 8, NR = GT / 16;
+    __shared__ float s_mn[8][D], s_mx[8][D];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cc = threadIdx.x & 15, rs = threadIdx.x >> 4;
+    const int64_t bh = blockIdx.y;
+    const int64_t b = bh / p.H, h = bh % p.H;
+    const int64_t j0 = int64_t(blockIdx.x) * GT;
+    const T* xb = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + 8 * cc;
+    float v[NR][8];
+    bool valid[NR];
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+        const int64_t j = j0 + rs + 16 * k;
+        int64_t src = 0;
+        valid[k] = j < p.n;
+        if (valid[k]) {
+            src = p.idx ? p.idx[bh * p.n + j] : p.first_row + j;
+            if (src < 0 || src >= p.T) {
+                raise_status(KVB_DEV_BOUNDS);
+                valid[k] = false;
+            }
+        }
+        if (valid[k]) {
+            load8<T>(xb + src * p.st, v[k]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
+        }
+    }
+    float mn[8], mx[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        mn[i] = INFINITY;
+        mx[i] = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < NR; ++k)
+            if (valid[k]) {
+                mn[i] = fminf(mn[i], v[k][i]);
+                mx[i] = fmaxf(mx[i], v[k][i]);
+            }
+        mn[i] = fminf(mn[i], __shfl_xor_sync(0xffffffffu, mn[i], 16));
+        mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 16));
+    }
+    if (lane < 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            s_mn[warp][8 * cc + i] = mn[i];
+            s_mx[warp][8 * cc + i] = mx[i];
+        }
+    }
+    __syncthreads();
+    const int64_t nv = imax64(0, imin64(GT, p.n - j0));
+    float lo[8], sc[8], y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float a = INFINITY, z = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            a = fminf(a, s_mn[w][8 * cc + i]);
+            z = fmaxf(z, s_mx[w][8 * cc + i]);
+        }
+        if (nv > 0) {
+            lo[i] = as_stored(a);
+            sc[i] = fmaxf(as_stored(__fdiv_rn(__fsub_rn(z, lo[i]), float(TOP))), 5.9604644775390625e-8f);
+        } else {
+            lo[i] = 0.f;
+            sc[i] = 0.f;
+        }
+        y[i] = nv > 0 ? __frcp_rn(sc[i]) : 0.f;
+    }
+    if (rs == 0) {
+        uint32_t m[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m[i] = pack_half2(lo[i], sc[i]);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint32_t*>(p.meta) + ((bh * (p.n_alloc / GT)) + blockIdx.x) * D + 8 * cc);
+        dst[0] = make_uint4(m[0], m[1], m[2], m[3]);
+        dst[1] = make_uint4(m[4], m[5], m[6], m[7]);
+    }
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+        const int64_t j = j0 + rs + 16 * k;
+        uint32_t c[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float q = rintf(div_rn_markstein(__fsub_rn(v[k][i], lo[i]), sc[i], y[i]));
+            q = fminf(fmaxf(q, 0.f), float(TOP));
+            c[i] = valid[k] ? uint32_t(q) : 0u;
+            if (p.xhat && valid[k]) p.xhat[(bh * p.n + j) * D + 8 * cc + i] = __fadd_rn(__fmul_rn(q, sc[i]), lo[i]);
+        }
+        const uint32_t c0 = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+        const uint32_t c1 = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
+        store_packed<BITS>(p.codes + (bh * p.n_alloc + j) * RB, pack_planar_lane<BITS>(c0, c1), cc);
+    }
 }
 
 }  // namespace kvb

@@ -9,6 +9,8 @@
 // rule the oracle uses (a stable descending sort); the reference's torch.topk leaves it open
 // (STRATA_KV.py:1023).
 #pragma once
+#include <type_traits>
+
 #include "kvb_common.cuh"
 
 namespace kvb {
@@ -102,9 +104,20 @@ __global__ void __launch_bounds__(SEL_THREADS) rank_split_kernel(const RankSplit
         for (int shift = NBITS - 8; shift >= 0; shift -= 8) {
             for (int i = threadIdx.x; i < 256; i += blockDim.x) s_hist[i] = 0;
             __syncthreads();
-            for (int64_t i = threadIdx.x; i < p.n; i += blockDim.x) {
-                const uint64_t u = order_key(keys[i]);
-                if ((u & mask) == prefix) atomicAdd(&s_hist[(u >> shift) & 255], 1);
+            // warp-aggregated: lanes with the same digit add once (keys of similar magnitude share
+            // their top digits, which would otherwise serialise 1024 threads on one counter)
+            const int lane = threadIdx.x & 31;
+            for (int64_t base = 0; base < p.n; base += blockDim.x) {
+                const int64_t i = base + threadIdx.x;
+                bool act = false;
+                int dg = 0;
+                if (i < p.n) {
+                    const uint64_t u = order_key(keys[i]);
+                    act = (u & mask) == prefix;
+                    dg = int((u >> shift) & 255);
+                }
+                const unsigned peers = __match_any_sync(0xffffffffu, act ? dg : 256 + lane);
+                if (act && lane == __ffs(peers) - 1) atomicAdd(&s_hist[dg], __popc(peers));
             }
             __syncthreads();
             if (threadIdx.x == 0) {
@@ -136,7 +149,9 @@ __global__ void __launch_bounds__(SEL_THREADS) rank_split_kernel(const RankSplit
     for (int64_t base = 0; base < p.n; base += blockDim.x) {
         const int64_t i = base + threadIdx.x;
         const bool valid = i < p.n;
-        const uint64_t u = valid ? order_key(keys[valid ? i : 0]) : 0;
+        const K kv = keys[valid ? i : 0];
+        if (valid && kv != kv) raise_status(KVB_DEV_NAN);
+        const uint64_t u = valid ? order_key(kv) : 0;
         uint32_t eqbits = 0;
         for (int k = 0; k < nb; ++k)
             if (valid && u == s_tau[k]) eqbits |= 1u << k;
@@ -176,6 +191,50 @@ __global__ void key_energy_kernel(const T* k, int64_t B, int64_t H, int64_t T_, 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (lane == 0) out[row] = s;
+}
+
+// d = 128, 16-bit rows on 16-byte boundaries: 16 lanes per row, one 128-bit load each, four rows
+// per half-warp issued before any arithmetic.  Squares of fp16 / bf16 values are exact in float32;
+// their sum is taken in float64 (exact for any realistic dynamic range, so the ranking does not
+// depend on summation order).  grid = (ceil(T / 64), B * H), block 256.
+template <typename T>
+__global__ void __launch_bounds__(256) key_energy128_kernel(const T* k, int64_t H, int64_t T_, int64_t sb, int64_t sh,
+                                                            int64_t st, double* out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int l16 = lane & 15, half = lane >> 4;
+    const int64_t bh = blockIdx.y;
+    const T* x = k + (bh / H) * sb + (bh % H) * sh + 8 * l16;
+    const int64_t t0 = int64_t(blockIdx.x) * 64 + warp * 2 + half;
+    uint4 raw[4];
+#pragma unroll
+    for (int ps = 0; ps < 4; ++ps) {
+        const int64_t t = t0 + 16 * ps;
+        raw[ps] = t < T_ ? *reinterpret_cast<const uint4*>(x + t * st) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int ps = 0; ps < 4; ++ps) {
+        const uint32_t w[4] = {raw[ps].x, raw[ps].y, raw[ps].z, raw[ps].w};
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float a, b;
+            if constexpr (std::is_same<T, __half>::value) {
+                const __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
+                a = __low2float(h2);
+                b = __high2float(h2);
+            } else {
+                const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+                a = __low2float(h2);
+                b = __high2float(h2);
+            }
+            s += double(a * a);
+            s += double(b * b);
+        }
+#pragma unroll
+        for (int m = 8; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+        const int64_t t = t0 + 16 * ps;
+        if (l16 == 0 && t < T_) out[bh * T_ + t] = s;
+    }
 }
 
 }  // namespace kvb

@@ -7,12 +7,13 @@
 //   TMA (cp.async.bulk.tensor, 128-byte swizzle)  X tile 128 x 128 fp16 -> shared memory (4 stages)
 //   tcgen05.mma kind::f16, M 128, N 32, K 16 x 8 x 2: C = X B_hi + X B_lo into a TMEM accumulator
 //        (the basis split into two fp16 parts, so coefficients carry ~22 significant bits);
-//        double-buffered accumulators (64 TMEM columns) so the epilogue of tile i overlaps tile i+1
+//        four accumulators (128 TMEM columns) so the epilogues of four tiles overlap the next MMAs
 //   tcgen05.ld 32x32b.x32: thread = token row, its 32 fp32 coefficients in registers
 //   epilogue: RMS (float64 sum of float32 squares), fp16 scale, codes, planar pack, 16-byte stores.
 //
 // Warp roles: warp 0 issues TMA loads, warp 1 allocates TMEM and issues the MMAs (one elected
-// lane), warps 2-5 run the epilogue (warp w reads TMEM lanes 32 (w % 4) .. +31).  Every mbarrier wait
+// lane), warps 2-17 run the epilogue in 4 groups of 4, group j on the tiles of accumulator j (warp w
+// reads TMEM lanes 32 (w % 4) .. +31), so four tiles' epilogues run while the next MMAs issue.  Every mbarrier wait
 // is bounded; on a timeout the kernel records it, drains its own copies and frees TMEM.
 #pragma once
 #include <cuda.h>
@@ -25,12 +26,14 @@ constexpr int SP_TILE = 128;          // tokens per tile (MMA M)
 constexpr int SP_R = 32;              // coefficients kept (MMA N)
 constexpr int SP_D = 128;             // head dim (MMA K)
 constexpr int SP_STAGES = 4;
-constexpr int SP_THREADS = 192;
+constexpr int SP_NACC = 4;                                  // TMEM accumulators (and epilogue warp groups)
+constexpr int SP_TMEM_COLS = 128;                           // SP_NACC x 32 columns
+constexpr int SP_THREADS = (2 + 4 * SP_NACC) * 32;          // TMA warp, MMA warp, 16 epilogue warps
 constexpr int SP_A_BYTES = SP_TILE * SP_D * 2;              // 32 KB per stage (two 64-channel halves)
 constexpr int SP_B_BYTES = 2 * SP_R * SP_D * 2;             // hi + lo basis of one head, 16 KB
 
 struct SpectralParams {
-    CUtensorMap tmap_x;               // X viewed 2D: inner 128 channels, outer B*H*T rows; box 64 x 128
+    CUtensorMap tmap_x;               // X as 4D (128 channels, T, H, B) with the caller's strides; box 64 x 128 x 1 x 1
     CUtensorMap tmap_b;               // basis^T viewed 2D: inner 128, outer 2*H*32 rows (hi block, lo block); box 64 x 32
     int64_t H, T, n_alloc;
     int64_t tiles_per_head, ntiles;
@@ -55,6 +58,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             smem_u32(dst)),
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
         : "memory");
 }
 
@@ -90,6 +102,61 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Quotient a / b rounded to nearest even, from y = RN(1 / b): q0 = RN(a y), the exact remainder
+// r = a - q0 b (one FMA), q1 = RN(q0 + r y).  Markstein's theorem (P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990) gives
+// q1 = RN(a / b) whenever y is the correctly rounded reciprocal and nothing over- or underflows;
+// here b is an fp16 scale >= 2^-24 and |a / b| is bounded by the code range, so both hold.
+__device__ __forceinline__ float div_rn_from_rcp(float a, float b, float y) {
+    const float q0 = __fmul_rn(a, y);
+    const float r = __fmaf_rn(-q0, b, a);
+    return __fmaf_rn(r, y, q0);
+}
+
+// Mid-rise code of one token's 32 coefficients (strata_quantize STRATA_KV.py:1158-1168 with the
+// RMS of rms_f32: float32 squares summed in float64, one rounding of the mean), planar-packed to
+// 32 * BITS / 8 bytes (byte k holds coefficient pl * 32 / P + k in bits [pl * BITS, ...)).
+template <int BITS>
+__device__ __forceinline__ void midrise_code32(const float (&c)[32], float step, uint8_t* dst, __half* scale) {
+    constexpr int TOP = (1 << BITS) - 1, P = 8 / BITS, RB = SP_R * BITS / 8;
+    constexpr float HALF = 0.5f * float(TOP);
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ss += double(__fmul_rn(c[i], c[i]));
+    const float rms = __fsqrt_rn(float(ss / 32.0));
+    const float sc = fmaxf(as_stored(__fmul_rn(step, rms)), 5.9604644775390625e-8f);
+    const float y = __frcp_rn(sc);
+    uint32_t code[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float v = fminf(fmaxf(rintf(__fadd_rn(div_rn_from_rcp(c[i], sc, y), HALF)), 0.f), float(TOP));
+        code[i] = uint32_t(v);
+    }
+    uint32_t w[RB / 4];
+#pragma unroll
+    for (int q = 0; q < RB / 4; ++q) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int k = 4 * q + b;
+            uint32_t byte = 0;
+#pragma unroll
+            for (int pl = 0; pl < P; ++pl) byte |= code[pl * (SP_R / P) + k] << (pl * BITS);
+            word |= byte << (8 * b);
+        }
+        w[q] = word;
+    }
+    if constexpr (RB == 8) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    } else {
+#pragma unroll
+        for (int q = 0; q < RB / 16; ++q)
+            reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    }
+    *scale = __float2half_rn(sc);
+}
+
+template <int BITS>
 __global__ void __launch_bounds__(SP_THREADS, 1) spectral_encode_kernel(const __grid_constant__ SpectralParams p) {
     extern __shared__ __align__(1024) uint8_t sp_smem_raw[];
     // 1024-byte aligned region for the swizzled operands
@@ -100,9 +167,9 @@ __global__ void __launch_bounds__(SP_THREADS, 1) spectral_encode_kernel(const __
     uint64_t* empty_a = full_a + SP_STAGES;
     uint64_t* full_b = empty_a + SP_STAGES;               // [2]
     uint64_t* empty_b = full_b + 2;                       // [2]
-    uint64_t* acc_full = empty_b + 2;                     // [2]
-    uint64_t* acc_empty = acc_full + 2;                   // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* acc_full = empty_b + 2;                     // [SP_NACC]
+    uint64_t* acc_empty = acc_full + SP_NACC;             // [SP_NACC]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + SP_NACC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -117,15 +184,17 @@ __global__ void __launch_bounds__(SP_THREADS, 1) spectral_encode_kernel(const __
         for (int i = 0; i < 2; ++i) {
             mbar_init(&full_b[i], 1);
             mbar_init(&empty_b[i], 1);
+        }
+        for (int i = 0; i < SP_NACC; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 4);                  // one arrive per epilogue warp
+            mbar_init(&acc_empty[i], 4);                  // one arrive per warp of the accumulator's group
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(64));
+                     "r"(SP_TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -158,10 +227,11 @@ __global__ void __launch_bounds__(SP_THREADS, 1) spectral_encode_kernel(const __
                 const int s = it % SP_STAGES;
                 if (it >= SP_STAGES && !mbar_wait(&empty_a[s], ((it / SP_STAGES) - 1) & 1)) { *abort_flag = 1; break; }
                 mbar_arrive_expect_tx(&full_a[s], SP_A_BYTES);
-                const int row = int(head * p.T + t0);
+                // rows past T of the last tile of a head are out of the tensor: zero-filled
+                const int hh = int(head % p.H), bb = int(head / p.H);
                 uint8_t* dst = sa + s * SP_A_BYTES;
-                tma_load_2d(dst, &p.tmap_x, 0, row, &full_a[s]);
-                tma_load_2d(dst + SP_A_BYTES / 2, &p.tmap_x, 64, row, &full_a[s]);
+                tma_load_4d(dst, &p.tmap_x, 0, int(t0), hh, bb, &full_a[s]);
+                tma_load_4d(dst + SP_A_BYTES / 2, &p.tmap_x, 64, int(t0), hh, bb, &full_a[s]);
             }
         }
     } else if (warp == 1) {
@@ -179,9 +249,9 @@ __global__ void __launch_bounds__(SP_THREADS, 1) spectral_encode_kernel(const __
                     ++nb;
                 }
                 const int s = it % SP_STAGES;
-                const int ab = it & 1;
+                const int ab = it % SP_NACC;
                 if (!mbar_wait(&full_a[s], (it / SP_STAGES) & 1)) { *abort_flag = 1; break; }
-                if (it >= 2 && !mbar_wait(&acc_empty[ab], ((it >> 1) - 1) & 1)) { *abort_flag = 1; break; }
+                if (it >= SP_NACC && !mbar_wait(&acc_empty[ab], ((it / SP_NACC) - 1) & 1)) { *abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t a0 = smem_u32(sa + s * SP_A_BYTES);
                 const uint32_t b0 = smem_u32(sb + ((nb - 1) & 1) * SP_B_BYTES);
@@ -199,19 +269,19 @@ __global__ void __launch_bounds__(SP_THREADS, 1) spectral_encode_kernel(const __
                 umma_commit(&acc_full[ab]);
             }
             // after an abort, let the MMAs already issued finish before TMEM is released
-            if (*abort_flag && it > 0) mbar_wait(&acc_full[(it - 1) & 1], ((it - 1) >> 1) & 1, 10000000ull);
+            if (*abort_flag && it > 0) mbar_wait(&acc_full[(it - 1) % SP_NACC], ((it - 1) / SP_NACC) & 1, 10000000ull);
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue: SP_NACC groups of 4 warps, group j takes tiles it = j mod SP_NACC ----------------
+        const int ew = warp - 2;
+        const int grp = ew >> 2;
         const int q = warp & 3;                          // TMEM lane quarter this warp may access
         const int row = q * 32 + lane;                   // token row inside the tile
-        const int top = (1 << p.bits) - 1;
-        const float half_top = 0.5f * float(top);
-        const int rb = SP_R * p.bits / 8;
-        uint32_t it = 0;
-        for (int64_t tile = t_begin; tile < t_end; ++tile, ++it) {
-            const int ab = it & 1;
-            const bool ok = mbar_wait(&acc_full[ab], (it >> 1) & 1, *abort_flag ? 1000000ull : 2000000000ull);
+        constexpr int RB = SP_R * BITS / 8;
+        uint32_t it = grp;
+        for (int64_t tile = t_begin + grp; tile < t_end; tile += SP_NACC, it += SP_NACC) {
+            const int ab = int(it % SP_NACC);
+            const bool ok = mbar_wait(&acc_full[ab], (it / SP_NACC) & 1, *abort_flag ? 1000000ull : 2000000000ull);
             if (!ok) { *abort_flag = 1; break; }
             tc_fence_after();
             float c[32];
@@ -227,33 +297,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) spectral_encode_kernel(const __
 #pragma unroll
                 for (int i = 0; i < 8; ++i) dst[i] = make_float4(c[4 * i], c[4 * i + 1], c[4 * i + 2], c[4 * i + 3]);
             }
-            double ss = 0.0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) ss += double(__fmul_rn(c[i], c[i]));
-            const float rms = sqrtf(float(ss / 32.0));
-            const float sc = fmaxf(as_stored(__fmul_rn(p.step, rms)), 5.9604644775390625e-8f);
-            uint32_t code[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float v = fminf(fmaxf(rintf(__fadd_rn(__fdiv_rn(c[i], sc), half_top)), 0.f), float(top));
-                code[i] = uint32_t(v);
-            }
-            // planar pack: byte k holds coefficient pl * 32 / P + k in bits [pl * bits, ...)
-            uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            const int P = 8 / p.bits;
-            for (int k = 0; k < rb; ++k) {
-                uint32_t byte = 0;
-                for (int pl = 0; pl < P; ++pl) byte |= code[pl * (SP_R / P) + k] << (pl * p.bits);
-                w[k >> 2] |= byte << (8 * (k & 3));
-            }
-            uint8_t* dst = p.codes + (head * p.n_alloc + tok) * rb;
-            if (rb == 16) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-            else if (rb == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
-            else {
-                reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            }
-            p.scales[head * p.n_alloc + tok] = __float2half_rn(sc);
+            midrise_code32<BITS>(c, p.step, p.codes + (head * p.n_alloc + tok) * RB, p.scales + head * p.n_alloc + tok);
         }
     }
 
@@ -267,7 +311,7 @@ __global__ void __launch_bounds__(SP_THREADS, 1) spectral_encode_kernel(const __
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64));
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(SP_TMEM_COLS));
 }
 
 }  // namespace kvb

@@ -46,7 +46,8 @@ SIGNATURES = {
     "kvb_scores_workspace_size": (C.c_size_t, [_i64, _i64, _i64]),
     "kvb_query_scores": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i64, _i32, _p, _p,
                                 C.c_size_t, _p]),
-    "kvb_spectral_encode": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _f32, _p, _p, _i64, _p, _i32, _p]),
+    "kvb_spectral_encode": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i32, _f32, _p, _p, _i64, _p, _i32,
+                                   _p]),
     "kvb_decode_workspace_size": (C.c_size_t, [C.POINTER(Cache), _i32, _i32, _i32]),
     "kvb_decode": (_i32, [C.POINTER(Cache), _p, _i32, _i32, _i32, _f32, C.POINTER(C.c_int64), _p, _i32, _i32,
                           _p, C.c_size_t, _p]),

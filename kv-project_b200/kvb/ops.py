@@ -109,12 +109,11 @@ def key_energy(k: torch.Tensor) -> torch.Tensor:
 def rank_split(keys: torch.Tensor, counts, want=None):
     """keys (..., n) float32 / float64.  Class c gets ranks [sum(counts[:c]), sum(counts[:c+1])) by
     key descending (ties: lower index first); the last class gets the rest.  Returns one int64
-    tensor (..., count_c) per class (ascending indices); classes not in `want` are None."""
+    tensor (..., count_c) per class (ascending indices); classes not in `want` are None.  NaN keys
+    set bit 2 of the device status word (device_status()); nothing here synchronises."""
     _cuda(keys)
     if keys.dtype not in (torch.float32, torch.float64):
         raise ValueError("rank_split: keys must be float32 or float64")
-    if torch.isnan(keys).any():
-        raise ValueError("rank_split: NaN keys")
     lead, n = keys.shape[:-1], keys.shape[-1]
     k2 = keys.reshape(-1, n)
     if k2.stride(-1) != 1:
@@ -374,7 +373,8 @@ def spectral_encode(x: torch.Tensor, basis_hilo: torch.Tensor, bits: int = 4, wa
     _cuda(x, basis_hilo)
     if x.dtype != torch.float16 or x.dim() != 4 or x.shape[-1] != 128:
         raise ValueError("spectral_encode: x must be fp16 (B, H, T, 128)")
-    x = x.contiguous()
+    if x.stride(-1) != 1 or any(s_ % 8 for s_ in x.stride()[:3]):
+        x = x.contiguous()                  # the tensor map needs 16-byte strides; other layouts are copied
     B, H, T, d = x.shape
     if basis_hilo.dtype != torch.float16 or tuple(basis_hilo.shape) != (2, H, SPECTRAL_R, d):
         raise ValueError("spectral_encode: basis must be fp16 (2, H, 32, 128) (see split_basis)")
@@ -385,7 +385,8 @@ def spectral_encode(x: torch.Tensor, basis_hilo: torch.Tensor, bits: int = 4, wa
     if n_alloc > T:
         codes[:, :, T:].zero_()
     coef = torch.empty((B, H, T, SPECTRAL_R), dtype=torch.float32, device=x.device) if want_coef else None
-    L.check(L.lib().kvb_spectral_encode(_ptr(x), B, H, T, _ptr(basis_hilo), bits, C.c_float(UNIFORM_STEP[bits]),
+    L.check(L.lib().kvb_spectral_encode(_ptr(x), B, H, T, x.stride(0), x.stride(1), x.stride(2), _ptr(basis_hilo),
+                                        bits, C.c_float(UNIFORM_STEP[bits]),
                                         _ptr(codes), _ptr(scales), n_alloc, _ptr(coef), n_ctas,
                                         C.c_void_p(_stream(x.device))), "kvb_spectral_encode")
     return {"codes": codes, "meta": scales, "n": T, "n_alloc": n_alloc, "bits": bits, "group": SPECTRAL_R,

@@ -61,9 +61,13 @@ def test_four_classes(cuda_dev):
         np.testing.assert_array_equal(outs[c].cpu().numpy(), np.sort(order[:, edges[c]:edges[c + 1]], -1))
 
 
-def test_nan_keys_rejected(cuda_dev):
+def test_nan_keys_flagged(cuda_dev):
+    """A NaN key sets bit 2 of the device status word (no host synchronisation in rank_split)."""
     import kvb
+    kvb.device_status()                               # clear
     s = torch.zeros(1, 10, device=cuda_dev)
     s[0, 3] = float("nan")
-    with pytest.raises(ValueError):
-        kvb.rank_split(s, [2])
+    kvb.rank_split(s, [2])
+    assert kvb.device_status() & 4
+    kvb.rank_split(torch.zeros(1, 10, device=cuda_dev), [2])
+    assert kvb.device_status() == 0

@@ -19,10 +19,16 @@ def _inputs(B, H, T, seed):
     return bases, K, V
 
 
-@pytest.mark.parametrize("B,H,T,bits", [(1, 2, 256, 4), (2, 3, 1000, 4), (1, 2, 129, 2), (1, 1, 300, 8)])
-def test_projection_and_code(cuda_dev, B, H, T, bits):
+@pytest.mark.parametrize("B,H,T,bits,amp", [(1, 2, 256, 4, 1.0), (2, 3, 1000, 4, 1.0), (1, 2, 129, 2, 1.0),
+                                             (1, 1, 300, 8, 1.0), (2, 8, 4096, 4, 1.0), (1, 4, 2048, 4, 1e-3),
+                                             (1, 4, 2048, 2, 300.0), (1, 4, 1111, 8, 40.0)])
+def test_projection_and_code(cuda_dev, B, H, T, bits, amp):
+    """Coefficients to float32 accuracy; codes and scales bit-exact given those coefficients (the
+    code's division runs through a correctly rounded reciprocal + Markstein correction: millions of
+    quotients over several exponent ranges here)."""
     import kvb
     bases, K, V = _inputs(B, H, T, seed=T + bits)
+    K = (K.float() * amp).half()
     br = bases[:, :, :32].float()
     hilo = kvb.ops.split_basis(br.to(cuda_dev))
     r = kvb.ops.spectral_encode(K.to(cuda_dev), hilo, bits, want_coef=True)
@@ -34,6 +40,21 @@ def test_projection_and_code(cuda_dev, B, H, T, bits):
     c, s, _ = O.strata_quantize(coef, bits)
     np.testing.assert_array_equal(unpack(r["codes"], bits, T), c)
     np.testing.assert_array_equal(r["meta"][:, :, :T].float().cpu().numpy(), s)
+
+
+def test_projection_strided_input(cuda_dev):
+    """x as a (B, H, T, d) view of (B, T, H, d) storage (a model's projection layout): the 4D tensor
+    map reads it in place, same codes as the contiguous copy."""
+    import kvb
+    bases, K, V = _inputs(2, 4, 700, seed=5)
+    hilo = kvb.ops.split_basis(bases[:, :, :32].float().to(cuda_dev))
+    Kc = K.to(cuda_dev).contiguous()
+    Ks = Kc.transpose(1, 2).contiguous().transpose(1, 2)
+    assert not Ks.is_contiguous()
+    a = kvb.ops.spectral_encode(Kc, hilo, 4, want_coef=True)
+    b = kvb.ops.spectral_encode(Ks, hilo, 4, want_coef=True)
+    assert torch.equal(a["codes"], b["codes"]) and torch.equal(a["meta"], b["meta"])
+    assert torch.equal(a["coef"], b["coef"])
 
 
 @pytest.mark.parametrize("rep,Tq", [(4, 1), (4, 2)])
