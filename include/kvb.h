@@ -52,6 +52,11 @@ int kvb_version(void);
  * `stream`, copies the word to *out and clears it when `clear` is non-zero. */
 kvb_status kvb_device_status(unsigned* out, int clear, void* stream);
 
+/* Where the first bounded wait gave up since the last clear (0 if none): bit 31 set, site code in
+ * bits 0-7 (kernel-specific), CTA index in bits 8-15, the waiting role's counter in bits 16-30.
+ * Synchronises `stream`; clears when `clear` is non-zero.  For diagnosis of a KVB_DEV_TIMEOUT. */
+kvb_status kvb_device_diag(unsigned* out, int clear, void* stream);
+
 /* ------------------------------------------------------------------------------------------ *
  * K1: quantise + planar-pack.  Replaces kivi_quant (STRATA_KV.py:826-856), strata_quantize +
  * pack_planar (STRATA_KV.py:1158-1182) and the per-stratum gather of StrataMethod.pack
@@ -70,6 +75,18 @@ kvb_status kvb_device_status(unsigned* out, int clear, void* stream);
  *         MIDRISE:           (B, H, n_alloc) fp16 scales (group must equal d);
  *   xhat  optional (nullable) float32 (B, H, n, d): what a reader dequantises.
  * `step` is the MIDRISE step in RMS units (uniform_step(bits)[0], STRATA_KV.py:1133). */
+/* As kvb_quant_pack in per-token mode (k_mode KVB_K_PER_TOKEN), with the codes written in the value
+ * block layout read by the tensor-core decode: for every 128-token block of each (b, h), d rows
+ * (one per channel) of 16 * bits bytes; byte k of channel row c holds the codes of tokens
+ * p * 128 / P + k (P = 8 / bits) in bits [p * bits, (p + 1) * bits) - the planar packing applied
+ * along tokens.  Codes, metadata and xhat are the same numbers kvb_quant_pack produces.  Needs
+ * d == 128, fp16 / bf16 input with 16-byte aligned rows, n_alloc % 128 == 0, 16-byte aligned
+ * meta.  No counterpart in the reference (an internal layout of this library's decode). */
+kvb_status kvb_quant_pack_blocked(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t d,
+                                  int64_t sb, int64_t sh, int64_t st, const int64_t* idx, int64_t first_row,
+                                  int64_t n, int64_t n_alloc, int bits, int group, int code_kind, float step,
+                                  uint8_t* codes, void* meta, float* xhat, void* stream);
+
 kvb_status kvb_quant_pack(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t d,
                           int64_t sb, int64_t sh, int64_t st,
                           const int64_t* idx, int64_t first_row, int64_t n, int64_t n_alloc,
@@ -124,12 +141,18 @@ kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, i
  * + strata_tier_kernel (STRATA_KV.py:1762-1796, :1450-1469), LayerState.attend / chunked_attention
  * (STRATA_KV.py:716, :641) over KIVI codes, and QuasarState.attend (QUASAR_KV.py:1942-1967, one
  * stage) over spectral coefficients. */
+#define KVB_V_TOKEN_MAJOR 0   /* value codes as kvb_quant_pack writes them */
+#define KVB_V_BLOCK128 1      /* value codes as kvb_quant_pack_blocked writes them (tensor-core decode) */
+
 typedef struct kvb_stratum {
     int kbits, vbits;         /* code widths of keys and values: 2, 4 or 8 each */
+    int v_layout;             /* KVB_V_TOKEN_MAJOR or KVB_V_BLOCK128 */
+    int reserved;             /* 0 */
     int64_t n;                /* stored tokens per (b, h) */
-    int64_t n_alloc;          /* row capacity per (b, h), multiple of 16 */
+    int64_t n_alloc;          /* row capacity per (b, h), multiple of 16 (of 128 for KVB_V_BLOCK128) */
     const uint8_t* kc;        /* (B, Hkv, n_alloc, d_code * kbits / 8) planar */
-    const uint8_t* vc;        /* (B, Hkv, n_alloc, d_code * vbits / 8) planar */
+    const uint8_t* vc;        /* token-major: (B, Hkv, n_alloc, d_code * vbits / 8) planar;
+                               * block: (B, Hkv, n_alloc / 128, d_code, 16 * vbits) */
     const void* kmeta;        /* as kvb_quant_pack's meta for the key code */
     const void* vmeta;        /* as kvb_quant_pack's meta for the value code (per token) */
 } kvb_stratum;

@@ -21,6 +21,7 @@
 #include "kvb_decode.cuh"
 #include "kvb_scores.cuh"
 #include "kvb_spectral.cuh"
+#include "kvb_decode_tc.cuh"
 
 #define KVB_VERSION 100
 
@@ -69,6 +70,24 @@ kvb_status kvb_device_status(unsigned* out, int clear, void* stream) {
         const unsigned z = 0;
         if ((st = cuda_check(cudaMemcpyToSymbolAsync(kvb::g_status, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s),
                              "clear status")))
+            return st;
+        if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
+    }
+    return KVB_OK;
+}
+
+kvb_status kvb_device_diag(unsigned* out, int clear, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned v = 0;
+    kvb_status st = cuda_check(cudaMemcpyFromSymbolAsync(&v, kvb::g_diag, sizeof(v), 0, cudaMemcpyDeviceToHost, s),
+                               "read diag");
+    if (st) return st;
+    if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
+    if (out) *out = v;
+    if (clear) {
+        const unsigned z = 0;
+        if ((st = cuda_check(cudaMemcpyToSymbolAsync(kvb::g_diag, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s),
+                             "clear diag")))
             return st;
         if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
     }
@@ -172,6 +191,39 @@ kvb_status kvb_quant_pack(const void* x, int x_dtype, int64_t B, int64_t H, int6
 #undef KVB_QTD
 #undef KVB_QT
     return launch_check("quant_token_kernel");
+}
+
+kvb_status kvb_quant_pack_blocked(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t d,
+                                  int64_t sb, int64_t sh, int64_t st, const int64_t* idx, int64_t first_row,
+                                  int64_t n, int64_t n_alloc, int bits, int group, int code_kind, float step,
+                                  uint8_t* codes, void* meta, float* xhat, void* stream) {
+    if (!x || !codes || !meta) return fail(KVB_EINVAL, "quant_pack_blocked: null pointer");
+    if (x_dtype != KVB_F16 && x_dtype != KVB_BF16) return fail(KVB_EUNSUPPORTED, "quant_pack_blocked: fp16 / bf16 only");
+    if (d != 128) return fail(KVB_EUNSUPPORTED, "quant_pack_blocked: d must be 128");
+    if (bits != 2 && bits != 4 && bits != 8) return fail(KVB_EINVAL, "quant_pack_blocked: bits must be 2, 4 or 8");
+    if (B <= 0 || H <= 0 || n < 0 || n_alloc < n || n_alloc % 128) return fail(KVB_EINVAL, "quant_pack_blocked: sizes");
+    if (!idx && (first_row < 0 || first_row + n > T)) return fail(KVB_EINVAL, "quant_pack_blocked: row range");
+    if (!aligned(x, 16) || sb % 8 || sh % 8 || st % 8) return fail(KVB_EINVAL, "quant_pack_blocked: 16-byte rows needed");
+    if (!aligned(codes, 16) || !aligned(meta, 16)) return fail(KVB_EINVAL, "quant_pack_blocked: output alignment");
+    if (B * H > 65535) return fail(KVB_EINVAL, "quant_pack_blocked: B * H > 65535");
+    int gsel;
+    if (code_kind == KVB_CODE_MIDRISE) gsel = group == 128 ? 0 : -1;
+    else gsel = (group == 32 || group == 64 || group == 128) ? group : -1;
+    if (gsel < 0) return fail(KVB_EINVAL, "quant_pack_blocked: group must be 32, 64 or 128 (128 for the mid-rise code)");
+    if (n_alloc == 0) return KVB_OK;
+    kvb::QuantFastParams f{x, H, T, sb, sh, st, idx, first_row, n, n_alloc, step, codes, meta, xhat};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    dim3 grid(unsigned(n_alloc / 128), unsigned(B * H));
+#define KVB_QB(T_, B_, G_) kvb::quant_vblock128_kernel<T_, B_, G_><<<grid, 256, 0, s>>>(f)
+#define KVB_QBG(T_, B_)                                                  \
+    if (gsel == 0) KVB_QB(T_, B_, 0); else if (gsel == 32) KVB_QB(T_, B_, 32); \
+    else if (gsel == 64) KVB_QB(T_, B_, 64); else KVB_QB(T_, B_, 128)
+#define KVB_QBB(T_) if (bits == 2) { KVB_QBG(T_, 2); } else if (bits == 4) { KVB_QBG(T_, 4); } else { KVB_QBG(T_, 8); }
+    if (x_dtype == KVB_F16) { KVB_QBB(__half) } else { KVB_QBB(__nv_bfloat16) }
+#undef KVB_QBB
+#undef KVB_QBG
+#undef KVB_QB
+    return launch_check("quant_vblock128_kernel");
 }
 
 // =============================================================================================
@@ -410,6 +462,15 @@ int tokens_per_chunk(int D, int kbits, int vbits, int k_mode) {
     return kvb::chunk_tokens(D, kbits, vbits, k_mode == KVB_K_PER_CHANNEL);
 }
 
+// The tensor-core decode (decode_tc) reads caches whose value codes are in the 128-token block
+// layout; it works in 128-token chunks (one MMA tile).
+bool uses_tc(const kvb_cache* c) {
+    return c->n_strata > 0 && c->strata[0].v_layout == KVB_V_BLOCK128;
+}
+int chunk_of(const kvb_cache* c, int s) {
+    return uses_tc(c) ? kvb::TC_T : tokens_per_chunk(c->d_code, c->strata[s].kbits, c->strata[s].vbits, c->k_mode);
+}
+
 kvb_status validate_cache(const kvb_cache* c, DecodeShape& sh, int Hq, int Tq) {
     if (!c) return fail(KVB_EINVAL, "decode: null cache");
     if (c->B <= 0 || c->Hkv <= 0 || Hq <= 0 || Hq % c->Hkv || Tq <= 0 || Tq > 16)
@@ -439,8 +500,20 @@ kvb_status validate_cache(const kvb_cache* c, DecodeShape& sh, int Hq, int Tq) {
         }
     }
     if (c->lift == nullptr && c->d_code != c->d) return fail(KVB_EINVAL, "decode: d_code != d needs a lift matrix");
+    const bool tc = uses_tc(c);
     for (int i = 0; i < c->n_strata; ++i) {
         const kvb_stratum& s = c->strata[i];
+        if (s.v_layout != KVB_V_TOKEN_MAJOR && s.v_layout != KVB_V_BLOCK128)
+            return fail(KVB_EINVAL, "decode: stratum %d v_layout", i);
+        if ((s.v_layout == KVB_V_BLOCK128) != tc)
+            return fail(KVB_EINVAL, "decode: all strata must share one value layout");
+        if (tc) {
+            if (sh.D != 128 || c->k_mode != KVB_K_PER_TOKEN || s.kbits != s.vbits || s.n_alloc % 128)
+                return fail(KVB_EUNSUPPORTED, "decode: block value layout needs d_code 128, per-token keys, equal "
+                            "key / value widths and n_alloc %% 128 == 0");
+            if (sh.GK > 2 || sh.GV > 2)
+                return fail(KVB_EUNSUPPORTED, "decode: block value layout supports at most 2 groups per token");
+        }
         const bool okb = (s.kbits == s.vbits && (s.kbits == 2 || s.kbits == 4 || s.kbits == 8)) ||
                          (s.kbits == 4 && s.vbits == 2);
         if (!okb) return fail(KVB_EUNSUPPORTED, "decode: stratum %d widths (%d, %d)", i, s.kbits, s.vbits);
@@ -482,7 +555,7 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
     int64_t chunks_per_head = 0, w_head = 0;
     for (int s = 0; s < c->n_strata; ++s) {
         const kvb_stratum& st = c->strata[s];
-        P.tok[s] = tokens_per_chunk(c->d_code, st.kbits, st.vbits, c->k_mode);
+        P.tok[s] = chunk_of(c, s);
         nch[s] = (st.n + P.tok[s] - 1) / P.tok[s];
         const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + 8;
         wfull[s] = int64_t(P.tok[s]) * bpt;
@@ -608,6 +681,72 @@ kvb_status dispatch_main(const DecodeShape& sh, const kvb_cache* c, const Plan& 
 #undef KVB_CASE
     return fail(KVB_EUNSUPPORTED, "decode: no kernel for d_code=%d rows=%d key groups=%d value groups=%d mode=%d code=%d",
                 sh.D, sh.R, sh.GK, sh.GV, sh.kmode, sh.code);
+}
+
+// ---- tensor-core decode (block value layout) ----
+// 2D uint8 tensor map over `rows` rows of `rb` bytes, box rb x 128 rows, swizzle matched to rb
+kvb_status make_map_rows(CUtensorMap* m, const void* base, int64_t rows, int rb) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return fail(KVB_ECUDA, "decode: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {cuuint64_t(rb), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(rb)};
+    const cuuint32_t box[2] = {cuuint32_t(rb), cuuint32_t(kvb::TC_T)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapSwizzle sw = rb == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                  : rb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KVB_ECUDA, "decode: cuTensorMapEncodeTiled (codes) failed (%d)", int(r));
+    return KVB_OK;
+}
+
+template <int R, int GK, int GV, int CK, int N, int NWG>
+kvb_status launch_tc(const kvb::TcParams& tp, int n_ctas, cudaStream_t s) {
+    const size_t smem = 1024 + size_t(NWG) * kvb::TC_RING + size_t(NWG) * N * 128 * 3 +
+                        size_t(NWG) * (2 * R + R * 128) * 4 + size_t(NWG) * 64 * 4 +
+                        (size_t(NWG) * (2 * kvb::TC_NSLOT + 8) * 8 + 16) + 2 * kvb::TC_NSLOT * 4 +
+                        kvb::TC_MAX_CTA_PIECES * 16 + 4 * sizeof(kvb::StratumDev);
+    auto kern = kvb::decode_tc<R, GK, GV, CK, N, NWG>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return cuda_check(e, "decode_tc smem attribute");
+    kern<<<n_ctas, 64 + NWG * 128, smem, s>>>(tp);
+    return launch_check("decode_tc");
+}
+
+kvb_status dispatch_tc(const DecodeShape& sh, const kvb_cache* c, const Plan& P, const kvb::DecodeParams& dp,
+                       cudaStream_t s) {
+    using namespace kvb;
+    static thread_local TcParams tp;
+    std::memcpy(&tp.d, &dp, sizeof(DecodeParams));
+    bool has8 = false;
+    for (int i = 0; i < c->n_strata; ++i) {
+        const kvb_stratum& sd = c->strata[i];
+        const int64_t rows = int64_t(c->B) * c->Hkv * sd.n_alloc;
+        kvb_status st = make_map_rows(&tp.tm_k[i], sd.kc, rows, 16 * sd.kbits);
+        if (st) return st;
+        if ((st = make_map_rows(&tp.tm_v[i], sd.vc, rows, 16 * sd.vbits))) return st;
+        has8 |= sd.kbits == 8;
+    }
+    for (int cta = 0; cta < P.n_ctas; ++cta)
+        if (P.cta_begin[cta + 1] - P.cta_begin[cta] > TC_MAX_CTA_PIECES)
+            return fail(KVB_EUNSUPPORTED, "decode: more than %d pieces on one CTA", TC_MAX_CTA_PIECES);
+    const int G = sh.GK > sh.GV ? sh.GK : sh.GV;
+    const int N = 3 * G * sh.R <= 32 ? 32 : 64;
+    const int nct = P.n_ctas;
+#define KVB_TC(R_, GK_, GV_, CK_, N_, W_)                                                                  \
+    if (sh.R == R_ && sh.GK == GK_ && sh.GV == GV_ && sh.code == CK_ && N == N_ && (W_ == 2) == !(N_ == 64 && has8)) \
+        return launch_tc<R_, GK_, GV_, CK_, N_, W_>(tp, nct, s);
+    KVB_TC(4, 2, 2, KV_ASYM, 32, 2)
+    KVB_TC(4, 1, 1, KV_ASYM, 32, 2)
+    KVB_TC(8, 1, 1, KV_ASYM, 32, 2)
+    KVB_TC(8, 2, 2, KV_ASYM, 64, 2)
+    KVB_TC(8, 2, 2, KV_ASYM, 64, 1)
+    KVB_TC(4, 1, 1, KV_MIDRISE, 32, 2)
+    KVB_TC(8, 1, 1, KV_MIDRISE, 32, 2)
+#undef KVB_TC
+    return fail(KVB_EUNSUPPORTED, "decode: block value layout with rows=%d key groups=%d value groups=%d code=%d",
+                sh.R, sh.GK, sh.GV, sh.code);
 }
 
 }  // namespace
@@ -759,7 +898,7 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
         if (ev_begin && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_begin), s, ev_flags),
                                          "record event")))
             return st;
-        if ((st = dispatch_main(sh, c, P, dp, s))) return st;
+        if ((st = uses_tc(c) ? dispatch_tc(sh, c, P, dp, s) : dispatch_main(sh, c, P, dp, s))) return st;
         if (ev_end && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_end), s, ev_flags),
                                        "record event")))
             return st;

@@ -310,13 +310,73 @@ struct QuantFastParams {
     float* xhat;
 };
 
-// GROUP: channels per (lo, scale) group (32, 64, 128) or 0 for the mid-rise code.  grid = (ceil(
-// n_alloc / 64), B * H), block 256: 8 warps x 2 rows x 4 passes = 64 rows per CTA.
+// Codes of one 128-channel row held 8 channels per lane by 16 lanes (l16): group extrema by xor
+// shuffles inside the group's lanes, scale / zero point as the reference computes them, division
+// through the group scale's reciprocal + Markstein correction.  GROUP: channels per (lo, scale)
+// group (32, 64, 128) or 0 for the mid-rise code.  All 32 lanes of the warp must call it.
+template <int BITS, int GROUP>
+__device__ __forceinline__ void qrow_codes(const float (&v)[8], bool valid, float step, uint32_t (&c)[8], float& lo,
+                                           float& sc) {
+    constexpr int TOP = (1 << BITS) - 1;
+    constexpr int LPG = GROUP ? GROUP / 8 : 16;
+    if constexpr (GROUP == 0) {
+        double ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += double(__fmul_rn(v[i], v[i]));
+#pragma unroll
+        for (int m = 8; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+        const float rms = __fsqrt_rn(float(ss / 128.0));
+        sc = fmaxf(as_stored(__fmul_rn(step, rms)), 5.9604644775390625e-8f);
+        lo = 0.f;
+    } else {
+        float mn = v[0], mx = v[0];
+#pragma unroll
+        for (int i = 1; i < 8; ++i) {
+            mn = fminf(mn, v[i]);
+            mx = fmaxf(mx, v[i]);
+        }
+#pragma unroll
+        for (int m = LPG / 2; m >= 1; m >>= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, m));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+        }
+        lo = as_stored(mn);
+        sc = fmaxf(as_stored(__fdiv_rn(__fsub_rn(mx, lo), float(TOP))), 5.9604644775390625e-8f);
+    }
+    const float y = __frcp_rn(sc);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float q;
+        if constexpr (GROUP == 0) q = rintf(__fadd_rn(div_rn_markstein(v[i], sc, y), 0.5f * float(TOP)));
+        else q = rintf(div_rn_markstein(__fsub_rn(v[i], lo), sc, y));
+        q = fminf(fmaxf(q, 0.f), float(TOP));
+        c[i] = valid ? uint32_t(q) : 0u;
+    }
+}
+
+// Reconstruction of code q (what the reference's dequantiser computes), for the optional xhat
+template <int BITS, int GROUP>
+__device__ __forceinline__ float qrow_xhat(uint32_t q, float lo, float sc) {
+    constexpr float HALF = 0.5f * float((1 << BITS) - 1);
+    return GROUP == 0 ? __fmul_rn(__fsub_rn(float(q), HALF), sc) : __fadd_rn(__fmul_rn(float(q), sc), lo);
+}
+
+// Row meta (fp16 scale, or the group's (lo, scale) pair) from the lanes that own a group
+template <int GROUP>
+__device__ __forceinline__ void qrow_meta(void* meta, int64_t row, int l16, bool valid, float lo, float sc) {
+    constexpr int LPG = GROUP ? GROUP / 8 : 16;
+    constexpr int G = GROUP ? 128 / GROUP : 1;
+    if constexpr (GROUP == 0) {
+        if (l16 == 0) static_cast<__half*>(meta)[row] = __float2half_rn(valid ? sc : 0.f);
+    } else {
+        if (l16 % LPG == 0) static_cast<uint32_t*>(meta)[row * G + l16 / LPG] = valid ? pack_half2(lo, sc) : 0u;
+    }
+}
+
+// grid = (ceil(n_alloc / 64), B * H), block 256: 8 warps x 2 rows x 4 passes = 64 rows per CTA.
 template <typename T, int BITS, int GROUP>
 __global__ void __launch_bounds__(256) quant_token128_kernel(const QuantFastParams p) {
-    constexpr int D = 128, TOP = (1 << BITS) - 1, RB = D * BITS / 8;
-    constexpr int LPG = GROUP ? GROUP / 8 : 16;         // lanes per group
-    constexpr int G = GROUP ? D / GROUP : 1;
+    constexpr int D = 128, RB = D * BITS / 8;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int l16 = lane & 15, half = lane >> 4;
     const int64_t bh = blockIdx.y;
@@ -348,56 +408,99 @@ __global__ void __launch_bounds__(256) quant_token128_kernel(const QuantFastPara
 #pragma unroll
     for (int ps = 0; ps < 4; ++ps) {
         const int64_t j = jbase + 16 * ps;
-        if (j >= p.n_alloc) continue;                  // uniform per half-warp row; no shuffles skipped unevenly
-        float lo, sc;
-        if constexpr (GROUP == 0) {
-            double ss = 0.0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) ss += double(__fmul_rn(v[ps][i], v[ps][i]));
-#pragma unroll
-            for (int m = 8; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-            const float rms = __fsqrt_rn(float(ss / double(D)));
-            sc = fmaxf(as_stored(__fmul_rn(p.step, rms)), 5.9604644775390625e-8f);
-            lo = 0.f;
-        } else {
-            float mn = v[ps][0], mx = v[ps][0];
-#pragma unroll
-            for (int i = 1; i < 8; ++i) {
-                mn = fminf(mn, v[ps][i]);
-                mx = fmaxf(mx, v[ps][i]);
-            }
-#pragma unroll
-            for (int m = LPG / 2; m >= 1; m >>= 1) {
-                mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, m));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
-            }
-            lo = as_stored(mn);
-            sc = fmaxf(as_stored(__fdiv_rn(__fsub_rn(mx, lo), float(TOP))), 5.9604644775390625e-8f);
-        }
-        const float y = __frcp_rn(sc);
+        if (j >= p.n_alloc) continue;                  // uniform per warp (both rows of a pair)
         uint32_t c[8];
+        float lo, sc;
+        qrow_codes<BITS, GROUP>(v[ps], valid[ps], p.step, c, lo, sc);
+        if (p.xhat && valid[ps])
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            float q;
-            if constexpr (GROUP == 0) q = rintf(__fadd_rn(div_rn_markstein(v[ps][i], sc, y), 0.5f * float(TOP)));
-            else q = rintf(div_rn_markstein(__fsub_rn(v[ps][i], lo), sc, y));
-            q = fminf(fmaxf(q, 0.f), float(TOP));
-            c[i] = valid[ps] ? uint32_t(q) : 0u;
-            if (p.xhat && valid[ps]) {
-                const float xh = GROUP == 0 ? __fmul_rn(__fsub_rn(q, 0.5f * float(TOP)), sc) : __fadd_rn(__fmul_rn(q, sc), lo);
-                p.xhat[(bh * p.n + j) * D + 8 * l16 + i] = xh;
-            }
-        }
+            for (int i = 0; i < 8; ++i) p.xhat[(bh * p.n + j) * D + 8 * l16 + i] = qrow_xhat<BITS, GROUP>(c[i], lo, sc);
         const uint32_t c0 = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
         const uint32_t c1 = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
         store_packed<BITS>(p.codes + (bh * p.n_alloc + j) * RB, pack_planar_lane<BITS>(c0, c1), l16);
-        if constexpr (GROUP == 0) {
-            if (l16 == 0) static_cast<__half*>(p.meta)[bh * p.n_alloc + j] = __float2half_rn(valid[ps] ? sc : 0.f);
-        } else {
-            if (l16 % LPG == 0)
-                static_cast<uint32_t*>(p.meta)[(bh * p.n_alloc + j) * G + l16 / LPG] =
-                    valid[ps] ? pack_half2(lo, sc) : 0u;
+        qrow_meta<GROUP>(p.meta, bh * p.n_alloc + j, l16, valid[ps], lo, sc);
+    }
+}
+
+// The same codes written in the value-operand block layout of the tensor-core decode: per 128-token
+// block, 128 channel rows of 16 * BITS bytes; byte k of channel row c holds the codes of tokens
+// pl * 128 / P + k (P = 8 / BITS) of channel c in bits [pl * BITS, ...) - the planar packing of the
+// token-major layout applied along tokens.  Metadata stays per token.  grid = (n_alloc / 128, B * H),
+// block 256: the block's codes are computed as in quant_token128_kernel into shared memory, then
+// transposed 4 x 4 bytes at a time (byte permutes) and stored with 128-bit stores.
+template <typename T, int BITS, int GROUP>
+__global__ void __launch_bounds__(256) quant_vblock128_kernel(const QuantFastParams p) {
+    constexpr int D = 128, RB = D * BITS / 8, P = 8 / BITS;
+    __shared__ __align__(16) uint32_t s_c[128][32];     // codes as bytes: [token][channel quad]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int l16 = lane & 15, half = lane >> 4;
+    const int64_t bh = blockIdx.y;
+    const int64_t b = bh / p.H, h = bh % p.H;
+    const T* xb = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + 8 * l16;
+    const int64_t j0 = int64_t(blockIdx.x) * 128;
+#pragma unroll
+    for (int grp = 0; grp < 2; ++grp) {
+        float v[4][8];
+        bool valid[4];
+#pragma unroll
+        for (int ps = 0; ps < 4; ++ps) {
+            const int r = warp * 16 + (grp * 4 + ps) * 2 + half;
+            const int64_t j = j0 + r;
+            int64_t src = 0;
+            valid[ps] = j < p.n;
+            if (valid[ps]) {
+                src = p.idx ? p.idx[bh * p.n + j] : p.first_row + j;
+                if (src < 0 || src >= p.T) {
+                    raise_status(KVB_DEV_BOUNDS);
+                    valid[ps] = false;
+                }
+            }
+            if (valid[ps]) {
+                load8<T>(xb + src * p.st, v[ps]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[ps][i] = 0.f;
+            }
         }
+#pragma unroll
+        for (int ps = 0; ps < 4; ++ps) {
+            const int r = warp * 16 + (grp * 4 + ps) * 2 + half;
+            const int64_t j = j0 + r;
+            uint32_t c[8];
+            float lo, sc;
+            qrow_codes<BITS, GROUP>(v[ps], valid[ps], p.step, c, lo, sc);
+            if (p.xhat && valid[ps])
+#pragma unroll
+                for (int i = 0; i < 8; ++i) p.xhat[(bh * p.n + j) * D + 8 * l16 + i] = qrow_xhat<BITS, GROUP>(c[i], lo, sc);
+            s_c[r][2 * l16] = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+            s_c[r][2 * l16 + 1] = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
+            qrow_meta<GROUP>(p.meta, bh * p.n_alloc + j, l16, valid[ps], lo, sc);
+        }
+    }
+    __syncthreads();
+    // item (channel quad cq, 16-byte column kg of the packed rows): 4 rows x 16 bytes
+    constexpr int NKG = RB / 16;
+    uint8_t* out = p.codes + (bh * p.n_alloc + j0) * RB;            // the block: 128 rows of RB bytes
+    for (int it = threadIdx.x; it < 32 * NKG; it += 256) {
+        const int cq = it & 31, kg = it >> 5;
+        uint32_t o[4][4] = {};                                      // [channel j][word]
+#pragma unroll
+        for (int pl = 0; pl < P; ++pl)
+#pragma unroll
+            for (int wq = 0; wq < 4; ++wq) {
+                // tokens pl * 128 / P + 16 kg + 4 wq + (0..3): one 4 x 4 byte block
+                const int t0 = pl * (128 / P) + 16 * kg + 4 * wq;
+                const uint32_t a0 = s_c[t0][cq], a1 = s_c[t0 + 1][cq], a2 = s_c[t0 + 2][cq], a3 = s_c[t0 + 3][cq];
+                const uint32_t x0 = __byte_perm(a0, a1, 0x5140), x1 = __byte_perm(a2, a3, 0x5140);
+                const uint32_t x2 = __byte_perm(a0, a1, 0x7362), x3 = __byte_perm(a2, a3, 0x7362);
+                const uint32_t bcol[4] = {__byte_perm(x0, x1, 0x5410), __byte_perm(x0, x1, 0x7632),
+                                          __byte_perm(x2, x3, 0x5410), __byte_perm(x2, x3, 0x7632)};
+#pragma unroll
+                for (int jc = 0; jc < 4; ++jc) o[jc][wq] |= bcol[jc] << (pl * BITS);
+            }
+#pragma unroll
+        for (int jc = 0; jc < 4; ++jc)
+            *reinterpret_cast<uint4*>(out + (4 * cq + jc) * RB + 16 * kg) = make_uint4(o[jc][0], o[jc][1], o[jc][2], o[jc][3]);
     }
 }
 

@@ -20,8 +20,12 @@ KVB_K_PER_TOKEN, KVB_K_PER_CHANNEL = 0, 1
 _i64, _i32, _p, _f32 = C.c_int64, C.c_int, C.c_void_p, C.c_float
 
 
+KVB_V_TOKEN_MAJOR, KVB_V_BLOCK128 = 0, 1
+
+
 class Stratum(C.Structure):
-    _fields_ = [("kbits", C.c_int), ("vbits", C.c_int), ("n", C.c_int64), ("n_alloc", C.c_int64),
+    _fields_ = [("kbits", C.c_int), ("vbits", C.c_int), ("v_layout", C.c_int), ("reserved", C.c_int),
+                ("n", C.c_int64), ("n_alloc", C.c_int64),
                 ("kc", C.c_void_p), ("vc", C.c_void_p), ("kmeta", C.c_void_p), ("vmeta", C.c_void_p)]
 
 
@@ -38,8 +42,11 @@ SIGNATURES = {
     "kvb_last_error": (C.c_char_p, []),
     "kvb_version": (C.c_int, []),
     "kvb_device_status": (_i32, [C.POINTER(C.c_uint), _i32, _p]),
+    "kvb_device_diag": (_i32, [C.POINTER(C.c_uint), _i32, _p]),
     "kvb_quant_pack": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                               _i32, _i32, _i32, _i32, _f32, _p, _p, _p, _p]),
+    "kvb_quant_pack_blocked": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,
+                                      _i32, _i32, _i32, _f32, _p, _p, _p, _p]),
     "kvb_rank_split": (_i32, [_p, _i32, _i64, _i64, _i64, _i32, C.POINTER(C.c_int64), C.POINTER(C.c_void_p),
                               C.POINTER(C.c_int64), _p]),
     "kvb_key_energy": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),

@@ -2,7 +2,8 @@
 
   build_mixed     config 1: per-token importance = key energy, head-synchronous 8 / 4 / 2-bit
                   strata (10 % / 30 % / 60 %), KIVI per-token groups for keys and values
-                  (kivi_quant(..., along_tokens=False) per stratum, STRATA_KV.py:826).
+                  (kivi_quant(..., along_tokens=False) per stratum, STRATA_KV.py:826); tc=True
+                  stores the values in the block layout of the tcgen05 decode.
   build_kivi      configs 0 / 4: KIVI keys per channel over token groups, values per token
                   (KIVIMethod.entries, STRATA_KV.py:797-803).
   build_eviction  config 2: SnapKV-style scores of decode queries, top-`budget` heavy hitters +
@@ -23,18 +24,30 @@ def strata_counts(T: int, tenths8: int = 1, tenths4: int = 3):
     return n8, n4, T - n8 - n4
 
 
-def build_mixed(K: torch.Tensor, V: torch.Tensor, group: int = 64, tenths=(1, 3)):
+def tc_layout_ok(x: torch.Tensor, group: int) -> bool:
+    """Whether values can be stored in the block layout of the tensor-core decode (d = 128, fp16 /
+    bf16 rows on 16-byte strides, groups of 32 / 64 / 128 channels)."""
+    return (x.shape[-1] == 128 and x.dtype in (torch.float16, torch.bfloat16) and group in (32, 64, 128)
+            and x.stride(-1) == 1 and all(s % 8 == 0 for s in x.stride()[:3]))
+
+
+def build_mixed(K: torch.Tensor, V: torch.Tensor, group: int = 64, tenths=(1, 3), tc: bool = False):
+    """tc: store values in the block layout read by the tcgen05 decode (decode_tc; exact to the same
+    tolerance, currently slower than the mma.sync decode on these shapes); the default keeps the
+    token-major layout of the mma.sync decode (decode_main).  None: the block layout whenever the
+    shapes allow it."""
     B, H, T, d = K.shape
     n8, n4, _ = strata_counts(T, *tenths)
     imp = ops.key_energy(K)
     i8, i4, i2 = ops.rank_split(imp, [n8, n4])
     cache = ops.PackedCache(B, H, d, k_group=group, v_group=group)
+    blocked = tc_layout_ok(V, group) if tc is None else tc
     sets = {}
     for bits, idx in ((8, i8), (4, i4), (2, i2)):
         if idx is None:
             continue
-        kq = ops.quant_pack(K, bits, group, idx=idx)
-        vq = ops.quant_pack(V, bits, group, idx=idx)
+        vq = ops.quant_pack(V, bits, group, idx=idx, blocked=blocked)
+        kq = ops.quant_pack(K, bits, group, idx=idx, n_alloc=vq["n_alloc"])
         cache.add_stratum(kq, vq)
         sets[bits] = idx
     return cache, sets

@@ -50,14 +50,19 @@ def round_up(x: int, m: int) -> int:
 # ------------------------------------------------------------------------------------------------
 def quant_pack(x: torch.Tensor, bits: int, group: int, *, per_channel: bool = False, midrise: bool = False,
                idx: torch.Tensor = None, first_row: int = 0, n: int = None, n_alloc: int = None,
-               want_xhat: bool = False, step: float = None) -> dict:
+               want_xhat: bool = False, step: float = None, blocked: bool = False) -> dict:
     """Quantise rows of x (B, H, T, d) and planar-pack them.
 
     Rows: idx (B, H, n) int64 gathers source rows; otherwise rows first_row .. first_row + n - 1.
     per_channel: KIVI keys (min / max per channel over `group` stored rows); else per-token groups
     of `group` channels (KIVI values / the mixed strata), or, with midrise, the STRATA code.
+    blocked: (values, per token, d = 128) codes in the 128-token channel-major block layout the
+    tensor-core decode reads, codes (B, H, n_alloc / 128, 128, 16 * bits), n_alloc % 128 == 0.
     Returns codes (B, H, n_alloc, d * bits / 8) uint8, meta (fp16 pairs / scales as documented in
-    kvb.h), n, n_alloc, optional xhat (B, H, n, d) float32."""
+    kvb.h), n, n_alloc, optional xhat (B, H, n, d) float32, layout."""
+    if blocked:
+        return _quant_pack_blocked(x, bits, group, midrise=midrise, idx=idx, first_row=first_row, n=n,
+                                   n_alloc=n_alloc, want_xhat=want_xhat, step=step)
     _cuda(x, idx)
     if x.dim() != 4 or x.stride(-1) != 1:
         raise ValueError("quant_pack: x must be (B, H, T, d) with unit channel stride")
@@ -88,7 +93,54 @@ def quant_pack(x: torch.Tensor, bits: int, group: int, *, per_channel: bool = Fa
         L.KVB_K_PER_CHANNEL if per_channel else L.KVB_K_PER_TOKEN,
         L.KVB_CODE_MIDRISE if midrise else L.KVB_CODE_ASYM, C.c_float(st),
         _ptr(codes), _ptr(meta), _ptr(xhat), C.c_void_p(_stream(x.device))), "kvb_quant_pack")
-    return {"codes": codes, "meta": meta, "xhat": xhat, "n": n, "n_alloc": n_alloc, "bits": bits, "group": group}
+    return {"codes": codes, "meta": meta, "xhat": xhat, "n": n, "n_alloc": n_alloc, "bits": bits, "group": group,
+            "layout": L.KVB_V_TOKEN_MAJOR}
+
+
+def _quant_pack_blocked(x, bits, group, *, midrise, idx, first_row, n, n_alloc, want_xhat, step):
+    _cuda(x, idx)
+    if x.dim() != 4 or x.stride(-1) != 1 or x.shape[-1] != 128:
+        raise ValueError("quant_pack(blocked): x must be (B, H, T, 128) with unit channel stride")
+    B, H, T, d = x.shape
+    if idx is not None:
+        if idx.dtype != torch.int64 or idx.shape[:2] != (B, H):
+            raise ValueError("quant_pack: idx must be int64 (B, H, n)")
+        idx = idx.contiguous()
+        n = idx.shape[2]
+    elif n is None:
+        n = T - first_row
+    n_alloc = round_up(max(n, 1), 128) if n_alloc is None else n_alloc
+    codes = torch.empty((B, H, n_alloc // 128, 128, 16 * bits), dtype=torch.uint8, device=x.device)
+    if midrise:
+        meta = torch.empty((B, H, n_alloc), dtype=torch.float16, device=x.device)
+    else:
+        meta = torch.empty((B, H, n_alloc, 128 // group, 2), dtype=torch.float16, device=x.device)
+    xhat = torch.empty((B, H, n, d), dtype=torch.float32, device=x.device) if want_xhat else None
+    st = UNIFORM_STEP[bits] if (midrise and step is None) else (step or 0.0)
+    L.check(L.lib().kvb_quant_pack_blocked(
+        _ptr(x), dtype_code(x), B, H, T, d, x.stride(0), x.stride(1), x.stride(2), _ptr(idx), first_row, n, n_alloc,
+        bits, d if midrise else group, L.KVB_CODE_MIDRISE if midrise else L.KVB_CODE_ASYM, C.c_float(st),
+        _ptr(codes), _ptr(meta), _ptr(xhat), C.c_void_p(_stream(x.device))), "kvb_quant_pack_blocked")
+    return {"codes": codes, "meta": meta, "xhat": xhat, "n": n, "n_alloc": n_alloc, "bits": bits, "group": group,
+            "layout": L.KVB_V_BLOCK128}
+
+
+def unblock_codes(codes: torch.Tensor) -> torch.Tensor:
+    """Block-layout value codes (B, H, n_alloc / 128, 128, 16 * bits) -> the token-major planar layout
+    (B, H, n_alloc, 16 * bits) (torch ops on the device; for inspection and tests)."""
+    B, H, nb, d, rb = codes.shape
+    bits = rb // 16
+    P = 8 // bits
+    x = codes.to(torch.int32)
+    # unpack along tokens: token pl * 128 / P + k of channel c is in byte k, bits [pl * bits, ...)
+    tok = torch.cat([(x >> (pl * bits)) & ((1 << bits) - 1) for pl in range(P)], -1)     # (B, H, nb, d, 128)
+    tok = tok.transpose(-1, -2)                                                            # (B, H, nb, 128, d)
+    # repack along channels (planar): byte i holds channel pl * d / P + i
+    planes = [tok[..., pl * (d // P):(pl + 1) * (d // P)] << (pl * bits) for pl in range(P)]
+    out = planes[0]
+    for t in planes[1:]:
+        out = out | t
+    return out.to(torch.uint8).reshape(B, H, nb * 128, rb)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -154,6 +206,14 @@ def query_scores(q: torch.Tensor, k: torch.Tensor, scaling: float, n_cand: int, 
     return out
 
 
+def device_diag(clear: bool = True, device=None) -> int:
+    """Where the first bounded wait gave up (0 if none); see kvb_device_diag in kvb.h."""
+    v = C.c_uint(0)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    L.check(L.lib().kvb_device_diag(C.byref(v), int(clear), C.c_void_p(_stream(dev))), "kvb_device_diag")
+    return v.value
+
+
 def device_status(clear: bool = True, device=None) -> int:
     v = C.c_uint(0)
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
@@ -185,7 +245,8 @@ class PackedCache:
         if kq["n"] != vq["n"] or kq["n_alloc"] != vq["n_alloc"]:
             raise ValueError("key and value codes of a stratum must hold the same tokens")
         self.strata.append({"kbits": kq["bits"], "vbits": vq["bits"], "n": kq["n"], "n_alloc": kq["n_alloc"],
-                            "kc": kq["codes"], "vc": vq["codes"], "km": kq["meta"], "vm": vq["meta"]})
+                            "kc": kq["codes"], "vc": vq["codes"], "km": kq["meta"], "vm": vq["meta"],
+                            "v_layout": vq.get("layout", L.KVB_V_TOKEN_MAJOR)})
         return self
 
     def set_exact(self, K, V, n_exact=None, n0=None, pos0=0):
@@ -205,6 +266,7 @@ class PackedCache:
         c.n_strata = len(self.strata)
         for i, s in enumerate(self.strata):
             c.strata[i].kbits, c.strata[i].vbits = s["kbits"], s["vbits"]
+            c.strata[i].v_layout = s.get("v_layout", L.KVB_V_TOKEN_MAJOR)
             c.strata[i].n, c.strata[i].n_alloc = s["n"], s["n_alloc"]
             c.strata[i].kc, c.strata[i].vc = s["kc"].data_ptr(), s["vc"].data_ptr()
             c.strata[i].kmeta, c.strata[i].vmeta = s["km"].data_ptr(), s["vm"].data_ptr()
@@ -223,7 +285,7 @@ class PackedCache:
         tot = 0
         for s in self.strata:
             n = s["n"]
-            tot += n * (s["kc"].shape[-1] + s["vc"].shape[-1]) * self.B * self.Hkv
+            tot += n * (self.d_code * (s["kbits"] + s["vbits"]) // 8) * self.B * self.Hkv
             for m in ("km", "vm"):
                 t = s[m]
                 if t.dim() == 5 and m == "km" and self.per_channel:

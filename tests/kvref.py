@@ -11,7 +11,11 @@ def np32(t: torch.Tensor) -> np.ndarray:
 
 
 def unpack(codes: torch.Tensor, bits: int, n: int) -> np.ndarray:
-    """(B, H, n_alloc, RB) planar bytes -> (B, H, n, d) integer codes (oracle unpack_planar)."""
+    """(B, H, n_alloc, RB) planar bytes -> (B, H, n, d) integer codes (oracle unpack_planar); block-
+    layout value codes (B, H, n_alloc / 128, 128, 16 * bits) are unblocked first."""
+    if codes.dim() == 5:
+        import kvb
+        codes = kvb.ops.unblock_codes(codes)
     return O.unpack_planar(codes[:, :, :n].cpu().numpy(), bits).astype(np.uint8)
 
 

@@ -24,13 +24,16 @@ def mixed_reference(K, V, sets, group=64):
     return Kh, Vh
 
 
+@pytest.mark.parametrize("tc", [True, False])
 @pytest.mark.parametrize("B,Hkv,rep,T,Tq", [(2, 2, 4, 1000, 1), (1, 2, 4, 5000, 2), (2, 1, 8, 777, 1),
                                              (1, 8, 4, 20000, 1)])
-def test_mixed_strata_decode(cuda_dev, B, Hkv, rep, T, Tq):
+def test_mixed_strata_decode(cuda_dev, B, Hkv, rep, T, Tq, tc):
+    """tc: values in the block layout (tcgen05 decode, decode_tc) or token-major (mma.sync decode)."""
     import kvb
     K, V = kvb.workloads.lognormal_kv(B, Hkv, T, 128, torch.bfloat16, seed=T)
     q = kvb.workloads.queries(B, Hkv * rep, Tq, 128, torch.bfloat16, seed=T)
-    cache, sets = kvb.cache.build_mixed(K.to(cuda_dev), V.to(cuda_dev))
+    cache, sets = kvb.cache.build_mixed(K.to(cuda_dev), V.to(cuda_dev), tc=tc)
+    assert all(s["v_layout"] == int(tc) for s in cache.strata)
     # strata sets are exactly the oracle's (energy ranking, ties to the lower index)
     ref_sets = O.mixed_strata(O.l2_importance(np32(K)))
     for b in (8, 4, 2):
@@ -87,8 +90,9 @@ def test_kivi_decode_with_sinks(cuda_dev):
     assert np.abs(out - ref).max() <= TOL
 
 
+@pytest.mark.parametrize("tc", [True, False])
 @pytest.mark.parametrize("rep,Tq", [(4, 1), (4, 2)])
-def test_strata_midrise_decode(cuda_dev, rep, Tq):
+def test_strata_midrise_decode(cuda_dev, rep, Tq, tc):
     """STRATA: rotated, centred mid-rise strata (2 / 4 / 8 bits) + exact rows incl. appended ones,
     query rotated once, output lifted by R plus (sum p) mu_V (StrataState.attend)."""
     import kvb
@@ -101,9 +105,11 @@ def test_strata_midrise_decode(cuda_dev, rep, Tq):
     tiers, cache = [], kvb.PackedCache(1, Hkv, d, midrise=True)
     for b, n in counts.items():
         Y = torch.randn(1, Hkv, n, d, generator=gen) * 1.3
-        kq = kvb.quant_pack(Y.to(cuda_dev), b, d, midrise=True)
         Yv = torch.randn(1, Hkv, n, d, generator=gen)
-        vq = kvb.quant_pack(Yv.to(cuda_dev), b, d, midrise=True)
+        dt = torch.float16 if tc else torch.float32      # the block layout takes 16-bit inputs
+        vq = kvb.quant_pack(Yv.to(cuda_dev, dt), b, d, midrise=True, blocked=tc)
+        kq = kvb.quant_pack(Y.to(cuda_dev, dt), b, d, midrise=True, n_alloc=vq["n_alloc"])
+        Y, Yv = Y.to(dt).float(), Yv.to(dt).float()
         cache.add_stratum(kq, vq)
         ck, sk, _ = O.strata_quantize(Y.numpy(), b)
         cv, sv, _ = O.strata_quantize(Yv.numpy(), b)
@@ -156,3 +162,17 @@ def test_tiny_contexts(cuda_dev, T):
     Kh = O.kivi_quant(np32(K), 2, 64, False, 0)["xhat"]
     Vh = O.kivi_quant(np32(V), 2, 64, False, 0)["xhat"]
     assert np.abs(out - attend_reference(np32(q), 128 ** -0.5, Kh, Vh)).max() <= TOL
+
+
+@pytest.mark.parametrize("rep,Tq", [(4, 1), (8, 1), (4, 2)])
+def test_tc_matches_mma_decode(cuda_dev, rep, Tq):
+    """The same mixed cache in both value layouts: tcgen05 and mma.sync decodes agree closely."""
+    import kvb
+    K, V = kvb.workloads.lognormal_kv(2, 2, 3000, 128, torch.bfloat16, seed=21)
+    q = kvb.workloads.queries(2, 2 * rep, Tq, 128, torch.bfloat16, seed=21).to(cuda_dev)
+    a, _ = kvb.cache.build_mixed(K.to(cuda_dev), V.to(cuda_dev), tc=True)
+    b, _ = kvb.cache.build_mixed(K.to(cuda_dev), V.to(cuda_dev), tc=False)
+    oa = kvb.decode(a, q, 128 ** -0.5, qpos=[3000] * Tq, out_dtype=torch.float32)
+    ob = kvb.decode(b, q, 128 ** -0.5, qpos=[3000] * Tq, out_dtype=torch.float32)
+    assert kvb.device_status() == 0
+    assert (oa - ob).abs().max().item() <= 1e-3

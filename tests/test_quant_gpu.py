@@ -108,3 +108,26 @@ def test_bad_rows_are_rejected_not_read(cuda_dev):
     kvb.device_status(clear=True)
     kvb.quant_pack(x, 4, 64, idx=idx)
     assert kvb.device_status(clear=True) & 2
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("group,midrise", [(32, False), (64, False), (128, False), (128, True)])
+@pytest.mark.parametrize("gather", [False, True])
+def test_blocked_layout_same_codes(cuda_dev, bits, group, midrise, gather):
+    """kvb_quant_pack_blocked writes the same codes / metadata / xhat as kvb_quant_pack, in the
+    128-token channel-major block layout (unblocked here on the device)."""
+    import kvb
+    T = 700
+    x = kvb.workloads.lognormal_kv(2, 3, T, 128, torch.bfloat16, seed=bits + group)[0].to(cuda_dev)
+    idx = None
+    if gather:
+        g = torch.Generator().manual_seed(bits)
+        idx = torch.stack([torch.stack([torch.randperm(T, generator=g)[:333].sort().values for _ in range(3)])
+                           for _ in range(2)]).to(cuda_dev)
+    a = kvb.quant_pack(x, bits, group, midrise=midrise, idx=idx, want_xhat=True, blocked=True)
+    b = kvb.quant_pack(x, bits, group, midrise=midrise, idx=idx, want_xhat=True, n_alloc=a["n_alloc"])
+    assert a["n_alloc"] % 128 == 0 and a["codes"].dim() == 5
+    assert torch.equal(kvb.ops.unblock_codes(a["codes"]), b["codes"])
+    assert torch.equal(a["meta"], b["meta"])
+    assert torch.equal(a["xhat"], b["xhat"])
+    assert kvb.device_status() == 0

@@ -58,7 +58,7 @@ def test_noalloc_python_wrapper_and_size_limit(cuda_dev):
     # a request whose scratch exceeds the built-in array is refused with a clear error
     big = kvb.PackedCache(64, 64, 128, k_group=64, v_group=64)
     for s in cache.strata:
-        big.strata.append(dict(s, n=1, n_alloc=16))
+        big.strata.append(dict(s, n=1, n_alloc=128))     # 128: the block value layout's granule
     qb = torch.zeros(64, 64 * 8, 1, 128, dtype=torch.bfloat16, device=cuda_dev)
     with pytest.raises(ValueError, match="scratch"):
         kvb.ops.decode_noalloc(big, qb, 0.1, torch.empty(64, 1, 512, 128, dtype=torch.bfloat16, device=cuda_dev))
