@@ -67,6 +67,8 @@ def args_():
     p.add_argument("--batch", type=int, default=None, help="batch per rank (default: the config's)")
     p.add_argument("--context", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--tc", action="store_true",
+                   help="config 1: values in the block layout, decoded by the tcgen05 kernel (decode_tc)")
     return p.parse_args()
 
 
@@ -177,7 +179,7 @@ def build_decode(a, rank, dev):
             seed = 43 + layer                        # the same model on every rank; ranks hold slices
         if w == "c1":
             K, V = W.lognormal_kv(B, Hkv, T, d, dtype, device=dev, seed=43 + 1000 * rank, layer=layer)
-            cache, _ = kvb.cache.build_mixed(K, V)
+            cache, _ = kvb.cache.build_mixed(K, V, tc=a.tc)
         elif w == "c0":
             K, V = W.outlier_kv(B, Hkv, T, d, dtype, device=dev, seed=42 + 1000 * rank)
             cache = kvb.cache.build_kivi(K, V, 4, 2, 128, 32)
@@ -463,7 +465,7 @@ def decode_arm(a):
         peak, peak_kind = peaks()
         gbs = world * bytes_step / (ms * 1e-3) / 1e9
         achieved = (sum(bytes_layer) / L) / (main_ms_avg * 1e-3) / 1e9
-        traffic = TRAFFIC.get(a.workload) if (a.layers, a.batch, a.context) == (None, None, None) else None
+        traffic = TRAFFIC.get(a.workload) if (a.layers, a.batch, a.context, a.tc) == (None, None, None, False) else None
         w = a.workload
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
@@ -482,13 +484,15 @@ def decode_arm(a):
                        "bytes_per_step_per_gpu": bytes_step},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "kernel": "decode_main", "bytes_per_launch": sum(bytes_layer) // L,
+                         "kernel": "decode_tc" if a.tc and w == "c1" else "decode_main",
+                         "bytes_per_launch": sum(bytes_layer) // L,
                          "us_per_launch": round(main_ms_avg * 1000, 2),
                          "traffic": None if traffic is None else round(traffic)},
             "e2e": {"value": round(world * bytes_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": q.numel() * esz,
                     "d2h_bytes_per_step": out.numel() * esz},
             "gpu_launches": (3 + int(split)) * L * a.steps,
+            "decode_kernel": "decode_tc (tcgen05)" if a.tc and w == "c1" else "decode_main (mma.sync)",
             "clocks": clk.summary(),
         }
         if w == "c1":
