@@ -473,8 +473,9 @@ def decode_arm(a):
             "pct_of_peak": round(100 * gbs / world / peak, 1), "higher_is_better": True,
             "scaling": "strong" if w in ("c4", "c4s") else "weak",
             "vs_baseline": None, "dtype": "u8 codes / fp16 MMA / fp32 softmax", "data": "synthetic",
-            "config": {"workload": DESC[w], "layers": L, "batch_per_gpu": B, "global_batch": B * world,
-                       "context": T, "Hq": Hq, "Hkv": Hkv, "d": d, "act_dtype": dt,
+            "config": {"workload": DESC[w], "layers": L, "batch_per_gpu": B,
+                       "global_batch": B if w == "c4s" else B * world,
+                       "context": T, **({"context_per_gpu": -(-T // world)} if w == "c4s" else {}), "Hq": Hq, "Hkv": Hkv, "d": d, "act_dtype": dt,
                        "l2": ("inputs larger than L2" if sum(bytes_layer) > 126e6 else
                               "packed cache smaller than L2: timed warm (launch-bound config)"),
                        "parallelism": {"c4": f"batch split over {world} ranks, no collective",

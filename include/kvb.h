@@ -137,6 +137,57 @@ kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, i
                                int64_t n_alloc, float* coef, int n_ctas, void* stream);
 
 /* ------------------------------------------------------------------------------------------ *
+ * K5: per-vector row codes (token-like stored vectors and format variants).  Rows follow
+ * kvb_quant_pack's convention: for each (b, h), stored row j < n is source row idx[b, h, j] when
+ * idx is given, else first_row + j, of x (B, H, T, d) with element strides (sb, sh, st) and unit
+ * channel stride.  Packed rows are MSB-first bit streams (code i in bits [i b, (i + 1) b), most
+ * significant first), which for d * b % 8 == 0 is the reference's pack_codes of the row-major
+ * codes (STRATA_KV.py:2728-2733). */
+#define KVB_ABSMAX_STRATA 0   /* s = max(fp16(max|x| / qmax), 2^-24): absmax_quant STRATA_KV.py:549-554 */
+#define KVB_ABSMAX_TILT 1     /* s = max(max|x|, 1e-8) / qmax in float32: fake_quant_tokens TILT_KV.py:721-727 */
+
+/* Symmetric absmax code of every row, qmax = 2^(bits-1) - 1, codes clamp(rint(x / s), -qmax, qmax)
+ * stored as codes + qmax (the bytes payload_bytes charges, STRATA_KV.py:2765-2766).  bits in 2..8,
+ * d % 32 == 0, d <= 256.  packed (B, H, n, d * bits / 8); scale (B, H, n) float32 (an fp16 value
+ * for KVB_ABSMAX_STRATA); xhat nullable (B, H, n, d) float32 = codes * s (what the reference's
+ * fake_quant_tokens returns).  Replaces fake_quant_tokens of the chunk methods (STRATA_KV.py:557-564,
+ * :587-591; TILT_KV.py:756-765). */
+kvb_status kvb_absmax_quant(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t d,
+                            int64_t sb, int64_t sh, int64_t st, const int64_t* idx, int64_t first_row, int64_t n,
+                            int bits, int variant, uint8_t* packed, float* scale, float* xhat, void* stream);
+
+/* MSB-first packing of `rows` rows of w codes (uint8, < 2^bits): out (rows, w * bits / 8); bits in
+ * 1..8, w * bits % 8 == 0.  pack_rows QUASAR_KV.py:1185-1190, pack_codes STRATA_KV.py:2728. */
+kvb_status kvb_pack_rows(const uint8_t* codes, int64_t rows, int64_t w, int bits, uint8_t* out, void* stream);
+
+/* Table decode of MSB-first rows: out[r, i] = (accumulate ? out[r, i] : 0) + levels[code_i] (times
+ * row_scale[r] when given), float32 (rows, w).  levels: 2^bits float32 on the device.  One call per
+ * stage of an embedded code sums the stages in order (byte_lut QUASAR_KV.py:1194-1203,
+ * embedded_quantize :1172-1182). */
+kvb_status kvb_decode_rows_lut(const uint8_t* packed, int64_t rows, int64_t w, int bits, const float* levels,
+                               const float* row_scale, int accumulate, float* out, void* stream);
+
+/* HEDGE per-token code at d = 128 (hedge_quant / centered_code HEDGE_KV.py:1103-1130): y = (x - mu) R^T
+ * (float32; mu nullable (H, 128) float32, R (128, 128) float32 row-major), then at bits 1..4 the
+ * Lloyd-Max levels (2^bits float32, `levels`) times s = max(fp16(RMS(y)), 2^-24), codes =
+ * bucketize(y / s, level midpoints); at bits 8 s = max(fp16(max|y| / 127), 2^-24), codes =
+ * clamp(rint(y / s), -127, 127) + 127.  packed (B, H, n, 16 * bits) MSB-first; scale (B, H, n)
+ * float32; y, xhat nullable (B, H, n, 128) float32, xhat = (level s) R + mu. */
+kvb_status kvb_hedge_quant(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t sb, int64_t sh,
+                           int64_t st, const int64_t* idx, int64_t first_row, int64_t n, const float* mu,
+                           const float* R, int bits, const float* levels, uint8_t* packed, float* scale, float* y,
+                           float* xhat, void* stream);
+
+/* TILT chunk selection (finalize_chunk TILT_KV.py:743-760, eviction and tail part): for each of U x H
+ * chunks of C <= 128 keys (k (U, H, C, 128), element strides su, sh, sc, unit channel stride) and
+ * nq observed queries qref (U, H, nq, 128) float32 (already scaled), share[c] = mean over queries of
+ * softmax_c(qref . k_c); idx (U, H, m) receives the m largest shares' positions (ties: lower
+ * position first) in ascending order; share (U, H, C) nullable.  A NaN share sets KVB_DEV_NAN. */
+kvb_status kvb_chunk_select(const void* k, int k_dtype, int64_t U, int64_t H, int64_t C, int64_t su, int64_t sh,
+                            int64_t sc, const float* qref, int64_t nq, int64_t m, int64_t* idx, float* share,
+                            void* stream);
+
+/* ------------------------------------------------------------------------------------------ *
  * K3: fused split-K flash decode over a packed, head-synchronous cache.  Replaces StrataState.attend
  * + strata_tier_kernel (STRATA_KV.py:1762-1796, :1450-1469), LayerState.attend / chunked_attention
  * (STRATA_KV.py:716, :641) over KIVI codes, and QuasarState.attend (QUASAR_KV.py:1942-1967, one

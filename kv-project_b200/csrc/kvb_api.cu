@@ -16,6 +16,7 @@
 
 #include "../../include/kvb.h"
 #include "kvb_common.cuh"
+#include "kvb_rowcode.cuh"
 #include "kvb_quant.cuh"
 #include "kvb_select.cuh"
 #include "kvb_decode.cuh"
@@ -349,6 +350,127 @@ kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, 
         return launch_check("scores_pool_kernel");
     }
     return KVB_OK;
+}
+
+}  // extern "C"
+
+// =============================================================================================
+// K5: per-vector row codes
+// =============================================================================================
+extern "C" {
+
+kvb_status kvb_absmax_quant(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t d, int64_t sb,
+                            int64_t sh, int64_t st, const int64_t* idx, int64_t first_row, int64_t n, int bits,
+                            int variant, uint8_t* packed, float* scale, float* xhat, void* stream) {
+    if (!x || !packed || !scale) return fail(KVB_EINVAL, "absmax_quant: null pointer");
+    if (B <= 0 || H <= 0 || T <= 0 || n < 0) return fail(KVB_EINVAL, "absmax_quant: sizes");
+    if (bits < 2 || bits > 8) return fail(KVB_EINVAL, "absmax_quant: bits must be in 2..8");
+    if (d % 32 || d < 32 || d > 256) return fail(KVB_EUNSUPPORTED, "absmax_quant: d must be a multiple of 32, <= 256");
+    if (variant != KVB_ABSMAX_STRATA && variant != KVB_ABSMAX_TILT) return fail(KVB_EINVAL, "absmax_quant: variant");
+    if (!idx && (first_row < 0 || first_row + n > T)) return fail(KVB_EINVAL, "absmax_quant: rows out of range");
+    if (n == 0) return KVB_OK;
+    kvb::AbsmaxParams p{x, B, H, T, d, sb, sh, st, idx, first_row, n, bits, variant, packed, scale, xhat};
+    const int64_t rows = B * H * n;
+    const unsigned grid = unsigned((rows + 7) / 8);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define KVB_AM(T_, N_) kvb::absmax_rows_kernel<T_, N_><<<grid, 256, 0, s>>>(p)
+#define KVB_AMD(T_)                                                                                 \
+    switch (d / 32) {                                                                               \
+        case 1: KVB_AM(T_, 1); break;                                                               \
+        case 2: KVB_AM(T_, 2); break;                                                               \
+        case 3: KVB_AM(T_, 3); break;                                                               \
+        case 4: KVB_AM(T_, 4); break;                                                               \
+        case 5: KVB_AM(T_, 5); break;                                                               \
+        case 6: KVB_AM(T_, 6); break;                                                               \
+        case 7: KVB_AM(T_, 7); break;                                                               \
+        default: KVB_AM(T_, 8); break;                                                              \
+    }
+    if (x_dtype == KVB_F32) { KVB_AMD(float) }
+    else if (x_dtype == KVB_F16) { KVB_AMD(__half) }
+    else if (x_dtype == KVB_BF16) { KVB_AMD(__nv_bfloat16) }
+    else return fail(KVB_EINVAL, "absmax_quant: dtype");
+#undef KVB_AMD
+#undef KVB_AM
+    return launch_check("absmax_rows_kernel");
+}
+
+kvb_status kvb_pack_rows(const uint8_t* codes, int64_t rows, int64_t w, int bits, uint8_t* out, void* stream) {
+    if (!codes || !out) return fail(KVB_EINVAL, "pack_rows: null pointer");
+    if (rows < 0 || w <= 0 || w > (1 << 24) || bits < 1 || bits > 8 || (w * bits) % 8)
+        return fail(KVB_EINVAL, "pack_rows: need bits in 1..8 and w * bits % 8 == 0");
+    if (rows == 0) return KVB_OK;
+    const int64_t total = rows * w * bits / 8;
+    const unsigned grid = unsigned(std::min<int64_t>((total + 255) / 256, 148 * 16));
+    kvb::pack_rows_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(codes, rows, int(w), bits, out);
+    return launch_check("pack_rows_kernel");
+}
+
+kvb_status kvb_decode_rows_lut(const uint8_t* packed, int64_t rows, int64_t w, int bits, const float* levels,
+                               const float* row_scale, int accumulate, float* out, void* stream) {
+    if (!packed || !levels || !out) return fail(KVB_EINVAL, "decode_rows_lut: null pointer");
+    if (rows < 0 || w <= 0 || w > (1 << 24) || bits < 1 || bits > 8 || (w * bits) % 8)
+        return fail(KVB_EINVAL, "decode_rows_lut: need bits in 1..8 and w * bits % 8 == 0");
+    if (rows == 0) return KVB_OK;
+    const int64_t total = rows * w;
+    const unsigned grid = unsigned(std::min<int64_t>((total + 255) / 256, 148 * 16));
+    kvb::decode_rows_lut_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(packed, rows, int(w), bits, levels,
+                                                                                   row_scale, accumulate, out);
+    return launch_check("decode_rows_lut_kernel");
+}
+
+kvb_status kvb_hedge_quant(const void* x, int x_dtype, int64_t B, int64_t H, int64_t T, int64_t sb, int64_t sh,
+                           int64_t st, const int64_t* idx, int64_t first_row, int64_t n, const float* mu,
+                           const float* R, int bits, const float* levels, uint8_t* packed, float* scale, float* y,
+                           float* xhat, void* stream) {
+    if (!x || !R || !packed || !scale) return fail(KVB_EINVAL, "hedge_quant: null pointer");
+    if (B <= 0 || H <= 0 || T <= 0 || n < 0) return fail(KVB_EINVAL, "hedge_quant: sizes");
+    if (!(bits >= 1 && bits <= 4) && bits != 8) return fail(KVB_EINVAL, "hedge_quant: bits must be 1-4 or 8");
+    if (bits <= 4 && !levels) return fail(KVB_EINVAL, "hedge_quant: levels needed at 1-4 bits");
+    if (!idx && (first_row < 0 || first_row + n > T)) return fail(KVB_EINVAL, "hedge_quant: rows out of range");
+    if (n == 0) return KVB_OK;
+    kvb::HedgeParams p{x, B, H, T, sb, sh, st, idx, first_row, n, mu, R, bits, levels, packed, scale, y, xhat};
+    const unsigned grid = unsigned((B * H * n + kvb::HG_ROWS - 1) / kvb::HG_ROWS);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int sm = int(kvb::HG_SMEM);
+    if (x_dtype == KVB_F32) {
+        cudaFuncSetAttribute(kvb::hedge_rows_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        kvb::hedge_rows_kernel<float><<<grid, 256, sm, s>>>(p);
+    } else if (x_dtype == KVB_F16) {
+        cudaFuncSetAttribute(kvb::hedge_rows_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        kvb::hedge_rows_kernel<__half><<<grid, 256, sm, s>>>(p);
+    } else if (x_dtype == KVB_BF16) {
+        cudaFuncSetAttribute(kvb::hedge_rows_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        kvb::hedge_rows_kernel<__nv_bfloat16><<<grid, 256, sm, s>>>(p);
+    } else {
+        return fail(KVB_EINVAL, "hedge_quant: dtype");
+    }
+    return launch_check("hedge_rows_kernel");
+}
+
+kvb_status kvb_chunk_select(const void* k, int k_dtype, int64_t U, int64_t H, int64_t C, int64_t su, int64_t sh,
+                            int64_t sc, const float* qref, int64_t nq, int64_t m, int64_t* idx, float* share,
+                            void* stream) {
+    if (!k || !qref || (!idx && m > 0)) return fail(KVB_EINVAL, "chunk_select: null pointer");
+    if (U <= 0 || H <= 0 || C <= 0 || C > 128 || nq <= 0) return fail(KVB_EINVAL, "chunk_select: sizes (C <= 128)");
+    if (m < 0 || m > C) return fail(KVB_EINVAL, "chunk_select: m must be in [0, C]");
+    if (U * H > 0x7FFFFFFF) return fail(KVB_EINVAL, "chunk_select: too many chunks");
+    kvb::ChunkSelectParams p{k, U, H, C, su, sh, sc, qref, nq, m, idx, share};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int sm = int(kvb::CS_SMEM);
+    const unsigned grid = unsigned(U * H);
+    if (k_dtype == KVB_F32) {
+        cudaFuncSetAttribute(kvb::chunk_select_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        kvb::chunk_select_kernel<float><<<grid, 256, sm, s>>>(p);
+    } else if (k_dtype == KVB_F16) {
+        cudaFuncSetAttribute(kvb::chunk_select_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        kvb::chunk_select_kernel<__half><<<grid, 256, sm, s>>>(p);
+    } else if (k_dtype == KVB_BF16) {
+        cudaFuncSetAttribute(kvb::chunk_select_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        kvb::chunk_select_kernel<__nv_bfloat16><<<grid, 256, sm, s>>>(p);
+    } else {
+        return fail(KVB_EINVAL, "chunk_select: dtype");
+    }
+    return launch_check("chunk_select_kernel");
 }
 
 }  // extern "C"

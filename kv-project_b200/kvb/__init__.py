@@ -2,16 +2,16 @@
 
 Drop-in native replacement for the decode-time hot path shared by the KV-cache compression
 methods of TahirSher/KV-Project: quantise + pack (K1), importance scores + budgeted eviction /
-strata assignment (K2), fused split-K flash decoding over packed codes (K3) and the spectral code
-(K4).  All compute runs in ``libkvb.so`` (hand-written CUDA for sm_100a behind the C ABI of
+strata assignment (K2), fused split-K flash decoding over packed codes (K3), the spectral code
+(K4) and per-vector row codes (K5: absmax tails, HEDGE, TILT chunk selection, MSB-first packing).  All compute runs in ``libkvb.so`` (hand-written CUDA for sm_100a behind the C ABI of
 ``include/kvb.h``); this package only moves tensors and builds descriptors.
 """
 
-from . import _lib, ops, cache, workloads, state, seqsplit   # noqa: F401
+from . import _lib, ops, cache, workloads, state, seqsplit, codebooks   # noqa: F401
 from .ops import (PackedCache, quant_pack, key_energy, rank_split, query_scores, decode, decode_plan,  # noqa: F401
                   device_status, UNIFORM_STEP)
 from .state import KvbStrataState, KvbCodedState, tier_as_kvb  # noqa: F401
 
-__all__ = ["ops", "cache", "workloads", "state", "seqsplit", "PackedCache", "quant_pack", "key_energy", "rank_split",
+__all__ = ["ops", "cache", "workloads", "state", "seqsplit", "codebooks", "PackedCache", "quant_pack", "key_energy", "rank_split",
            "query_scores", "decode", "decode_plan", "device_status", "UNIFORM_STEP",
            "KvbStrataState", "KvbCodedState", "tier_as_kvb"]

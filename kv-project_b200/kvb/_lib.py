@@ -15,6 +15,7 @@ KVB_OK, KVB_EINVAL, KVB_ECUDA, KVB_ETIMEDOUT, KVB_EUNSUPPORTED = 0, 1, 2, 3, 4
 KVB_F32, KVB_F16, KVB_BF16, KVB_F64 = 0, 1, 2, 3
 KVB_CODE_ASYM, KVB_CODE_MIDRISE = 0, 1
 KVB_K_PER_TOKEN, KVB_K_PER_CHANNEL = 0, 1
+KVB_ABSMAX_STRATA, KVB_ABSMAX_TILT = 0, 1
 
 # every entry point of include/kvb.h, with its ctypes signature (restype, argtypes)
 _i64, _i32, _p, _f32 = C.c_int64, C.c_int, C.c_void_p, C.c_float
@@ -55,6 +56,13 @@ SIGNATURES = {
                                 C.c_size_t, _p]),
     "kvb_spectral_encode": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i32, _f32, _p, _p, _i64, _p, _i32,
                                    _p]),
+    "kvb_absmax_quant": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i32, _i32,
+                                _p, _p, _p, _p]),
+    "kvb_pack_rows": (_i32, [_p, _i64, _i64, _i32, _p, _p]),
+    "kvb_decode_rows_lut": (_i32, [_p, _i64, _i64, _i32, _p, _p, _i32, _p, _p]),
+    "kvb_hedge_quant": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _p,
+                               _p, _p, _p, _p, _p]),
+    "kvb_chunk_select": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _p]),
     "kvb_decode_workspace_size": (C.c_size_t, [C.POINTER(Cache), _i32, _i32, _i32]),
     "kvb_decode": (_i32, [C.POINTER(Cache), _p, _i32, _i32, _i32, _f32, C.POINTER(C.c_int64), _p, _i32, _i32,
                           _p, C.c_size_t, _p]),

@@ -418,6 +418,143 @@ def decode_plan(cache: PackedCache, n_ctas: int):
 SPECTRAL_R = 32
 
 
+# ------------------------------------------------------------------------------------------------
+# K5: per-vector row codes
+# ------------------------------------------------------------------------------------------------
+def _rows(x, idx, first_row, n):
+    _cuda(x, idx)
+    if x.dim() != 4 or x.stride(-1) != 1:
+        raise ValueError("kvb: x must be (B, H, T, d) with unit channel stride")
+    B, H, T, d = x.shape
+    if idx is not None:
+        if idx.dtype != torch.int64 or idx.dim() != 3 or tuple(idx.shape[:2]) != (B, H):
+            raise ValueError("kvb: idx must be int64 (B, H, n)")
+        idx = idx.contiguous()
+        n = idx.shape[2]
+    elif n is None:
+        n = T - first_row
+    return B, H, T, d, idx, n
+
+
+def absmax_quant(x: torch.Tensor, bits: int, *, variant: str = "strata", idx: torch.Tensor = None,
+                 first_row: int = 0, n: int = None, want_xhat: bool = False) -> dict:
+    """Per-vector symmetric absmax code of rows of x (B, H, T, d), optionally gathered by idx (B, H, n).
+    variant "strata": fp16 scale (absmax_quant STRATA_KV.py:549); "tilt": float32 scale
+    (fake_quant_tokens TILT_KV.py:721).  Returns packed (B, H, n, d * bits / 8) MSB-first codes + qmax,
+    scale (B, H, n) float32, optional xhat (B, H, n, d) float32 = codes * scale."""
+    B, H, T, d, idx, n = _rows(x, idx, first_row, n)
+    var = {"strata": L.KVB_ABSMAX_STRATA, "tilt": L.KVB_ABSMAX_TILT}[variant]
+    packed = torch.empty((B, H, n, d * bits // 8), dtype=torch.uint8, device=x.device)
+    scale = torch.empty((B, H, n), dtype=torch.float32, device=x.device)
+    xhat = torch.empty((B, H, n, d), dtype=torch.float32, device=x.device) if want_xhat else None
+    L.check(L.lib().kvb_absmax_quant(_ptr(x), dtype_code(x), B, H, T, d, x.stride(0), x.stride(1), x.stride(2),
+                                     _ptr(idx), first_row, n, bits, var, _ptr(packed), _ptr(scale), _ptr(xhat),
+                                     C.c_void_p(_stream(x.device))), "kvb_absmax_quant")
+    return {"packed": packed, "scale": scale, "xhat": xhat, "bits": bits, "n": n}
+
+
+def pack_rows(codes: torch.Tensor, bits: int) -> torch.Tensor:
+    """(..., w) uint8 codes < 2^bits -> (..., w * bits / 8) MSB-first bytes (pack_rows QUASAR_KV.py:1185)."""
+    _cuda(codes)
+    if codes.dtype != torch.uint8:
+        raise ValueError("pack_rows: codes must be uint8")
+    codes = codes.contiguous()
+    w = codes.shape[-1]
+    rows = codes.numel() // w if w else 0
+    out = torch.empty(codes.shape[:-1] + (w * bits // 8,), dtype=torch.uint8, device=codes.device)
+    L.check(L.lib().kvb_pack_rows(_ptr(codes), rows, w, bits, _ptr(out), C.c_void_p(_stream(codes.device))),
+            "kvb_pack_rows")
+    return out
+
+
+def decode_rows_lut(packed: torch.Tensor, bits: int, levels: torch.Tensor, *, row_scale: torch.Tensor = None,
+                    out: torch.Tensor = None) -> torch.Tensor:
+    """Table decode of MSB-first rows (..., w * bits / 8) -> (..., w) float32 = levels[code] (* row_scale);
+    with `out` given the stage is added to it (byte_lut QUASAR_KV.py:1194, stages summed in order)."""
+    _cuda(packed, levels, row_scale, out)
+    if packed.dtype != torch.uint8 or levels.dtype != torch.float32 or levels.numel() != 1 << bits:
+        raise ValueError("decode_rows_lut: packed uint8, levels float32 of 2^bits entries")
+    packed = packed.contiguous()
+    rb = packed.shape[-1]
+    w = rb * 8 // bits
+    rows = packed.numel() // rb if rb else 0
+    acc = out is not None
+    if out is None:
+        out = torch.empty(packed.shape[:-1] + (w,), dtype=torch.float32, device=packed.device)
+    elif out.dtype != torch.float32 or not out.is_contiguous() or tuple(out.shape) != tuple(packed.shape[:-1]) + (w,):
+        raise ValueError("decode_rows_lut: out must be contiguous float32 (..., w)")
+    if row_scale is not None:
+        row_scale = row_scale.contiguous().float()
+        if row_scale.numel() != rows:
+            raise ValueError("decode_rows_lut: row_scale needs one value per row")
+    L.check(L.lib().kvb_decode_rows_lut(_ptr(packed), rows, w, bits, _ptr(levels.contiguous()), _ptr(row_scale),
+                                        int(acc), _ptr(out), C.c_void_p(_stream(packed.device))),
+            "kvb_decode_rows_lut")
+    return out
+
+
+def hedge_quant(x: torch.Tensor, R: torch.Tensor, bits: int, levels: torch.Tensor = None, *, mu: torch.Tensor = None,
+                idx: torch.Tensor = None, first_row: int = 0, n: int = None, want_y: bool = False,
+                want_xhat: bool = False) -> dict:
+    """HEDGE per-token code of rows of x (B, H, T, 128) (hedge_quant / centered_code HEDGE_KV.py:1103-1130):
+    y = (x - mu) R^T, Lloyd-Max levels (bits 1-4; `levels` float32 2^bits, see codebooks.lloyd_max) or
+    int8 absmax (bits 8).  mu: (H, 128) or None.  Returns packed (B, H, n, 16 * bits) MSB-first, scale
+    (B, H, n) float32, optional y and xhat = (level * s) R + mu, (B, H, n, 128) float32."""
+    B, H, T, d, idx, n = _rows(x, idx, first_row, n)
+    if d != 128:
+        raise NotImplementedError("hedge_quant: head dim 128 only")
+    _cuda(R, levels, mu)
+    R = R.float().contiguous()
+    if tuple(R.shape) != (128, 128):
+        raise ValueError("hedge_quant: R must be (128, 128)")
+    if mu is not None:
+        mu = mu.float().reshape(H, 128).contiguous()
+    if bits <= 4:
+        if levels is None or levels.numel() != 1 << bits:
+            raise ValueError("hedge_quant: 2^bits levels needed at 1-4 bits")
+        levels = levels.float().contiguous()
+    dev = x.device
+    packed = torch.empty((B, H, n, 16 * bits), dtype=torch.uint8, device=dev)
+    scale = torch.empty((B, H, n), dtype=torch.float32, device=dev)
+    y = torch.empty((B, H, n, 128), dtype=torch.float32, device=dev) if want_y else None
+    xhat = torch.empty((B, H, n, 128), dtype=torch.float32, device=dev) if want_xhat else None
+    L.check(L.lib().kvb_hedge_quant(_ptr(x), dtype_code(x), B, H, T, x.stride(0), x.stride(1), x.stride(2), _ptr(idx),
+                                    first_row, n, _ptr(mu), _ptr(R), bits, _ptr(levels if bits <= 4 else None),
+                                    _ptr(packed), _ptr(scale), _ptr(y), _ptr(xhat), C.c_void_p(_stream(dev))),
+            "kvb_hedge_quant")
+    return {"packed": packed, "scale": scale, "y": y, "xhat": xhat, "bits": bits, "n": n}
+
+
+def chunk_select(k: torch.Tensor, qref: torch.Tensor, m: int, want_share: bool = False):
+    """TILT chunk selection (finalize_chunk TILT_KV.py:743-760): k (U, H, C, 128) with C <= 128, qref
+    (U, H, nq, 128) scaled observed queries.  Returns idx (U, H, m) int64 (the m largest shares, ties
+    to the lower position, ascending) and, optionally, share (U, H, C) float32."""
+    _cuda(k, qref)
+    if k.dim() != 4 or k.shape[-1] != 128 or k.stride(-1) != 1:
+        raise ValueError("chunk_select: k must be (U, H, C, 128) with unit channel stride")
+    U, H, Cn, _ = k.shape
+    qref = qref.float().contiguous()
+    if qref.dim() != 4 or tuple(qref.shape[:2]) != (U, H) or qref.shape[-1] != 128:
+        raise ValueError("chunk_select: qref must be (U, H, nq, 128)")
+    idx = torch.empty((U, H, m), dtype=torch.int64, device=k.device)
+    share = torch.empty((U, H, Cn), dtype=torch.float32, device=k.device) if want_share else None
+    L.check(L.lib().kvb_chunk_select(_ptr(k), dtype_code(k), U, H, Cn, k.stride(0), k.stride(1), k.stride(2),
+                                     _ptr(qref), qref.shape[2], m, _ptr(idx), _ptr(share),
+                                     C.c_void_p(_stream(k.device))), "kvb_chunk_select")
+    return idx, share
+
+
+def chunk_tails(k: torch.Tensor, v: torch.Tensor, qref: torch.Tensor, m: int, keep_bits: int = 8) -> dict:
+    """The token part of TILT's finalize_chunk for the eviction family (TILT_KV.py:758-766): the m
+    top-share keys of every chunk and their values, each stored as an absmax code with a float32
+    scale (fake_quant_tokens TILT_KV.py:721).  Two kernels: chunk_select, then absmax_quant over the
+    gathered rows of k and of v.  Returns idx and the k / v codes, scales and reconstructions."""
+    idx, _ = chunk_select(k, qref, m)
+    kq = absmax_quant(k, keep_bits, variant="tilt", idx=idx, want_xhat=True)
+    vq = absmax_quant(v, keep_bits, variant="tilt", idx=idx, want_xhat=True)
+    return {"idx": idx, "k": kq, "v": vq}
+
+
 def split_basis(basis_r: torch.Tensor) -> torch.Tensor:
     """basis_r (H, d, r) float -> (2, H, r, d) fp16: transposed basis split as hi + lo (exact to ~22
     bits), the operand layout kvb_spectral_encode expects."""

@@ -5,7 +5,8 @@ box never runs this):
 
     KVB_REFERENCE=/path/to/KV-Project python tests/golden/make_golden.py
 
-It imports the reference modules read-only (``STRATA_KV.py``, ``QUASAR_KV.py``), calls their own
+It imports the reference modules read-only (``STRATA_KV.py``, ``QUASAR_KV.py``, ``HEDGE_KV.py``,
+``TILT_KV.py``), calls their own
 functions on seeded inputs and stores inputs and outputs as small ``.npz`` files beside this
 script.  ``tests/test_oracle_golden.py`` checks the numpy oracle against every array here.
 """
@@ -220,5 +221,69 @@ def main():
     print("wrote", sizes)
 
 
+def rowcodes():
+    """Per-vector row codes: STRATA / TILT absmax, HEDGE Lloyd-Max + rotation, TILT chunk top-m,
+    QUASAR pack_rows + byte_lut (rowcodes.npz; its own generator, so the other files are untouched)."""
+    S, Q = load_reference()
+    import HEDGE_KV as Hd            # noqa: E402  (reference modules, read-only)
+    import TILT_KV as Ti             # noqa: E402
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(4321)
+    out = {}
+    # absmax codes of both reference variants (STRATA: fp16 scale; TILT: float32 scale)
+    x = torch.randn(40, 128, generator=g) * torch.linspace(0.1, 4.0, 128)
+    x[3] = 0.0
+    x[5, 17] = 300.0
+    x[7] *= 1e-6
+    out["am_x"] = np32(x)
+    for b in (2, 3, 4, 5, 8):
+        c, s = S.absmax_quant(x, b)
+        out[f"am{b}_codes"], out[f"am{b}_s"] = np32(c), np32(s)
+        out[f"am{b}_packed"] = S.pack_codes(c + 2 ** (b - 1) - 1, b).numpy()
+        out[f"tilt{b}_xhat"] = np32(Ti.fake_quant_tokens(x, b))
+    # HEDGE: Lloyd-Max levels, rotation, per-token codes of every width (centred and plain)
+    for b in (1, 2, 3, 4):
+        out[f"lm{b}"] = np32(Hd.lloyd_max_gaussian(b))
+    R = Hd.rotation_matrix(128, "layer0")
+    out["hedge_R"] = np32(R)
+    X = (torch.randn(2, 24, 128, generator=g) * torch.exp(-torch.arange(128) / 40.0) + 0.3).to(torch.bfloat16).float()
+    X[1, 5] = 0.0
+    mu = S.as_stored(X.mean(1, keepdim=True))
+    out["hedge_x"], out["hedge_mu"] = np32(X), np32(mu)
+    for b in (1, 2, 3, 4, 8):
+        xh, c, s = Hd.centered_code(X, mu, R, b)
+        out[f"hedge{b}_xhat"], out[f"hedge{b}_codes"], out[f"hedge{b}_s"] = np32(xh), c.numpy(), np32(s)
+    out["hedge_y"] = np32((X - mu) @ R.T)
+    # TILT chunk finalisation, eviction family: top-m of the observed-query share + 8-bit tails
+    B, Hkv, C, d, nq, m = 2, 1, 128, 128, 64, 23
+    k = torch.randn(B, Hkv, C, d, generator=g) * (1.0 + torch.rand(1, 1, 1, d, generator=g))
+    v = torch.randn(B, Hkv, C, d, generator=g)
+    qref = torch.randn(B, Hkv, nq, d, generator=g) * d ** -0.5
+    meth = Ti.ChunkMethod("evict", "evict", 1.5)
+    res = Ti.finalize_chunk(k, v, qref, meth, {"tokens": m, "atoms": 0}, 8, None, (0, 0))
+    share = torch.einsum("bhqd,bhcd->bhqc", qref, k).softmax(-1).mean(2)
+    out.update(tilt_k=np32(k), tilt_v=np32(v), tilt_q=np32(qref), tilt_share=np32(share),
+               tilt_idx=res["tok"]["idx"].numpy(), tilt_kq=np32(res["tok"]["k"]), tilt_vq=np32(res["tok"]["v"]),
+               tilt_m=np.array(m))
+    # QUASAR embedded (2, 2, 4) stage code: pack_rows bytes and the byte_lut tables that decode them
+    stages = (2, 2, 4)
+    u = torch.randn(12, 32, generator=g)
+    codes, cum = Q.embedded_quantize(u, stages)
+    out["emb_u"] = np32(u)
+    for t, b in enumerate(stages):
+        out[f"emb_levels{t}"] = np32(Q.stage_codebooks(stages)[t])
+        out[f"emb_codes{t}"] = codes[t].numpy()
+        out[f"emb_rows{t}"] = Q.pack_rows(codes[t], b).numpy()
+        out[f"emb_lut{t}"] = np32(Q.byte_lut(stages, t))
+        out[f"emb_cum{t}"] = np32(cum[t])
+    np.savez_compressed(HERE / "rowcodes.npz", **out)
+    print("wrote rowcodes.npz", (HERE / "rowcodes.npz").stat().st_size)
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["rowcodes"]:
+        rowcodes()
+    else:
+        main()
+        rowcodes()

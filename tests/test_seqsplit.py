@@ -138,3 +138,52 @@ def test_lse_merge_empty_part(cuda_dev):
     ref = (w[..., None] * parts[[0, 2], :5]).sum(0) / w.sum(0)[..., None]
     assert (out[:5] - ref).abs().max().item() <= 1e-5
     assert (out[5] == 0).all()
+
+
+def _nccl_rank_main(rank, world, port, ret):
+    import datetime
+    import torch.distributed as dist
+    import kvb
+    from kvb import seqsplit as SS
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        B, Hkv, rep, Tq, T, d = 2, 2, 8, 1, 3000, 128
+        K, V = kvb.workloads.outlier_kv(B, Hkv, T, d, torch.bfloat16, seed=13)
+        q = kvb.workloads.queries(B, Hkv * rep, Tq, d, torch.bfloat16, seed=13).to(dev)
+        K, V = K.to(dev), V.to(dev)
+        build = lambda k, v: kvb.cache.build_kivi(k, v, 4, 4, 128, 128)
+        cache = SS.shard_cache(build, K, V, rank, world)
+        dec = SS.SeqSplitDecoder()
+        out = dec.attend(cache, q, d ** -0.5, out_dtype=torch.float32)
+        out2 = dec.attend(cache, q, d ** -0.5, out_dtype=torch.float32)     # buffers reused
+        full = kvb.decode(build(K, V), q, d ** -0.5, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        ret[rank] = (float((out - full).abs().max()), bool(torch.equal(out, out2)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_seqsplit_nccl_two_ranks():
+    """The NCCL path of SeqSplitDecoder on 2 GPUs (one process each): every rank's merged output equals
+    the one-GPU decode of the whole context."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as man:
+        ret = man.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_nccl_rank_main, args=(r, 2, port, ret)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+        assert sorted(ret.keys()) == [0, 1]
+        for err, same in ret.values():
+            assert err <= 1e-4 and same
