@@ -25,6 +25,9 @@
 #include "kvb_decode_tc.cuh"
 
 #define KVB_VERSION 100
+#ifndef KVB_PDL
+#define KVB_PDL 1             // programmatic dependent launch of the main kernel after the prologue
+#endif
 
 namespace {
 
@@ -679,7 +682,11 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
         const kvb_stratum& st = c->strata[s];
         P.tok[s] = chunk_of(c, s);
         nch[s] = (st.n + P.tok[s] - 1) / P.tok[s];
-        const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + 8;
+        // work per token in byte-equivalents: its code bytes plus a fixed per-token cost (code
+        // extraction, MMAs, softmax) worth ~139 bytes at d_code 128, measured on B200 from one-width
+        // caches (34.3 / 45.3 / 66.8 ps per token-head at 2 / 4 / 8 bits, linear in the code bytes).
+        // Balancing bytes alone gave 2-bit-heavy CTAs ~1.9x the time of 8-bit-heavy ones.
+        const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + (139 * c->d_code + 64) / 128;
         wfull[s] = int64_t(P.tok[s]) * bpt;
         wlast[s] = (st.n - (nch[s] - 1) * P.tok[s]) * bpt;
         chunks_per_head += nch[s];
@@ -745,12 +752,32 @@ WsLayout ws_layout(const kvb_cache* c, const DecodeShape& sh, int n_pieces) {
 }
 
 // ---- instantiation table ----
+// Launch with programmatic stream serialization when `pdl` is set: the kernel may start before the
+// preceding kernel in the stream completes; it must call griddepcontrol.wait before reading that
+// kernel's outputs (decode_main does).
+template <typename P>
+cudaError_t launch_maybe_pdl(void (*fn)(P), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                             const P& arg) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, arg);
+}
+
 template <int D, int R, int GK, int GV, int KM, int CK>
-kvb_status launch_main(const kvb::DecodeParams& p, int n_ctas, size_t smem, cudaStream_t s) {
+kvb_status launch_main(const kvb::DecodeParams& p, int n_ctas, size_t smem, cudaStream_t s, bool pdl) {
     auto fn = kvb::decode_main<D, R, GK, GV, KM, CK>;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return cuda_check(e, "decode_main smem attribute");
-    fn<<<n_ctas, kvb::DEC_THREADS, smem, s>>>(p);
+    if ((e = launch_maybe_pdl(fn, dim3(n_ctas), dim3(kvb::DEC_THREADS), smem, s, pdl, p)) != cudaSuccess)
+        return cuda_check(e, "decode_main launch");
     return launch_check("decode_main");
 }
 
@@ -766,7 +793,7 @@ int stage_bytes_for(const kvb_cache* c, const Plan& P) {
 }
 
 template <int D, int R, int GK, int GV, int KM, int CK>
-kvb_status run_main(const kvb_cache* c, const Plan& P, kvb::DecodeParams& p, cudaStream_t s) {
+kvb_status run_main(const kvb_cache* c, const Plan& P, kvb::DecodeParams& p, cudaStream_t s, bool pdl) {
     const int sb = std::max(128, stage_bytes_for<D, R, GK, GV, KM, CK>(c, P));
     const int red = (2 * kvb::DEC_CWARPS * R + kvb::DEC_CWARPS * R * D) * 4;
     const int fixed = 128 + (red + 127) / 128 * 128;
@@ -774,15 +801,15 @@ kvb_status run_main(const kvb_cache* c, const Plan& P, kvb::DecodeParams& p, cud
     if (ns < 2) return fail(KVB_EUNSUPPORTED, "decode: stage of %d bytes does not fit twice in shared memory", sb);
     p.stage_bytes = sb;
     p.nstage = ns;
-    return launch_main<D, R, GK, GV, KM, CK>(p, P.n_ctas, size_t(fixed) + size_t(ns) * sb, s);
+    return launch_main<D, R, GK, GV, KM, CK>(p, P.n_ctas, size_t(fixed) + size_t(ns) * sb, s, pdl);
 }
 
 kvb_status dispatch_main(const DecodeShape& sh, const kvb_cache* c, const Plan& P, kvb::DecodeParams& p,
-                         cudaStream_t s) {
+                         cudaStream_t s, bool pdl) {
     using namespace kvb;
 #define KVB_CASE(D_, R_, GK_, GV_, KM_, CK_)                                                           \
     if (sh.D == D_ && sh.R == R_ && sh.GK == GK_ && sh.GV == GV_ && sh.kmode == KM_ && sh.code == CK_) \
-        return run_main<D_, R_, GK_, GV_, KM_, CK_>(c, P, p, s);
+        return run_main<D_, R_, GK_, GV_, KM_, CK_>(c, P, p, s, pdl);
     // KIVI per-token keys (mixed-precision strata, config 1)
     KVB_CASE(128, 4, 2, 2, KM_TOKEN, KV_ASYM)
     KVB_CASE(128, 8, 2, 2, KM_TOKEN, KV_ASYM)
@@ -962,6 +989,11 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
     if (c->n_exact > 0 && c->exact_dtype != q_dtype) return fail(KVB_EINVAL, "decode: exact rows must have q's dtype");
     if (!aligned(workspace, 256)) return fail(KVB_EINVAL, "decode: workspace must be 256-byte aligned");
     const int nct = resolve_ctas(n_ctas);
+    // programmatic dependent launch of the main kernel (its first cache copies overlap the prologue),
+    // except when events bracket it (an event between two launches must see the first one complete).
+    // Measured on B200 at config 1: 1.3 % per step; the same for the merge kernel was 2.7 % slower,
+    // and merging in the main kernel's tail (the CTA completing a head) gained nothing.
+    const bool pdl = KVB_PDL && !(ev_begin || ev_end);
     Plan P;
     build_plan(c, nct, P);
     if (P.n_pieces > kvb::DEC_MAX_PIECES) return fail(KVB_EUNSUPPORTED, "decode: %d pieces > %d", P.n_pieces, kvb::DEC_MAX_PIECES);
@@ -1020,7 +1052,7 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
         if (ev_begin && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_begin), s, ev_flags),
                                          "record event")))
             return st;
-        if ((st = uses_tc(c) ? dispatch_tc(sh, c, P, dp, s) : dispatch_main(sh, c, P, dp, s))) return st;
+        if ((st = uses_tc(c) ? dispatch_tc(sh, c, P, dp, s) : dispatch_main(sh, c, P, dp, s, pdl))) return st;
         if (ev_end && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_end), s, ev_flags),
                                        "record event")))
             return st;
@@ -1058,12 +1090,13 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
     for (int h = 0; h <= P.n_heads; ++h) mp.head_begin[h] = P.head_begin[h];
     const int Ra = rep * Tq;
     const size_t msm = size_t(Ra) * (2 * c->d + c->d_code) * 4 + 3 * Ra * 4 + 256 * 4;
-#define KVB_MERGE(T_)                                                                       \
-    kvb::decode_merge<T_, T_><<<heads, 256, msm, s>>>(mp);
+    cudaError_t le;
+#define KVB_MERGE(T_) le = launch_maybe_pdl(kvb::decode_merge<T_, T_>, dim3(heads), dim3(256), msm, s, false, mp);
     if (q_dtype == KVB_F32) { KVB_MERGE(float) }
     else if (q_dtype == KVB_F16) { KVB_MERGE(__half) }
     else { KVB_MERGE(__nv_bfloat16) }
 #undef KVB_MERGE
+    if (le != cudaSuccess) return cuda_check(le, "decode_merge launch");
     return launch_check("decode_merge");
 }
 }  // namespace

@@ -9,11 +9,11 @@
 //   1. prologue  (one CTA per (b, kv head)): query rows of the head -> code-space query (optional
 //      rotation / basis projection), power-of-two prescale, group sums, logit bias.
 //   2. main      (persistent, one CTA per SM): a host-built plan hands every CTA a contiguous,
-//      byte-balanced run of "chunks" (192..768 tokens of one stratum of one head).  Chunks stream
-//      into a shared-memory ring with cp.async.bulk (TMA) + mbarriers; the last of the 12 warps to
-//      release a stage refills it.  Every warp takes pairs of 16-token tiles
-//      (kvb_decode_tile.cuh).  At the end of each (head, stratum) piece the 12 warps merge their
-//      (max, sum, acc) exactly and write one split-K partial.
+//      work-balanced run of "chunks" (192..768 tokens of one stratum of one head; work = code bytes
+//      + a fixed per-token cost).  Chunks stream into a shared-memory ring with cp.async.bulk
+//      (TMA) + mbarriers; the last of the 12 warps to release a stage refills it.  Every warp takes
+//      pairs of 16-token tiles (kvb_decode_tile.cuh).  At the end of each (head, stratum) piece the
+//      12 warps merge their (max, sum, acc) exactly and write one split-K partial.
 //   3. merge     (one CTA per head): exact rows (fp32 on CUDA cores), log-sum-exp merge of the
 //      partials (STRATA_KV.py:1784-1792), optional lift back to model space, output in q's dtype.
 //
@@ -75,6 +75,9 @@ struct DecodeParams {
 template <typename T, int R>
 __global__ void __launch_bounds__(128) decode_prologue(const PrologueParams p) {
     extern __shared__ float s_q[];          // [R][d] model-space query rows, then [R][d_code]
+    // the main kernel may launch now (programmatic dependent launch): it starts its cache copies and
+    // waits (griddepcontrol.wait) for this grid's results before using them
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int bh = blockIdx.x, b = bh / p.Hkv, h = bh % p.Hkv;
     const int d = p.d, dc = p.d_code;
     const T* q = static_cast<const T*>(p.q);
@@ -325,6 +328,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
     };
     if (warp == 0)
         for (int k = 0; k < p.nstage; ++k) fill(uint32_t(k));
+    // Programmatic dependent launch (when the host enables it): the first bulk copies above (the
+    // cache does not depend on the prologue) run while the prologue finishes; its query prep is
+    // read only after this wait (a no-op in a plain launch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // Every warp consumes every chunk; the last warp to release a stage refills it with the chunk
     // nstage ahead, so no warp is reserved for copies and all 12 warps compute.
