@@ -254,6 +254,17 @@ kvb_status kvb_rank_split(const void* keys, int key_dtype, int64_t rows, int64_t
         p.out_stride[c] = out_stride[c];
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (n <= kvb::RS_NMAX) {
+        const int sm = int(((n + 3) & ~3) * 4 + 32 * 256 * 4 + kvb::RS_CAND * 4);
+        if (key_dtype == KVB_F32) {
+            cudaFuncSetAttribute(kvb::rank_split_smem_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+            kvb::rank_split_smem_kernel<float><<<unsigned(rows), kvb::SEL_THREADS, sm, s>>>(p);
+        } else {
+            cudaFuncSetAttribute(kvb::rank_split_smem_kernel<double>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+            kvb::rank_split_smem_kernel<double><<<unsigned(rows), kvb::SEL_THREADS, sm, s>>>(p);
+        }
+        return launch_check("rank_split_smem_kernel");
+    }
     if (key_dtype == KVB_F32) kvb::rank_split_kernel<float><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p);
     else kvb::rank_split_kernel<double><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p);
     return launch_check("rank_split_kernel");

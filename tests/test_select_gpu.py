@@ -18,7 +18,7 @@ def test_key_energy_exact(cuda_dev):
     np.testing.assert_array_equal(e, O.l2_importance(k.float().numpy()))
 
 
-@pytest.mark.parametrize("T", [20, 1000, 4097, 32768])
+@pytest.mark.parametrize("T", [20, 1000, 4097, 32768, 45056, 65536])   # 65536: the global-memory kernel
 def test_strata_split_matches_oracle(cuda_dev, T):
     import kvb
     gen = torch.Generator().manual_seed(T)
@@ -33,7 +33,7 @@ def test_strata_split_matches_oracle(cuda_dev, T):
             np.testing.assert_array_equal(got.cpu().numpy(), ref[b])
 
 
-@pytest.mark.parametrize("n,k", [(1, 1), (100, 0), (100, 100), (32640, 2048), (5000, 4999)])
+@pytest.mark.parametrize("n,k", [(1, 1), (100, 0), (100, 100), (32640, 2048), (5000, 4999), (60000, 777)])
 def test_topk_float32(cuda_dev, n, k):
     import kvb
     gen = torch.Generator().manual_seed(n + k)
@@ -58,6 +58,21 @@ def test_four_classes(cuda_dev):
     order = np.lexsort((np.tile(np.arange(3000), (5, 1)), -s.numpy()), axis=-1)
     edges = [0, 10, 110, 1110, 3000]
     for c in range(4):
+        np.testing.assert_array_equal(outs[c].cpu().numpy(), np.sort(order[:, edges[c]:edges[c + 1]], -1))
+
+
+@pytest.mark.parametrize("n", [3000, 40000, 50000])
+def test_float64_close_keys(cuda_dev, n):
+    """Keys that share their high 32 bits (differ only in the low word of the float64) and exact
+    ties among them: the boundary is resolved on the full key, ties by lower index."""
+    import kvb
+    gen = torch.Generator().manual_seed(n)
+    base = 100.0 + torch.randint(0, 3, (4, n), generator=gen).double()
+    s = base + torch.randint(0, 5, (4, n), generator=gen).double() * 2.0 ** -40
+    outs = kvb.rank_split(s.to(cuda_dev), [n // 7, n // 3])
+    order = np.lexsort((np.tile(np.arange(n), (4, 1)), -s.numpy()), axis=-1)
+    edges = [0, n // 7, n // 7 + n // 3, n]
+    for c in range(3):
         np.testing.assert_array_equal(outs[c].cpu().numpy(), np.sort(order[:, edges[c]:edges[c + 1]], -1))
 
 
