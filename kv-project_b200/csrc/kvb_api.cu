@@ -25,6 +25,9 @@
 #include "kvb_decode_tc.cuh"
 
 #define KVB_VERSION 100
+#ifndef KVB_TOKEN_COST
+#define KVB_TOKEN_COST 60     // fixed per-token decode work in byte-equivalents at d_code 128 (see build_plan)
+#endif
 #ifndef KVB_PDL
 #define KVB_PDL 1             // programmatic dependent launch of the main kernel after the prologue
 #endif
@@ -694,10 +697,11 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
         P.tok[s] = chunk_of(c, s);
         nch[s] = (st.n + P.tok[s] - 1) / P.tok[s];
         // work per token in byte-equivalents: its code bytes plus a fixed per-token cost (code
-        // extraction, MMAs, softmax) worth ~139 bytes at d_code 128, measured on B200 from one-width
-        // caches (34.3 / 45.3 / 66.8 ps per token-head at 2 / 4 / 8 bits, linear in the code bytes).
-        // Balancing bytes alone gave 2-bit-heavy CTAs ~1.9x the time of 8-bit-heavy ones.
-        const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + (139 * c->d_code + 64) / 128;
+        // extraction, MMAs, softmax).  One-width caches alone give ~139 bytes at d_code 128 (34.3 /
+        // 45.3 / 66.8 ps per token-head at 2 / 4 / 8 bits on B200), but in a mixed cache the
+        // byte-heavy CTAs also compete for DRAM: a sweep of the constant on config 1 (main kernel
+        // 104.5 us at 8, 95.9 at 139, 92.3 at 60, 92.5 at 40) puts the best split near 60.
+        const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + (KVB_TOKEN_COST * c->d_code + 64) / 128;
         wfull[s] = int64_t(P.tok[s]) * bpt;
         wlast[s] = (st.n - (nch[s] - 1) * P.tok[s]) * bpt;
         chunks_per_head += nch[s];

@@ -84,8 +84,8 @@ def test_plan_covers_every_chunk_once(B, H, T, n_ctas):
     for h in range(B * H):
         ps = pieces[head_begin[h]:head_begin[h + 1]]
         assert np.all(ps[:, 0] == h)
-    # balance: no CTA gets more than (average + one chunk) of work (code bytes + 139 per token)
-    bpt = {s: 128 * (bits[s][0] + bits[s][1]) // 8 + 139 for s in range(3)}
+    # balance: no CTA gets more than (average + one chunk) of work (code bytes + 60 per token)
+    bpt = {s: 128 * (bits[s][0] + bits[s][1]) // 8 + 60 for s in range(3)}
     w = np.zeros(n_ctas)
     for cta in range(n_ctas):
         for h, s, lo, hi in pieces[cta_begin[cta]:cta_begin[cta + 1]]:
