@@ -53,7 +53,7 @@ COMPRESS = ("c1-pack", "c2-evict", "c3-project")
 
 # DRAM bytes (read + write) of one decode_main launch from an ncu capture of this bench's workload
 # (`ncu --set full -k regex:decode_main`, see profiles/); None where no capture was taken.
-TRAFFIC = {"c1": 248.84e6 + 5.64e6}
+TRAFFIC = {"c1": 248.81e6 + 3.85e6}
 
 
 def args_():
@@ -67,6 +67,8 @@ def args_():
     p.add_argument("--batch", type=int, default=None, help="batch per rank (default: the config's)")
     p.add_argument("--context", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--strata", default="1,3",
+                   help="config 1: tenths of the tokens at 8 and 4 bits (the rest 2-bit); e.g. 0,0 = all 2-bit")
     p.add_argument("--tc", action="store_true",
                    help="config 1: values in the block layout, decoded by the tcgen05 kernel (decode_tc)")
     return p.parse_args()
@@ -179,7 +181,7 @@ def build_decode(a, rank, dev):
             seed = 43 + layer                        # the same model on every rank; ranks hold slices
         if w == "c1":
             K, V = W.lognormal_kv(B, Hkv, T, d, dtype, device=dev, seed=43 + 1000 * rank, layer=layer)
-            cache, _ = kvb.cache.build_mixed(K, V, tc=a.tc)
+            cache, _ = kvb.cache.build_mixed(K, V, tenths=tuple(int(x) for x in a.strata.split(",")), tc=a.tc)
         elif w == "c0":
             K, V = W.outlier_kv(B, Hkv, T, d, dtype, device=dev, seed=42 + 1000 * rank)
             cache = kvb.cache.build_kivi(K, V, 4, 2, 128, 32)
@@ -465,7 +467,8 @@ def decode_arm(a):
         peak, peak_kind = peaks()
         gbs = world * bytes_step / (ms * 1e-3) / 1e9
         achieved = (sum(bytes_layer) / L) / (main_ms_avg * 1e-3) / 1e9
-        traffic = TRAFFIC.get(a.workload) if (a.layers, a.batch, a.context, a.tc) == (None, None, None, False) else None
+        traffic = TRAFFIC.get(a.workload) if (a.layers, a.batch, a.context, a.tc, a.strata) == \
+            (None, None, None, False, "1,3") else None
         w = a.workload
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
@@ -497,7 +500,9 @@ def decode_arm(a):
             "clocks": clk.summary(),
         }
         if w == "c1":
-            line["config"]["strata"] = "10% 8-bit / 30% 4-bit / 60% 2-bit, KIVI per-token groups of 64"
+            t8, t4 = (int(x) for x in a.strata.split(","))
+            line["config"]["strata"] = (f"{10 * t8}% 8-bit / {10 * t4}% 4-bit / {100 - 10 * (t8 + t4)}% 2-bit, "
+                                        f"KIVI per-token groups of 64")
         if world == 1 and not a.no_cpu_baseline:
             dt_s, packed, threads, desc = cpu_reference_sample(w, context=a.context)
             line["cpu_baseline"] = {"value": round(packed / dt_s / 1e9, 4), "unit": "GB/s", "cores": threads,
