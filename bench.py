@@ -67,6 +67,8 @@ def args_():
     p.add_argument("--batch", type=int, default=None, help="batch per rank (default: the config's)")
     p.add_argument("--context", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
+                   help="c4s on N > 1 ranks: peer-memory exchange kernel (p2p) or NCCL all-gather + merge")
     p.add_argument("--strata", default="1,3",
                    help="config 1: tenths of the tokens at 8 and 4 bits (the rest 2-bit); e.g. 0,0 = all 2-bit")
     p.add_argument("--tc", action="store_true",
@@ -371,7 +373,9 @@ def decode_arm(a):
     bytes_step = sum(bytes_layer) + q.numel() * esz + out.numel() * esz
 
     split = a.workload == "c4s" and world > 1
-    dec = kvb.seqsplit.SeqSplitDecoder() if split else None
+    dec = None
+    if split:
+        dec = kvb.seqsplit.P2PSeqSplitDecoder() if a.xchg == "p2p" else kvb.seqsplit.SeqSplitDecoder()
 
     def attend(layer, qq, events=None):
         if split:
@@ -482,9 +486,10 @@ def decode_arm(a):
                        "l2": ("inputs larger than L2" if sum(bytes_layer) > 126e6 else
                               "packed cache smaller than L2: timed warm (launch-bound config)"),
                        "parallelism": {"c4": f"batch split over {world} ranks, no collective",
-                                       "c4s": f"context split over {world} ranks, NCCL all-gather + LSE merge "
-                                              f"per layer"}.get(w, f"dp{world} (batch x kv-head shards, "
-                                                                    f"no collective)"),
+                                       "c4s": f"context split over {world} ranks, " + (
+                                           "peer-memory exchange + LSE merge kernel (kvb_xchg_merge) per layer"
+                                           if a.xchg == "p2p" else "NCCL all-gather + LSE merge per layer")
+                                       }.get(w, f"dp{world} (batch x kv-head shards, no collective)"),
                        "bytes_per_step_per_gpu": bytes_step},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
@@ -512,6 +517,8 @@ def decode_arm(a):
         dist.barrier()
         del graph
         torch.cuda.synchronize()
+        if isinstance(dec, kvb.seqsplit.P2PSeqSplitDecoder):
+            dec.close()
         dist.destroy_process_group()
 
 

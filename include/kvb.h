@@ -137,6 +137,26 @@ kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, int64_t T, i
                                int64_t n_alloc, float* coef, int n_ctas, void* stream);
 
 /* ------------------------------------------------------------------------------------------ *
+ * Sequence split across ranks over peer memory (one process per GPU on one NVLink / NVSwitch node).
+ * Each rank allocates an exchange region (kvb_xchg_alloc, zero-initialised flags), shares its IPC
+ * handle with the other ranks (any host channel, e.g. a torch.distributed all-gather of the 64
+ * bytes) and maps theirs (kvb_xchg_open).  kvb_xchg_merge then replaces the all-gather of every
+ * rank's (output, lse) part and the LSE merge (kvb_lse_merge) with one kernel: this rank's rows go
+ * straight into every peer's region, a per-slice flag is published, and each slice is merged once
+ * every rank's flag for it has arrived (bounded wait; KVB_DEV_TIMEOUT on expiry).  All ranks must
+ * make the same sequence of calls with the same rows and d; the call count is kept on the device,
+ * so the call can sit in a CUDA graph.  Plain stores into peer memory only. */
+size_t kvb_xchg_bytes(int64_t rows, int d, int world);
+kvb_status kvb_xchg_alloc(size_t bytes, void** region, unsigned char* handle /* 64 bytes out */);
+kvb_status kvb_xchg_open(const unsigned char* handle /* 64 bytes */, void** region);
+kvb_status kvb_xchg_close(void* peer_region);
+kvb_status kvb_xchg_free(void* region);
+/* part (rows, d) float32 and lse (rows) float32: this rank's decode_lse output; regions: `world`
+ * device pointers (this rank's own region at [rank], the mapped peers' elsewhere); out (rows, d). */
+kvb_status kvb_xchg_merge(const float* part, const float* lse, int64_t rows, int d, int rank, int world,
+                          void* const* regions, void* out, int out_dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------ *
  * K5: per-vector row codes (token-like stored vectors and format variants).  Rows follow
  * kvb_quant_pack's convention: for each (b, h), stored row j < n is source row idx[b, h, j] when
  * idx is given, else first_row + j, of x (B, H, T, d) with element strides (sb, sh, st) and unit

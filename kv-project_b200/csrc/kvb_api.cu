@@ -17,6 +17,7 @@
 #include "../../include/kvb.h"
 #include "kvb_common.cuh"
 #include "kvb_rowcode.cuh"
+#include "kvb_xchg.cuh"
 #include "kvb_quant.cuh"
 #include "kvb_select.cuh"
 #include "kvb_decode.cuh"
@@ -367,6 +368,79 @@ kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, 
         return launch_check("scores_pool_kernel");
     }
     return KVB_OK;
+}
+
+}  // extern "C"
+
+// =============================================================================================
+// Sequence-split exchange over peer memory
+// =============================================================================================
+extern "C" {
+
+size_t kvb_xchg_bytes(int64_t rows, int d, int world) {
+    if (rows <= 0 || d <= 0 || world <= 0 || world > kvb::XC_MAX_RANKS) return 0;
+    return size_t(2) * world * rows * (d + 1) * 4 + size_t(world + 1) * kvb::XC_SLICES * 4;
+}
+
+kvb_status kvb_xchg_alloc(size_t bytes, void** region, unsigned char* handle) {
+    if (!region || !handle || bytes == 0) return fail(KVB_EINVAL, "xchg_alloc: arguments");
+    void* p = nullptr;
+    kvb_status st;
+    if ((st = cuda_check(cudaMalloc(&p, bytes), "xchg_alloc: cudaMalloc"))) return st;
+    if ((st = cuda_check(cudaMemset(p, 0, bytes), "xchg_alloc: cudaMemset"))) {
+        cudaFree(p);
+        return st;
+    }
+    cudaIpcMemHandle_t h;
+    if ((st = cuda_check(cudaIpcGetMemHandle(&h, p), "xchg_alloc: cudaIpcGetMemHandle"))) {
+        cudaFree(p);
+        return st;
+    }
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    std::memcpy(handle, &h, 64);
+    *region = p;
+    return KVB_OK;
+}
+
+kvb_status kvb_xchg_open(const unsigned char* handle, void** region) {
+    if (!handle || !region) return fail(KVB_EINVAL, "xchg_open: arguments");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, 64);
+    return cuda_check(cudaIpcOpenMemHandle(region, h, cudaIpcMemLazyEnablePeerAccess), "xchg_open");
+}
+
+kvb_status kvb_xchg_close(void* peer_region) {
+    if (!peer_region) return fail(KVB_EINVAL, "xchg_close: null");
+    return cuda_check(cudaIpcCloseMemHandle(peer_region), "xchg_close");
+}
+
+kvb_status kvb_xchg_free(void* region) {
+    if (!region) return fail(KVB_EINVAL, "xchg_free: null");
+    return cuda_check(cudaFree(region), "xchg_free");
+}
+
+kvb_status kvb_xchg_merge(const float* part, const float* lse, int64_t rows, int d, int rank, int world,
+                          void* const* regions, void* out, int out_dtype, void* stream) {
+    if (!part || !lse || !regions || !out) return fail(KVB_EINVAL, "xchg_merge: null pointer");
+    if (rows <= 0 || d <= 0 || d > 1024 || world <= 0 || world > kvb::XC_MAX_RANKS || rank < 0 || rank >= world)
+        return fail(KVB_EINVAL, "xchg_merge: sizes (world <= %d)", kvb::XC_MAX_RANKS);
+    if (out_dtype != KVB_F32 && out_dtype != KVB_F16 && out_dtype != KVB_BF16) return fail(KVB_EINVAL, "xchg_merge: out dtype");
+    kvb::XchgParams p{};
+    p.part = part;
+    p.lse = lse;
+    p.rows = rows;
+    p.d = d;
+    p.rank = rank;
+    p.world = world;
+    p.out_dtype = out_dtype == KVB_F32 ? 0 : out_dtype == KVB_F16 ? 1 : 2;
+    for (int r = 0; r < world; ++r) {
+        if (!regions[r]) return fail(KVB_EINVAL, "xchg_merge: region %d is null", r);
+        p.region[r] = static_cast<float*>(regions[r]);
+    }
+    p.out = out;
+    p.timeout_ns = 2000000000ull;
+    kvb::xchg_merge_kernel<<<kvb::XC_SLICES, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    return launch_check("xchg_merge_kernel");
 }
 
 }  // extern "C"

@@ -2,18 +2,26 @@
 
 Each rank holds a contiguous, group-aligned token range of every (batch, KV head) and decodes it
 with ``kvb_decode_lse``: a normalised float32 output and the natural-log mass of its range per
-(batch, query position, query head).  Both live in one exchange buffer, gathered from every rank
-with a single all-gather (NCCL over NVLink on the GPUs; any torch.distributed backend works), and
-``kvb_lse_merge`` combines the parts exactly (the LSE merge of StrataState.attend,
-STRATA_KV.py:1784-1792, across ranks instead of across strata).  Exact rows (sinks, appended
-tokens) belong to one rank, the owner of the last range.
+(batch, query position, query head).  Two ways to combine the ranks' parts (the LSE merge of
+StrataState.attend, STRATA_KV.py:1784-1792, across ranks instead of across strata):
+
+  SeqSplitDecoder     one exchange buffer per rank, a single all-gather (NCCL over NVLink on the
+                      GPUs; any torch.distributed backend works), then ``kvb_lse_merge``;
+  P2PSeqSplitDecoder  ``kvb_xchg_merge``: one kernel stores this rank's rows straight into every
+                      peer's exchange region over NVLink (CUDA IPC mappings, plain peer stores),
+                      flags each row slice, waits for the other ranks' flags and merges.
+
+Exact rows (sinks, appended tokens) belong to one rank, the owner of the last range.
 """
 
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from . import ops
 
 
@@ -76,6 +84,80 @@ class SeqSplitDecoder:
         all_gather_into(gath, buf, self.group)
         parts, lses = gathered_views(gath, B, Tq, Hq, d)
         return ops.lse_merge(parts, lses, out=out, out_dtype=out_dtype or q.dtype)
+
+
+class P2PSeqSplitDecoder:
+    """Sequence-split decode whose cross-rank step runs over peer memory: per (B, Tq, Hq, d) shape
+    each rank allocates an exchange region in libkvb (zeroed), the 64-byte CUDA IPC handles are
+    all-gathered once over the process group, and every attend() is decode_lse + one
+    ``kvb_xchg_merge`` kernel.  All ranks must call attend() with the same shapes in the same order
+    (as they do for the collective version).  Ranks must share one node with peer access (NVLink /
+    NVSwitch); call close() before destroying the process group."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self._state = {}
+
+    def _setup(self, rows, d, device):
+        key = (rows, d, device)
+        if key in self._state:
+            return self._state[key]
+        lib = L.lib()
+        with torch.cuda.device(device):
+            nbytes = lib.kvb_xchg_bytes(rows, d, self.world)
+            if nbytes == 0:
+                raise ValueError(f"P2PSeqSplitDecoder: unsupported world size {self.world}")
+            own = C.c_void_p()
+            handle = (C.c_ubyte * 64)()
+            L.check(lib.kvb_xchg_alloc(nbytes, C.byref(own), handle), "kvb_xchg_alloc")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=self.group)
+            regions = (C.c_void_p * self.world)()
+            opened = []
+            for r in range(self.world):
+                if r == self.rank:
+                    regions[r] = own.value
+                    continue
+                ptr = C.c_void_p()
+                hb = (C.c_ubyte * 64).from_buffer_copy(handles[r])
+                L.check(lib.kvb_xchg_open(hb, C.byref(ptr)), "kvb_xchg_open")
+                regions[r] = ptr.value
+                opened.append(ptr.value)
+        part = torch.empty((rows, d), dtype=torch.float32, device=device)
+        lse = torch.empty((rows,), dtype=torch.float32, device=device)
+        self._state[key] = (own.value, opened, regions, part, lse)
+        return self._state[key]
+
+    def attend(self, cache: "ops.PackedCache", q: torch.Tensor, scaling: float, qpos=None, out=None,
+               out_dtype=None) -> torch.Tensor:
+        B, Hq, Tq, d = q.shape
+        rows = B * Tq * Hq
+        _, _, regions, part, lse = self._setup(rows, d, q.device)
+        ops.decode_lse(cache, q, scaling, part.view(B, Tq, Hq, d), lse.view(B, Tq, Hq), qpos=qpos)
+        odt = out_dtype or q.dtype
+        if out is None:
+            out = torch.empty((B, Tq, Hq, d), dtype=odt, device=q.device)
+        elif tuple(out.shape) != (B, Tq, Hq, d) or not out.is_contiguous():
+            raise ValueError("P2PSeqSplitDecoder: out must be contiguous (B, Tq, Hq, d)")
+        L.check(L.lib().kvb_xchg_merge(ops._ptr(part), ops._ptr(lse), rows, d, self.rank, self.world, regions,
+                                        ops._ptr(out), ops.dtype_code(out), C.c_void_p(ops._stream(q.device))),
+                "kvb_xchg_merge")
+        return out
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (after a barrier: no peer may still write)."""
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        lib = L.lib()
+        for own, opened, _, _, _ in self._state.values():
+            for ptr in opened:
+                L.check(lib.kvb_xchg_close(C.c_void_p(ptr)), "kvb_xchg_close")
+        dist.barrier(group=self.group)
+        for own, _, _, _, _ in self._state.values():
+            L.check(lib.kvb_xchg_free(C.c_void_p(own)), "kvb_xchg_free")
+        self._state.clear()
 
 
 def shard_cache(build, K: torch.Tensor, V: torch.Tensor, rank: int, world: int, align: int = 128):

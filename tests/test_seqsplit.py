@@ -187,3 +187,72 @@ def test_seqsplit_nccl_two_ranks():
         assert sorted(ret.keys()) == [0, 1]
         for err, same in ret.values():
             assert err <= 1e-4 and same
+
+
+def _p2p_rank_main(rank, world, port, ret):
+    import datetime
+    import torch.distributed as dist
+    import kvb
+    from kvb import seqsplit as SS
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    p2p = None
+    try:
+        B, Hkv, rep, Tq, T, d = 2, 2, 8, 1, 3000, 128
+        K, V = kvb.workloads.outlier_kv(B, Hkv, T, d, torch.bfloat16, seed=17)
+        q = kvb.workloads.queries(B, Hkv * rep, Tq, d, torch.bfloat16, seed=17).to(dev)
+        K, V = K.to(dev), V.to(dev)
+        build = lambda k, v: kvb.cache.build_kivi(k, v, 4, 4, 128, 128)
+        cache = SS.shard_cache(build, K, V, rank, world)
+        ref = SS.SeqSplitDecoder().attend(cache, q, d ** -0.5, out_dtype=torch.float32)
+        p2p = SS.P2PSeqSplitDecoder()
+        outs = [p2p.attend(cache, q, d ** -0.5, out_dtype=torch.float32) for _ in range(3)]
+        # inside a CUDA graph: the call count lives on the device, so replays keep exchanging
+        out_g = torch.empty_like(outs[0])
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            p2p.attend(cache, q, d ** -0.5, out=out_g)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            p2p.attend(cache, q, d ** -0.5, out=out_g)
+        for _ in range(3):
+            out_g.zero_()
+            g.replay()
+        torch.cuda.synchronize()
+        full = kvb.decode(build(K, V), q, d ** -0.5, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        ret[rank] = (all(torch.equal(o, ref) for o in outs), bool(torch.equal(out_g, ref)),
+                     float((outs[0] - full).abs().max()), kvb.device_status())
+        del g
+    finally:
+        if p2p is not None:
+            p2p.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_seqsplit_p2p_two_ranks():
+    """The peer-memory exchange (kvb_xchg_merge) on 2 GPUs: bit-identical to the NCCL all-gather +
+    kvb_lse_merge path, repeatable (parity / epoch advance), correct under CUDA-graph replay, and equal
+    to the one-GPU decode of the whole context."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as man:
+        ret = man.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_p2p_rank_main, args=(r, 2, port, ret)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+        assert sorted(ret.keys()) == [0, 1]
+        for same, same_graph, err, status in ret.values():
+            assert same and same_graph and err <= 1e-4 and status == 0
