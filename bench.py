@@ -19,13 +19,15 @@ Other workloads (--workload), each printing the same JSON line for its own confi
   c3          config 3: B 16, 16384 tokens, 32 spectral coefficients, 4-bit mid-rise per token
   c4          config 4: 70B shape, B 32 sharded over ranks (strong scaling), 131072 tokens, 4-bit g128;
               the layers that fit in HBM are resident and timed (config.layers)
-  c4s         config 4 with batch 4: the 131072-token context split over ranks (strong scaling), one
-              NCCL all-gather of (output, lse) parts + kvb_lse_merge per layer
+  c4s         config 4 with batch 4: the 131072-token context split over ranks (strong scaling); per
+              layer the ranks' (output, lse) parts meet in one peer-memory exchange + merge kernel
+              (--xchg p2p, default) or an NCCL all-gather + kvb_lse_merge (--xchg nccl)
   c1-pack     compress side of config 1 (key energy, rank split, 6 quantise+pack calls per layer)
   c2-evict    compress side of config 2 (accumulated scores of 64 queries, top-k, 2 packs per layer)
   c3-project  compress side of config 3 (tcgen05 basis projection + mid-rise code of K and V)
 
   python bench.py [--gpus N --steps K --warmup W] [--workload W]   # kvb (CUDA) arm
+  python bench.py --strata 0,0                                      # config 1 with every token at 2 bits
   python bench.py --impl reference [--workload W]                   # reference CPU path (oracle port)
 Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N  (c0-c3: weak scaling, each rank its own
 batch; c4: the batch of 32 is split over the ranks)

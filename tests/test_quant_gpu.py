@@ -131,3 +131,31 @@ def test_blocked_layout_same_codes(cuda_dev, bits, group, midrise, gather):
     assert torch.equal(a["meta"], b["meta"])
     assert torch.equal(a["xhat"], b["xhat"])
     assert kvb.device_status() == 0
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_extreme_rows(cuda_dev, bits, dtype):
+    """Rows the storage format clamps or degenerates on: constant rows (zero range: scale floored at
+    2^-24), all-zero rows, magnitudes past the fp16 range (zero point and scale clamped to 65504 by
+    as_stored), tiny magnitudes (subnormal fp16 scales).  Bit-exact against the oracle."""
+    import kvb
+    gen = torch.Generator().manual_seed(7 + bits)
+    B, H, T, d = 1, 2, 48, 128
+    x = torch.randn(B, H, T, d, generator=gen)
+    x[0, 0, 0] = 3.25                      # constant row
+    x[0, 0, 1] = 0.0                       # zero row
+    x[0, 0, 2] *= 1e6                      # beyond fp16
+    x[0, 0, 3, :64] = -7e4                 # one group pinned at -70000
+    x[0, 1, 4] *= 1e-6                     # scale in the fp16 subnormal range
+    x[0, 1, 5, ::2] = 1e-30                # values below every fp16 step
+    x = x.to(dtype)
+    for group in (64, 128):
+        r = kvb.quant_pack(x.to(cuda_dev), bits, group, want_xhat=True)
+        ref = O.kivi_quant(np32(x), bits, group, False, 0)
+        np.testing.assert_array_equal(unpack(r["codes"], bits, T), ref["codes"])
+        lo, sc = token_meta(r["meta"], T)
+        np.testing.assert_array_equal(lo, ref["lo"])
+        np.testing.assert_array_equal(sc, ref["scale"])
+        np.testing.assert_array_equal(np32(r["xhat"]), ref["xhat"])
+    assert kvb.device_status() == 0
