@@ -123,13 +123,15 @@ __global__ void __launch_bounds__(128) decode_prologue(const PrologueParams p) {
     }
     const float sc = ldexpf(1.f, e);
     for (int o = threadIdx.x; o < R * dc; o += blockDim.x) out[qp_qc(R) + o] = s_qc[o] * sc;
+    // per-group query sums, one warp per (row, group): lanes take channels lane, lane + 32, ...
     const int G = dc / p.k_group;
-    for (int o = threadIdx.x; o < R * 8; o += blockDim.x) {
+    for (int o = threadIdx.x >> 5; o < R * 8; o += blockDim.x >> 5) {
         const int r = o / 8, g = o % 8;
         float s = 0.f;
         if (g < G)
-            for (int c = g * p.k_group; c < (g + 1) * p.k_group; ++c) s += s_qc[r * dc + c] * sc;
-        out[qp_qsum(R, dc) + o] = s;
+            for (int c = g * p.k_group + (threadIdx.x & 31); c < (g + 1) * p.k_group; c += 32) s += s_qc[r * dc + c] * sc;
+        s = warp_sum(s);
+        if ((threadIdx.x & 31) == 0) out[qp_qsum(R, dc) + o] = s;
     }
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
         float s = 0.f;
@@ -495,16 +497,41 @@ __global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ Merg
         const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
         s_q[o] = to_f32(q[((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * d + c]);
     }
-    const int pb = p.head_begin[bh], pe = p.head_begin[bh + 1];
+    const int pb = p.head_begin[bh], pe = p.head_begin[bh + 1], np = pe - pb;
     const size_t pstride = size_t(2 * R + R * dc);
-    // coded partials
-    if (tid < Ra) {
+    const float* part = p.part + size_t(pb) * pstride;
+    // coded partials.  The merge sits between two layers' main kernels, so its latency counts: when
+    // they fit, every piece's (max, mass) is fetched at once into shared memory (s_p, s_out as
+    // scratch) and the per-piece weights 2^(m - M) are kept there; each (row, channel) thread then
+    // issues its pieces' loads eight at a time.  Same arithmetic and order as one load at a time.
+    const bool staged = np * Ra <= 256 && np * Ra <= Ra * d;
+    if (staged) {
+        for (int o = tid; o < np * Ra; o += blockDim.x) {
+            const int k = o / Ra, r = o - k * Ra;
+            s_p[o] = part[k * pstride + r];
+            s_out[o] = part[k * pstride + R + r];
+        }
+        __syncthreads();
+        if (tid < Ra) {
+            float M = -INFINITY;
+            for (int k = 0; k < np; ++k) M = fmaxf(M, s_p[k * Ra + tid]);
+            float L = 0.f;
+            for (int k = 0; k < np; ++k) {
+                const float m = s_p[k * Ra + tid];
+                const float w = (m == -INFINITY) ? 0.f : ex2(m - M);
+                L += (m == -INFINITY) ? 0.f : w * s_out[k * Ra + tid];
+                s_p[k * Ra + tid] = w;
+            }
+            s_rowM[tid] = M;
+            s_rowLc[tid] = L;
+        }
+    } else if (tid < Ra) {
         float M = -INFINITY;
-        for (int k = pb; k < pe; ++k) M = fmaxf(M, p.part[k * pstride + tid]);
+        for (int k = 0; k < np; ++k) M = fmaxf(M, part[k * pstride + tid]);
         float L = 0.f;
-        for (int k = pb; k < pe; ++k) {
-            const float m = p.part[k * pstride + tid];
-            L += (m == -INFINITY) ? 0.f : ex2(m - M) * p.part[k * pstride + R + tid];
+        for (int k = 0; k < np; ++k) {
+            const float m = part[k * pstride + tid];
+            L += (m == -INFINITY) ? 0.f : ex2(m - M) * part[k * pstride + R + tid];
         }
         s_rowM[tid] = M;
         s_rowLc[tid] = L;
@@ -512,10 +539,23 @@ __global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ Merg
     __syncthreads();
     for (int o = tid; o < Ra * dc; o += blockDim.x) {
         const int r = o / dc, c = o % dc;
+        const float* src = part + 2 * R + r * dc + c;
         float a = 0.f;
-        for (int k = pb; k < pe; ++k) {
-            const float m = p.part[k * pstride + r];
-            if (m != -INFINITY) a += ex2(m - s_rowM[r]) * p.part[k * pstride + 2 * R + r * dc + c];
+        for (int k0 = 0; k0 < np; k0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = k0 + j < np ? src[(k0 + j) * pstride] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (k0 + j >= np) break;
+                if (staged) {
+                    const float w = s_p[(k0 + j) * Ra + r];
+                    if (w != 0.f) a += w * v[j];
+                } else {
+                    const float m = part[(k0 + j) * pstride + r];
+                    if (m != -INFINITY) a += ex2(m - s_rowM[r]) * v[j];
+                }
+            }
         }
         s_acc[o] = a;
     }
