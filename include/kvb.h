@@ -288,9 +288,8 @@ kvb_status kvb_lse_merge(const float* parts, int64_t part_stride, const float* l
 
 /* Decode attention for callers that cannot allocate device memory.  No counterpart in the reference
  * (which allocates with PyTorch freely); added for hosts that hand an operator only its input and
- * output buffers: serving engines whose memory planner reserves all device memory up front, code that
- * runs while another framework is capturing a CUDA graph (where cudaMalloc / cudaFree are not
- * allowed), and plugin interfaces without an allocator.
+ * output buffers: serving engines whose memory planner reserves all device memory up front and lets
+ * no operator call cudaMalloc afterwards, and plugin interfaces that give an operator no allocator.
  * Same arguments and result as kvb_decode, minus the workspace: the split-K scratch lives in a
  * file-scope __device__ array of KVB_NOALLOC_SCRATCH_BYTES (8 MiB) that every device loading the
  * library keeps until process exit.  Requests needing more scratch return KVB_EINVAL (the message

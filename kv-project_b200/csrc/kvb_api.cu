@@ -1192,9 +1192,9 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
 
 // =============================================================================================
 // Allocation-free decode.  For callers that may not allocate device memory at all (serving engines
-// whose planner owns every byte, code running inside another framework's CUDA-graph capture,
-// allocator-less plugin interfaces), the split-K scratch is a file-scope __device__ array instead
-// of a caller workspace.  Host code may not pass `g_noalloc_scratch` itself to a kernel: on the host
+// whose planner owns every byte, allocator-less plugin interfaces), the split-K scratch is a
+// file-scope __device__ array instead of a caller workspace.  Host code may not pass
+// `g_noalloc_scratch` itself to a kernel: on the host
 // that name is only a stand-in symbol, not a device address.  Its real address is looked up once per
 // device (cudaGetSymbolAddress with that device current) and cached here.
 // =============================================================================================

@@ -376,8 +376,8 @@ def lse_merge(parts: torch.Tensor, lse: torch.Tensor, out: torch.Tensor = None, 
 
 def decode_noalloc(cache: PackedCache, q: torch.Tensor, scaling: float, out: torch.Tensor, qpos=None,
                    n_ctas: int = 0) -> torch.Tensor:
-    """Decode attention for callers that cannot allocate device memory (an engine that owns every
-    byte of the GPU, a CUDA-graph capture run by another framework, an allocator-less plugin host):
+    """Decode attention for callers that cannot allocate device memory (an engine whose planner owns
+    every byte of the GPU, an allocator-less plugin host):
     `out` (B, Tq, Hq, d) is supplied by the caller and the split-K scratch is the library's built-in
     8 MiB device array, so neither this wrapper nor the library allocates.  Calls share that array:
     do not run two of them concurrently.  Raises ValueError when a request needs more scratch than

@@ -1,8 +1,8 @@
 """The allocation-free decode entry point (kvb_decode_noalloc) against the workspace one.
 
 kvb_decode_noalloc exists for callers that are not allowed to allocate device memory: serving
-engines whose memory planner has already claimed the GPU, code running inside another framework's
-CUDA-graph capture, and plugin interfaces that pass an operator only its input and output buffers.
+engines whose memory planner has already claimed the GPU and lets no operator allocate afterwards,
+and plugin interfaces that pass an operator only its input and output buffers.
 Its split-K scratch is a fixed __device__ array inside libkvb.so.  This file runs last (named
 test_zz_*) so that a failure here never hides the results of the other tests, and each test passes
 on its own in a fresh process as well as after the rest of the suite.
