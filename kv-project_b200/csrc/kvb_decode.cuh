@@ -200,7 +200,7 @@ __device__ __forceinline__ void build_channel_unit(uint8_t* frag, const uint32_t
             for (int hh = 0; hh < 2; ++hh) {
                 const int ch = LK::kch(t, 2 * k + s, hh);
                 const float sc = unpack_half2(kraw[ch]).y;
-                const float v = __ldg(qc + r * D + ch) * sc * (1.f / LK::kf(2 * k + s));
+                const float v = qc[r * D + ch] * sc * (1.f / LK::kf(2 * k + s));
                 const float hi = __half2float(__float2half_rn(v));
                 const float lo = __half2float(__float2half_rn(v - hi));
                 hv[hh][0] = hi;
@@ -226,7 +226,7 @@ __device__ __forceinline__ void build_channel_unit(uint8_t* frag, const uint32_t
         const float lo = unpack_half2(kraw[ch]).x;
         float w[R];
 #pragma unroll
-        for (int rr = 0; rr < R; ++rr) w[rr] = __ldg(qc + rr * D + ch) * lo;
+        for (int rr = 0; rr < R; ++rr) w[rr] = qc[rr * D + ch] * lo;
         const float b = reduce_rows<R>(w, lane);
         if ((lane & (32 / R - 1)) == 0) bias[reduce_row_of<R>(lane) * 4 + KP] = b;
     }
@@ -350,6 +350,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
             const StageLay L = stage_lay<D, R, GK, GV, KMODE, CODE>(KB, VB, sd.tok, p.k_group);
             typename TL::Ctx X;
             TL::build_ctx(X, qp, lane);
+            if constexpr (KMODE == KM_CHANNEL) {
+                // the head's prescaled query rows, read by every chunk's fragment build: staged once
+                // per piece in the merge buffer (free until this piece's end-of-piece merge)
+                for (int o = threadIdx.x; o < R * D; o += DEC_THREADS) red[o] = qp[qp_qc(R) + o];
+                __syncthreads();
+            }
             const typename TL::Off O = TL::lane_off(L, lane);
             constexpr int TOK = chunk_tokens(D, KB, VB, KMODE == KM_CHANNEL);
             constexpr int PW = TOK / 16 / DEC_CWARPS;            // tiles per warp in a full chunk
@@ -382,8 +388,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
                         const int ntok = int(imin64(sd.tok, sd.n - tok0));
                         const int ng = (ntok + p.k_group - 1) / p.k_group;
                         uint8_t* st = stages + s * p.stage_bytes;
-                        build_channel_frags<D, R, GK, GV, KMODE, CODE, KB>(st + L.km, st + L.kr, ng, qp + qp_qc(R),
-                                                                           warp, lane);
+                        build_channel_frags<D, R, GK, GV, KMODE, CODE, KB>(st + L.km, st + L.kr, ng, red, warp, lane);
                     }
                     __syncthreads();
                 }
