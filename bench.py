@@ -449,28 +449,11 @@ def decode_arm(a):
     out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
     q_dev = torch.empty_like(q)
 
-    # the copies run on their own stream, pipelined per layer (layer l's queries land while earlier
-    # layers decode; its output leaves while later layers decode); every byte still crosses PCIe
-    # inside each timed step
-    cs = torch.cuda.Stream(device=dev)
-    ev_in = [torch.cuda.Event() for _ in range(L)]
-    ev_out = [torch.cuda.Event() for _ in range(L)]
-
     def e2e_step():
-        comp = torch.cuda.current_stream()
-        cs.wait_stream(comp)
-        with torch.cuda.stream(cs):
-            for layer in range(L):
-                q_dev[layer].copy_(q_host[layer], non_blocking=True)
-                ev_in[layer].record(cs)
+        q_dev.copy_(q_host, non_blocking=True)
         for layer in range(L):
-            comp.wait_event(ev_in[layer])
             attend(layer, q_dev)
-            ev_out[layer].record(comp)
-            cs.wait_event(ev_out[layer])
-            with torch.cuda.stream(cs):
-                out_host[layer].copy_(out[layer], non_blocking=True)
-        comp.wait_stream(cs)
+        out_host.copy_(out, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
