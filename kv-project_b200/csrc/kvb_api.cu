@@ -1148,43 +1148,54 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
     }
 
     // 3. merge
-    static thread_local kvb::MergeParams mp;
-    std::memset(&mp, 0, sizeof(mp));
-    mp.B = c->B;
-    mp.Hkv = c->Hkv;
-    mp.Hq = Hq;
-    mp.Tq = Tq;
-    mp.rep = rep;
-    mp.R_act = rep * Tq;
-    mp.R = sh.R;
-    mp.d = c->d;
-    mp.d_code = c->d_code;
-    mp.out_dtype = out_dtype == KVB_F32 ? 0 : out_dtype == KVB_F16 ? 1 : 2;
-    mp.q_dtype = q_dtype;
-    mp.exact_dtype = c->exact_dtype;
-    mp.scaling = scaling;
-    mp.part = part;
-    mp.q = q;
-    mp.k_exact = c->k_exact;
-    mp.v_exact = c->v_exact;
-    mp.exact_cap = c->exact_cap;
-    mp.n_exact = c->n_exact;
-    mp.n0 = c->n0;
-    mp.pos0 = c->pos0;
-    for (int t = 0; t < Tq; ++t) mp.qpos[t] = qpos ? qpos[t] : 0;
-    mp.lift = c->lift;
-    mp.mu_v = c->mu_v;
-    mp.out = out;
-    mp.lse = lse;
-    for (int h = 0; h <= P.n_heads; ++h) mp.head_begin[h] = P.head_begin[h];
     const int Ra = rep * Tq;
     const size_t msm = size_t(Ra) * (2 * c->d + c->d_code) * 4 + 3 * Ra * 4 + 256 * 4;
     cudaError_t le;
-#define KVB_MERGE(T_) le = launch_maybe_pdl(kvb::decode_merge<T_, T_>, dim3(heads), dim3(256), msm, s, false, mp);
-    if (q_dtype == KVB_F32) { KVB_MERGE(float) }
-    else if (q_dtype == KVB_F16) { KVB_MERGE(__half) }
-    else { KVB_MERGE(__nv_bfloat16) }
-#undef KVB_MERGE
+    auto launch_merge = [&](auto& mp) -> cudaError_t {
+        std::memset(&mp, 0, sizeof(mp));
+        mp.B = c->B;
+        mp.Hkv = c->Hkv;
+        mp.Hq = Hq;
+        mp.Tq = Tq;
+        mp.rep = rep;
+        mp.R_act = Ra;
+        mp.R = sh.R;
+        mp.d = c->d;
+        mp.d_code = c->d_code;
+        mp.out_dtype = out_dtype == KVB_F32 ? 0 : out_dtype == KVB_F16 ? 1 : 2;
+        mp.q_dtype = q_dtype;
+        mp.exact_dtype = c->exact_dtype;
+        mp.scaling = scaling;
+        mp.part = part;
+        mp.q = q;
+        mp.k_exact = c->k_exact;
+        mp.v_exact = c->v_exact;
+        mp.exact_cap = c->exact_cap;
+        mp.n_exact = c->n_exact;
+        mp.n0 = c->n0;
+        mp.pos0 = c->pos0;
+        for (int t = 0; t < Tq; ++t) mp.qpos[t] = qpos ? qpos[t] : 0;
+        mp.lift = c->lift;
+        mp.mu_v = c->mu_v;
+        mp.out = out;
+        mp.lse = lse;
+        for (int h = 0; h <= P.n_heads; ++h) mp.head_begin[h] = P.head_begin[h];
+        using MP = std::remove_reference_t<decltype(mp)>;
+        constexpr int NH = sizeof(MP::head_begin) / sizeof(int) - 1;
+        if (q_dtype == KVB_F32)
+            return launch_maybe_pdl(kvb::decode_merge<float, float, NH>, dim3(heads), dim3(256), msm, s, false, mp);
+        if (q_dtype == KVB_F16)
+            return launch_maybe_pdl(kvb::decode_merge<__half, __half, NH>, dim3(heads), dim3(256), msm, s, false, mp);
+        return launch_maybe_pdl(kvb::decode_merge<__nv_bfloat16, __nv_bfloat16, NH>, dim3(heads), dim3(256), msm, s,
+                                false, mp);
+    };
+    if (P.n_heads <= kvb::MERGE_SMALL_HEADS) {
+        static thread_local kvb::MergeParams<kvb::MERGE_SMALL_HEADS> mps;
+        le = launch_merge(mps);
+    } else {
+        static thread_local kvb::MergeParams<kvb::MERGE_MAX_HEADS> mpl;
+        le = launch_merge(mpl);
+    }
     if (le != cudaSuccess) return cuda_check(le, "decode_merge launch");
     return launch_check("decode_merge");
 }

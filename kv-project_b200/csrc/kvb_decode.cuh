@@ -466,7 +466,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
 // ------------------------------------------------------------------------------------------
 // 3. merge: grid (B * Hkv), block 256
 // ------------------------------------------------------------------------------------------
+// The per-head piece ranges ride in the kernel parameters; two capacities keep the parameter block
+// (copied on every launch) small for the usual head counts.
 constexpr int MERGE_MAX_HEADS = 4096;
+constexpr int MERGE_SMALL_HEADS = 256;
+template <int NH>
 struct MergeParams {
     int B, Hkv, Hq, Tq, rep, R_act, R, d, d_code, out_dtype, q_dtype, exact_dtype;
     float scaling;
@@ -480,11 +484,11 @@ struct MergeParams {
     const float* mu_v;      // (Hkv, d) or null
     void* out;
     float* lse;             // (B, Tq, Hq) natural-log sum of exp(scaled logits), or null
-    int head_begin[MERGE_MAX_HEADS + 1];
+    int head_begin[NH + 1];
 };
 
-template <typename TQ, typename TE>
-__global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ MergeParams p) {
+template <typename TQ, typename TE, int NH>
+__global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ MergeParams<NH> p) {
     extern __shared__ float sm[];
     __shared__ float s_w[8];
     const int bh = blockIdx.x, b = bh / p.Hkv, h = bh % p.Hkv;
