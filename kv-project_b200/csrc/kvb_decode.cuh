@@ -66,8 +66,18 @@ struct DecodeParams {
     float* part;            // per piece: m2[R] | l[R] | acc[R][D]
     int n_pieces;
     int cta_begin[DEC_MAX_CTAS + 1];
-    int4 piece[DEC_MAX_PIECES];            // (head, stratum, chunk_lo, chunk_hi)
+    int2 piece[DEC_MAX_PIECES];            // packed (head, stratum | chunk_lo << 2 | chunk_hi << 17)
 };
+
+// A piece (head, stratum, chunk range [lo, hi)) in 8 bytes: the piece table is most of the main
+// kernel's parameter block, which is copied on every launch.  Chunk indices stay below 2^15.
+constexpr int DEC_MAX_CHUNK = 1 << 15;
+__host__ __device__ __forceinline__ int2 pack_piece(int head, int stratum, int lo, int hi) {
+    return make_int2(head, stratum | (lo << 2) | (hi << 17));
+}
+__host__ __device__ __forceinline__ int4 unpack_piece(int2 v) {
+    return make_int4(v.x, v.y & 3, (v.y >> 2) & 0x7FFF, (v.y >> 17) & 0x7FFF);
+}
 
 // ------------------------------------------------------------------------------------------
 // 1. prologue: grid (B * Hkv), block 128
@@ -277,13 +287,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
         int pi = pc0;
         uint32_t base = 0;
         for (; pi < pc1; ++pi) {
-            const uint32_t nc = uint32_t(p.piece[pi].w - p.piece[pi].z);
+            const int4 pq = unpack_piece(p.piece[pi]);
+            const uint32_t nc = uint32_t(pq.w - pq.z);
             if (k < base + nc) break;
             base += nc;
         }
         if (pi >= pc1) return;
         {
-            const int4 pc = p.piece[pi];
+            const int4 pc = unpack_piece(p.piece[pi]);
             const int ch = pc.z + int(k - base);
             const StratumDev& sd = p.st[pc.y];
             const int head = pc.x;
@@ -339,7 +350,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_const
     // nstage ahead, so no warp is reserved for copies and all 12 warps compute.
     uint32_t it = 0;
     for (int pi = pc0; pi < pc1; ++pi) {
-        const int4 pc = p.piece[pi];
+        const int4 pc = unpack_piece(p.piece[pi]);
         const StratumDev& sd = p.st[pc.y];
         const float* qp = p.qp + size_t(pc.x) * p.qp_stride;
         float* part = p.part + size_t(pi) * (2 * R + R * D);

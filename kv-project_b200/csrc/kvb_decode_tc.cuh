@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(64 + NWG * 128, 1) decode_tc(const __grid_cons
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pc0 = p.cta_begin[blockIdx.x];
     const int np = p.cta_begin[blockIdx.x + 1] - pc0;              // <= TC_MAX_CTA_PIECES (host check)
-    for (int x = threadIdx.x; x < np; x += blockDim.x) s_piece[x] = p.piece[pc0 + x];
+    for (int x = threadIdx.x; x < np; x += blockDim.x) s_piece[x] = unpack_piece(p.piece[pc0 + x]);
     if (threadIdx.x < 4) s_st[threadIdx.x] = p.st[threadIdx.x];
 
     if (threadIdx.x == 0) {

@@ -241,12 +241,19 @@ class PackedCache:
         self.qmap = self.lift = self.mu_k = self.mu_v = None
         self._ws = {}
 
+    def __setattr__(self, name, value):
+        # any attribute change (exact rows appended, a new query map ...) drops the cached descriptor
+        object.__setattr__(self, name, value)
+        if name != "_c":
+            object.__setattr__(self, "_c", None)
+
     def add_stratum(self, kq: dict, vq: dict):
         if kq["n"] != vq["n"] or kq["n_alloc"] != vq["n_alloc"]:
             raise ValueError("key and value codes of a stratum must hold the same tokens")
         self.strata.append({"kbits": kq["bits"], "vbits": vq["bits"], "n": kq["n"], "n_alloc": kq["n_alloc"],
                             "kc": kq["codes"], "vc": vq["codes"], "km": kq["meta"], "vm": vq["meta"],
                             "v_layout": vq.get("layout", L.KVB_V_TOKEN_MAJOR)})
+        self._c = None
         return self
 
     def set_exact(self, K, V, n_exact=None, n0=None, pos0=0):
@@ -257,6 +264,10 @@ class PackedCache:
         return self
 
     def struct(self) -> L.Cache:
+        """The kvb_cache descriptor, built once and reused until an attribute of the cache changes
+        (the strata and their tensors are not edited in place after add_stratum)."""
+        if self._c is not None:
+            return self._c
         c = L.Cache()
         c.B, c.Hkv, c.d, c.d_code = self.B, self.Hkv, self.d, self.d_code
         c.code_kind = L.KVB_CODE_MIDRISE if self.midrise else L.KVB_CODE_ASYM
@@ -278,6 +289,7 @@ class PackedCache:
         for name in ("qmap", "lift", "mu_k", "mu_v"):
             t = getattr(self, name)
             setattr(c, name, None if t is None else t.data_ptr())
+        self._c = c
         return c
 
     def stored_bytes(self) -> int:
