@@ -1,7 +1,7 @@
 #!/usr/bin/env python
-"""Packed-KV decode attention benchmark (the BASELINE metric; default: config 1).
+"""Packed-KV decode attention benchmark (the headline decode metric; default: config 1).
 
-Default workload: Llama-3-8B attention shape, 32 layers, B = 8 per GPU,
+Default workload (benchmark config 1): Llama-3-8B attention shape, 32 layers, B = 8 per GPU,
 32 query / 8 KV heads, head_dim 128, context 32768, bf16 activations; per (b, kv head) every token
 is coded at 8 / 4 / 2 bits (10 % / 30 % / 60 % by key L2 norm, head-synchronous strata), KIVI
 asymmetric per-token groups of 64 channels with fp16 zero point and scale.  Inputs are seeded

@@ -25,7 +25,9 @@ HERE = Path(__file__).resolve().parent
 
 
 def load_reference():
-    ref = os.environ.get("KVB_REFERENCE", "/root/reference")
+    ref = os.environ.get("KVB_REFERENCE")
+    if not ref:
+        raise SystemExit("set KVB_REFERENCE to the directory holding the reference sources")
     scratch = tempfile.mkdtemp(prefix="kvb_golden_")
     os.environ.setdefault("KV_PROJECT_ROOT", scratch)
     os.environ.setdefault("KV_STRATA_OUTPUT_DIR", os.path.join(scratch, "out"))
