@@ -346,11 +346,12 @@ __device__ __forceinline__ void qrow_codes(const float (&v)[8], bool valid, floa
     const float y = __frcp_rn(sc);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
+        // round-half-even conversion that saturates below at 0 (NaN -> 0), then the upper clamp:
+        // the same codes as rint + clamp to [0, TOP] in float, in two instructions instead of four
         float q;
-        if constexpr (GROUP == 0) q = rintf(__fadd_rn(div_rn_markstein(v[i], sc, y), 0.5f * float(TOP)));
-        else q = rintf(div_rn_markstein(__fsub_rn(v[i], lo), sc, y));
-        q = fminf(fmaxf(q, 0.f), float(TOP));
-        c[i] = valid ? uint32_t(q) : 0u;
+        if constexpr (GROUP == 0) q = __fadd_rn(div_rn_markstein(v[i], sc, y), 0.5f * float(TOP));
+        else q = div_rn_markstein(__fsub_rn(v[i], lo), sc, y);
+        c[i] = valid ? min(__float2uint_rn(q), uint32_t(TOP)) : 0u;
     }
 }
 
