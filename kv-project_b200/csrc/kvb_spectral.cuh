@@ -129,8 +129,8 @@ __device__ __forceinline__ void midrise_code32(const float (&c)[32], float step,
     uint32_t code[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const float v = fminf(fmaxf(rintf(__fadd_rn(div_rn_from_rcp(c[i], sc, y), HALF)), 0.f), float(TOP));
-        code[i] = uint32_t(v);
+        // saturating round-half-even conversion + integer clamp == rint + clamp to [0, TOP]
+        code[i] = min(__float2uint_rn(__fadd_rn(div_rn_from_rcp(c[i], sc, y), HALF)), uint32_t(TOP));
     }
     uint32_t w[RB / 4];
 #pragma unroll
