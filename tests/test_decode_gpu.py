@@ -176,3 +176,28 @@ def test_tc_matches_mma_decode(cuda_dev, rep, Tq):
     ob = kvb.decode(b, q, 128 ** -0.5, qpos=[3000] * Tq, out_dtype=torch.float32)
     assert kvb.device_status() == 0
     assert (oa - ob).abs().max().item() <= 1e-3
+
+
+def test_cta_counts_and_plan_reuse(cuda_dev):
+    """The split-K plan (and the parameter tables built from it) is reused between calls of one
+    cache shape and rebuilt when the shape or the CTA count changes: alternating two caches of
+    different shapes and several CTA counts gives, every time, the output of a first call."""
+    import kvb
+    ka, va = kvb.workloads.lognormal_kv(1, 2, 3000, 128, torch.bfloat16, device=cuda_dev, seed=21)
+    kb, vb = kvb.workloads.lognormal_kv(2, 2, 1500, 128, torch.bfloat16, device=cuda_dev, seed=22)
+    ca, _ = kvb.cache.build_mixed(ka, va)
+    cb = kvb.cache.build_kivi(kb, vb, 4, 2, 128, 32)
+    qa = kvb.workloads.queries(1, 8, 1, 128, torch.bfloat16, device=cuda_dev, seed=23)
+    qb = kvb.workloads.queries(2, 8, 1, 128, torch.bfloat16, device=cuda_dev, seed=24)
+    ref_a = kvb.decode(ca, qa, 128 ** -0.5, out_dtype=torch.float32)
+    ref_b = kvb.decode(cb, qb, 128 ** -0.5, out_dtype=torch.float32)
+    for _ in range(2):
+        for n_ctas in (0, 1, 7, 300):
+            oa = kvb.decode(ca, qa, 128 ** -0.5, out_dtype=torch.float32, n_ctas=n_ctas)
+            ob = kvb.decode(cb, qb, 128 ** -0.5, out_dtype=torch.float32, n_ctas=n_ctas)
+            # other CTA counts split the context elsewhere: each split's running max sets the fp16
+            # rounding of its value weights, so outputs move by the kernel's own error (~5e-5)
+            tol = 0.0 if n_ctas == 0 else 2e-4
+            assert (oa - ref_a).abs().max().item() <= tol
+            assert (ob - ref_b).abs().max().item() <= tol
+    assert kvb.device_status() == 0
