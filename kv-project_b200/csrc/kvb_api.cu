@@ -123,7 +123,8 @@ kvb_status kvb_quant_pack(const void* x, int x_dtype, int64_t B, int64_t H, int6
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // d = 128, 16-bit rows on 16-byte boundaries: the 128-bit-load kernels
     const bool fast = d == 128 && (x_dtype == KVB_F16 || x_dtype == KVB_BF16) && aligned(x, 16) && sb % 8 == 0 &&
-                      sh % 8 == 0 && st % 8 == 0 && aligned(meta, 16) && n_alloc > 0;
+                      sh % 8 == 0 && st % 8 == 0 && aligned(meta, 16) && n_alloc > 0 && T < (int64_t(1) << 31) &&
+                      st >= 0 && st < (int64_t(1) << 31);
     if (fast) {
         kvb::QuantFastParams f{x, H, T, sb, sh, st, idx, first_row, n, n_alloc, step, codes, meta, xhat};
         const bool f16 = x_dtype == KVB_F16;

@@ -253,9 +253,9 @@ __device__ __forceinline__ float div_rn_markstein(float a, float b, float y) {
     return __fmaf_rn(r, y, q0);
 }
 
+// 8 channels of a 16-bit row held as 4 words -> float32 (exact)
 template <typename T>
-__device__ __forceinline__ void load8(const T* src, float (&v)[8]) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(src);
+__device__ __forceinline__ void unpack8(const uint4 raw, float (&v)[8]) {
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -269,6 +269,53 @@ __device__ __forceinline__ void load8(const T* src, float (&v)[8]) {
             v[2 * i + 1] = __high2float(h);
         }
     }
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* src, float (&v)[8]) {
+    unpack8<T>(*reinterpret_cast<const uint4*>(src), v);
+}
+
+// Elementwise min of two packed 16-bit pairs (fp16 or bf16): NaN loses to a number, +0 > -0, as
+// fminf / fmaxf order them, and exact, so the extrema of the packed inputs equal those of their
+// float32 conversions.
+template <typename T>
+__device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
+    using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+    const T2 r = __hmin2(*reinterpret_cast<const T2*>(&a), *reinterpret_cast<const T2*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+template <typename T>
+__device__ __forceinline__ uint32_t max2(uint32_t a, uint32_t b) {
+    using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+    const T2 r = __hmax2(*reinterpret_cast<const T2*>(&a), *reinterpret_cast<const T2*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+template <typename T>
+__device__ __forceinline__ float half_lo(uint32_t w) {
+    if constexpr (std::is_same<T, __half>::value) return __half2float(__ushort_as_half(uint16_t(w)));
+    else return __uint_as_float(w << 16);
+}
+template <typename T>
+__device__ __forceinline__ float half_hi(uint32_t w) {
+    if constexpr (std::is_same<T, __half>::value) return __half2float(__ushort_as_half(uint16_t(w >> 16)));
+    else return __uint_as_float(w & 0xffff0000u);
+}
+
+// The 8 channels (16 bytes) this lane quantises of gathered row j: source row idxr[j] (idxr = the
+// (b, h) row of the gather indices) or first_row + j; zeros past n and for a source index outside
+// [0, T), which is also flagged.  Returns whether the row is real.
+template <typename T, typename P>
+__device__ __forceinline__ bool fetch_row8(const P& p, const T* xb, const int64_t* idxr, int64_t j, uint4& raw) {
+    raw = make_uint4(0u, 0u, 0u, 0u);
+    if (j >= p.n) return false;
+    const int64_t src = idxr ? idxr[j] : p.first_row + j;
+    if (uint64_t(src) >= uint64_t(p.T)) {
+        raise_status(KVB_DEV_BOUNDS);
+        return false;
+    }
+    raw = *reinterpret_cast<const uint4*>(xb + src * p.st);
+    return true;
 }
 
 // 8 codes (bytes) of this lane -> the planar-packed bytes it owns, as 2 words; lanes whose l16 is
@@ -310,15 +357,19 @@ struct QuantFastParams {
     float* xhat;
 };
 
-// Codes of one 128-channel row held 8 channels per lane by 16 lanes (l16): group extrema by xor
-// shuffles inside the group's lanes, scale / zero point as the reference computes them, division
-// through the group scale's reciprocal + Markstein correction.  GROUP: channels per (lo, scale)
-// group (32, 64, 128) or 0 for the mid-rise code.  All 32 lanes of the warp must call it.
-template <int BITS, int GROUP>
-__device__ __forceinline__ void qrow_codes(const float (&v)[8], bool valid, float step, uint32_t (&c)[8], float& lo,
+// Codes of one 128-channel row held 8 channels per lane by 16 lanes (l16), the lane's channels as
+// the 4 packed 16-bit words raw: group extrema on the packed pairs (min and negated max share one
+// pair, so one shuffle per butterfly level), scale / zero point as the reference computes them,
+// division through the group scale's reciprocal + Markstein correction.  GROUP: channels per
+// (lo, scale) group (32, 64, 128) or 0 for the mid-rise code.  All 32 lanes of the warp must call
+// it.  A row that is not real arrives as zeros, which already code to 0 with GROUP > 0.
+template <int BITS, int GROUP, typename T>
+__device__ __forceinline__ void qrow_codes(const uint4 raw, bool valid, float step, uint32_t (&c)[8], float& lo,
                                            float& sc) {
     constexpr int TOP = (1 << BITS) - 1;
     constexpr int LPG = GROUP ? GROUP / 8 : 16;
+    float v[8];
+    unpack8<T>(raw, v);
     if constexpr (GROUP == 0) {
         double ss = 0.0;
 #pragma unroll
@@ -329,29 +380,32 @@ __device__ __forceinline__ void qrow_codes(const float (&v)[8], bool valid, floa
         sc = fmaxf(as_stored(__fmul_rn(step, rms)), 5.9604644775390625e-8f);
         lo = 0.f;
     } else {
-        float mn = v[0], mx = v[0];
+        const uint32_t m2 = min2<T>(min2<T>(raw.x, raw.y), min2<T>(raw.z, raw.w));
+        const uint32_t x2 = max2<T>(max2<T>(raw.x, raw.y), max2<T>(raw.z, raw.w)) ^ 0x80008000u;   // -max
+        // (min, -max) of the lane: min over {(m.lo, -x.lo), (m.hi, -x.hi)}
+        uint32_t e = min2<T>(__byte_perm(m2, x2, 0x5410), __byte_perm(m2, x2, 0x7632));
 #pragma unroll
-        for (int i = 1; i < 8; ++i) {
-            mn = fminf(mn, v[i]);
-            mx = fmaxf(mx, v[i]);
-        }
-#pragma unroll
-        for (int m = LPG / 2; m >= 1; m >>= 1) {
-            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, m));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
-        }
+        for (int m = LPG / 2; m >= 1; m >>= 1) e = min2<T>(e, __shfl_xor_sync(0xffffffffu, e, m));
+        const float mn = half_lo<T>(e), mx = -half_hi<T>(e);
         lo = as_stored(mn);
-        sc = fmaxf(as_stored(__fdiv_rn(__fsub_rn(mx, lo), float(TOP))), 5.9604644775390625e-8f);
+        // (mx - lo) / TOP, correctly rounded: Markstein's correction from RN(1 / TOP) (a compile-time
+        // constant); an infinite or NaN difference passes through as the IEEE quotient would
+        constexpr float RTOP = 1.0f / float(TOP);
+        const float a = __fsub_rn(mx, lo);
+        const float qa = div_rn_markstein(a, float(TOP), RTOP);
+        sc = fmaxf(as_stored(fabsf(a) < INFINITY ? qa : a), 5.9604644775390625e-8f);
     }
     const float y = __frcp_rn(sc);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         // round-half-even conversion that saturates below at 0 (NaN -> 0), then the upper clamp:
         // the same codes as rint + clamp to [0, TOP] in float, in two instructions instead of four
-        float q;
-        if constexpr (GROUP == 0) q = __fadd_rn(div_rn_markstein(v[i], sc, y), 0.5f * float(TOP));
-        else q = div_rn_markstein(__fsub_rn(v[i], lo), sc, y);
-        c[i] = valid ? min(__float2uint_rn(q), uint32_t(TOP)) : 0u;
+        if constexpr (GROUP == 0) {
+            const float q = __fadd_rn(div_rn_markstein(v[i], sc, y), 0.5f * float(TOP));
+            c[i] = valid ? min(__float2uint_rn(q), uint32_t(TOP)) : 0u;
+        } else {
+            c[i] = min(__float2uint_rn(div_rn_markstein(__fsub_rn(v[i], lo), sc, y)), uint32_t(TOP));
+        }
     }
 }
 
@@ -375,6 +429,9 @@ __device__ __forceinline__ void qrow_meta(void* meta, int64_t row, int l16, bool
 }
 
 // grid = (ceil(n_alloc / 64), B * H), block 256: 8 warps x 2 rows x 4 passes = 64 rows per CTA.
+// Row r of the CTA (pass ps: r = 2 warp + half + 16 ps) is gathered row j0 + r; all 64-bit offsets
+// are taken once per CTA and rows index from them in 32 bits.  The host sends only T < 2^31 and
+// 0 <= st < 2^31 here, so a checked source row times the row stride is one 32 x 32 -> 64 multiply.
 template <typename T, int BITS, int GROUP>
 __global__ void __launch_bounds__(256) quant_token128_kernel(const QuantFastParams p) {
     constexpr int D = 128, RB = D * BITS / 8;
@@ -382,44 +439,47 @@ __global__ void __launch_bounds__(256) quant_token128_kernel(const QuantFastPara
     const int l16 = lane & 15, half = lane >> 4;
     const int64_t bh = blockIdx.y;
     const int64_t b = bh / p.H, h = bh % p.H;
+    const int64_t j0 = int64_t(blockIdx.x) * 64;
+    const int r0 = warp * 2 + half;
+    const int nreal = int(imin64(p.n - j0, 64));         // rows of this CTA that are gathered rows
+    const int nstore = int(imin64(p.n_alloc - j0, 64));  // rows of this CTA that are stored
     const T* xb = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + 8 * l16;
-    const int64_t jbase = int64_t(blockIdx.x) * 64 + warp * 2 + half;
+    const int64_t* idxr = p.idx ? p.idx + bh * p.n + j0 : nullptr;
+    const int64_t src0 = p.first_row + j0;
+    const uint32_t T32 = uint32_t(p.T), st32 = uint32_t(p.st);
     // issue all four passes' loads first (memory-level parallelism), then compute
-    float v[4][8];
-    bool valid[4];
+    uint4 raw[4];
+    bool valid[4], bad = false;
 #pragma unroll
     for (int ps = 0; ps < 4; ++ps) {
-        const int64_t j = jbase + 16 * ps;
-        int64_t src = 0;
-        valid[ps] = j < p.n;
-        if (valid[ps]) {
-            src = p.idx ? p.idx[bh * p.n + j] : p.first_row + j;
-            if (src < 0 || src >= p.T) {
-                raise_status(KVB_DEV_BOUNDS);
-                valid[ps] = false;
-            }
-        }
-        if (valid[ps]) {
-            load8<T>(xb + src * p.st, v[ps]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[ps][i] = 0.f;
+        const int r = r0 + 16 * ps;
+        raw[ps] = make_uint4(0u, 0u, 0u, 0u);
+        valid[ps] = false;
+        if (r < nreal) {
+            const int64_t src = idxr ? idxr[r] : src0 + r;
+            valid[ps] = uint64_t(src) < uint64_t(T32);
+            bad |= !valid[ps];
+            if (valid[ps]) raw[ps] = *reinterpret_cast<const uint4*>(xb + uint64_t(uint32_t(src)) * st32);
         }
     }
+    if (bad) raise_status(KVB_DEV_BOUNDS);
+    uint8_t* const cb = p.codes + (bh * p.n_alloc + j0) * RB;
+    const int64_t mrow = bh * p.n_alloc + j0;
+    float* const xh = p.xhat ? p.xhat + (bh * p.n + j0) * D + 8 * l16 : nullptr;
 #pragma unroll
     for (int ps = 0; ps < 4; ++ps) {
-        const int64_t j = jbase + 16 * ps;
-        if (j >= p.n_alloc) continue;                  // uniform per warp (both rows of a pair)
+        const int r = r0 + 16 * ps;
+        if (r >= nstore) continue;                       // uniform per warp (both rows of a pair)
         uint32_t c[8];
         float lo, sc;
-        qrow_codes<BITS, GROUP>(v[ps], valid[ps], p.step, c, lo, sc);
-        if (p.xhat && valid[ps])
+        qrow_codes<BITS, GROUP, T>(raw[ps], valid[ps], p.step, c, lo, sc);
+        if (xh && valid[ps])
 #pragma unroll
-            for (int i = 0; i < 8; ++i) p.xhat[(bh * p.n + j) * D + 8 * l16 + i] = qrow_xhat<BITS, GROUP>(c[i], lo, sc);
+            for (int i = 0; i < 8; ++i) xh[r * D + i] = qrow_xhat<BITS, GROUP>(c[i], lo, sc);
         const uint32_t c0 = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
         const uint32_t c1 = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
-        store_packed<BITS>(p.codes + (bh * p.n_alloc + j) * RB, pack_planar_lane<BITS>(c0, c1), l16);
-        qrow_meta<GROUP>(p.meta, bh * p.n_alloc + j, l16, valid[ps], lo, sc);
+        store_packed<BITS>(cb + r * RB, pack_planar_lane<BITS>(c0, c1), l16);
+        qrow_meta<GROUP>(p.meta, mrow + r, l16, valid[ps], lo, sc);
     }
 }
 
@@ -439,37 +499,21 @@ __global__ void __launch_bounds__(256) quant_vblock128_kernel(const QuantFastPar
     const int64_t b = bh / p.H, h = bh % p.H;
     const T* xb = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + 8 * l16;
     const int64_t j0 = int64_t(blockIdx.x) * 128;
+    const int64_t* idxr = p.idx ? p.idx + bh * p.n : nullptr;
 #pragma unroll
     for (int grp = 0; grp < 2; ++grp) {
-        float v[4][8];
+        uint4 raw[4];
         bool valid[4];
 #pragma unroll
-        for (int ps = 0; ps < 4; ++ps) {
-            const int r = warp * 16 + (grp * 4 + ps) * 2 + half;
-            const int64_t j = j0 + r;
-            int64_t src = 0;
-            valid[ps] = j < p.n;
-            if (valid[ps]) {
-                src = p.idx ? p.idx[bh * p.n + j] : p.first_row + j;
-                if (src < 0 || src >= p.T) {
-                    raise_status(KVB_DEV_BOUNDS);
-                    valid[ps] = false;
-                }
-            }
-            if (valid[ps]) {
-                load8<T>(xb + src * p.st, v[ps]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[ps][i] = 0.f;
-            }
-        }
+        for (int ps = 0; ps < 4; ++ps)
+            valid[ps] = fetch_row8<T>(p, xb, idxr, j0 + warp * 16 + (grp * 4 + ps) * 2 + half, raw[ps]);
 #pragma unroll
         for (int ps = 0; ps < 4; ++ps) {
             const int r = warp * 16 + (grp * 4 + ps) * 2 + half;
             const int64_t j = j0 + r;
             uint32_t c[8];
             float lo, sc;
-            qrow_codes<BITS, GROUP>(v[ps], valid[ps], p.step, c, lo, sc);
+            qrow_codes<BITS, GROUP, T>(raw[ps], valid[ps], p.step, c, lo, sc);
             if (p.xhat && valid[ps])
 #pragma unroll
                 for (int i = 0; i < 8; ++i) p.xhat[(bh * p.n + j) * D + 8 * l16 + i] = qrow_xhat<BITS, GROUP>(c[i], lo, sc);

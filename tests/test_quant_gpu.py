@@ -100,14 +100,22 @@ def test_golden_strata_codes(golden, cuda_dev):
         np.testing.assert_array_equal(unpack(r["codes"], b, y.shape[2])[0, 0][same], g[f"sq{b}_codes"][same])
 
 
-def test_bad_rows_are_rejected_not_read(cuda_dev):
-    """An out-of-range gather index sets the device bounds flag instead of reading out of bounds."""
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_bad_rows_are_rejected_not_read(cuda_dev, dtype):
+    """An out-of-range gather index (past T, or negative) sets the device bounds flag instead of
+    reading out of bounds; the row is stored as zero codes and zero metadata, the others as usual.
+    float32 takes the generic kernel, bf16 the 128-bit-load one."""
     import kvb
-    x = torch.randn(1, 1, 10, 128, device=cuda_dev)
-    idx = torch.tensor([[[0, 3, 11]]], device=cuda_dev)
-    kvb.device_status(clear=True)
-    kvb.quant_pack(x, 4, 64, idx=idx)
-    assert kvb.device_status(clear=True) & 2
+    x = torch.randn(1, 1, 10, 128, device=cuda_dev).to(dtype)
+    for bad in (11, -1):
+        idx = torch.tensor([[[0, 3, bad, 9]]], device=cuda_dev)
+        kvb.device_status(clear=True)
+        r = kvb.quant_pack(x, 4, 64, idx=idx)
+        assert kvb.device_status(clear=True) & 2
+        assert int(r["codes"][0, 0, 2].abs().sum()) == 0 and int(r["meta"][0, 0, 2].abs().sum()) == 0
+        ok = kvb.quant_pack(x, 4, 64, idx=idx[..., [0, 1, 3]])
+        assert kvb.device_status() == 0
+        assert torch.equal(r["codes"][0, 0, [0, 1, 3]], ok["codes"][0, 0, :3])
 
 
 @pytest.mark.parametrize("bits", [2, 4, 8])
