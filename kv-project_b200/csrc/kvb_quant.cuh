@@ -428,58 +428,184 @@ __device__ __forceinline__ void qrow_meta(void* meta, int64_t row, int l16, bool
     }
 }
 
-// grid = (ceil(n_alloc / 64), B * H), block 256: 8 warps x 2 rows x 4 passes = 64 rows per CTA.
-// Row r of the CTA (pass ps: r = 2 warp + half + 16 ps) is gathered row j0 + r; all 64-bit offsets
-// are taken once per CTA and rows index from them in 32 bits.  The host sends only T < 2^31 and
-// 0 <= st < 2^31 here, so a checked source row times the row stride is one 32 x 32 -> 64 multiply.
+// Lane layout of the token-major kernel: 8 lanes per row, lane l8 holding the channels
+// pl * PW + CPL * l8 + [0, CPL) of every bit plane pl (P = 8 / BITS planes of PW = 128 / P
+// channels, CPL = 16 / P channels of each per lane).  Packed byte k of a row holds channel
+// pl * PW + k in bits [pl * BITS, ...), so the lane forms the packed bytes CPL * l8 .. + CPL - 1
+// by itself, and a warp codes 4 rows per instruction.  A (lo, scale) group either spans whole planes
+// (WHOLE: every lane holds some of it; NGL = 128 / GROUP groups per lane) or lies inside one plane
+// (GROUP / CPL lanes hold it; one group per plane per lane).
+template <int BITS, int GROUP>
+struct Lane8 {
+    static constexpr int P = 8 / BITS, PW = 128 / P, CPL = 16 / P, WPP = CPL / 2;   // WPP: 16-bit pairs
+    static constexpr bool WHOLE = GROUP == 0 || GROUP >= PW;
+    static constexpr int NGL = GROUP == 0 ? 1 : (WHOLE ? 128 / GROUP : P);
+    static constexpr int SPAN = WHOLE ? 8 : GROUP / CPL;                            // lanes per group
+    __device__ static constexpr int group_of_plane(int pl) { return GROUP == 0 ? 0 : (WHOLE ? pl * PW / GROUP : pl); }
+};
+
+// grid = (ceil(n_alloc / 64), B * H), block 256: 8 warps x 4 rows x 2 passes = 64 rows per CTA.
+// Row r of the CTA (pass ps: r = 4 warp + lane / 8 + 32 ps) is gathered row j0 + r; all 64-bit
+// offsets are taken once per CTA and rows index from them in 32 bits.  The host sends only
+// T < 2^31 and 0 <= st < 2^31 here, so a checked source row times the row stride is one
+// 32 x 32 -> 64 multiply.  Rows past n arrive as zeros (codes 0 with GROUP > 0; zero metadata).
 template <typename T, int BITS, int GROUP>
 __global__ void __launch_bounds__(256) quant_token128_kernel(const QuantFastParams p) {
-    constexpr int D = 128, RB = D * BITS / 8;
+    using L = Lane8<BITS, GROUP>;
+    constexpr int D = 128, RB = D * BITS / 8, TOP = (1 << BITS) - 1;
+    constexpr int P = L::P, PW = L::PW, CPL = L::CPL, WPP = L::WPP, NGL = L::NGL;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int l16 = lane & 15, half = lane >> 4;
+    const int l8 = lane & 7;
     const int64_t bh = blockIdx.y;
     const int64_t b = bh / p.H, h = bh % p.H;
     const int64_t j0 = int64_t(blockIdx.x) * 64;
-    const int r0 = warp * 2 + half;
+    const int r0 = warp * 4 + (lane >> 3);
     const int nreal = int(imin64(p.n - j0, 64));         // rows of this CTA that are gathered rows
     const int nstore = int(imin64(p.n_alloc - j0, 64));  // rows of this CTA that are stored
-    const T* xb = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + 8 * l16;
+    const T* xb = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + CPL * l8;
     const int64_t* idxr = p.idx ? p.idx + bh * p.n + j0 : nullptr;
     const int64_t src0 = p.first_row + j0;
     const uint32_t T32 = uint32_t(p.T), st32 = uint32_t(p.st);
-    // issue all four passes' loads first (memory-level parallelism), then compute
-    uint4 raw[4];
-    bool valid[4], bad = false;
+    // issue both passes' loads first (memory-level parallelism), then compute
+    uint32_t w[2][P * WPP];                               // [pass][plane * WPP + pair]
+    bool valid[2], bad = false;
 #pragma unroll
-    for (int ps = 0; ps < 4; ++ps) {
-        const int r = r0 + 16 * ps;
-        raw[ps] = make_uint4(0u, 0u, 0u, 0u);
+    for (int ps = 0; ps < 2; ++ps) {
+        const int r = r0 + 32 * ps;
+#pragma unroll
+        for (int k = 0; k < P * WPP; ++k) w[ps][k] = 0u;
         valid[ps] = false;
         if (r < nreal) {
             const int64_t src = idxr ? idxr[r] : src0 + r;
             valid[ps] = uint64_t(src) < uint64_t(T32);
             bad |= !valid[ps];
-            if (valid[ps]) raw[ps] = *reinterpret_cast<const uint4*>(xb + uint64_t(uint32_t(src)) * st32);
+            if (valid[ps]) {
+                const T* row = xb + uint64_t(uint32_t(src)) * st32;
+#pragma unroll
+                for (int pl = 0; pl < P; ++pl) {
+                    if constexpr (WPP == 2) {
+                        const uint2 u = *reinterpret_cast<const uint2*>(row + pl * PW);
+                        w[ps][pl * 2] = u.x;
+                        w[ps][pl * 2 + 1] = u.y;
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < WPP / 4; ++q) {
+                            const uint4 u = *reinterpret_cast<const uint4*>(row + pl * PW + 8 * q);
+                            w[ps][pl * WPP + 4 * q] = u.x;
+                            w[ps][pl * WPP + 4 * q + 1] = u.y;
+                            w[ps][pl * WPP + 4 * q + 2] = u.z;
+                            w[ps][pl * WPP + 4 * q + 3] = u.w;
+                        }
+                    }
+                }
+            }
         }
     }
     if (bad) raise_status(KVB_DEV_BOUNDS);
-    uint8_t* const cb = p.codes + (bh * p.n_alloc + j0) * RB;
+    uint8_t* const cb = p.codes + (bh * p.n_alloc + j0) * RB + CPL * l8;
     const int64_t mrow = bh * p.n_alloc + j0;
-    float* const xh = p.xhat ? p.xhat + (bh * p.n + j0) * D + 8 * l16 : nullptr;
+    float* const xh = p.xhat ? p.xhat + (bh * p.n + j0) * D + CPL * l8 : nullptr;
 #pragma unroll
-    for (int ps = 0; ps < 4; ++ps) {
-        const int r = r0 + 16 * ps;
-        if (r >= nstore) continue;                       // uniform per warp (both rows of a pair)
-        uint32_t c[8];
-        float lo, sc;
-        qrow_codes<BITS, GROUP, T>(raw[ps], valid[ps], p.step, c, lo, sc);
-        if (xh && valid[ps])
+    for (int ps = 0; ps < 2; ++ps) {
+        const int r = r0 + 32 * ps;
+        float lo[NGL], sc[NGL], y[NGL];
+        if constexpr (GROUP == 0) {
+            double ss = 0.0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) xh[r * D + i] = qrow_xhat<BITS, GROUP>(c[i], lo, sc);
-        const uint32_t c0 = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
-        const uint32_t c1 = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
-        store_packed<BITS>(cb + r * RB, pack_planar_lane<BITS>(c0, c1), l16);
-        qrow_meta<GROUP>(p.meta, mrow + r, l16, valid[ps], lo, sc);
+            for (int k = 0; k < P * WPP; ++k) {
+                const float a = half_lo<T>(w[ps][k]), c = half_hi<T>(w[ps][k]);
+                ss += double(__fmul_rn(a, a));
+                ss += double(__fmul_rn(c, c));
+            }
+#pragma unroll
+            for (int m = 4; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+            const float rms = __fsqrt_rn(float(ss / 128.0));
+            sc[0] = fmaxf(as_stored(__fmul_rn(p.step, rms)), 5.9604644775390625e-8f);
+            lo[0] = 0.f;
+        } else {
+#pragma unroll
+            for (int gl = 0; gl < NGL; ++gl) {
+                // the group's 16-bit pairs in this lane -> (min, -max) pair -> over the group's lanes
+                uint32_t m2 = 0u, x2 = 0u;
+                bool first = true;
+#pragma unroll
+                for (int pl = 0; pl < P; ++pl) {
+                    if (L::group_of_plane(pl) != gl) continue;
+#pragma unroll
+                    for (int k = 0; k < WPP; ++k) {
+                        const uint32_t v = w[ps][pl * WPP + k];
+                        m2 = first ? v : min2<T>(m2, v);
+                        x2 = first ? v : max2<T>(x2, v);
+                        first = false;
+                    }
+                }
+                x2 ^= 0x80008000u;
+                uint32_t e = min2<T>(__byte_perm(m2, x2, 0x5410), __byte_perm(m2, x2, 0x7632));
+#pragma unroll
+                for (int m = L::SPAN / 2; m >= 1; m >>= 1) e = min2<T>(e, __shfl_xor_sync(0xffffffffu, e, m));
+                const float mn = half_lo<T>(e), mx = -half_hi<T>(e);
+                lo[gl] = as_stored(mn);
+                // (mx - lo) / TOP, correctly rounded: Markstein's correction from RN(1 / TOP) (a
+                // compile-time constant); an infinite or NaN difference passes through as the IEEE
+                // quotient would
+                constexpr float RTOP = 1.0f / float(TOP);
+                const float a = __fsub_rn(mx, lo[gl]);
+                const float qa = div_rn_markstein(a, float(TOP), RTOP);
+                sc[gl] = fmaxf(as_stored(fabsf(a) < INFINITY ? qa : a), 5.9604644775390625e-8f);
+            }
+        }
+#pragma unroll
+        for (int gl = 0; gl < NGL; ++gl) y[gl] = __frcp_rn(sc[gl]);
+        // codes, packed in the lane: output word k / 2 takes the pair k of every plane
+        uint32_t out[WPP / 2];
+#pragma unroll
+        for (int q = 0; q < WPP / 2; ++q) out[q] = 0u;
+#pragma unroll
+        for (int pl = 0; pl < P; ++pl) {
+            const int gl = L::group_of_plane(pl);
+#pragma unroll
+            for (int k = 0; k < WPP; ++k) {
+                const float v[2] = {half_lo<T>(w[ps][pl * WPP + k]), half_hi<T>(w[ps][pl * WPP + k])};
+                uint32_t c[2];
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    // round-half-even conversion that saturates below at 0 (NaN -> 0), then the
+                    // upper clamp: the codes of rint + clamp to [0, TOP] in float
+                    if constexpr (GROUP == 0) {
+                        const float q = __fadd_rn(div_rn_markstein(v[t], sc[0], y[0]), 0.5f * float(TOP));
+                        c[t] = valid[ps] ? min(__float2uint_rn(q), uint32_t(TOP)) : 0u;
+                    } else {
+                        c[t] = min(__float2uint_rn(div_rn_markstein(__fsub_rn(v[t], lo[gl]), sc[gl], y[gl])),
+                                   uint32_t(TOP));
+                    }
+                }
+                out[k / 2] |= (c[0] | (c[1] << 8)) << (16 * (k & 1) + pl * BITS);
+                if (xh && valid[ps])
+                    *reinterpret_cast<float2*>(xh + r * D + pl * PW + 2 * k) =
+                        make_float2(qrow_xhat<BITS, GROUP>(c[0], lo[gl], sc[gl]), qrow_xhat<BITS, GROUP>(c[1], lo[gl], sc[gl]));
+            }
+        }
+        if (r < nstore) {
+            uint8_t* dst = cb + r * RB;
+            if constexpr (WPP == 2) *reinterpret_cast<uint32_t*>(dst) = out[0];
+            else if constexpr (WPP == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(out[0], out[1]);
+            else *reinterpret_cast<uint4*>(dst) = make_uint4(out[0], out[1], out[2], out[3]);
+            if constexpr (GROUP == 0) {
+                if (l8 == 0) static_cast<__half*>(p.meta)[mrow + r] = __float2half_rn(valid[ps] ? sc[0] : 0.f);
+            } else {
+                constexpr int G = 128 / GROUP;
+                uint32_t* m = static_cast<uint32_t*>(p.meta) + (mrow + r) * G;
+                if constexpr (L::WHOLE) {
+#pragma unroll
+                    for (int gl = 0; gl < NGL; ++gl)
+                        if (l8 == gl) m[gl] = valid[ps] ? pack_half2(lo[gl], sc[gl]) : 0u;
+                } else if ((CPL * l8) % GROUP == 0) {
+#pragma unroll
+                    for (int pl = 0; pl < P; ++pl)
+                        m[(pl * PW + CPL * l8) / GROUP] = valid[ps] ? pack_half2(lo[pl], sc[pl]) : 0u;
+                }
+            }
+        }
     }
 }
 
