@@ -193,16 +193,16 @@ __device__ __forceinline__ uint32_t hi_word(uint64_t u) {
 }
 
 // One radix pass: 8-bit digit at `shift` of the words w(i) that match `prefix` under `mask`.
-// Per-warp private histograms (plain shared-memory atomics, no cross-warp contention), summed per
-// bin, then warp 0 finds the digit holding rank `rem` with a suffix scan.  get(i, act) -> word.
-// All threads call it; returns the new rem (rank inside the chosen digit) and the digit.
+// radix_hist: per-warp private histograms (plain shared-memory atomics, no cross-warp contention),
+// summed per bin into hist[256].  radix_select: warp 0 finds the digit holding rank `rem` with a
+// suffix scan over hist.  get(i, act) -> word.  All threads call both; radix_select returns the new
+// rem (rank inside the chosen digit) and the digit.
 // (Measured on B200: faster than 4-bit digits with packed per-thread counters, which need twice
 // the passes, and than warp-aggregated atomics through __match_any_sync.)
 template <typename Get>
-__device__ __forceinline__ int64_t radix_pass(int n, int shift, uint32_t prefix, uint32_t mask, int64_t rem,
-                                              int (*whist)[256], int* hist, int* s_digit, int64_t* s_rem,
-                                              uint32_t& digit_out, Get get) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+__device__ __forceinline__ void radix_hist(int n, int shift, uint32_t prefix, uint32_t mask, int (*whist)[256],
+                                           int* hist, Get get) {
+    const int tid = threadIdx.x, warp = tid >> 5;
     for (int i = tid; i < 32 * 256; i += SEL_THREADS) whist[i >> 8][i & 255] = 0;
     __syncthreads();
     for (int i = tid; i < n; i += SEL_THREADS) {
@@ -218,6 +218,11 @@ __device__ __forceinline__ int64_t radix_pass(int n, int shift, uint32_t prefix,
         hist[tid] = c;
     }
     __syncthreads();
+}
+
+__device__ __forceinline__ int64_t radix_select(const int* hist, int64_t rem, int* s_digit, int64_t* s_rem,
+                                                uint32_t& digit_out) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (warp == 0) {
         // suffix sums over the bins from the top (lane l owns bins 255 - 8 l .. 248 - 8 l)
         int c[8], tot = 0;
@@ -251,6 +256,135 @@ __device__ __forceinline__ int64_t radix_pass(int n, int shift, uint32_t prefix,
     return r;
 }
 
+template <typename Get>
+__device__ __forceinline__ int64_t radix_pass(int n, int shift, uint32_t prefix, uint32_t mask, int64_t rem,
+                                              int (*whist)[256], int* hist, int* s_digit, int64_t* s_rem,
+                                              uint32_t& digit_out, Get get) {
+    radix_hist(n, shift, prefix, mask, whist, hist, get);
+    return radix_select(hist, rem, s_digit, s_rem, digit_out);
+}
+
+// Compaction of one row into its NB + 1 classes (NB boundaries, a compile-time count so the
+// per-boundary state and the output pointers stay in registers).  Each warp owns a contiguous index
+// range.  Pass A counts, per warp, the keys equal to each boundary key and those strictly above
+// it; a scan over warps gives each warp its rank among the equal keys.  The kept sets of the
+// cumulative boundaries are nested (a lower boundary key is larger, or the same key with fewer of
+// its equal keys taken, lowest indices first), so class c of a warp holds in(c) - in(c - 1) keys,
+// in(k) = its keys strictly above boundary k + its share of the first s_need[k] equal keys: the
+// class offsets come from one more scan, and pass B writes the indices in ascending order.
+template <typename K, int NB>
+__device__ __forceinline__ void rs_compact(const RankSplitParams& p, const K* keys, const uint32_t* s_hi, int n,
+                                           int64_t row, const int* s_mode, const uint32_t* s_T, const uint64_t* s_tau,
+                                           const int64_t* s_need, int (*s_w)[33]) {
+    constexpr int NK = NB > 0 ? NB : 1;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int mode[NK];
+    uint32_t Tk[NK];
+    uint64_t tau[NK];
+    int64_t need[NK];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+        mode[k] = s_mode[k];
+        Tk[k] = s_T[k];
+        tau[k] = s_tau[k];
+        need[k] = s_need[k];
+    }
+    const int per = ((n + 31) / 32 + 31) / 32 * 32;
+    const int w0 = min(n, warp * per), w1 = min(n, w0 + per);
+    const uint32_t lt = (1u << lane) - 1u;
+    // the full key only where the high word is some boundary's
+    auto load_u = [&](int i, uint32_t h) -> uint64_t {
+        bool cand = false;
+#pragma unroll
+        for (int k = 0; k < NB; ++k) cand |= mode[k] == 0 && h == Tk[k];
+        return cand ? (sizeof(K) == 8 ? order_key(keys[i]) : uint64_t(h)) : 0ull;
+    };
+    // pass A
+    int cnt[NK], gt[NK];
+#pragma unroll
+    for (int k = 0; k < NK; ++k) cnt[k] = gt[k] = 0;
+    for (int b = w0; b < w1; b += 32) {
+        const int i = b + lane;
+        const bool valid = i < w1;
+        const uint32_t h = valid ? s_hi[i] : 0u;
+        const uint64_t u = valid ? load_u(i, h) : 0ull;
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+            const bool m0 = mode[k] == 0;
+            cnt[k] += __popc(__ballot_sync(0xffffffffu, valid && m0 && h == Tk[k] && u == tau[k]));
+            gt[k] += __popc(__ballot_sync(0xffffffffu, valid && (mode[k] == 2 || (m0 && (h > Tk[k] || (h == Tk[k] && u > tau[k]))))));
+        }
+    }
+    if (lane == 0)
+#pragma unroll
+        for (int k = 0; k < NB; ++k) s_w[k][warp] = cnt[k];
+    __syncthreads();
+    if (tid < NB) {
+        int acc = 0;
+        for (int w = 0; w < 32; ++w) {
+            const int c = s_w[tid][w];
+            s_w[tid][w] = acc;
+            acc += c;
+        }
+    }
+    __syncthreads();
+    int run[NK];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) run[k] = s_w[k][warp];
+    __syncthreads();
+    if (lane == 0) {
+        int prev = 0;
+#pragma unroll
+        for (int c = 0; c <= NB; ++c) {
+            int in = w1 - w0;
+            if (c < NB) {
+                const int64_t take = need[c] - run[c];
+                in = gt[c] + (mode[c] == 0 ? int(take < 0 ? 0 : (take > cnt[c] ? cnt[c] : take)) : 0);
+            }
+            s_w[c][warp] = in - prev;
+            prev = in;
+        }
+    }
+    __syncthreads();
+    if (tid <= NB) {
+        int acc = 0;
+        for (int w = 0; w < 32; ++w) {
+            const int c = s_w[tid][w];
+            s_w[tid][w] = acc;
+            acc += c;
+        }
+    }
+    __syncthreads();
+    // pass B: write each class's indices in ascending order
+    int64_t* dst[NB + 1];
+#pragma unroll
+    for (int c = 0; c <= NB; ++c) dst[c] = p.out[c] ? p.out[c] + row * p.out_stride[c] + s_w[c][warp] : nullptr;
+    for (int b = w0; b < w1; b += 32) {
+        const int i = b + lane;
+        const bool valid = i < w1;
+        const uint32_t h = valid ? s_hi[i] : 0u;
+        const uint64_t u = valid ? load_u(i, h) : 0ull;
+        int cls = 0;
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+            const bool eq = valid && mode[k] == 0 && h == Tk[k] && u == tau[k];
+            const unsigned be = __ballot_sync(0xffffffffu, eq);
+            const bool in = mode[k] == 2 ||
+                            (mode[k] == 0 && (h > Tk[k] || (h == Tk[k] && (u > tau[k] || (eq && run[k] + __popc(be & lt) < need[k])))));
+            run[k] += __popc(be);
+            cls += !in;
+        }
+#pragma unroll
+        for (int c = 0; c <= NB; ++c) {
+            const unsigned bc = __ballot_sync(0xffffffffu, valid && cls == c);
+            if (dst[c]) {
+                if (valid && cls == c) dst[c][__popc(bc & lt)] = i;
+                dst[c] += __popc(bc);
+            }
+        }
+    }
+}
+
 template <typename K>
 __global__ void __launch_bounds__(SEL_THREADS, 1) rank_split_smem_kernel(const RankSplitParams p) {
     extern __shared__ uint32_t s_hi[];                   // [n] high words, [32][256] warp histograms, [RS_CAND]
@@ -263,6 +397,9 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) rank_split_smem_kernel(const R
     __shared__ int s_digit;
     __shared__ int64_t s_rem;
     __shared__ uint32_t s_and, s_or;
+    __shared__ int s_lvl_hist[4][256];                   // high-word histograms of the last boundary's passes
+    __shared__ uint32_t s_lvl_prefix[4];
+    __shared__ int s_lvl_ok[4];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t row = blockIdx.x;
     const K* keys = static_cast<const K*>(p.keys) + row * p.key_stride;
@@ -275,6 +412,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) rank_split_smem_kernel(const R
         s_and = 0xFFFFFFFFu;
         s_or = 0u;
     }
+    if (tid < 4) s_lvl_ok[tid] = 0;
     __syncthreads();
     bool nan = false;
     uint32_t a_and = 0xFFFFFFFFu, a_or = 0u;
@@ -308,10 +446,19 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) rank_split_smem_kernel(const R
         }
         uint32_t prefix = s_and & cmask, mask = cmask;
         int64_t rem = cum;
-        for (int shift = top >= 7 ? top - 7 : 0;; shift = shift >= 8 ? shift - 8 : 0) {
+        // a pass whose prefix equals the previous boundary's at the same level has its histogram
+        // already (always the first pass: every boundary starts from the row's common bits)
+        for (int lvl = 0, shift = top >= 7 ? top - 7 : 0;; ++lvl, shift = shift >= 8 ? shift - 8 : 0) {
             uint32_t dg;
-            rem = radix_pass(n, shift, prefix, mask, rem, whist, s_hist, &s_digit, &s_rem, dg,
-                             [&](int i, bool& act) { act = true; return s_hi[i]; });
+            if (!(s_lvl_ok[lvl] && s_lvl_prefix[lvl] == prefix)) {
+                radix_hist(n, shift, prefix, mask, whist, s_lvl_hist[lvl],
+                           [&](int i, bool& act) { act = true; return s_hi[i]; });
+                if (tid == 0) {
+                    s_lvl_ok[lvl] = 1;
+                    s_lvl_prefix[lvl] = prefix;
+                }
+            }
+            rem = radix_select(s_lvl_hist[lvl], rem, &s_digit, &s_rem, dg);
             prefix |= dg << shift;
             mask |= 255u << shift;
             if (shift == 0) break;
@@ -357,92 +504,11 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) rank_split_smem_kernel(const R
     __syncthreads();
 
     // ---- compaction over contiguous per-warp ranges ----
-    const int per = ((n + 31) / 32 + 31) / 32 * 32;
-    const int w0 = min(n, warp * per), w1 = min(n, w0 + per);
-    const uint32_t lt = (1u << lane) - 1u;
-    auto load_u = [&](int i, uint32_t h, uint64_t& u) -> void {
-        bool cand = false;
-        for (int k = 0; k < nb; ++k) cand |= s_mode[k] == 0 && h == s_T[k];
-        u = cand ? (sizeof(K) == 8 ? order_key(keys[i]) : uint64_t(h)) : 0ull;
-    };
-    // pass A: keys equal to each boundary key, per warp
-    int cnt[SEL_MAX_CLASSES] = {0, 0, 0, 0};
-    for (int b = w0; b < w1; b += 32) {
-        const int i = b + lane;
-        const bool valid = i < w1;
-        const uint32_t h = valid ? s_hi[i] : 0u;
-        uint64_t u = 0;
-        if (valid) load_u(i, h, u);
-        for (int k = 0; k < nb; ++k)
-            cnt[k] += __popc(__ballot_sync(0xffffffffu, valid && s_mode[k] == 0 && h == s_T[k] && u == s_tau[k]));
-    }
-    if (lane == 0)
-        for (int k = 0; k < nb; ++k) s_w[k][warp] = cnt[k];
-    __syncthreads();
-    if (tid < nb) {
-        int acc = 0;
-        for (int w = 0; w < 32; ++w) {
-            const int c = s_w[tid][w];
-            s_w[tid][w] = acc;
-            acc += c;
-        }
-    }
-    __syncthreads();
-    int eq_run[SEL_MAX_CLASSES];
-    for (int k = 0; k < nb; ++k) eq_run[k] = s_w[k][warp];
-    __syncthreads();
-    // classes of one slice (also advances the equal-key ranks)
-    auto classify = [&](int i, bool valid, int (&run)[SEL_MAX_CLASSES]) -> int {
-        const uint32_t h = valid ? s_hi[i] : 0u;
-        uint64_t u = 0;
-        if (valid) load_u(i, h, u);
-        int cls = 0;
-        for (int k = 0; k < nb; ++k) {
-            const bool eq = valid && s_mode[k] == 0 && h == s_T[k] && u == s_tau[k];
-            const unsigned be = __ballot_sync(0xffffffffu, eq);
-            bool in;
-            if (s_mode[k] == 1) in = false;
-            else if (s_mode[k] == 2) in = true;
-            else in = h > s_T[k] || (h == s_T[k] && (u > s_tau[k] || (eq && run[k] + __popc(be & lt) < s_need[k])));
-            run[k] += __popc(be);
-            if (!in) ++cls;
-        }
-        return cls;
-    };
-    // pass B: class counts per warp
-    int run[SEL_MAX_CLASSES] = {eq_run[0], eq_run[1], eq_run[2], eq_run[3]};
-    int ccnt[SEL_MAX_CLASSES] = {0, 0, 0, 0};
-    for (int b = w0; b < w1; b += 32) {
-        const int i = b + lane;
-        const bool valid = i < w1;
-        const int cls = classify(i, valid, run);
-        for (int c = 0; c <= nb; ++c) ccnt[c] += __popc(__ballot_sync(0xffffffffu, valid && cls == c));
-    }
-    if (lane == 0)
-        for (int c = 0; c <= nb; ++c) s_w[c][warp] = ccnt[c];
-    __syncthreads();
-    if (tid <= nb) {
-        int acc = 0;
-        for (int w = 0; w < 32; ++w) {
-            const int c = s_w[tid][w];
-            s_w[tid][w] = acc;
-            acc += c;
-        }
-    }
-    __syncthreads();
-    // pass C: write each class's indices in ascending order
-    int off[SEL_MAX_CLASSES];
-    for (int c = 0; c <= nb; ++c) off[c] = s_w[c][warp];
-    for (int k = 0; k < nb; ++k) run[k] = eq_run[k];
-    for (int b = w0; b < w1; b += 32) {
-        const int i = b + lane;
-        const bool valid = i < w1;
-        const int cls = classify(i, valid, run);
-        for (int c = 0; c <= nb; ++c) {
-            const unsigned bc = __ballot_sync(0xffffffffu, valid && cls == c);
-            if (valid && cls == c && p.out[c]) p.out[c][row * p.out_stride[c] + off[c] + __popc(bc & lt)] = i;
-            off[c] += __popc(bc);
-        }
+    switch (nb) {
+        case 0: rs_compact<K, 0>(p, keys, s_hi, n, row, s_mode, s_T, s_tau, s_need, s_w); break;
+        case 1: rs_compact<K, 1>(p, keys, s_hi, n, row, s_mode, s_T, s_tau, s_need, s_w); break;
+        case 2: rs_compact<K, 2>(p, keys, s_hi, n, row, s_mode, s_T, s_tau, s_need, s_w); break;
+        default: rs_compact<K, 3>(p, keys, s_hi, n, row, s_mode, s_T, s_tau, s_need, s_w); break;
     }
 }
 
