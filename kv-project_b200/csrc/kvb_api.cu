@@ -349,12 +349,16 @@ kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, 
     dim3 grid(kvb::SC_SPLIT, unsigned(heads));
     for (int pass = 1; pass <= 2; ++pass) {
         p.pass = pass;
+        auto launch = [&](auto kernel, int sm) {
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+            kernel<<<grid, 256, sm, s>>>(p);
+        };
         if (dtype == KVB_BF16) {
-            if (d == 128) kvb::scores_kernel<__nv_bfloat16, 128><<<grid, 256, 0, s>>>(p);
-            else kvb::scores_kernel<__nv_bfloat16, 64><<<grid, 256, 0, s>>>(p);
+            if (d == 128) launch(kvb::scores_kernel<__nv_bfloat16, 128>, kvb::sc_smem_bytes<128>());
+            else launch(kvb::scores_kernel<__nv_bfloat16, 64>, kvb::sc_smem_bytes<64>());
         } else {
-            if (d == 128) kvb::scores_kernel<__half, 128><<<grid, 256, 0, s>>>(p);
-            else kvb::scores_kernel<__half, 64><<<grid, 256, 0, s>>>(p);
+            if (d == 128) launch(kvb::scores_kernel<__half, 128>, kvb::sc_smem_bytes<128>());
+            else launch(kvb::scores_kernel<__half, 64>, kvb::sc_smem_bytes<64>());
         }
         kvb_status st = launch_check("scores_kernel");
         if (st) return st;

@@ -16,7 +16,19 @@ namespace kvb {
 
 constexpr int SC_ROWS = 256;          // query rows per (b, kv head), padded
 constexpr int SC_KT = 64;             // keys per tile
-constexpr int SC_SPLIT = 16;          // key splits per head
+constexpr int SC_SPLIT = 37;          // key splits per head (heads x 37 is a multiple of 148 SMs for heads % 4 == 0)
+constexpr int SC_STAGES = 4;          // key tiles in flight per CTA (cp.async ring)
+
+template <int D>
+constexpr int sc_smem_bytes() { return SC_STAGES * SC_KT * (D / 2 + 4) * 4; }
+
+// 16-byte asynchronous global -> shared copy; bytes < 16 zero-fills the rest (0: nothing is read)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 struct ScoreParams {
     const void* q;
@@ -46,11 +58,13 @@ __device__ __forceinline__ void mma_bf16_or_f16<__nv_bfloat16>(float (&d)[4], co
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// grid (SC_SPLIT, heads), block 256: warp w owns query rows [32 w, 32 w + 32)
+// grid (SC_SPLIT, heads), block 256: warp w owns query rows [32 w, 32 w + 32).  Dynamic shared
+// memory: SC_STAGES key tiles (sc_smem_bytes<D>()), filled by cp.async SC_STAGES - 1 tiles ahead
+// of the tile being multiplied.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
     constexpr int KROW = D / 2 + 4;                                 // padded row (words): conflict-free B loads
-    __shared__ __align__(16) uint32_t s_k[SC_KT * KROW];           // keys [64][D] as half2 words
+    extern __shared__ __align__(16) uint32_t s_kring[];            // [SC_STAGES][64][KROW] keys as half2 words
     __shared__ float s_col[8][SC_KT];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int head = blockIdx.y, b = head / int(p.Hkv), h = head % int(p.Hkv);
@@ -91,15 +105,31 @@ __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
 
     const int64_t per = ((p.T + SC_SPLIT - 1) / SC_SPLIT + SC_KT - 1) / SC_KT * SC_KT;
     const int64_t k0 = int64_t(blockIdx.x) * per, k1 = imin64(p.T, k0 + per);
-    for (int64_t kt = k0; kt < k1; kt += SC_KT) {
-        __syncthreads();
-        for (int o = threadIdx.x; o < SC_KT * D / 8; o += blockDim.x) {       // 16-byte chunks
-            const int row = o / (D / 8), c8 = o % (D / 8);
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (kt + row < p.T) v = *reinterpret_cast<const uint4*>(kp + (kt + row) * D + c8 * 8);
-            *reinterpret_cast<uint4*>(s_k + row * KROW + c8 * 4) = v;
+    const int nt = k1 > k0 ? int((k1 - k0 + SC_KT - 1) / SC_KT) : 0;
+    const uint32_t ring = smem_u32(s_kring);
+    // tile i -> stage i % SC_STAGES; rows past T are zero-filled (nothing read; the source address
+    // is clamped to row T - 1 so that it stays inside the tensor)
+    auto issue = [&](int i) {
+        if (i < nt) {
+            const int64_t kt = k0 + int64_t(i) * SC_KT;
+            const uint32_t st = ring + uint32_t((i % SC_STAGES) * SC_KT * KROW * 4);
+            for (int o = threadIdx.x; o < SC_KT * D / 8; o += blockDim.x) {   // 16-byte chunks
+                const int row = o / (D / 8), c8 = o % (D / 8);
+                const bool in = kt + row < p.T;
+                cp_async16(st + uint32_t((row * KROW + c8 * 4) * 4), kp + (in ? kt + row : p.T - 1) * D + c8 * 8,
+                           in ? 16u : 0u);
+            }
         }
-        __syncthreads();
+        cp_async_commit();                                           // one group per tile slot, empty or not
+    };
+#pragma unroll
+    for (int i = 0; i < SC_STAGES - 1; ++i) issue(i);
+    for (int it = 0; it < nt; ++it) {
+        const int64_t kt = k0 + int64_t(it) * SC_KT;
+        cp_async_wait<SC_STAGES - 2>();                              // this thread's copies of tile it landed
+        __syncthreads();                                             // everyone's, and stage (it - 1) is free
+        issue(it + SC_STAGES - 1);
+        const uint32_t* s_k = s_kring + (it % SC_STAGES) * SC_KT * KROW;
         float acc[2][8][4];
 #pragma unroll
         for (int m = 0; m < 2; ++m)
@@ -172,6 +202,7 @@ __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
             }
         }
     }
+    cp_async_wait<0>();
     if (p.pass == 1) {
         // combine the 4 lanes (t) sharing each row, then store this split's (max, sum)
 #pragma unroll
