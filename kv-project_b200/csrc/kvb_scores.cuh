@@ -10,6 +10,8 @@
 // pooling is linear and identical for every query head, so pooling the head mean equals the
 // reference's mean of pooled heads).
 #pragma once
+#include <type_traits>
+
 #include "kvb_common.cuh"
 
 namespace kvb {
@@ -149,26 +151,35 @@ __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
             }
         }
         if (p.pass == 1) {
+            // keys past T exist only in the last tile of the last split: only that tile masks them
+            const int lim = int(imin64(p.T - kt, SC_KT)) - 2 * t;       // this lane's column c is in if c < lim
+            auto online = [&](auto full_tag) {
+                constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
+                for (int m = 0; m < 2; ++m)
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    float mx = -INFINITY;
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float v[8][2], mx = -INFINITY;
 #pragma unroll
-                    for (int n = 0; n < 8; ++n)
+                        for (int n = 0; n < 8; ++n)
 #pragma unroll
-                        for (int e = 0; e < 2; ++e)
-                            if (kt + 8 * n + 2 * t + e < p.T) mx = fmaxf(mx, acc[m][n][2 * hh + e] * p.lam);
-                    const float mn = fmaxf(rm[m][hh], mx);
-                    float s = rl[m][hh] * ((rm[m][hh] == -INFINITY) ? 0.f : ex2(rm[m][hh] - mn));
+                            for (int e = 0; e < 2; ++e) {
+                                v[n][e] = acc[m][n][2 * hh + e] * p.lam;
+                                if (FULL || 8 * n + e < lim) mx = fmaxf(mx, v[n][e]);
+                            }
+                        const float mn = fmaxf(rm[m][hh], mx);
+                        float s = rl[m][hh] * ((rm[m][hh] == -INFINITY) ? 0.f : ex2(rm[m][hh] - mn));
 #pragma unroll
-                    for (int n = 0; n < 8; ++n)
+                        for (int n = 0; n < 8; ++n)
 #pragma unroll
-                        for (int e = 0; e < 2; ++e)
-                            if (kt + 8 * n + 2 * t + e < p.T) s += ex2(acc[m][n][2 * hh + e] * p.lam - mn);
-                    rm[m][hh] = mn;
-                    rl[m][hh] = s;
-                }
+                            for (int e = 0; e < 2; ++e)
+                                if (FULL || 8 * n + e < lim) s += ex2(v[n][e] - mn);
+                        rm[m][hh] = mn;
+                        rl[m][hh] = s;
+                    }
+            };
+            if (lim + 2 * t == SC_KT) online(std::true_type{});
+            else online(std::false_type{});
         } else {
             float col[8][2];
 #pragma unroll
