@@ -67,7 +67,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
     constexpr int KROW = D / 2 + 4;                                 // padded row (words): conflict-free B loads
     extern __shared__ __align__(16) uint32_t s_kring[];            // [SC_STAGES][64][KROW] keys as half2 words
-    __shared__ float s_col[8][SC_KT];
+    __shared__ __align__(16) float s_col[8][SC_KT];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int head = blockIdx.y, b = head / int(p.Hkv), h = head % int(p.Hkv);
     const T* q = static_cast<const T*>(p.q);
@@ -181,7 +181,8 @@ __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
             if (lim + 2 * t == SC_KT) online(std::true_type{});
             else online(std::false_type{});
         } else {
-            float col[8][2];
+            // this lane's 16 columns (j = 2 n + e: column 8 n + 2 t + e) summed over its rows
+            float c16[16];
 #pragma unroll
             for (int n = 0; n < 8; ++n)
 #pragma unroll
@@ -192,17 +193,23 @@ __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
 #pragma unroll
                         for (int hh = 0; hh < 2; ++hh)
                             if (rv[m][hh]) s += ex2(acc[m][n][2 * hh + e] * p.lam - lse[m][hh]);
-                    s += __shfl_xor_sync(0xffffffffu, s, 4);
-                    s += __shfl_xor_sync(0xffffffffu, s, 8);
-                    s += __shfl_xor_sync(0xffffffffu, s, 16);
-                    col[n][e] = s;
+                    c16[2 * n + e] = s;
                 }
-            if (g == 0) {
+            // sum over the 8 lanes of a column (lane bits 4, 3, 2 = g) by a halving butterfly: at each
+            // level a lane keeps the half of its columns selected by that lane bit and adds the
+            // partner's copy of it, so lane (g, t) ends with columns 8 g + 2 t + {0, 1}
+            const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+            float c8[8], c4[4], c2[2];
 #pragma unroll
-                for (int n = 0; n < 8; ++n)
+            for (int i = 0; i < 8; ++i)
+                c8[i] = (b4 ? c16[8 + i] : c16[i]) + __shfl_xor_sync(0xffffffffu, b4 ? c16[i] : c16[8 + i], 16);
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) s_col[warp][8 * n + 2 * t + e] = col[n][e];
-            }
+            for (int i = 0; i < 4; ++i)
+                c4[i] = (b3 ? c8[4 + i] : c8[i]) + __shfl_xor_sync(0xffffffffu, b3 ? c8[i] : c8[4 + i], 8);
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+                c2[i] = (b2 ? c4[2 + i] : c4[i]) + __shfl_xor_sync(0xffffffffu, b2 ? c4[i] : c4[2 + i], 4);
+            *reinterpret_cast<float2*>(&s_col[warp][8 * g + 2 * t]) = make_float2(c2[0], c2[1]);
             __syncthreads();
             if (threadIdx.x < SC_KT) {
                 const int64_t j = kt + threadIdx.x;
