@@ -270,8 +270,16 @@ kvb_status kvb_rank_split(const void* keys, int key_dtype, int64_t rows, int64_t
         }
         return launch_check("rank_split_smem_kernel");
     }
-    if (key_dtype == KVB_F32) kvb::rank_split_kernel<float><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p);
-    else kvb::rank_split_kernel<double><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p);
+    auto big = [&](auto key_tag) {
+        using K = decltype(key_tag);
+        switch (n_classes - 1) {
+            case 1: kvb::rank_split_kernel<K, 1><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p); break;
+            case 2: kvb::rank_split_kernel<K, 2><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p); break;
+            default: kvb::rank_split_kernel<K, 3><<<unsigned(rows), kvb::SEL_THREADS, 0, s>>>(p); break;
+        }
+    };
+    if (key_dtype == KVB_F32) big(float{});
+    else big(double{});
     return launch_check("rank_split_kernel");
 }
 

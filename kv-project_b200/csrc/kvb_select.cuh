@@ -75,7 +75,9 @@ __device__ __forceinline__ void block_scan_flags(uint32_t bits, int* pre, int* t
     __syncthreads();
 }
 
-template <typename K>
+// NB = n_classes - 1 boundaries, a compile-time count so that the per-boundary state and the output
+// pointers stay in registers.
+template <typename K, int NB>
 __global__ void __launch_bounds__(SEL_THREADS) rank_split_kernel(const RankSplitParams p) {
     __shared__ int s_hist[256];
     __shared__ int s_cnt[9 * 32 + 8];
@@ -85,7 +87,7 @@ __global__ void __launch_bounds__(SEL_THREADS) rank_split_kernel(const RankSplit
     __shared__ int64_t s_rem;
     const int64_t row = blockIdx.x;
     const K* keys = static_cast<const K*>(p.keys) + row * p.key_stride;
-    const int nb = p.n_classes - 1;                  // boundaries
+    constexpr int nb = NB;                           // boundaries
     constexpr int NBITS = sizeof(K) * 8;
 
     // ---- radix select of every boundary ----
@@ -147,6 +149,9 @@ __global__ void __launch_bounds__(SEL_THREADS) rank_split_kernel(const RankSplit
     // ---- classify in index order and compact ----
     int64_t eq_seen[SEL_MAX_CLASSES] = {0, 0, 0, 0};
     int64_t cls_off[SEL_MAX_CLASSES] = {0, 0, 0, 0};
+    int64_t* outp[NB + 1];
+#pragma unroll
+    for (int c = 0; c <= NB; ++c) outp[c] = p.out[c] ? p.out[c] + row * p.out_stride[c] : nullptr;
     for (int64_t base = 0; base < p.n; base += blockDim.x) {
         const int64_t i = base + threadIdx.x;
         const bool valid = i < p.n;
@@ -154,11 +159,13 @@ __global__ void __launch_bounds__(SEL_THREADS) rank_split_kernel(const RankSplit
         if (valid && kv != kv) raise_status(KVB_DEV_NAN);
         const uint64_t u = valid ? order_key(kv) : 0;
         uint32_t eqbits = 0;
+#pragma unroll
         for (int k = 0; k < nb; ++k)
             if (valid && u == s_tau[k]) eqbits |= 1u << k;
         int pre[SEL_MAX_CLASSES], tot[SEL_MAX_CLASSES];
         block_scan_flags<SEL_MAX_CLASSES>(eqbits, pre, tot, s_cnt);
         int cls = 0;
+#pragma unroll
         for (int k = 0; k < nb; ++k) {
             bool in;
             if (s_tau[k] == ~0ull && s_need[k] == 0) in = false;               // empty upper part
@@ -166,11 +173,15 @@ __global__ void __launch_bounds__(SEL_THREADS) rank_split_kernel(const RankSplit
             else in = u > s_tau[k] || (u == s_tau[k] && eq_seen[k] + pre[k] < s_need[k]);
             if (!in) ++cls;
         }
+#pragma unroll
         for (int k = 0; k < nb; ++k) eq_seen[k] += tot[k];
         uint32_t cbits = valid ? (1u << cls) : 0u;
         int cpre[SEL_MAX_CLASSES], ctot[SEL_MAX_CLASSES];
         block_scan_flags<SEL_MAX_CLASSES>(cbits, cpre, ctot, s_cnt);
-        if (valid && p.out[cls]) p.out[cls][row * p.out_stride[cls] + cls_off[cls] + cpre[cls]] = i;
+#pragma unroll
+        for (int c = 0; c <= NB; ++c)
+            if (valid && cls == c && outp[c]) outp[c][cls_off[c] + cpre[c]] = i;
+#pragma unroll
         for (int c = 0; c < SEL_MAX_CLASSES; ++c) cls_off[c] += ctot[c];
     }
 }
