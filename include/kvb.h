@@ -297,7 +297,8 @@ kvb_status kvb_lse_merge(const float* parts, int64_t part_stride, const float* l
  * device looks up the array's device address (cudaGetSymbolAddress, with that device current); make
  * that first call before any stream capture.  All calls share the one array and nothing in it needs
  * to start at zero, but calls that overlap on the GPU (concurrent streams, or several host threads)
- * race on it: serialise them.  The current device must be the device of `stream`. */
+ * race on it: serialise them.  The current device must be the device of `stream` (KVB_EINVAL
+ * otherwise). */
 #define KVB_NOALLOC_SCRATCH_BYTES (8u << 20)
 kvb_status kvb_decode_noalloc(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                               const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* stream);

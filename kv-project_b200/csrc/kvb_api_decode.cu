@@ -1,0 +1,551 @@
+// kvb_api_decode.cu - the decode entry points of include/kvb.h (kvb_decode, kvb_decode_lse,
+// kvb_decode_events, kvb_decode_plan, kvb_decode_workspace_size, kvb_lse_merge, kvb_decode_noalloc):
+// validation, the split-K plan, the prologue / merge launches and dispatch to the main kernel.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <type_traits>
+#include <vector>
+
+#include "kvb_decode_host.cuh"
+#include "kvb_decode_tc.cuh"
+
+#ifndef KVB_TOKEN_COST
+#define KVB_TOKEN_COST 60     // fixed per-token decode work in byte-equivalents at d_code 128 (see build_plan)
+#endif
+#ifndef KVB_PDL
+#define KVB_PDL 1             // programmatic dependent launch of the main kernel after the prologue
+#endif
+
+using kvbd::DecodeShape;
+using kvbd::Plan;
+using kvbd::launch_maybe_pdl;
+using kvbd::dispatch_tc;
+
+namespace {
+
+// CTAs of the main kernel: the caller's count, else every SM times the resident CTAs per SM.
+int resolve_decode_ctas(int n_ctas) {
+    if (n_ctas > 0) return std::min(n_ctas, kvb::DEC_MAX_CTAS);
+    return std::min(resolve_ctas(0) * kvb::DEC_CTAS_PER_SM, kvb::DEC_MAX_CTAS);
+}
+
+int tokens_per_chunk(int D, int kbits, int vbits, int k_mode) {
+    return kvb::chunk_tokens(D, kbits, vbits, k_mode == KVB_K_PER_CHANNEL);
+}
+
+// The tensor-core decode (decode_tc) reads caches whose value codes are in the 128-token block
+// layout; it works in 128-token chunks (one MMA tile).
+bool uses_tc(const kvb_cache* c) {
+    return c->n_strata > 0 && c->strata[0].v_layout == KVB_V_BLOCK128;
+}
+int chunk_of(const kvb_cache* c, int s) {
+    return uses_tc(c) ? kvb::TC_T : tokens_per_chunk(c->d_code, c->strata[s].kbits, c->strata[s].vbits, c->k_mode);
+}
+
+kvb_status validate_cache(const kvb_cache* c, DecodeShape& sh, int Hq, int Tq) {
+    if (!c) return fail(KVB_EINVAL, "decode: null cache");
+    if (c->B <= 0 || c->Hkv <= 0 || Hq <= 0 || Hq % c->Hkv || Tq <= 0 || Tq > 16)
+        return fail(KVB_EINVAL, "decode: heads / Tq (need Hq %% Hkv == 0, 1 <= Tq <= 16)");
+    const int rep = Hq / c->Hkv;
+    const int Ra = rep * Tq;
+    if (Ra > 8) return fail(KVB_EUNSUPPORTED, "decode: rep * Tq = %d > 8 query rows per KV head", Ra);
+    sh.R = Ra <= 4 ? 4 : 8;
+    sh.D = c->d_code;
+    sh.kmode = c->k_mode;
+    sh.code = c->code_kind;
+    if (c->n_strata < 0 || c->n_strata > 4) return fail(KVB_EINVAL, "decode: n_strata");
+    if (c->d % 32 || c->d > 256 || c->d <= 0) return fail(KVB_EINVAL, "decode: d");
+    if (c->code_kind == KVB_CODE_MIDRISE) {
+        sh.GK = sh.GV = 1;
+        if (c->k_mode != KVB_K_PER_TOKEN) return fail(KVB_EINVAL, "decode: midrise code is per token");
+    } else {
+        if (c->v_group <= 0 || c->d_code % c->v_group) return fail(KVB_EINVAL, "decode: v_group");
+        sh.GV = c->d_code / c->v_group;
+        if (c->k_mode == KVB_K_PER_TOKEN) {
+            if (c->k_group <= 0 || c->d_code % c->k_group) return fail(KVB_EINVAL, "decode: k_group");
+            sh.GK = c->d_code / c->k_group;
+        } else {
+            sh.GK = 1;
+            if (c->k_group != 16 && c->k_group != 32 && c->k_group != 64 && c->k_group != 128)
+                return fail(KVB_EINVAL, "decode: per-channel k_group must be 16, 32, 64 or 128");
+        }
+    }
+    if (c->lift == nullptr && c->d_code != c->d) return fail(KVB_EINVAL, "decode: d_code != d needs a lift matrix");
+    const bool tc = uses_tc(c);
+    for (int i = 0; i < c->n_strata; ++i) {
+        const kvb_stratum& s = c->strata[i];
+        if (s.v_layout != KVB_V_TOKEN_MAJOR && s.v_layout != KVB_V_BLOCK128)
+            return fail(KVB_EINVAL, "decode: stratum %d v_layout", i);
+        if ((s.v_layout == KVB_V_BLOCK128) != tc)
+            return fail(KVB_EINVAL, "decode: all strata must share one value layout");
+        if (tc) {
+            if (sh.D != 128 || c->k_mode != KVB_K_PER_TOKEN || s.kbits != s.vbits || s.n_alloc % 128)
+                return fail(KVB_EUNSUPPORTED, "decode: block value layout needs d_code 128, per-token keys, equal "
+                            "key / value widths and n_alloc %% 128 == 0");
+            if (sh.GK > 2 || sh.GV > 2)
+                return fail(KVB_EUNSUPPORTED, "decode: block value layout supports at most 2 groups per token");
+        }
+        const bool okb = (s.kbits == s.vbits && (s.kbits == 2 || s.kbits == 4 || s.kbits == 8)) ||
+                         (s.kbits == 4 && s.vbits == 2);
+        if (!okb) return fail(KVB_EUNSUPPORTED, "decode: stratum %d widths (%d, %d)", i, s.kbits, s.vbits);
+        if (sh.D * s.kbits < 128 || sh.D * s.vbits < 128)
+            return fail(KVB_EUNSUPPORTED, "decode: d_code * bits must be >= 128");
+        if (s.n < 0 || s.n_alloc < ((s.n + 15) / 16) * 16 || s.n_alloc % 16)
+            return fail(KVB_EINVAL, "decode: stratum %d n / n_alloc", i);
+        if (c->k_mode == KVB_K_PER_CHANNEL && s.n_alloc % c->k_group)
+            return fail(KVB_EINVAL, "decode: n_alloc must be a multiple of k_group");
+        if (c->k_mode == KVB_K_PER_CHANNEL && tokens_per_chunk(sh.D, s.kbits, s.vbits, c->k_mode) % c->k_group)
+            return fail(KVB_EUNSUPPORTED, "decode: per-channel key groups of %d tokens with %d/%d-bit codes "
+                        "(chunks of %d tokens must hold whole groups)", c->k_group, s.kbits, s.vbits,
+                        tokens_per_chunk(sh.D, s.kbits, s.vbits, c->k_mode));
+        if (s.n > 0 && (!s.kc || !s.vc || !s.kmeta || !s.vmeta)) return fail(KVB_EINVAL, "decode: null stratum pointer");
+        if (!aligned(s.kc, 16) || !aligned(s.vc, 16) || !aligned(s.kmeta, 16) || !aligned(s.vmeta, 16))
+            return fail(KVB_EINVAL, "decode: stratum %d pointers must be 16-byte aligned", i);
+    }
+    if (c->n_exact < 0 || c->n_exact > c->exact_cap || c->n0 < 0 || c->n0 > c->n_exact)
+        return fail(KVB_EINVAL, "decode: exact rows");
+    if (c->n_exact > 0 && (!c->k_exact || !c->v_exact)) return fail(KVB_EINVAL, "decode: null exact rows");
+    if (c->n_exact > 0 && c->exact_dtype != KVB_F16 && c->exact_dtype != KVB_BF16 && c->exact_dtype != KVB_F32)
+        return fail(KVB_EINVAL, "decode: exact dtype");
+    return KVB_OK;
+}
+
+kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
+    const int heads = c->B * c->Hkv;
+    P.n_ctas = n_ctas;
+    P.n_heads = heads;
+    P.tok.assign(4, 0);
+    std::vector<int64_t> nch(c->n_strata), wfull(c->n_strata), wlast(c->n_strata);
+    int64_t chunks_per_head = 0, w_head = 0;
+    for (int s = 0; s < c->n_strata; ++s) {
+        const kvb_stratum& st = c->strata[s];
+        P.tok[s] = chunk_of(c, s);
+        nch[s] = (st.n + P.tok[s] - 1) / P.tok[s];
+        // work per token in byte-equivalents: its code bytes plus a fixed per-token cost (code
+        // extraction, MMAs, softmax).  One-width caches alone give ~139 bytes at d_code 128 (34.3 /
+        // 45.3 / 66.8 ps per token-head at 2 / 4 / 8 bits on B200), but in a mixed cache the
+        // byte-heavy CTAs also compete for DRAM: a sweep of the constant on config 1 (main kernel
+        // 104.5 us at 8, 95.9 at 139, 92.3 at 60, 92.5 at 40) puts the best split near 60.
+        const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + (KVB_TOKEN_COST * c->d_code + 64) / 128;
+        wfull[s] = int64_t(P.tok[s]) * bpt;
+        wlast[s] = (st.n - (nch[s] - 1) * P.tok[s]) * bpt;
+        chunks_per_head += nch[s];
+        w_head += nch[s] ? (nch[s] - 1) * wfull[s] + wlast[s] : 0;
+    }
+    const double W = double(w_head) * heads;
+    P.cta_begin.assign(n_ctas + 1, 0);
+    P.head_begin.assign(heads + 1, 0);
+    P.piece.clear();
+    int cur_cta = 0;
+    int last_key_cta = -1, last_head = -1, last_s = -1;
+    double cum = 0.0;
+    for (int h = 0; h < heads; ++h) {
+        P.head_begin[h] = int(P.piece.size() / 4);
+        for (int s = 0; s < c->n_strata; ++s) {
+            for (int64_t k = 0; k < nch[s]; ++k) {
+                const double w = double(k + 1 == nch[s] ? wlast[s] : wfull[s]);
+                int cta = W > 0 ? int((cum + 0.5 * w) * n_ctas / W) : 0;
+                cta = std::min(std::max(cta, cur_cta), n_ctas - 1);
+                cum += w;
+                if (cta != last_key_cta || h != last_head || s != last_s) {
+                    while (cur_cta < cta) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
+                    P.piece.push_back(h);
+                    P.piece.push_back(s);
+                    P.piece.push_back(int(k));
+                    P.piece.push_back(int(k + 1));
+                    last_key_cta = cta;
+                    last_head = h;
+                    last_s = s;
+                } else {
+                    P.piece.back() = int(k + 1);
+                }
+            }
+        }
+    }
+    while (cur_cta < n_ctas) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
+    P.head_begin[heads] = int(P.piece.size() / 4);
+    P.n_pieces = int(P.piece.size() / 4);
+    return KVB_OK;
+}
+
+
+// Everything build_plan reads.
+struct PlanKey {
+    int v[8 + 4 * 4];
+    int64_t n[4];
+    bool operator==(const PlanKey& o) const {
+        return std::memcmp(v, o.v, sizeof(v)) == 0 && std::memcmp(n, o.n, sizeof(n)) == 0;
+    }
+};
+
+PlanKey plan_key(const kvb_cache* c, int n_ctas) {
+    PlanKey k;
+    std::memset(&k, 0, sizeof(k));
+    k.v[0] = c->B;
+    k.v[1] = c->Hkv;
+    k.v[2] = c->d_code;
+    k.v[3] = c->n_strata;
+    k.v[4] = c->code_kind;
+    k.v[5] = c->k_mode;
+    k.v[6] = c->k_group;
+    k.v[7] = n_ctas;
+    for (int s = 0; s < c->n_strata && s < 4; ++s) {
+        k.v[8 + 4 * s] = c->strata[s].kbits;
+        k.v[9 + 4 * s] = c->strata[s].vbits;
+        k.v[10 + 4 * s] = c->strata[s].v_layout;
+        k.v[11 + 4 * s] = c->v_group;
+        k.n[s] = c->strata[s].n;
+    }
+    return k;
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct WsLayout {
+    size_t qp, part, total;
+    int qp_stride;
+};
+
+WsLayout ws_layout(const kvb_cache* c, const DecodeShape& sh, int n_pieces) {
+    WsLayout L;
+    L.qp_stride = kvb::qp_size(sh.R, sh.D);
+    L.qp = 256;
+    L.part = align256(L.qp + size_t(c->B) * c->Hkv * L.qp_stride * 4);
+    L.total = align256(L.part + size_t(n_pieces) * (2 * sh.R + sh.R * sh.D) * 4);
+    return L;
+}
+
+kvb_status dispatch_main(const DecodeShape& sh, const kvb_cache* c, const Plan& P, kvb::DecodeParams& p,
+                         cudaStream_t s, bool pdl) {
+    using namespace kvb;
+#define KVB_CASE(D_, R_, GK_, GV_, KM_, CK_)                                                           \
+    if (sh.D == D_ && sh.R == R_ && sh.GK == GK_ && sh.GV == GV_ && sh.kmode == KM_ && sh.code == CK_) \
+        return kvbd::run_main<D_, R_, GK_, GV_, KM_, CK_>(c, P, p, s, pdl);
+    // KIVI per-token keys (mixed-precision strata, config 1)
+    KVB_CASE(128, 4, 2, 2, KM_TOKEN, KV_ASYM)
+    KVB_CASE(128, 8, 2, 2, KM_TOKEN, KV_ASYM)
+    KVB_CASE(128, 4, 1, 1, KM_TOKEN, KV_ASYM)
+    KVB_CASE(128, 8, 1, 1, KM_TOKEN, KV_ASYM)
+    // KIVI per-channel keys (configs 0, 2, 4)
+    KVB_CASE(128, 4, 1, 4, KM_CHANNEL, KV_ASYM)
+    KVB_CASE(128, 4, 1, 2, KM_CHANNEL, KV_ASYM)
+    KVB_CASE(128, 4, 1, 1, KM_CHANNEL, KV_ASYM)
+    KVB_CASE(128, 8, 1, 1, KM_CHANNEL, KV_ASYM)
+    KVB_CASE(128, 8, 1, 2, KM_CHANNEL, KV_ASYM)
+    // STRATA / spectral mid-rise codes
+    KVB_CASE(128, 4, 1, 1, KM_TOKEN, KV_MIDRISE)
+    KVB_CASE(128, 8, 1, 1, KM_TOKEN, KV_MIDRISE)
+    KVB_CASE(64, 4, 1, 1, KM_TOKEN, KV_MIDRISE)
+    KVB_CASE(32, 4, 1, 1, KM_TOKEN, KV_MIDRISE)
+    KVB_CASE(32, 8, 1, 1, KM_TOKEN, KV_MIDRISE)
+#undef KVB_CASE
+    return fail(KVB_EUNSUPPORTED, "decode: no kernel for d_code=%d rows=%d key groups=%d value groups=%d mode=%d code=%d",
+                sh.D, sh.R, sh.GK, sh.GV, sh.kmode, sh.code);
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t kvb_decode_plan(const kvb_cache* c, int n_ctas, int32_t* plan_out, int64_t plan_capacity) {
+    if (!c || n_ctas <= 0) return -1;
+    Plan P;
+    build_plan(c, std::min(n_ctas, kvb::DEC_MAX_CTAS), P);
+    const int64_t need = 3 + (P.n_ctas + 1) + 4 * int64_t(P.n_pieces) + (P.n_heads + 1);
+    if (plan_out && plan_capacity >= need) {
+        int64_t o = 0;
+        plan_out[o++] = P.n_ctas;
+        plan_out[o++] = P.n_pieces;
+        plan_out[o++] = P.n_heads;
+        for (int v : P.cta_begin) plan_out[o++] = v;
+        for (int v : P.piece) plan_out[o++] = v;
+        for (int v : P.head_begin) plan_out[o++] = v;
+    }
+    return need;
+}
+
+size_t kvb_decode_workspace_size(const kvb_cache* c, int Hq, int Tq, int n_ctas) {
+    DecodeShape sh{};
+    if (validate_cache(c, sh, Hq, Tq)) return 0;
+    Plan P;
+    build_plan(c, resolve_decode_ctas(n_ctas), P);
+    return ws_layout(c, sh, P.n_pieces).total;
+}
+
+}  // extern "C"
+
+namespace {
+kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                       const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas, void* workspace,
+                       size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end);
+}  // namespace
+
+extern "C" {
+
+kvb_status kvb_decode(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                      const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    return decode_impl(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, nullptr, n_ctas, workspace,
+                       workspace_bytes, stream, nullptr, nullptr);
+}
+
+kvb_status kvb_decode_events(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                             const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* workspace,
+                             size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end) {
+    return decode_impl(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, nullptr, n_ctas, workspace,
+                       workspace_bytes, stream, ev_begin, ev_end);
+}
+
+kvb_status kvb_decode_lse(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                          const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    if (!lse) return fail(KVB_EINVAL, "decode_lse: null lse");
+    if (!aligned(lse, 4)) return fail(KVB_EINVAL, "decode_lse: lse alignment");
+    return decode_impl(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, lse, n_ctas, workspace,
+                       workspace_bytes, stream, nullptr, nullptr);
+}
+
+}  // extern "C"
+
+namespace {
+kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                       const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas, void* workspace,
+                       size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end) {
+    DecodeShape sh{};
+    kvb_status st = validate_cache(c, sh, Hq, Tq);
+    if (st) return st;
+    if (!q || !out || !workspace) return fail(KVB_EINVAL, "decode: null q / out / workspace");
+    if (q_dtype != KVB_F32 && q_dtype != KVB_F16 && q_dtype != KVB_BF16) return fail(KVB_EINVAL, "decode: q dtype");
+    if (out_dtype != KVB_F32 && out_dtype != KVB_F16 && out_dtype != KVB_BF16) return fail(KVB_EINVAL, "decode: out dtype");
+    if (c->n_exact > c->n0 && !qpos) return fail(KVB_EINVAL, "decode: qpos needed for appended exact rows");
+    if (c->n_exact > 0 && c->exact_dtype != q_dtype) return fail(KVB_EINVAL, "decode: exact rows must have q's dtype");
+    if (!aligned(workspace, 256)) return fail(KVB_EINVAL, "decode: workspace must be 256-byte aligned");
+    const int nct = resolve_decode_ctas(n_ctas);
+    // programmatic dependent launch of the main kernel (its first cache copies overlap the prologue),
+    // except when events bracket it (an event between two launches must see the first one complete).
+    // Measured on B200 at config 1: 1.3 % per step; the same for the merge kernel was 2.7 % slower,
+    // and merging in the main kernel's tail (the CTA completing a head) gained nothing.
+    const bool pdl = KVB_PDL && !(ev_begin || ev_end);
+    // The plan depends only on the cache's shape and the CTA count; consecutive calls on caches of
+    // one shape (the layers of a model) reuse it, and the piece table already in the kernel
+    // parameters, instead of rebuilding both on the host every call.
+    PlanKey key = plan_key(c, nct);
+    static thread_local PlanKey plan_key_last;
+    static thread_local Plan plan_last;
+    static thread_local bool plan_valid = false;
+    if (!plan_valid || !(key == plan_key_last)) {
+        plan_last = Plan();
+        build_plan(c, nct, plan_last);
+        plan_key_last = key;
+        plan_valid = true;
+    }
+    const Plan& P = plan_last;
+    if (P.n_pieces > kvb::DEC_MAX_PIECES) return fail(KVB_EUNSUPPORTED, "decode: %d pieces > %d", P.n_pieces, kvb::DEC_MAX_PIECES);
+    for (int i = 0; i < P.n_pieces; ++i)
+        if (P.piece[4 * i + 3] >= kvb::DEC_MAX_CHUNK)
+            return fail(KVB_EUNSUPPORTED, "decode: more than %d chunks in one stratum", kvb::DEC_MAX_CHUNK - 1);
+    if (P.n_heads > kvb::MERGE_MAX_HEADS) return fail(KVB_EUNSUPPORTED, "decode: too many heads");
+    const WsLayout W = ws_layout(c, sh, P.n_pieces);
+    if (workspace_bytes < W.total) return fail(KVB_EINVAL, "decode: workspace %zu < %zu bytes", workspace_bytes, W.total);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* qp = reinterpret_cast<float*>(ws + W.qp);
+    float* part = reinterpret_cast<float*>(ws + W.part);
+    const int rep = Hq / c->Hkv;
+
+    // 1. prologue
+    kvb::PrologueParams pp{q, q_dtype, c->B, c->Hkv, Hq, Tq, rep, rep * Tq, c->d, c->d_code,
+                           c->code_kind == KVB_CODE_MIDRISE ? c->d_code
+                                                            : (c->k_mode == KVB_K_PER_TOKEN ? c->k_group : c->d_code),
+                           scaling, c->qmap, c->mu_k, qp, W.qp_stride};
+    const size_t psm = size_t(sh.R) * (c->d + c->d_code) * 4;
+    const unsigned heads = unsigned(c->B * c->Hkv);
+#define KVB_PRO(T_)                                                                        \
+    if (sh.R == 4) kvb::decode_prologue<T_, 4><<<heads, 128, psm, s>>>(pp);               \
+    else kvb::decode_prologue<T_, 8><<<heads, 128, psm, s>>>(pp);
+    if (q_dtype == KVB_F32) { KVB_PRO(float) }
+    else if (q_dtype == KVB_F16) { KVB_PRO(__half) }
+    else { KVB_PRO(__nv_bfloat16) }
+#undef KVB_PRO
+    if ((st = launch_check("decode_prologue"))) return st;
+
+    // 2. main
+    if (P.n_pieces > 0) {
+        static thread_local kvb::DecodeParams dp;
+        static thread_local PlanKey dp_key;
+        static thread_local bool dp_valid = false;
+        const bool same_plan = dp_valid && dp_key == key;
+        if (!same_plan) std::memset(&dp, 0, sizeof(dp));
+        dp.B = c->B;
+        dp.Hkv = c->Hkv;
+        dp.R_act = rep * Tq;
+        dp.k_group = c->k_group;
+        dp.n_strata = c->n_strata;
+        dp.qp_stride = W.qp_stride;
+        for (int i = 0; i < c->n_strata; ++i) {
+            const kvb_stratum& sd = c->strata[i];
+            dp.st[i] = kvb::StratumDev{sd.kbits, sd.vbits, P.tok[i], 0, sd.n, sd.n_alloc, sd.kc, sd.vc, sd.kmeta, sd.vmeta};
+        }
+        dp.qp = qp;
+        dp.part = part;
+        dp.n_pieces = P.n_pieces;
+        if (!same_plan) {
+            for (int i = 0; i <= P.n_ctas; ++i) dp.cta_begin[i] = P.cta_begin[i];
+            for (int i = 0; i < P.n_pieces; ++i)
+                dp.piece[i] = kvb::pack_piece(P.piece[4 * i], P.piece[4 * i + 1], P.piece[4 * i + 2], P.piece[4 * i + 3]);
+            dp_key = key;
+            dp_valid = true;
+        }
+        // inside a stream capture the events become external event nodes, so they also fire on replay
+        unsigned ev_flags = cudaEventRecordDefault;
+        if (ev_begin || ev_end) {
+            cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+            if ((st = cuda_check(cudaStreamIsCapturing(s, &cs), "capture status"))) return st;
+            if (cs == cudaStreamCaptureStatusActive) ev_flags = cudaEventRecordExternal;
+        }
+        if (ev_begin && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_begin), s, ev_flags),
+                                         "record event")))
+            return st;
+        if ((st = uses_tc(c) ? dispatch_tc(sh, c, P, dp, s) : dispatch_main(sh, c, P, dp, s, pdl))) return st;
+        if (ev_end && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_end), s, ev_flags),
+                                       "record event")))
+            return st;
+    }
+
+    // 3. merge
+    const int Ra = rep * Tq;
+    const size_t msm = size_t(Ra) * (2 * c->d + c->d_code) * 4 + 3 * Ra * 4 + 256 * 4;
+    cudaError_t le;
+    auto launch_merge = [&](auto& mp) -> cudaError_t {
+        std::memset(&mp, 0, sizeof(mp));
+        mp.B = c->B;
+        mp.Hkv = c->Hkv;
+        mp.Hq = Hq;
+        mp.Tq = Tq;
+        mp.rep = rep;
+        mp.R_act = Ra;
+        mp.R = sh.R;
+        mp.d = c->d;
+        mp.d_code = c->d_code;
+        mp.out_dtype = out_dtype == KVB_F32 ? 0 : out_dtype == KVB_F16 ? 1 : 2;
+        mp.q_dtype = q_dtype;
+        mp.exact_dtype = c->exact_dtype;
+        mp.scaling = scaling;
+        mp.part = part;
+        mp.q = q;
+        mp.k_exact = c->k_exact;
+        mp.v_exact = c->v_exact;
+        mp.exact_cap = c->exact_cap;
+        mp.n_exact = c->n_exact;
+        mp.n0 = c->n0;
+        mp.pos0 = c->pos0;
+        for (int t = 0; t < Tq; ++t) mp.qpos[t] = qpos ? qpos[t] : 0;
+        mp.lift = c->lift;
+        mp.mu_v = c->mu_v;
+        mp.out = out;
+        mp.lse = lse;
+        for (int h = 0; h <= P.n_heads; ++h) mp.head_begin[h] = P.head_begin[h];
+        using MP = std::remove_reference_t<decltype(mp)>;
+        constexpr int NH = sizeof(MP::head_begin) / sizeof(int) - 1;
+        if (q_dtype == KVB_F32)
+            return launch_maybe_pdl(kvb::decode_merge<float, float, NH>, dim3(heads), dim3(256), msm, s, false, mp);
+        if (q_dtype == KVB_F16)
+            return launch_maybe_pdl(kvb::decode_merge<__half, __half, NH>, dim3(heads), dim3(256), msm, s, false, mp);
+        return launch_maybe_pdl(kvb::decode_merge<__nv_bfloat16, __nv_bfloat16, NH>, dim3(heads), dim3(256), msm, s,
+                                false, mp);
+    };
+    if (P.n_heads <= kvb::MERGE_SMALL_HEADS) {
+        static thread_local kvb::MergeParams<kvb::MERGE_SMALL_HEADS> mps;
+        le = launch_merge(mps);
+    } else {
+        static thread_local kvb::MergeParams<kvb::MERGE_MAX_HEADS> mpl;
+        le = launch_merge(mpl);
+    }
+    if (le != cudaSuccess) return cuda_check(le, "decode_merge launch");
+    return launch_check("decode_merge");
+}
+}  // namespace
+
+// =============================================================================================
+// Allocation-free decode.  For callers that may not allocate device memory at all (serving engines
+// whose planner owns every byte, allocator-less plugin interfaces), the split-K scratch is a
+// file-scope __device__ array instead of a caller workspace.  Host code may not pass
+// `g_noalloc_scratch` itself to a kernel: on the host
+// that name is only a stand-in symbol, not a device address.  Its real address is looked up once per
+// device (cudaGetSymbolAddress with that device current) and cached here, per device and context.
+// =============================================================================================
+#include <mutex>
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KVB_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+CUcontext g_noalloc_ctx[kMaxDevices] = {};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    }
+    return fn;
+}
+
+// The array's address on the current device.  Cached per device together with the context it was
+// looked up in: after the primary context is reset (cudaDeviceReset) the module is loaded anew, so
+// a changed context means a new lookup.
+kvb_status noalloc_scratch(void** out) {
+    int dev = 0;
+    kvb_status st = cuda_check(cudaGetDevice(&dev), "decode_noalloc: current device");
+    if (st) return st;
+    if (dev < 0 || dev >= kMaxDevices) return fail(KVB_EUNSUPPORTED, "decode_noalloc: device ordinal %d", dev);
+    CUcontext ctx = nullptr;
+    if (CtxGetCurrentFn f = ctx_get_current()) f(&ctx);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev] || g_noalloc_ctx[dev] != ctx) {
+        void* p = nullptr;
+        if ((st = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "decode_noalloc: scratch address")))
+            return st;
+        g_noalloc_addr[dev] = p;
+        g_noalloc_ctx[dev] = ctx;
+    }
+    *out = g_noalloc_addr[dev];
+    return KVB_OK;
+}
+
+}  // namespace
+
+extern "C" kvb_status kvb_decode_noalloc(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                                         const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* stream) {
+    DecodeShape sh{};
+    kvb_status st = validate_cache(c, sh, Hq, Tq);
+    if (st) return st;
+    const size_t need = kvb_decode_workspace_size(c, Hq, Tq, n_ctas);
+    if (need == 0) return fail(KVB_EINVAL, "decode_noalloc: invalid request");
+    if (need > size_t(KVB_NOALLOC_SCRATCH_BYTES))
+        return fail(KVB_EINVAL,
+                    "decode_noalloc: this request needs %zu bytes of scratch, the built-in array holds %u; "
+                    "call kvb_decode with a workspace instead",
+                    need, unsigned(KVB_NOALLOC_SCRATCH_BYTES));
+    // the scratch address is the current device's; a stream of another device would run the kernels
+    // there against this device's memory
+    int cur = 0, sdev = 0;
+    if ((st = cuda_check(cudaGetDevice(&cur), "decode_noalloc: current device"))) return st;
+    if ((st = cuda_check(cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev), "decode_noalloc: stream device")))
+        return st;
+    if (sdev != cur)
+        return fail(KVB_EINVAL, "decode_noalloc: the stream belongs to device %d but device %d is current", sdev, cur);
+    void* scratch = nullptr;
+    if ((st = noalloc_scratch(&scratch))) return st;
+    return kvb_decode_events(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, n_ctas, scratch,
+                             size_t(KVB_NOALLOC_SCRATCH_BYTES), stream, nullptr, nullptr);
+}

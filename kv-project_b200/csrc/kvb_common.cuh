@@ -20,13 +20,14 @@
 namespace kvb {
 
 // One status word per device and library instance; read (and cleared) by kvb_device_status().
-__device__ unsigned g_status;
+// Defined once in kvb_api.cu; every translation unit's kernels reach it through the device link.
+extern __device__ unsigned g_status;
 
 __device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status, bits); }
 
 // Where the first bounded wait gave up: site code (bits 0-7), CTA (bits 8-15), a counter of the
 // waiting role (bits 16-30), bit 31 set.  Read with kvb_device_diag(); 0 when nothing timed out.
-__device__ unsigned g_diag;
+extern __device__ unsigned g_diag;
 __device__ __forceinline__ void note_wait_timeout(unsigned site, unsigned counter) {
     atomicCAS(&g_diag, 0u, 0x80000000u | (site & 0xFFu) | ((blockIdx.x & 0xFFu) << 8) | ((counter & 0x7FFFu) << 16));
 }

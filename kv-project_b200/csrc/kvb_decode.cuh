@@ -34,7 +34,7 @@ constexpr int DEC_THREADS = DEC_CWARPS * 32;
 constexpr int DEC_MAX_STAGES = 4;
 constexpr int DEC_MAX_PIECES = 1536;
 constexpr int DEC_MAX_CTAS = 512;
-constexpr int DEC_SMEM_BUDGET = 227 * 1024;
+constexpr int DEC_SMEM_BUDGET = (DEC_CTAS_PER_SM == 1 ? 227 : 113) * 1024;
 
 // ------------------------------------------------------------------------------------------
 // Parameters
@@ -261,7 +261,7 @@ __device__ __forceinline__ void build_channel_frags(uint8_t* km, const uint8_t* 
 }
 
 template <int D, int R, int GK, int GV, int KMODE, int CODE>
-__global__ void __launch_bounds__(DEC_THREADS, 1) decode_main(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(const __grid_constant__ DecodeParams p) {
     using C = DecCfg<D, R, GK, GV, KMODE, CODE>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -657,54 +657,6 @@ __global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ Merg
         const float L = s_rowL[tid];
         p.lse[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
             L > 0.f ? (s_rowM[tid] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
-    }
-}
-
-// Merge of P attention parts over disjoint token sets (a sequence split across ranks): row r of
-// part k is a normalised output o_k (d floats) with its natural-log mass lse_k; the merged row is
-// sum_k exp(lse_k - M) o_k / sum_k exp(lse_k - M), M = max_k lse_k (the LSE merge of
-// StrataState.attend STRATA_KV.py:1784-1792 applied across parts).  One warp per row.
-struct LseMergeParams {
-    const float* parts;     // part k, row r, channel c at parts[k * part_stride + r * d + c]
-    const float* lse;       // lse[k * lse_stride + r]
-    int64_t part_stride, lse_stride, rows;
-    int n_parts, d, out_dtype;
-    void* out;              // (rows, d)
-};
-
-__global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ LseMergeParams p) {
-    const int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (r >= p.rows) return;
-    float M = -INFINITY;
-    for (int k = 0; k < p.n_parts; ++k) M = fmaxf(M, p.lse[k * p.lse_stride + r]);
-    float wsum = 0.f;
-    for (int c0 = 0; c0 < p.d; c0 += 128) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        float ws = 0.f;
-        for (int k = 0; k < p.n_parts; ++k) {
-            const float l = p.lse[k * p.lse_stride + r];
-            if (l == -INFINITY) continue;
-            const float w = __expf(l - M);
-            ws += w;
-            const float* src = p.parts + k * p.part_stride + r * p.d + c0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int c = lane + 32 * e;
-                if (c0 + c < p.d) acc[e] = fmaf(w, src[c], acc[e]);
-            }
-        }
-        wsum = ws;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int c = c0 + lane + 32 * e;
-            if (c >= p.d) continue;
-            const float v = wsum > 0.f ? acc[e] / wsum : 0.f;
-            const size_t oi = size_t(r) * p.d + c;
-            if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
-            else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
-            else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
-        }
     }
 }
 

@@ -15,7 +15,14 @@
 
 namespace kvb {
 
-constexpr int DEC_CWARPS = 12;                              // warps per CTA (all consume)
+#ifndef KVB_DEC_WARPS
+#define KVB_DEC_WARPS 12
+#endif
+#ifndef KVB_DEC_CTAS_PER_SM
+#define KVB_DEC_CTAS_PER_SM 1
+#endif
+constexpr int DEC_CWARPS = KVB_DEC_WARPS;                   // warps per CTA (all consume)
+constexpr int DEC_CTAS_PER_SM = KVB_DEC_CTAS_PER_SM;        // resident main-kernel CTAs per SM
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr int KV_ASYM = 0, KV_MIDRISE = 1;
 constexpr int KM_TOKEN = 0, KM_CHANNEL = 1;
@@ -115,7 +122,9 @@ struct DecCfg {
 __host__ __device__ constexpr int chunk_tokens(int D, int kbits, int vbits, bool per_channel = false) {
     const int rb = D * kbits / 8 + D * vbits / 8;
     const int unit = DEC_CWARPS * 16;
-    const int m = 49152 / (unit * rb) > 1 ? 49152 / (unit * rb) : 1;
+    const int target = 49152 / DEC_CTAS_PER_SM;
+    const int m0 = target / (unit * rb) > 1 ? target / (unit * rb) : 1;
+    const int m = m0 > 1 ? m0 & ~1 : 1;         // 1 or even: warps take their tiles in pairs
     const int cap = per_channel ? 2 * unit : 4 * unit;
     return unit * m < cap ? unit * m : cap;
 }

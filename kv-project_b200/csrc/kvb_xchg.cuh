@@ -130,4 +130,52 @@ __global__ void __launch_bounds__(256) xchg_merge_kernel(const __grid_constant__
     }
 }
 
+// Merge of P attention parts over disjoint token sets (a sequence split across ranks): row r of
+// part k is a normalised output o_k (d floats) with its natural-log mass lse_k; the merged row is
+// sum_k exp(lse_k - M) o_k / sum_k exp(lse_k - M), M = max_k lse_k (the LSE merge of
+// StrataState.attend STRATA_KV.py:1784-1792 applied across parts).  One warp per row.
+struct LseMergeParams {
+    const float* parts;     // part k, row r, channel c at parts[k * part_stride + r * d + c]
+    const float* lse;       // lse[k * lse_stride + r]
+    int64_t part_stride, lse_stride, rows;
+    int n_parts, d, out_dtype;
+    void* out;              // (rows, d)
+};
+
+__global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ LseMergeParams p) {
+    const int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= p.rows) return;
+    float M = -INFINITY;
+    for (int k = 0; k < p.n_parts; ++k) M = fmaxf(M, p.lse[k * p.lse_stride + r]);
+    float wsum = 0.f;
+    for (int c0 = 0; c0 < p.d; c0 += 128) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float ws = 0.f;
+        for (int k = 0; k < p.n_parts; ++k) {
+            const float l = p.lse[k * p.lse_stride + r];
+            if (l == -INFINITY) continue;
+            const float w = __expf(l - M);
+            ws += w;
+            const float* src = p.parts + k * p.part_stride + r * p.d + c0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int c = lane + 32 * e;
+                if (c0 + c < p.d) acc[e] = fmaf(w, src[c], acc[e]);
+            }
+        }
+        wsum = ws;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int c = c0 + lane + 32 * e;
+            if (c >= p.d) continue;
+            const float v = wsum > 0.f ? acc[e] / wsum : 0.f;
+            const size_t oi = size_t(r) * p.d + c;
+            if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
+            else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
+            else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
+        }
+    }
+}
+
 }  // namespace kvb

@@ -3,7 +3,9 @@
     python -m kvb.build            # from kv-project_b200/, or through __graft_entry__.build()
 
 The library is written next to this file (``kvb/libkvb.so``) so that it travels with the source
-tree; nothing is installed into site-packages and no JIT cache is used.
+tree; nothing is installed into site-packages and no JIT cache is used.  The units of csrc/ are
+compiled in parallel with relocatable device code and device-linked into the one shared library
+(object files under kv-project_b200/_build/, which is not part of the sources).
 """
 
 from __future__ import annotations
@@ -19,14 +21,12 @@ CSRC = PKG.parent / "csrc"
 INCLUDE = PKG.parents[1] / "include"
 LIB = PKG / "libkvb.so"
 
-NVCC_FLAGS = [
-    "-gencode", "arch=compute_100a,code=sm_100a",
-    "-O3", "-lineinfo", "-std=c++17",
-    "--shared", "-Xcompiler", "-fPIC",
-    "-Xptxas", "-v",
-    "--expt-relaxed-constexpr",
-    "-lcudart",
-]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# every translation unit: relocatable device code, so the device status words and the kernels of
+# all units form one device-linked module of libkvb.so
+COMPILE_FLAGS = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC",
+                 "-Xptxas", "-v", "--expt-relaxed-constexpr"]
+LINK_FLAGS = [*ARCH, "-rdc=true", "--shared", "-Xcompiler", "-fPIC", "-lcudart"]
 
 
 def nvcc() -> str:
@@ -37,7 +37,7 @@ def nvcc() -> str:
 
 
 def sources():
-    return [CSRC / "kvb_api.cu"]
+    return sorted(CSRC.glob("*.cu"))
 
 
 def deps():
@@ -51,20 +51,41 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in deps())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and up_to_date():
+def _compile(src: Path, obj: Path, extra) -> subprocess.CompletedProcess:
+    cmd = [nvcc(), *COMPILE_FLAGS, *extra, "-I", str(INCLUDE), "-c", "-o", str(obj), str(src)]
+    return subprocess.run(cmd, capture_output=True, text=True)
+
+
+def build(force: bool = False, verbose: bool = False, extra=(), out: Path | None = None,
+          jobs: int | None = None) -> Path:
+    """Compile every csrc/*.cu (in parallel, `jobs` at a time) and device-link them into `out`
+    (default kvb/libkvb.so).  `extra`: additional nvcc flags for every unit (e.g. -D switches)."""
+    out = Path(out) if out else LIB
+    if not force and out == LIB and up_to_date():
         return LIB
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *NVCC_FLAGS, "-I", str(INCLUDE), "-o", str(tmp), *map(str, sources())]
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    log = res.stdout + res.stderr
+    from concurrent.futures import ThreadPoolExecutor
+    objdir = PKG.parent / "_build" / out.stem
+    objdir.mkdir(parents=True, exist_ok=True)
+    srcs = sources()
+    objs = [objdir / (s.stem + ".o") for s in srcs]
+    jobs = jobs or max(1, min(len(srcs), os.cpu_count() or 1))
+    with ThreadPoolExecutor(jobs) as ex:
+        results = list(ex.map(lambda so: _compile(so[0], so[1], list(extra)), zip(srcs, objs)))
+    log = "".join(f"=== {s.name}\n{r.stdout}{r.stderr}" for s, r in zip(srcs, results))
+    bad = [s.name for s, r in zip(srcs, results) if r.returncode != 0]
+    if bad:
+        (PKG / "build.log").write_text(log)
+        raise RuntimeError(f"nvcc failed on {bad}:\n{log[-6000:]}")
+    tmp = out.with_suffix(".so.tmp")
+    res = subprocess.run([nvcc(), *LINK_FLAGS, "-o", str(tmp), *map(str, objs)], capture_output=True, text=True)
+    log += "=== link\n" + res.stdout + res.stderr
     (PKG / "build.log").write_text(log)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{log[-6000:]}")
-    os.replace(tmp, LIB)
+        raise RuntimeError(f"nvcc link failed ({res.returncode}):\n{log[-6000:]}")
+    os.replace(tmp, out)
     if verbose:
         print(log)
-    return LIB
+    return out
 
 
 if __name__ == "__main__":

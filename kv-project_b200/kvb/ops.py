@@ -390,19 +390,26 @@ def decode_noalloc(cache: PackedCache, q: torch.Tensor, scaling: float, out: tor
                    n_ctas: int = 0) -> torch.Tensor:
     """Decode attention for callers that cannot allocate device memory (an engine whose planner owns
     every byte of the GPU, an allocator-less plugin host):
-    `out` (B, Tq, Hq, d) is supplied by the caller and the split-K scratch is the library's built-in
-    8 MiB device array, so neither this wrapper nor the library allocates.  Calls share that array:
-    do not run two of them concurrently.  Raises ValueError when a request needs more scratch than
-    the array holds (use `decode` with a workspace for those)."""
+    `q` must be contiguous and `out` (B, Tq, Hq, d) is supplied by the caller; the split-K scratch is
+    the library's built-in 8 MiB device array, so neither this wrapper nor the library allocates (a
+    strided `q` is refused rather than copied).  The call runs with q's device current, because the
+    library looks up the array's address on the current device.  Calls share that array: do not run
+    two of them concurrently.  Raises ValueError when a request needs more scratch than the array
+    holds (use `decode` with a workspace for those)."""
     _cuda(q, out)
-    q = q.contiguous()
+    if not q.is_contiguous():
+        raise ValueError("decode_noalloc: q must be contiguous (copying it would allocate)")
     B, Hq, Tq, d = q.shape
     if B != cache.B or d != cache.d or tuple(out.shape) != (B, Tq, Hq, d) or not out.is_contiguous():
         raise ValueError("decode_noalloc: q / out shapes do not match the cache")
+    if out.device != q.device:
+        raise ValueError("decode_noalloc: q and out must be on one device")
     c = cache.struct()
     qp = None if qpos is None else (C.c_int64 * Tq)(*[int(v) for v in qpos])
-    L.check(L.lib().kvb_decode_noalloc(C.byref(c), _ptr(q), dtype_code(q), Hq, Tq, C.c_float(scaling), qp, _ptr(out),
-                                       dtype_code(out), n_ctas, C.c_void_p(_stream(q.device))), "kvb_decode_noalloc")
+    with torch.cuda.device(q.device):
+        L.check(L.lib().kvb_decode_noalloc(C.byref(c), _ptr(q), dtype_code(q), Hq, Tq, C.c_float(scaling), qp,
+                                           _ptr(out), dtype_code(out), n_ctas, C.c_void_p(_stream(q.device))),
+                "kvb_decode_noalloc")
     return out
 
 
