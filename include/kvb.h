@@ -122,6 +122,19 @@ kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, 
                             int64_t nq, int64_t T, int64_t d, float scaling, int64_t n_cand, int pool,
                             float* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* SnapKV scores at the compression horizon, the reference's own mode (snapkv_scores
+ * STRATA_KV.py:932-954): q (B, Hq, w, d) holds the queries of the last w context positions H - w ..
+ * H - 1 (the observation window), k (B, Hkv, H, d) the context keys.  Window query i sees keys
+ * j <= H - w + i (the causal triu mask of :946); its softmax runs over every key it sees, window
+ * keys included; out (B, Hkv, H - w) float32 = the mean over the window queries and the group's
+ * query heads of those probabilities for the candidate columns j < H - w, avg_pool1d(pool) as in
+ * kvb_query_scores.  The window's own columns (the reference pads them with max + 1 so they are
+ * always kept) are not written: the caller keeps the window.  Same dtypes, limits (rep * w <= 256)
+ * and workspace (kvb_scores_workspace_size(B, Hkv, H - w)) as kvb_query_scores. */
+kvb_status kvb_snapkv_scores(const void* q, const void* k, int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                             int64_t w, int64_t H, int64_t d, float scaling, int pool, float* out, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------------------ *
  * K4: spectral code.  Replaces the basis projection of spectral_side (QUASAR_KV.py:1354-1382, with a
  * fixed per-head orthonormal basis) followed by the per-token mid-rise code of strata_quantize
@@ -303,8 +316,11 @@ kvb_status kvb_lse_merge(const float* parts, int64_t part_stride, const float* l
 kvb_status kvb_decode_noalloc(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                               const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* stream);
 
-/* Build the split-K plan (pure host computation, no CUDA calls): piece table for n_ctas CTAs.
- * Exposed for tests; kvb_decode builds and uploads it inside its workspace. */
+/* Build the split-K plan (pure host computation, no CUDA calls) for n_ctas CTAs.  plan_out receives
+ * [n_ctas, n_pieces, n_heads, cta_begin[n_ctas + 1], n_pieces x (head, stratum, first chunk, end
+ * chunk, slot), head_begin[n_heads + 1]]: pieces in CTA order, each with the slot of its partial;
+ * slots are head-major and head_begin indexes them.  Returns the number of int32 needed (the table
+ * is written only when plan_capacity suffices).  Exposed for tests; kvb_decode builds it itself. */
 int64_t kvb_decode_plan(const kvb_cache* c, int n_ctas, int32_t* plan_out, int64_t plan_capacity);
 
 #ifdef __cplusplus

@@ -82,7 +82,74 @@ EncodeTiledFn encode_tiled() {
 
 }  // namespace kvbh
 
+// Both score entry points (kvb_query_scores, kvb_snapkv_scores): two passes of scores_kernel + the
+// per-row log-sum-exp in between, optional pooling.
+static kvb_status query_scores_impl(const void* q, const void* k, int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                                    int64_t nq, int64_t T, int64_t d, float scaling, int64_t n_cand, int pool,
+                                    float* out, void* workspace, size_t workspace_bytes, void* stream, int causal) {
+    if (!q || !k || !out || !workspace) return fail(KVB_EINVAL, "query_scores: null pointer");
+    if (dtype != KVB_F16 && dtype != KVB_BF16) return fail(KVB_EINVAL, "query_scores: dtype must be f16 or bf16");
+    if (B <= 0 || Hkv <= 0 || Hq % Hkv || nq <= 0 || T <= 0 || n_cand <= 0 || n_cand > T)
+        return fail(KVB_EINVAL, "query_scores: sizes");
+    if ((Hq / Hkv) * nq > kvb::SC_ROWS) return fail(KVB_EUNSUPPORTED, "query_scores: rep * nq > 256");
+    if (d != 64 && d != 128) return fail(KVB_EUNSUPPORTED, "query_scores: d must be 64 or 128");
+    if (pool < 0 || (pool > 1 && pool % 2 == 0)) return fail(KVB_EINVAL, "query_scores: pool must be odd");
+    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(workspace, 256)) return fail(KVB_EINVAL, "query_scores: alignment");
+    if (workspace_bytes < kvb_scores_workspace_size(B, Hkv, n_cand)) return fail(KVB_EINVAL, "query_scores: workspace");
+    const size_t heads = size_t(B) * Hkv;
+    auto a = [](size_t x) { return (x + 255) / 256 * 256; };
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    kvb::ScoreParams p{};
+    p.q = q;
+    p.k = k;
+    p.B = B;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.nq = nq;
+    p.T = T;
+    p.d = d;
+    p.n_cand = n_cand;
+    p.rep = int(Hq / Hkv);
+    p.rows = int(p.rep * nq);
+    p.lam = scaling * kvb::LOG2E;
+    p.part = reinterpret_cast<float*>(ws);
+    p.lse = reinterpret_cast<float*>(ws + a(heads * kvb::SC_SPLIT * kvb::SC_ROWS * 2 * 4));
+    float* tmp = reinterpret_cast<float*>(ws + a(heads * kvb::SC_SPLIT * kvb::SC_ROWS * 2 * 4) + a(heads * kvb::SC_ROWS * 4));
+    p.out = pool > 1 ? tmp : out;
+    p.causal = causal;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    dim3 grid(kvb::SC_SPLIT, unsigned(heads));
+    for (int pass = 1; pass <= 2; ++pass) {
+        p.pass = pass;
+        auto launch = [&](auto kernel, int sm) {
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+            kernel<<<grid, 256, sm, s>>>(p);
+        };
+        if (dtype == KVB_BF16) {
+            if (d == 128) launch(kvb::scores_kernel<__nv_bfloat16, 128>, kvb::sc_smem_bytes<128>());
+            else launch(kvb::scores_kernel<__nv_bfloat16, 64>, kvb::sc_smem_bytes<64>());
+        } else {
+            if (d == 128) launch(kvb::scores_kernel<__half, 128>, kvb::sc_smem_bytes<128>());
+            else launch(kvb::scores_kernel<__half, 64>, kvb::sc_smem_bytes<64>());
+        }
+        kvb_status st = launch_check("scores_kernel");
+        if (st) return st;
+        if (pass == 1) {
+            kvb::scores_lse_kernel<<<unsigned(heads), kvb::SC_ROWS, 0, s>>>(p);
+            if ((st = launch_check("scores_lse_kernel"))) return st;
+        }
+    }
+    if (pool > 1) {
+        const int64_t nthreads = int64_t(heads) * n_cand;
+        kvb::scores_pool_kernel<<<unsigned((nthreads + 255) / 256), 256, 0, s>>>(tmp, out, int64_t(heads), n_cand, pool);
+        return launch_check("scores_pool_kernel");
+    }
+    return KVB_OK;
+}
+
 extern "C" {
+
+
 
 const char* kvb_last_error(void) { return g_last_error.c_str(); }
 int kvb_version(void) { return KVB_VERSION; }
@@ -345,63 +412,16 @@ size_t kvb_scores_workspace_size(int64_t B, int64_t Hkv, int64_t n_cand) {
 kvb_status kvb_query_scores(const void* q, const void* k, int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t nq,
                             int64_t T, int64_t d, float scaling, int64_t n_cand, int pool, float* out, void* workspace,
                             size_t workspace_bytes, void* stream) {
-    if (!q || !k || !out || !workspace) return fail(KVB_EINVAL, "query_scores: null pointer");
-    if (dtype != KVB_F16 && dtype != KVB_BF16) return fail(KVB_EINVAL, "query_scores: dtype must be f16 or bf16");
-    if (B <= 0 || Hkv <= 0 || Hq % Hkv || nq <= 0 || T <= 0 || n_cand <= 0 || n_cand > T)
-        return fail(KVB_EINVAL, "query_scores: sizes");
-    if ((Hq / Hkv) * nq > kvb::SC_ROWS) return fail(KVB_EUNSUPPORTED, "query_scores: rep * nq > 256");
-    if (d != 64 && d != 128) return fail(KVB_EUNSUPPORTED, "query_scores: d must be 64 or 128");
-    if (pool < 0 || (pool > 1 && pool % 2 == 0)) return fail(KVB_EINVAL, "query_scores: pool must be odd");
-    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(workspace, 256)) return fail(KVB_EINVAL, "query_scores: alignment");
-    if (workspace_bytes < kvb_scores_workspace_size(B, Hkv, n_cand)) return fail(KVB_EINVAL, "query_scores: workspace");
-    const size_t heads = size_t(B) * Hkv;
-    auto a = [](size_t x) { return (x + 255) / 256 * 256; };
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    kvb::ScoreParams p{};
-    p.q = q;
-    p.k = k;
-    p.B = B;
-    p.Hq = Hq;
-    p.Hkv = Hkv;
-    p.nq = nq;
-    p.T = T;
-    p.d = d;
-    p.n_cand = n_cand;
-    p.rep = int(Hq / Hkv);
-    p.rows = int(p.rep * nq);
-    p.lam = scaling * kvb::LOG2E;
-    p.part = reinterpret_cast<float*>(ws);
-    p.lse = reinterpret_cast<float*>(ws + a(heads * kvb::SC_SPLIT * kvb::SC_ROWS * 2 * 4));
-    float* tmp = reinterpret_cast<float*>(ws + a(heads * kvb::SC_SPLIT * kvb::SC_ROWS * 2 * 4) + a(heads * kvb::SC_ROWS * 4));
-    p.out = pool > 1 ? tmp : out;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    dim3 grid(kvb::SC_SPLIT, unsigned(heads));
-    for (int pass = 1; pass <= 2; ++pass) {
-        p.pass = pass;
-        auto launch = [&](auto kernel, int sm) {
-            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-            kernel<<<grid, 256, sm, s>>>(p);
-        };
-        if (dtype == KVB_BF16) {
-            if (d == 128) launch(kvb::scores_kernel<__nv_bfloat16, 128>, kvb::sc_smem_bytes<128>());
-            else launch(kvb::scores_kernel<__nv_bfloat16, 64>, kvb::sc_smem_bytes<64>());
-        } else {
-            if (d == 128) launch(kvb::scores_kernel<__half, 128>, kvb::sc_smem_bytes<128>());
-            else launch(kvb::scores_kernel<__half, 64>, kvb::sc_smem_bytes<64>());
-        }
-        kvb_status st = launch_check("scores_kernel");
-        if (st) return st;
-        if (pass == 1) {
-            kvb::scores_lse_kernel<<<unsigned(heads), kvb::SC_ROWS, 0, s>>>(p);
-            if ((st = launch_check("scores_lse_kernel"))) return st;
-        }
-    }
-    if (pool > 1) {
-        const int64_t nthreads = int64_t(heads) * n_cand;
-        kvb::scores_pool_kernel<<<unsigned((nthreads + 255) / 256), 256, 0, s>>>(tmp, out, int64_t(heads), n_cand, pool);
-        return launch_check("scores_pool_kernel");
-    }
-    return KVB_OK;
+    return query_scores_impl(q, k, dtype, B, Hq, Hkv, nq, T, d, scaling, n_cand, pool, out, workspace, workspace_bytes,
+                             stream, 0);
+}
+
+kvb_status kvb_snapkv_scores(const void* q, const void* k, int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t w,
+                             int64_t H, int64_t d, float scaling, int pool, float* out, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    if (w <= 0 || w >= H) return fail(KVB_EINVAL, "snapkv_scores: need 0 < window < H");
+    return query_scores_impl(q, k, dtype, B, Hq, Hkv, w, H, d, scaling, H - w, pool, out, workspace, workspace_bytes,
+                             stream, 1);
 }
 
 }  // extern "C"

@@ -12,7 +12,10 @@
 #include "kvb_decode_tc.cuh"
 
 #ifndef KVB_TOKEN_COST
-#define KVB_TOKEN_COST 60     // fixed per-token decode work in byte-equivalents at d_code 128 (see build_plan)
+#define KVB_TOKEN_COST 135    // fixed per-token decode work in byte-equivalents at d_code 128 (see build_plan)
+#endif
+#ifndef KVB_PLAN_HEAD_MAJOR
+#define KVB_PLAN_HEAD_MAJOR 0 // 1: deal chunks head by head (every CTA runs all widths of its heads)
 #endif
 #ifndef KVB_PDL
 #define KVB_PDL 1             // programmatic dependent launch of the main kernel after the prologue
@@ -118,55 +121,75 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
     P.n_heads = heads;
     P.tok.assign(4, 0);
     std::vector<int64_t> nch(c->n_strata), wfull(c->n_strata), wlast(c->n_strata);
-    int64_t chunks_per_head = 0, w_head = 0;
+    double W = 0.0;
     for (int s = 0; s < c->n_strata; ++s) {
         const kvb_stratum& st = c->strata[s];
         P.tok[s] = chunk_of(c, s);
         nch[s] = (st.n + P.tok[s] - 1) / P.tok[s];
         // work per token in byte-equivalents: its code bytes plus a fixed per-token cost (code
-        // extraction, MMAs, softmax).  One-width caches alone give ~139 bytes at d_code 128 (34.3 /
-        // 45.3 / 66.8 ps per token-head at 2 / 4 / 8 bits on B200), but in a mixed cache the
-        // byte-heavy CTAs also compete for DRAM: a sweep of the constant on config 1 (main kernel
-        // 104.5 us at 8, 95.9 at 139, 92.3 at 60, 92.5 at 40) puts the best split near 60.
+        // extraction, MMAs, softmax).  One-width caches on B200 take 4.99 / 6.58 / 9.61 ns x SM per
+        // token-head at 2 / 4 / 8 bits (d_code 128, KIVI groups of 64: 80 / 144 / 272 bytes), a
+        // straight line of slope 1 through bytes + ~130, and with the stratum-major order below
+        // most CTAs run one width, as in those measurements.
         const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + (KVB_TOKEN_COST * c->d_code + 64) / 128;
         wfull[s] = int64_t(P.tok[s]) * bpt;
         wlast[s] = (st.n - (nch[s] - 1) * P.tok[s]) * bpt;
-        chunks_per_head += nch[s];
-        w_head += nch[s] ? (nch[s] - 1) * wfull[s] + wlast[s] : 0;
+        W += double(nch[s] ? (nch[s] - 1) * wfull[s] + wlast[s] : 0) * heads;
     }
-    const double W = double(w_head) * heads;
     P.cta_begin.assign(n_ctas + 1, 0);
     P.head_begin.assign(heads + 1, 0);
     P.piece.clear();
+    P.slot.clear();
     int cur_cta = 0;
     int last_key_cta = -1, last_head = -1, last_s = -1;
     double cum = 0.0;
-    for (int h = 0; h < heads; ++h) {
-        P.head_begin[h] = int(P.piece.size() / 4);
-        for (int s = 0; s < c->n_strata; ++s) {
-            for (int64_t k = 0; k < nch[s]; ++k) {
-                const double w = double(k + 1 == nch[s] ? wlast[s] : wfull[s]);
-                int cta = W > 0 ? int((cum + 0.5 * w) * n_ctas / W) : 0;
-                cta = std::min(std::max(cta, cur_cta), n_ctas - 1);
-                cum += w;
-                if (cta != last_key_cta || h != last_head || s != last_s) {
-                    while (cur_cta < cta) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
-                    P.piece.push_back(h);
-                    P.piece.push_back(s);
-                    P.piece.push_back(int(k));
-                    P.piece.push_back(int(k + 1));
-                    last_key_cta = cta;
-                    last_head = h;
-                    last_s = s;
-                } else {
-                    P.piece.back() = int(k + 1);
-                }
+    // Chunks are dealt to CTAs in order, contiguous runs of equal work.  Stratum-major order (every
+    // head's 8-bit chunks, then every head's 4-bit chunks, ...) gives most CTAs a single code width:
+    // one inner loop in the instruction cache, one ring geometry, no width switches mid-CTA.
+    auto visit = [&](int h, int s) {
+        for (int64_t k = 0; k < nch[s]; ++k) {
+            const double w = double(k + 1 == nch[s] ? wlast[s] : wfull[s]);
+            int cta = W > 0 ? int((cum + 0.5 * w) * n_ctas / W) : 0;
+            cta = std::min(std::max(cta, cur_cta), n_ctas - 1);
+            cum += w;
+            if (cta != last_key_cta || h != last_head || s != last_s) {
+                while (cur_cta < cta) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
+                P.piece.push_back(h);
+                P.piece.push_back(s);
+                P.piece.push_back(int(k));
+                P.piece.push_back(int(k + 1));
+                last_key_cta = cta;
+                last_head = h;
+                last_s = s;
+            } else {
+                P.piece.back() = int(k + 1);
             }
         }
-    }
+    };
+#if KVB_PLAN_HEAD_MAJOR
+    for (int h = 0; h < heads; ++h)
+        for (int s = 0; s < c->n_strata; ++s) visit(h, s);
+#else
+    for (int s = 0; s < c->n_strata; ++s)
+        for (int h = 0; h < heads; ++h) visit(h, s);
+#endif
     while (cur_cta < n_ctas) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
-    P.head_begin[heads] = int(P.piece.size() / 4);
     P.n_pieces = int(P.piece.size() / 4);
+    // partial slots: pieces ordered by (head, stratum, first chunk), so a head's partials are
+    // contiguous for the merge kernel
+    std::vector<int> order(P.n_pieces);
+    for (int i = 0; i < P.n_pieces; ++i) order[i] = i;
+    std::sort(order.begin(), order.end(), [&](int a, int b) {
+        for (int f = 0; f < 3; ++f)
+            if (P.piece[4 * a + f] != P.piece[4 * b + f]) return P.piece[4 * a + f] < P.piece[4 * b + f];
+        return false;
+    });
+    P.slot.assign(P.n_pieces, 0);
+    for (int i = 0; i < P.n_pieces; ++i) P.slot[order[i]] = i;
+    for (int i = 0, h = 0; h <= heads; ++h) {
+        while (i < P.n_pieces && P.piece[4 * order[i]] < h) ++i;
+        P.head_begin[h] = i;
+    }
     return KVB_OK;
 }
 
@@ -253,14 +276,17 @@ int64_t kvb_decode_plan(const kvb_cache* c, int n_ctas, int32_t* plan_out, int64
     if (!c || n_ctas <= 0) return -1;
     Plan P;
     build_plan(c, std::min(n_ctas, kvb::DEC_MAX_CTAS), P);
-    const int64_t need = 3 + (P.n_ctas + 1) + 4 * int64_t(P.n_pieces) + (P.n_heads + 1);
+    const int64_t need = 3 + (P.n_ctas + 1) + 5 * int64_t(P.n_pieces) + (P.n_heads + 1);
     if (plan_out && plan_capacity >= need) {
         int64_t o = 0;
         plan_out[o++] = P.n_ctas;
         plan_out[o++] = P.n_pieces;
         plan_out[o++] = P.n_heads;
         for (int v : P.cta_begin) plan_out[o++] = v;
-        for (int v : P.piece) plan_out[o++] = v;
+        for (int i = 0; i < P.n_pieces; ++i) {
+            for (int f = 0; f < 4; ++f) plan_out[o++] = P.piece[4 * i + f];
+            plan_out[o++] = P.slot[i];
+        }
         for (int v : P.head_begin) plan_out[o++] = v;
     }
     return need;
@@ -394,7 +420,8 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
         if (!same_plan) {
             for (int i = 0; i <= P.n_ctas; ++i) dp.cta_begin[i] = P.cta_begin[i];
             for (int i = 0; i < P.n_pieces; ++i)
-                dp.piece[i] = kvb::pack_piece(P.piece[4 * i], P.piece[4 * i + 1], P.piece[4 * i + 2], P.piece[4 * i + 3]);
+                dp.piece[i] = kvb::pack_piece(P.piece[4 * i], P.piece[4 * i + 1], P.piece[4 * i + 2], P.piece[4 * i + 3],
+                                              P.slot[i]);
             dp_key = key;
             dp_valid = true;
         }

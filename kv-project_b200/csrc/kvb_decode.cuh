@@ -35,12 +35,15 @@ constexpr int DEC_MAX_STAGES = 4;
 constexpr int DEC_MAX_PIECES = 1536;
 constexpr int DEC_MAX_CTAS = 512;
 constexpr int DEC_SMEM_BUDGET = (DEC_CTAS_PER_SM == 1 ? 227 : 113) * 1024;
+// End-of-piece merge buffer: per-warp row maxima and sums, and DEC_RED_SLOTS slots of R x D partial
+// accumulators (with fewer slots than warps, the warps past the slots add into them in a second phase).
+__host__ __device__ constexpr int dec_red_bytes(int R, int D) { return (2 * DEC_CWARPS * R + DEC_RED_SLOTS * R * D) * 4; }
 
 // ------------------------------------------------------------------------------------------
 // Parameters
 // ------------------------------------------------------------------------------------------
 struct StratumDev {
-    int kbits, vbits, tok, pad;            // tok: tokens per chunk
+    int kbits, vbits, tok, stage_bytes;    // tok: tokens per chunk; stage_bytes: one chunk's stage (x128)
     int64_t n, n_alloc;
     const uint8_t* kc;
     const uint8_t* vc;
@@ -60,7 +63,7 @@ struct PrologueParams {
 
 struct DecodeParams {
     int B, Hkv, R_act, k_group, n_strata;
-    int stage_bytes, nstage, qp_stride;
+    int ring_bytes, qp_stride;             // ring_bytes: shared memory for the stage ring of every CTA
     StratumDev st[4];
     const float* qp;
     float* part;            // per piece: m2[R] | l[R] | acc[R][D]
@@ -69,15 +72,18 @@ struct DecodeParams {
     int2 piece[DEC_MAX_PIECES];            // packed (head, stratum | chunk_lo << 2 | chunk_hi << 17)
 };
 
-// A piece (head, stratum, chunk range [lo, hi)) in 8 bytes: the piece table is most of the main
-// kernel's parameter block, which is copied on every launch.  Chunk indices stay below 2^15.
+// A piece (head, stratum, chunk range [lo, hi)) and the slot of its split-K partial in 8 bytes: the
+// piece table is most of the main kernel's parameter block, which is copied on every launch.  Heads
+// and slots stay below 2^16, chunk indices below 2^15.  Pieces are listed in CTA order; their
+// partials are stored by slot, in head order, so each head's partials are contiguous for the merge.
 constexpr int DEC_MAX_CHUNK = 1 << 15;
-__host__ __device__ __forceinline__ int2 pack_piece(int head, int stratum, int lo, int hi) {
-    return make_int2(head, stratum | (lo << 2) | (hi << 17));
+__host__ __device__ __forceinline__ int2 pack_piece(int head, int stratum, int lo, int hi, int slot) {
+    return make_int2(head | (slot << 16), stratum | (lo << 2) | (hi << 17));
 }
 __host__ __device__ __forceinline__ int4 unpack_piece(int2 v) {
-    return make_int4(v.x, v.y & 3, (v.y >> 2) & 0x7FFF, (v.y >> 17) & 0x7FFF);
+    return make_int4(v.x & 0xFFFF, v.y & 3, (v.y >> 2) & 0x7FFF, (v.y >> 17) & 0x7FFF);
 }
+__host__ __device__ __forceinline__ int piece_slot(int2 v) { return int(unsigned(v.x) >> 16); }
 
 // ------------------------------------------------------------------------------------------
 // 1. prologue: grid (B * Hkv), block 128
@@ -267,19 +273,24 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     int* rel = reinterpret_cast<int*>(full + DEC_MAX_STAGES);      // release counters per stage
     float* red = reinterpret_cast<float*>(smem + 128);
-    const int red_bytes = (2 * DEC_CWARPS * R + DEC_CWARPS * R * D) * 4;
+    constexpr int red_bytes = dec_red_bytes(R, D);
     uint8_t* stages = smem + 128 + ((red_bytes + 127) / 128) * 128;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pc0 = p.cta_begin[blockIdx.x], pc1 = p.cta_begin[blockIdx.x + 1];
+    // This CTA's ring: as many stages of its largest chunk as fit (a CTA whose pieces are all 8-bit
+    // chunks keeps more bytes in flight than one with 2-bit chunks of more tokens).
+    int sb = 128;
+    for (int pi = pc0; pi < pc1; ++pi) sb = max(sb, p.st[unpack_piece(p.piece[pi]).y].stage_bytes);
+    const int nstage = min(DEC_MAX_STAGES, p.ring_bytes / sb);
     if (threadIdx.x == 0) {
-        for (int s = 0; s < p.nstage; ++s) {
+        for (int s = 0; s < DEC_MAX_STAGES; ++s) {
             mbar_init(&full[s], 1);
             rel[s] = 0;
         }
         fence_mbar_init();
     }
     __syncthreads();
-    const int pc0 = p.cta_begin[blockIdx.x], pc1 = p.cta_begin[blockIdx.x + 1];
 
     // Fill stage (k % nstage) with chunk k of this CTA's chunk sequence (whole warp: per-channel
     // key fragments are computed by all lanes; lane 0 issues the bulk copies).
@@ -301,12 +312,12 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
             const float* qp = p.qp + size_t(head) * p.qp_stride;
             const StageLay L = stage_lay<D, R, GK, GV, KMODE, CODE>(sd.kbits, sd.vbits, sd.tok, p.k_group);
             const int rbk = D * sd.kbits / 8, rbv = D * sd.vbits / 8;
-            const int s = k % p.nstage;
+            const int s = k % nstage;
             {
                 const int64_t tok0 = int64_t(ch) * sd.tok;
                 const int ntok = int(imin64(sd.tok, sd.n - tok0));
                 const int rows = (ntok + 15) & ~15;
-                uint8_t* st = stages + size_t(s) * p.stage_bytes;
+                uint8_t* st = stages + size_t(s) * sb;
                 const int64_t row0 = int64_t(head) * sd.n_alloc + tok0;
                 int bytes = rows * (rbk + rbv);
                 int kmb = 0, vmb;
@@ -340,7 +351,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
         }
     };
     if (warp == 0)
-        for (int k = 0; k < p.nstage; ++k) fill(uint32_t(k));
+        for (int k = 0; k < nstage; ++k) fill(uint32_t(k));
     // Programmatic dependent launch (when the host enables it): the first bulk copies above (the
     // cache does not depend on the prologue) run while the prologue finishes; its query prep is
     // read only after this wait (a no-op in a plain launch).
@@ -353,7 +364,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
         const int4 pc = unpack_piece(p.piece[pi]);
         const StratumDev& sd = p.st[pc.y];
         const float* qp = p.qp + size_t(pc.x) * p.qp_stride;
-        float* part = p.part + size_t(pi) * (2 * R + R * D);
+        float* part = p.part + size_t(piece_slot(p.piece[pi])) * (2 * R + R * D);
         bool ok = true;
         auto body = [&](auto kbc, auto vbc) {
             constexpr int KB = decltype(kbc)::value, VB = decltype(vbc)::value;
@@ -388,8 +399,8 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
 #pragma unroll
                     for (int e = 0; e < 4; ++e) S.acc[jv][mt][e] = 0.f;
             for (int ch = pc.z; ch < pc.w; ++ch) {
-                const int s = it % p.nstage;
-                const uint32_t ph = (it / p.nstage) & 1;
+                const int s = it % nstage;
+                const uint32_t ph = (it / nstage) & 1;
                 // after a timeout, keep polling briefly (a fill may still land) but skip the compute
                 if (!mbar_wait(&full[s], ph, ok ? 2000000000ull : 1000000ull)) ok = false;
                 if constexpr (KMODE == KM_CHANNEL) {
@@ -398,7 +409,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
                         const int64_t tok0 = int64_t(ch) * sd.tok;
                         const int ntok = int(imin64(sd.tok, sd.n - tok0));
                         const int ng = (ntok + p.k_group - 1) / p.k_group;
-                        uint8_t* st = stages + s * p.stage_bytes;
+                        uint8_t* st = stages + s * sb;
                         build_channel_frags<D, R, GK, GV, KMODE, CODE, KB>(st + L.km, st + L.kr, ng, red, warp, lane);
                     }
                     __syncthreads();
@@ -407,7 +418,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
                     const int64_t tok0 = int64_t(ch) * sd.tok;
                     const int ntok = int(imin64(sd.tok, sd.n - tok0));
                     const int ntiles = (ntok + 15) >> 4;
-                    const uint8_t* st = stages + s * p.stage_bytes;
+                    const uint8_t* st = stages + s * sb;
                     auto cfp = [&](int tl) -> const uint8_t* {
                         if constexpr (KMODE == KM_CHANNEL) return st + L.km + ((tl * 16) / p.k_group) * C::FRAG_BYTES;
                         else return nullptr;
@@ -444,7 +455,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
                     }
                 }
                 last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) fill(it + uint32_t(p.nstage));
+                if (last) fill(it + uint32_t(nstage));
                 ++it;
             }
             TL::flush(S, red, part, warp, lane);
@@ -469,8 +480,8 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
     // Every issued fill has been waited for above; if a wait gave up, give late copies a bounded
     // chance to land before the CTA's shared memory is released.
     if (threadIdx.x == 0 && it > 0) {
-        const uint32_t first = it > uint32_t(p.nstage) ? it - p.nstage : 0;
-        for (uint32_t k = first; k < it; ++k) mbar_wait(&full[k % p.nstage], (k / p.nstage) & 1, 10000000ull);
+        const uint32_t first = it > uint32_t(nstage) ? it - nstage : 0;
+        for (uint32_t k = first; k < it; ++k) mbar_wait(&full[k % nstage], (k / nstage) & 1, 10000000ull);
     }
 }
 

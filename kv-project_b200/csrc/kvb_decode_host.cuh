@@ -22,7 +22,8 @@ struct DecodeShape {
 struct Plan {
     int n_ctas = 0, n_pieces = 0, n_heads = 0;
     std::vector<int> cta_begin, head_begin;
-    std::vector<int> piece;   // 4 per piece
+    std::vector<int> piece;   // 4 per piece (head, stratum, first chunk, end chunk), in CTA order
+    std::vector<int> slot;    // per piece: index of its partial (head-major order; head_begin indexes slots)
     std::vector<int> tok;     // tokens per chunk per stratum
 };
 

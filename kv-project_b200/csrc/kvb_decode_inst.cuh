@@ -16,26 +16,20 @@ kvb_status launch_main(const kvb::DecodeParams& p, int n_ctas, size_t smem, cuda
 }
 
 template <int D, int R, int GK, int GV, int KM, int CK>
-int stage_bytes_for(const kvb_cache* c, const Plan& P) {
-    int mx = 0;
-    for (int s = 0; s < c->n_strata; ++s) {
-        const kvb::StageLay L =
-            kvb::stage_lay<D, R, GK, GV, KM, CK>(c->strata[s].kbits, c->strata[s].vbits, P.tok[s], c->k_group);
-        mx = std::max(mx, L.end);
-    }
-    return (mx + 127) / 128 * 128;
-}
-
-template <int D, int R, int GK, int GV, int KM, int CK>
 kvb_status run_main(const kvb_cache* c, const Plan& P, kvb::DecodeParams& p, cudaStream_t s, bool pdl) {
-    const int sb = std::max(128, stage_bytes_for<D, R, GK, GV, KM, CK>(c, P));
-    const int red = (2 * kvb::DEC_CWARPS * R + kvb::DEC_CWARPS * R * D) * 4;
-    const int fixed = 128 + (red + 127) / 128 * 128;
-    const int ns = std::min(kvb::DEC_MAX_STAGES, (kvb::DEC_SMEM_BUDGET - fixed) / sb);
-    if (ns < 2) return fail(KVB_EUNSUPPORTED, "decode: stage of %d bytes does not fit twice in shared memory", sb);
-    p.stage_bytes = sb;
-    p.nstage = ns;
-    return launch_main<D, R, GK, GV, KM, CK>(p, P.n_ctas, size_t(fixed) + size_t(ns) * sb, s, pdl);
+    // one chunk's stage per stratum; every CTA sizes its ring from the largest stage among its pieces
+    int mx = 128;
+    for (int i = 0; i < c->n_strata; ++i) {
+        const kvb::StageLay L =
+            kvb::stage_lay<D, R, GK, GV, KM, CK>(c->strata[i].kbits, c->strata[i].vbits, P.tok[i], c->k_group);
+        p.st[i].stage_bytes = std::max(128, (L.end + 127) / 128 * 128);
+        mx = std::max(mx, p.st[i].stage_bytes);
+    }
+    const int fixed = 128 + (kvb::dec_red_bytes(R, D) + 127) / 128 * 128;
+    const int ring = std::min((kvb::DEC_SMEM_BUDGET - fixed) / 128 * 128, kvb::DEC_MAX_STAGES * mx);
+    if (ring < 2 * mx) return fail(KVB_EUNSUPPORTED, "decode: stage of %d bytes does not fit twice in shared memory", mx);
+    p.ring_bytes = ring;
+    return launch_main<D, R, GK, GV, KM, CK>(p, P.n_ctas, size_t(fixed) + size_t(ring), s, pdl);
 }
 
 }  // namespace kvbd

@@ -847,7 +847,7 @@ __global__ void __launch_bounds__(64 + NWG * 128, 1) decode_tc(const __grid_cons
             tc_before();
             bar_sync(3, NTH);
             if (wg == 0) {
-                float* part = p.part + size_t(pc0 + pi) * (2 * R + R * 128);
+                float* part = p.part + size_t(piece_slot(p.piece[pc0 + pi])) * (2 * R + R * 128);
                 float M[R], beta[NWG][R];
 #pragma unroll
                 for (int r = 0; r < R; ++r) {

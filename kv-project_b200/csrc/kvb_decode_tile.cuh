@@ -21,7 +21,12 @@ namespace kvb {
 #ifndef KVB_DEC_CTAS_PER_SM
 #define KVB_DEC_CTAS_PER_SM 1
 #endif
+#ifndef KVB_DEC_RED_SLOTS
+#define KVB_DEC_RED_SLOTS KVB_DEC_WARPS
+#endif
 constexpr int DEC_CWARPS = KVB_DEC_WARPS;                   // warps per CTA (all consume)
+constexpr int DEC_RED_SLOTS = KVB_DEC_RED_SLOTS;            // accumulator slots of the end-of-piece merge
+static_assert(DEC_RED_SLOTS <= DEC_CWARPS && 2 * DEC_RED_SLOTS >= DEC_CWARPS, "merge slots: warps / 2 .. warps");
 constexpr int DEC_CTAS_PER_SM = KVB_DEC_CTAS_PER_SM;        // resident main-kernel CTAs per SM
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr int KV_ASYM = 0, KV_MIDRISE = 1;
@@ -533,9 +538,9 @@ struct Tile {
     __device__ static void flush(WarpState<C>& S, float* red, float* part, int warp, int lane) {
         const int g = lane >> 2, t = lane & 3;
         const int r0 = (2 * t) % R;
-        float* red_m = red;                          // [8][R]
-        float* red_l = red + DEC_CWARPS * R;         // [8][R]
-        float* red_acc = red + 2 * DEC_CWARPS * R;   // [8][R][D]
+        float* red_m = red;                          // [warps][R]
+        float* red_l = red + DEC_CWARPS * R;         // [warps][R]
+        float* red_acc = red + 2 * DEC_CWARPS * R;   // [DEC_RED_SLOTS][R][D]
         float lt[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
@@ -572,29 +577,38 @@ struct Tile {
             for (int w = 0; w < DEC_CWARPS; ++w) M = fmaxf(M, red_m[w * R + r0 + e]);
             beta[e] = (S.m[e] == -INFINITY) ? 0.f : ex2(S.m[e] - M);
         }
+        // this warp's weighted accumulator entries; each (row, channel) comes from exactly one lane
+        auto put = [&](bool add, int slot) {
 #pragma unroll
-        for (int jv = 0; jv < NVT; ++jv)
+            for (int jv = 0; jv < NVT; ++jv)
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
+                for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int v = 2 * mt + hh;
-                    const int ch = LV::vch(g, v);
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int v = 2 * mt + hh;
+                        const int ch = LV::vch(g, v);
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int c = 8 * jv + 2 * t + e;
-                        if (C::VC::dup(c) || C::VC::grp(c) != ch / (D / GV)) continue;
-                        const float val = (S.acc[jv][mt][2 * hh + e] - 1024.f * S.sp[jv][e]) * (1.f / LV::vf(v)) +
-                                          S.z[jv][e];
-                        red_acc[(warp * R + C::VC::row(c)) * D + ch] = beta[e] * val;
+                        for (int e = 0; e < 2; ++e) {
+                            const int c = 8 * jv + 2 * t + e;
+                            if (C::VC::dup(c) || C::VC::grp(c) != ch / (D / GV)) continue;
+                            const float val = (S.acc[jv][mt][2 * hh + e] - 1024.f * S.sp[jv][e]) * (1.f / LV::vf(v)) +
+                                              S.z[jv][e];
+                            float* dst = &red_acc[(slot * R + C::VC::row(c)) * D + ch];
+                            *dst = add ? *dst + beta[e] * val : beta[e] * val;
+                        }
                     }
-                }
+        };
+        if (warp < DEC_RED_SLOTS) put(false, warp);
+        if constexpr (DEC_RED_SLOTS < DEC_CWARPS) {
+            consumer_bar();
+            if (warp >= DEC_RED_SLOTS) put(true, warp - DEC_RED_SLOTS);
+        }
         consumer_bar();
         const int tid = warp * 32 + lane;
         for (int o = tid; o < R * D; o += DEC_CWARPS * 32) {
             float s = 0.f;
 #pragma unroll
-            for (int w = 0; w < DEC_CWARPS; ++w) s += red_acc[w * R * D + o];
+            for (int w = 0; w < DEC_RED_SLOTS; ++w) s += red_acc[w * R * D + o];
             part[2 * R + o] = s;
         }
         if (tid < R) {

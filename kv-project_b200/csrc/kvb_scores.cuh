@@ -1,5 +1,9 @@
 // kvb_scores.cuh - K2a: accumulated attention scores of decode queries (SnapKV-style eviction
-// scores, snapkv_scores STRATA_KV.py:932-953, with queries that see every key).
+// scores, snapkv_scores STRATA_KV.py:932-953): either decode queries that see every key, or (causal
+// mode) SnapKV's observation window itself - the nq queries are the last nq context positions
+// T - nq .. T - 1 and query i sees keys j <= T - nq + i (the triu mask of STRATA_KV.py:946); the
+// window's own keys count in every row's softmax denominator, and only the candidate columns
+// j < T - nq (visible to all window queries) are scored.
 //
 // For one (b, kv head): rows = rep * nq query rows (<= 256), T keys.  score[j] = mean over rows of
 // softmax_j(scaling * q_r . k_j).  Two passes over the keys, both as bf16 / fp16 mma.sync tiles
@@ -42,6 +46,7 @@ struct ScoreParams {
     float* lse;                       // [heads][SC_ROWS]
     float* out;                       // [heads][n_cand]
     int pass;
+    int causal;                       // 1: row r is window query r % nq at position T - nq + r % nq
 };
 
 template <typename T>
@@ -151,8 +156,19 @@ __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
             }
         }
         if (p.pass == 1) {
-            // keys past T exist only in the last tile of the last split: only that tile masks them
-            const int lim = int(imin64(p.T - kt, SC_KT)) - 2 * t;       // this lane's column c is in if c < lim
+            // keys past T exist only in the last tile of the last split; in causal mode a window row
+            // also stops at its own position.  Row (m, hh) of this lane reads column c iff c < lim[m][hh].
+            int lim[2][2];
+            bool full = true;
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    int64_t vis = p.T;
+                    if (p.causal) vis = p.T - p.nq + (warp * 32 + m * 16 + g + 8 * hh) % int(p.nq) + 1;
+                    lim[m][hh] = int(imin64(imax64(vis - kt, 0), SC_KT)) - 2 * t;
+                    full = full && lim[m][hh] + 2 * t == SC_KT;
+                }
             auto online = [&](auto full_tag) {
                 constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
@@ -165,7 +181,7 @@ __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
 #pragma unroll
                             for (int e = 0; e < 2; ++e) {
                                 v[n][e] = acc[m][n][2 * hh + e] * p.lam;
-                                if (FULL || 8 * n + e < lim) mx = fmaxf(mx, v[n][e]);
+                                if (FULL || 8 * n + e < lim[m][hh]) mx = fmaxf(mx, v[n][e]);
                             }
                         const float mn = fmaxf(rm[m][hh], mx);
                         float s = rl[m][hh] * ((rm[m][hh] == -INFINITY) ? 0.f : ex2(rm[m][hh] - mn));
@@ -173,12 +189,12 @@ __global__ void __launch_bounds__(256) scores_kernel(const ScoreParams p) {
                         for (int n = 0; n < 8; ++n)
 #pragma unroll
                             for (int e = 0; e < 2; ++e)
-                                if (FULL || 8 * n + e < lim) s += ex2(v[n][e] - mn);
+                                if (FULL || 8 * n + e < lim[m][hh]) s += ex2(v[n][e] - mn);
                         rm[m][hh] = mn;
                         rl[m][hh] = s;
                     }
             };
-            if (lim + 2 * t == SC_KT) online(std::true_type{});
+            if (full) online(std::true_type{});
             else online(std::false_type{});
         } else {
             // this lane's 16 columns (j = 2 n + e: column 8 n + 2 t + e) summed over its rows

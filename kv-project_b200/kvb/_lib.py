@@ -54,6 +54,8 @@ SIGNATURES = {
     "kvb_scores_workspace_size": (C.c_size_t, [_i64, _i64, _i64]),
     "kvb_query_scores": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i64, _i32, _p, _p,
                                 C.c_size_t, _p]),
+    "kvb_snapkv_scores": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _p, _p, C.c_size_t,
+                                 _p]),
     "kvb_spectral_encode": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i32, _f32, _p, _p, _i64, _p, _i32,
                                    _p]),
     "kvb_absmax_quant": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i32, _i32,

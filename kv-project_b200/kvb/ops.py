@@ -206,6 +206,26 @@ def query_scores(q: torch.Tensor, k: torch.Tensor, scaling: float, n_cand: int, 
     return out
 
 
+def snapkv_scores(q_window: torch.Tensor, k: torch.Tensor, scaling: float, pool: int = 5) -> torch.Tensor:
+    """SnapKV scores at the horizon H = k.shape[2] (snapkv_scores STRATA_KV.py:932-954):
+    q_window (B, Hq, w, d) = the queries of the last w context positions, causally masked; returns
+    the scores of the H - w candidate positions (B, Hkv, H - w) float32.  The window itself is
+    always kept by the caller (the reference pads its columns with max + 1)."""
+    _cuda(q_window, k)
+    if q_window.dtype != k.dtype or k.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("snapkv_scores: q and k must share dtype f16 / bf16")
+    q, k = q_window.contiguous(), k.contiguous()
+    B, Hq, w, d = q.shape
+    Hkv, H = k.shape[1], k.shape[2]
+    lib = L.lib()
+    wsb = lib.kvb_scores_workspace_size(B, Hkv, H - w)
+    ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=q.device)
+    out = torch.empty((B, Hkv, H - w), dtype=torch.float32, device=q.device)
+    L.check(lib.kvb_snapkv_scores(_ptr(q), _ptr(k), dtype_code(q), B, Hq, Hkv, w, H, d, C.c_float(scaling), pool,
+                                  _ptr(out), _ptr(ws), wsb, C.c_void_p(_stream(q.device))), "kvb_snapkv_scores")
+    return out
+
+
 def device_diag(clear: bool = True, device=None) -> int:
     """Where the first bounded wait gave up (0 if none); see kvb_device_diag in kvb.h."""
     v = C.c_uint(0)
@@ -414,7 +434,8 @@ def decode_noalloc(cache: PackedCache, q: torch.Tensor, scaling: float, out: tor
 
 
 def decode_plan(cache: PackedCache, n_ctas: int):
-    """The split-K plan (host computation): dict with cta_begin, pieces (head, stratum, lo, hi), head_begin."""
+    """The split-K plan (host computation): dict with cta_begin, pieces (head, stratum, lo, hi) in CTA
+    order, slots (index of each piece's partial, head-major) and head_begin (indexes slots)."""
     c = cache.struct()
     lib = L.lib()
     need = lib.kvb_decode_plan(C.byref(c), n_ctas, None, 0)
@@ -425,10 +446,11 @@ def decode_plan(cache: PackedCache, n_ctas: int):
     o = 3
     cta_begin = v[o:o + nc + 1]
     o += nc + 1
-    pieces = [tuple(v[o + 4 * i:o + 4 * i + 4]) for i in range(npc)]
-    o += 4 * npc
+    pieces = [tuple(v[o + 5 * i:o + 5 * i + 4]) for i in range(npc)]
+    slots = [v[o + 5 * i + 4] for i in range(npc)]
+    o += 5 * npc
     head_begin = v[o:o + nh + 1]
-    return {"n_ctas": nc, "cta_begin": cta_begin, "pieces": pieces, "head_begin": head_begin}
+    return {"n_ctas": nc, "cta_begin": cta_begin, "pieces": pieces, "slots": slots, "head_begin": head_begin}
 
 
 # ------------------------------------------------------------------------------------------------

@@ -283,9 +283,40 @@ def rowcodes():
     print("wrote rowcodes.npz", (HERE / "rowcodes.npz").stat().st_size)
 
 
+def snapkv128():
+    """SnapKV scores at the GPU kernel's head size (d = 128, fp16-exact inputs): the reference's
+    snapkv_scores (STRATA_KV.py:932-954, causal observation window) and its top-k set, in
+    snapkv128.npz (its own generator, so the other files are untouched).  Only the window queries
+    are stored: the reference reads no other position of q."""
+    S, _ = load_reference()
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(2468)
+    out = {}
+    for name, (B, Hkv, rep, H, w, kern) in {"a": (1, 2, 4, 320, 32, 5), "b": (2, 1, 8, 200, 16, 1)}.items():
+        d = 128
+        cfg = S.Config(SNAPKV_WINDOW=w, SNAPKV_KERNEL=kern, SMOKE=True)
+        q = (torch.randn(B, Hkv * rep, H, d, generator=g) * 1.5).half().float()
+        k = (torch.randn(B, Hkv, H, d, generator=g) * (1.0 + torch.rand(1, Hkv, 1, d, generator=g))).half().float()
+        sc = S.snapkv_scores(q, k, H, d ** -0.5, cfg)
+        body = sc[..., :H - w]
+        out[f"{name}_qw"] = np32(q[:, :, H - w:])
+        out[f"{name}_k"] = np32(k)
+        out[f"{name}_scores"] = np32(sc)
+        out[f"{name}_cfg"] = np.array([B, Hkv, rep, H, w, kern])
+        out[f"{name}_top40"] = body.topk(40, dim=-1).indices.sort(-1).values.numpy()
+        srt = body.sort(-1, descending=True).values
+        out[f"{name}_gap40"] = np32(srt[..., 39] - srt[..., 40])          # margin at the top-40 boundary
+    np.savez_compressed(HERE / "snapkv128.npz", **out)
+    print("wrote snapkv128.npz", (HERE / "snapkv128.npz").stat().st_size)
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["rowcodes"]:
         rowcodes()
+    elif sys.argv[1:] == ["snapkv128"]:
+        snapkv128()
     else:
         main()
         rowcodes()
+        snapkv128()

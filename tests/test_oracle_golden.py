@@ -150,3 +150,17 @@ def test_mixed_strata_counts_and_ties():
     np.testing.assert_array_equal(s[8][0, 0], [3, 7])            # tie at 5.0: lower indices first
     np.testing.assert_array_equal(s[4][0, 0], [0, 1, 2, 4, 5, 11])
     assert O.strata_counts(32768) == (3276, 9830, 19662)
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_snapkv128_scores_and_topk(golden, case):
+    """SnapKV at d = 128 (the GPU kernel's head size): the oracle against the reference's
+    snapkv_scores (causal observation window, STRATA_KV.py:932-954) and its top-40 set."""
+    g = golden("snapkv128")
+    B, Hkv, rep, H, w, kern = (int(x) for x in g[f"{case}_cfg"])
+    qw = g[f"{case}_qw"]
+    q = np.zeros((B, Hkv * rep, H, qw.shape[-1]), np.float32)
+    q[:, :, H - w:] = qw                                   # the reference reads only the window positions
+    sc = O.snapkv_scores(q, g[f"{case}_k"], H, qw.shape[-1] ** -0.5, w, kern)
+    np.testing.assert_allclose(sc, g[f"{case}_scores"], rtol=2e-6, atol=1e-9)
+    np.testing.assert_array_equal(O.topk_kept(g[f"{case}_scores"][..., :H - w], 40), g[f"{case}_top40"])

@@ -69,3 +69,27 @@ def test_eviction_pipeline(cuda_dev):
     ref = O.chunked_attention(np32(qd), d ** -0.5, np.array([T]), rk["xhat"], rv["xhat"], np.arange(n),
                               np.full(n, O.attention.BIG), None, 256)
     assert np.abs(out - ref).max() <= 2e-3
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_snapkv_scores_golden(cuda_dev, golden, case):
+    """kvb_snapkv_scores (causal observation window) against the reference's own snapkv_scores
+    (STRATA_KV.py:932-954, fixture generated from it): scores within float32 accumulation tolerance,
+    and the top-40 kept set of the GPU scores equals the reference's wherever the reference's
+    boundary margin exceeds the score error."""
+    import kvb
+    g = golden("snapkv128")
+    B, Hkv, rep, H, w, kern = (int(x) for x in g[f"{case}_cfg"])
+    qw = torch.from_numpy(g[f"{case}_qw"]).half().to(cuda_dev)
+    k = torch.from_numpy(g[f"{case}_k"]).half().to(cuda_dev)
+    got = kvb.snapkv_scores(qw, k, 128 ** -0.5, pool=kern)
+    assert kvb.device_status() == 0
+    ref = g[f"{case}_scores"][..., :H - w]
+    gn = got.cpu().numpy()
+    np.testing.assert_allclose(gn, ref, rtol=2e-4, atol=1e-9)
+    top = kvb.rank_split(got, [40], want=[0])[0].cpu().numpy()
+    err = np.abs(gn - ref).max()
+    for b in range(B):
+        for h in range(Hkv):
+            if g[f"{case}_gap40"][b, h] > 4 * err:
+                np.testing.assert_array_equal(top[b, h], g[f"{case}_top40"][b, h])
