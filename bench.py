@@ -10,8 +10,8 @@ values N(0,1), queries N(0,1)).
 
 One step = one decode token: attention of every layer's query over its packed cache (one kvb_decode
 call per layer: prologue + split-K main kernel + merge).  value = packed bytes read per step (all
-ranks) / max-over-ranks step time, in GB/s; the packed cache is 7.95 GB per GPU per step, far larger
-than L2, so no flush is needed between steps.
+ranks) / max-over-ranks step time, in GB/s; the packed cache is 7.95 GB per step (on one GPU), far
+larger than L2, so no flush is needed between steps.
 
 Other workloads (--workload), each printing the same JSON line for its own config:
   c0          config 0: B 1, 4096 tokens, K 4-bit per channel (128 tokens), V 2-bit per token (32 ch)
@@ -29,8 +29,9 @@ Other workloads (--workload), each printing the same JSON line for its own confi
   python bench.py [--gpus N --steps K --warmup W] [--workload W]   # kvb (CUDA) arm
   python bench.py --strata 0,0                                      # config 1 with every token at 2 bits
   python bench.py --impl reference [--workload W]                   # reference CPU path (oracle port)
-Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N  (c0-c3: weak scaling, each rank its own
-batch; c4: the batch of 32 is split over the ranks)
+Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N  (c1 / c4: strong scaling, the batch of one
+job (8 / 32 rows) is split over the ranks; c0, c2, c3: weak scaling, each rank its own batch; c4s: the
+context of one batch-4 job is split over the ranks)
 """
 
 from __future__ import annotations
@@ -54,8 +55,18 @@ DECODE = ("c1", "c0", "c2", "c3", "c4", "c4s")
 COMPRESS = ("c1-pack", "c2-evict", "c3-project")
 
 # DRAM bytes (read + write) of one decode_main launch from an ncu capture of this bench's workload
-# (`ncu --set full -k regex:decode_main`, see profiles/); None where no capture was taken.
-TRAFFIC = {"c1": 248.81e6 + 3.85e6}
+# (profiles/decode_main_config1.md), with the hash of the decode sources the capture ran on: the
+# figure is reported only while those sources are unchanged (else roofline.traffic is null).
+TRAFFIC = {}
+TRAFFIC_SOURCES = ("kvb_common.cuh", "kvb_decode.cuh", "kvb_decode_tile.cuh", "kvb_decode_inst.cuh")
+
+
+def decode_sources_hash() -> str:
+    import hashlib
+    h = hashlib.sha256()
+    for f in TRAFFIC_SOURCES:
+        h.update((ROOT / "kv-project_b200" / "csrc" / f).read_bytes())
+    return h.hexdigest()[:16]
 
 
 def args_():
@@ -141,10 +152,13 @@ def shape(a, world):
             "c2": (32, 4, 32768, 32, 8, "bf16"), "c3": (1, 16, 16384, 32, 8, "f16"),
             "c4": (80, 32, 131072, 64, 8, "bf16"), "c4s": (80, 4, 131072, 64, 8, "bf16")}[w]
     L, B, T, Hq, Hkv, dt = base
-    if w == "c4":                                   # strong scaling: the batch of 32 is split over ranks
+    if w in ("c1", "c4") and a.workload not in COMPRESS:
+        # strong scaling: the (batch, KV head) units of one job are split over the ranks by batch row
+        # (config 1: 64 units, 8 per GPU at 8 GPUs; config 4: 256 units)
         if B % world:
-            raise SystemExit(f"config 4: batch 32 does not split over {world} ranks")
+            raise SystemExit(f"{w}: batch {B} does not split over {world} ranks")
         B //= world
+    if w == "c4":
         per_layer = B * Hkv * T * 136               # 4-bit K + V codes (128 B) + per-channel / per-token fp16 pairs
         L = min(L, int(110e9 // per_layer))         # layers resident on one GPU (all 80 from 4 GPUs up)
     if a.workload in COMPRESS:
@@ -222,7 +236,70 @@ def build_decode(a, rank, dev):
 
 
 # ------------------------------------------------------------------------------------------------
-# reference arm: the reference's CPU decode path (dequantise-then-attend), oracle port
+# shared: analytic bytes and the config block (identical in both arms)
+# ------------------------------------------------------------------------------------------------
+def packed_bytes_per_head(w, T):
+    """Bytes of one (batch, KV head) of one layer's packed cache (codes + fp16 metadata), as
+    PackedCache.stored_bytes counts them, for the default layout of each decode workload."""
+    if w == "c1":
+        n8, n4 = T // 10, 3 * T // 10
+        n2 = T - n8 - n4
+        return n8 * (256 + 16) + n4 * (128 + 16) + n2 * (64 + 16)
+    if w == "c0":                                   # K 4-bit per channel g128, V 2-bit per token g32
+        return T * 64 + -(-T // 128) * 128 * 4 + T * 32 + T * 4 * 4
+    if w == "c2":                                   # 2176 kept: K 4-bit per channel g64, V 4-bit g64
+        n = 2048 + 128
+        return n * 64 + -(-n // 64) * 128 * 4 + n * 64 + n * 2 * 4
+    if w == "c3":                                   # 32 coefficients 4-bit + fp16 scale, K and V
+        return 2 * T * (16 + 2)
+    return T * 64 + -(-T // 128) * 128 * 4 + T * 64 + T * 4     # c4 / c4s: 4-bit g128
+
+
+def decode_config(a, w, world, L, B, T, Hq, Hkv, dt, bytes_step):
+    d = 128
+    cfg = {"workload": DESC[w], "layers": L, "batch_per_gpu": B,
+           "global_batch": B if w == "c4s" else B * world,
+           "context": T, **({"context_per_gpu": -(-T // world)} if w == "c4s" else {}), "Hq": Hq, "Hkv": Hkv, "d": d,
+           "act_dtype": dt,
+           "l2": ("inputs larger than L2" if bytes_step > 126e6 else
+                  "packed cache smaller than L2: timed warm (launch-bound config)"),
+           "parallelism": {"c1": f"batch split over {world} ranks ({B} x {Hkv} (batch, kv head) units "
+                                 f"per rank), no collective",
+                           "c4": f"batch split over {world} ranks, no collective",
+                           "c4s": f"context split over {world} ranks, " + (
+                               "peer-memory exchange + LSE merge kernel (kvb_xchg_merge) per layer"
+                               if a.xchg == "p2p" else "NCCL all-gather + LSE merge per layer")
+                           }.get(w, f"dp{world} (batch x kv-head shards, no collective)"),
+           "bytes_per_step_per_gpu": bytes_step}
+    if w == "c1":
+        t8, t4 = (int(x) for x in a.strata.split(","))
+        cfg["strata"] = (f"{10 * t8}% 8-bit / {10 * t4}% 4-bit / {100 - 10 * (t8 + t4)}% 2-bit, "
+                         f"KIVI per-token groups of 64")
+    return cfg
+
+
+def compress_config(w, L, B, T, Hq, Hkv, alg):
+    return {"workload": DESC[w], "layers_cycled": L, "batch_per_gpu": B, "context": T, "Hq": Hq,
+            "Hkv": Hkv, "d": 128, "l2": "inputs larger than L2", "bytes_per_step": alg}
+
+
+def compress_bytes(w, B, T, Hkv):
+    """(inputs read, packed output written) of one compress step of one layer."""
+    d = 128
+    if w == "c1-pack":
+        inp = 2 * 2 * B * Hkv * T * d + B * Hkv * T * d * 2          # K, V read for packing + K for energy
+        out = B * Hkv * packed_bytes_per_head("c1", T)
+    elif w == "c2-evict":
+        inp = 2 * B * Hkv * T * d * 2 + 2 * 2 * B * Hkv * 2176 * d   # K (score pass) + kept K / V
+        out = B * Hkv * packed_bytes_per_head("c2", T)
+    else:
+        inp = 2 * B * Hkv * T * d * 2 + 2 * 2 * Hkv * 32 * 128 * 2   # K and V + the basis (hi / lo)
+        out = B * Hkv * packed_bytes_per_head("c3", T)
+    return inp, out
+
+
+# ------------------------------------------------------------------------------------------------
+# reference arm: the reference's CPU path of each workload (numpy ports of its functions, oracle/)
 # ------------------------------------------------------------------------------------------------
 def _threads():
     import torch
@@ -236,23 +313,64 @@ def _threads():
     return threads
 
 
-def cpu_reference_sample(workload="c1", context=None, min_seconds=10.0, seed=42):
-    """Times the reference's CPU decode (chunked_attention STRATA_KV.py:641, or the coefficient-
-    domain attend QUASAR_KV.py:1942 for config 3; numpy ports in oracle/) over one batch row of one
-    layer of the workload's cache, dequantised.  Returns (seconds per sample, packed bytes the
-    sample represents, threads, description)."""
+def cpu_sample(workload="c1", context=None, seed=42):
+    """One bounded sample of a workload on the CPU: the reference's own path for it, restated in
+    numpy (oracle/): one batch row of one layer.  Decode: dequantise-then-attend (chunked_attention
+    STRATA_KV.py:641; the coefficient-domain attend QUASAR_KV.py:1942 for config 3).  Compress:
+    key energy + strata ranking + kivi_quant per stratum (config 1, STRATA_KV.py:826), SnapKV-style
+    scores + top-k + kivi_quant of the kept tokens (config 2, :932-1033), basis projection + mid-rise
+    code (config 3, QUASAR_KV.py:1354, STRATA_KV.py:1158).  Returns (run, bytes the sample stands
+    for in the workload's metric, description)."""
     import numpy as np
     import torch
     import oracle as O
     from kvb import workloads as W
-    workload = "c4" if workload == "c4s" else workload      # same per-row cache as config 4
-    T = context or {"c0": 4096, "c1": 32768, "c2": 32768, "c3": 16384, "c4": 32768}[workload]
-    Hq = 64 if workload == "c4" else 32
+    base = workload.split("-")[0]
+    base = "c4" if base == "c4s" else base          # same per-row cache as config 4
+    T = context or {"c0": 4096, "c1": 32768, "c2": 32768, "c3": 16384, "c4": 32768}[base]
+    Hq = 64 if base == "c4" else 32
     Hkv, d = 8, 128
-    dt = torch.float16 if workload in ("c0", "c3") else torch.bfloat16
-    q = W.queries(1, Hq, 1, d, dt, seed=seed).float().numpy()
+    dt = torch.float16 if base in ("c0", "c3") else torch.bfloat16
     pos, hide = np.arange(T), np.full(T, O.attention.BIG)
-    if workload == "c1":
+    if workload == "c1-pack":
+        K, V = W.lognormal_kv(1, Hkv, T, d, dt, seed=seed + 1, layer=0)
+        Kf, Vf = K.float().numpy(), V.float().numpy()
+
+        def run():
+            sets = O.mixed_strata(O.l2_importance(Kf))
+            for b, idx in sets.items():
+                ix = idx[..., None].repeat(d, -1)
+                O.kivi_quant(np.take_along_axis(Kf, ix, 2), b, 64, False, 0)
+                O.kivi_quant(np.take_along_axis(Vf, ix, 2), b, 64, False, 0)
+        i_b, o_b = compress_bytes(workload, 1, T, Hkv)
+        return run, i_b + o_b, f"key energy + strata ranking + kivi_quant x 6 (numpy port) over 1 batch row x {Hkv} KV heads x {T} tokens"
+    if workload == "c2-evict":
+        g = torch.Generator().manual_seed(seed)
+        Kf = torch.randn(1, Hkv, T, d, generator=g).to(dt).float().numpy()
+        Vf = torch.randn(1, Hkv, T, d, generator=g).to(dt).float().numpy()
+        qo = torch.randn(1, Hq, 64, d, generator=g).to(dt).float().numpy()
+
+        def run():
+            sc = O.query_scores(qo, Kf, d ** -0.5, T - 128)
+            kept = O.topk_kept(sc, 2048, 128)
+            ix = kept[..., None].repeat(d, -1)
+            O.kivi_quant(np.take_along_axis(Kf, ix, 2), 4, 64, True, 0)
+            O.kivi_quant(np.take_along_axis(Vf, ix, 2), 4, 64, False, 0)
+        i_b, o_b = compress_bytes(workload, 1, T, Hkv)
+        return run, i_b + o_b, f"query_scores (64 queries) + top-k + kivi_quant of the kept (numpy port) over 1 batch row x {Hkv} KV heads x {T} tokens"
+    if workload == "c3-project":
+        bases = W.qr_bases(Hkv, d, seed=45)
+        K, V = W.spectral_kv(1, Hkv, T, d, bases, dt, seed=45)
+        br = bases[:, :, :32].float().numpy()
+        Kf, Vf = K.float().numpy(), V.float().numpy()
+
+        def run():
+            O.spectral_encode(Kf, br, 4)
+            O.spectral_encode(Vf, br, 4)
+        i_b, o_b = compress_bytes(workload, 1, T, Hkv)
+        return run, i_b + o_b, f"basis projection + mid-rise 4-bit code of K and V (numpy port) over 1 batch row x {Hkv} KV heads x {T} tokens"
+    q = W.queries(1, Hq, 1, d, dt, seed=seed).float().numpy()
+    if base == "c1":
         K, V = W.lognormal_kv(1, Hkv, T, d, dt, seed=seed + 1, layer=0)
         Kf, Vf = K.float().numpy(), V.float().numpy()
         sets = O.mixed_strata(O.l2_importance(Kf))
@@ -262,17 +380,14 @@ def cpu_reference_sample(workload="c1", context=None, min_seconds=10.0, seed=42)
             gv = np.take_along_axis(Vf, idx[..., None].repeat(d, -1), 2)
             np.put_along_axis(Kh, idx[..., None].repeat(d, -1), O.kivi_quant(gk, b, 64, False, 0)["xhat"], 2)
             np.put_along_axis(Vh, idx[..., None].repeat(d, -1), O.kivi_quant(gv, b, 64, False, 0)["xhat"], 2)
-        n8, n4, n2 = O.strata_counts(T)
-        packed = Hkv * (n8 * (256 + 16) + n4 * (128 + 16) + n2 * (64 + 16))
         what = "mixed 8/4/2-bit KIVI strata"
-    elif workload in ("c0", "c4"):
+    elif base in ("c0", "c4"):
         K, V = W.outlier_kv(1, Hkv, T, d, dt, seed=seed)
-        kb, vb, vg = (4, 2, 32) if workload == "c0" else (4, 4, 128)
+        kb, vb, vg = (4, 2, 32) if base == "c0" else (4, 4, 128)
         Kh = O.kivi_quant(K.float().numpy(), kb, 128, True, 0)["xhat"]
         Vh = O.kivi_quant(V.float().numpy(), vb, vg, False, 0)["xhat"]
-        packed = Hkv * T * (d * (kb + vb) // 8) + Hkv * (T // 128) * d * 4 + Hkv * T * (d // vg) * 4
         what = f"KIVI K {kb}-bit per channel (128 tokens), V {vb}-bit per token ({vg} channels)"
-    elif workload == "c2":
+    elif base == "c2":
         n = 2048 + 128
         g = torch.Generator().manual_seed(seed)
         K = torch.randn(1, Hkv, n, d, generator=g).to(dt)
@@ -280,7 +395,6 @@ def cpu_reference_sample(workload="c1", context=None, min_seconds=10.0, seed=42)
         Kh = O.kivi_quant(K.float().numpy(), 4, 64, True, 0)["xhat"]
         Vh = O.kivi_quant(V.float().numpy(), 4, 64, False, 0)["xhat"]
         T, pos, hide = n, np.arange(n), np.full(n, O.attention.BIG)
-        packed = Hkv * n * 128 + Hkv * (n // 64) * d * 4 + Hkv * n * 2 * 4
         what = "KIVI 4-bit g64 over the 2176 kept tokens"
     else:                                            # c3: coefficient-domain decode
         bases = W.qr_bases(Hkv, d, seed=45)
@@ -288,40 +402,91 @@ def cpu_reference_sample(workload="c1", context=None, min_seconds=10.0, seed=42)
         br = bases[:, :, :32].float().numpy()
         _, kc, ks, _ = O.spectral_encode(K.float().numpy(), br, 4)
         _, vc, vs, _ = O.spectral_encode(V.float().numpy(), br, 4)
-        run = lambda: O.spectral_attend(q, d ** -0.5, br, kc, ks, vc, vs, 4)   # noqa: E731
-        packed = Hkv * T * 36
         what = "spectral 32 coefficients 4-bit, coefficient-domain attend"
-    if workload != "c3":
+        run = lambda: O.spectral_attend(q, d ** -0.5, br, kc, ks, vc, vs, 4)   # noqa: E731
+    if base != "c3":
         run = lambda: O.chunked_attention(q, d ** -0.5, np.array([T]), Kh, Vh, pos, hide, None, 256)  # noqa: E731
-    run()                                            # warm
-    t0 = time.perf_counter()
-    reps = 0
-    while reps < 200 and (reps < 3 or time.perf_counter() - t0 < min_seconds):
+    desc = (f"{'spectral_attend' if base == 'c3' else 'chunked_attention'} (numpy port, fp32) over 1 layer x "
+            f"1 batch row x {Hkv} KV heads x {T} dequantised tokens ({what})")
+    return run, Hkv * packed_bytes_per_head(base if workload != "c4s" else "c4", T if base != "c2" else 32768), desc
+
+
+def time_sample(run, reps, threads=None):
+    """Mean seconds per call of `run` over `reps` calls (after one warm call), optionally with the
+    BLAS / OpenMP pools limited to `threads`."""
+    import contextlib
+    ctx = contextlib.nullcontext()
+    if threads is not None:
+        try:
+            import threadpoolctl
+            ctx = threadpoolctl.threadpool_limits(threads)
+        except Exception:
+            pass
+    with ctx:
         run()
-        reps += 1
-    dt_s = (time.perf_counter() - t0) / reps
-    desc = (f"{'spectral_attend' if workload == 'c3' else 'chunked_attention'} (numpy port, fp32) over 1 layer x "
-            f"1 batch row x {Hkv} KV heads x {T} dequantised tokens ({what}), mean of {reps}")
-    return dt_s, packed, _threads(), desc
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            run()
+        return (time.perf_counter() - t0) / reps
+
+
+def cpu_reference_sample(workload="c1", context=None, min_seconds=10.0):
+    """cpu_baseline of the kvb arm: the reference CPU path on one sample, timed for >= min_seconds
+    (at least 3 calls) with every host thread.  Returns (seconds per sample, sample bytes, threads,
+    description)."""
+    run, nbytes, desc = cpu_sample(workload, context)
+    t1 = time_sample(run, 1)
+    reps = max(3, min(200, int(min_seconds / max(t1, 1e-6))))
+    return time_sample(run, reps), nbytes, _threads(), f"{desc}, mean of {reps}"
 
 
 def reference_arm(a):
+    """The reference's CPU implementation of the workload on the host cores (numpy port in oracle/;
+    the reference itself is Python scripts that are not on the GPU box).  One step = one bounded
+    sample (one batch row of one layer), timed for exactly --steps steps after --warmup warm-up
+    steps, so steps x ms_per_step is the time that actually ran; value = the sample's bytes (in the
+    workload's metric) / its time.  A second, shorter timing with the thread pools limited to one
+    thread is reported as cpu_baseline_1thread."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    w = a.workload.split("-")[0]
-    dt_s, packed, threads, desc = cpu_reference_sample(w, context=a.context)
+    w = a.workload
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    L, B, T, Hq, Hkv, _ = shape(argparse.Namespace(**{**vars(a), "workload": w}), world)
-    gbs = packed / dt_s / 1e9
-    step_bytes = packed * B * L                       # the sample is 1 of B rows of one layer
-    line = {"metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "impl": "reference",
-            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": round(step_bytes / (gbs * 1e9) * 1e3, 3), "higher_is_better": True,
-            "scaling": "strong" if w in ("c4", "c4s") else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": DESC[w], "layers": L, "batch_per_gpu": B, "context": T, "Hq": Hq, "Hkv": Hkv,
-                       "d": 128},
-            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc},
+    L, B, T, Hq, Hkv, dt = shape(a, world)
+    run, nbytes, desc = cpu_sample(w, context=a.context)
+    threads = _threads()
+    for _ in range(a.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        run()
+    sec = (time.perf_counter() - t0) / a.steps
+    sec1 = time_sample(run, max(1, min(3, a.steps)), threads=1)
+    gbs = nbytes / sec / 1e9
+    gbs1 = nbytes / sec1 / 1e9
+    if w in COMPRESS:
+        i_b, o_b = compress_bytes(w, B, T, Hkv)
+        metric = f"{DESC[w]} GB/s (inputs read + packed output written)"
+        cfg = compress_config(w, L, B, T, Hq, Hkv, i_b + o_b)
+        scaling = "weak"
+    else:
+        esz = 2
+        step_bytes = L * B * Hkv * packed_bytes_per_head(w if w != "c4s" else "c4s", -(-T // world) if w == "c4s" else T) \
+            + 2 * L * B * Hq * 128 * esz
+        metric = METRIC
+        cfg = decode_config(a, w, world, L, B, T, Hq, Hkv, dt, step_bytes)
+        scaling = "strong" if w in ("c1", "c4", "c4s") else "weak"
+    sample = f"{desc}; one step = this sample"
+    line = {"metric": metric, "value": round(gbs, 4), "unit": "GB/s", "impl": "reference",
+            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(sec * 1e3, 3),
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": cfg,
+            "step_sample": {"bytes": nbytes, "fraction_of_gpu_step": round(nbytes / cfg.get(
+                "bytes_per_step_per_gpu", cfg.get("bytes_per_step", nbytes)), 6)},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "cpu_baseline_1thread": {"value": round(gbs1, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                                     "ms_per_sample": round(sec1 * 1e3, 3)},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -473,26 +638,19 @@ def decode_arm(a):
         peak, peak_kind = peaks()
         gbs = world * bytes_step / (ms * 1e-3) / 1e9
         achieved = (sum(bytes_layer) / L) / (main_ms_avg * 1e-3) / 1e9
-        traffic = TRAFFIC.get(a.workload) if (a.layers, a.batch, a.context, a.tc, a.strata) == \
-            (None, None, None, False, "1,3") else None
+        traffic = None
+        rec = TRAFFIC.get(a.workload)
+        if rec and (a.layers, a.batch, a.context, a.tc, a.strata, world) == (None, None, None, False, "1,3", 1) \
+                and rec[1] == decode_sources_hash():
+            traffic = rec[0]
         w = a.workload
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms, 4), "us_per_step": round(ms * 1000, 1),
             "pct_of_peak": round(100 * gbs / world / peak, 1), "higher_is_better": True,
-            "scaling": "strong" if w in ("c4", "c4s") else "weak",
+            "scaling": "strong" if w in ("c1", "c4", "c4s") else "weak",
             "vs_baseline": None, "dtype": "u8 codes / fp16 MMA / fp32 softmax", "data": "synthetic",
-            "config": {"workload": DESC[w], "layers": L, "batch_per_gpu": B,
-                       "global_batch": B if w == "c4s" else B * world,
-                       "context": T, **({"context_per_gpu": -(-T // world)} if w == "c4s" else {}), "Hq": Hq, "Hkv": Hkv, "d": d, "act_dtype": dt,
-                       "l2": ("inputs larger than L2" if sum(bytes_layer) > 126e6 else
-                              "packed cache smaller than L2: timed warm (launch-bound config)"),
-                       "parallelism": {"c4": f"batch split over {world} ranks, no collective",
-                                       "c4s": f"context split over {world} ranks, " + (
-                                           "peer-memory exchange + LSE merge kernel (kvb_xchg_merge) per layer"
-                                           if a.xchg == "p2p" else "NCCL all-gather + LSE merge per layer")
-                                       }.get(w, f"dp{world} (batch x kv-head shards, no collective)"),
-                       "bytes_per_step_per_gpu": bytes_step},
+            "config": decode_config(a, w, world, L, B, T, Hq, Hkv, dt, bytes_step),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "kernel": "decode_tc" if a.tc and w == "c1" else "decode_main",
@@ -506,10 +664,6 @@ def decode_arm(a):
             "decode_kernel": "decode_tc (tcgen05)" if a.tc and w == "c1" else "decode_main (mma.sync)",
             "clocks": clk.summary(),
         }
-        if w == "c1":
-            t8, t4 = (int(x) for x in a.strata.split(","))
-            line["config"]["strata"] = (f"{10 * t8}% 8-bit / {10 * t4}% 4-bit / {100 - 10 * (t8 + t4)}% 2-bit, "
-                                        f"KIVI per-token groups of 64")
         if world == 1 and not a.no_cpu_baseline:
             dt_s, packed, threads, desc = cpu_reference_sample(w, context=a.context)
             line["cpu_baseline"] = {"value": round(packed / dt_s / 1e9, 4), "unit": "GB/s", "cores": threads,
@@ -569,20 +723,14 @@ def compress_arm(a):
 
     step(0)
     torch.cuda.synchronize()
+    in_bytes, out_bytes = compress_bytes(w, B, T, Hkv)
     if w == "c3-project":
-        out_bytes = sum(r["codes"].numel() + r["meta"].numel() * 2 for r in (res["k"], res["v"]))
-        in_bytes = 2 * layers[0][0].numel() * 2 + 2 * layers[0][2].numel() * 2
+        assert out_bytes == sum(r["codes"].numel() + r["meta"].numel() * 2 for r in (res["k"], res["v"]))
         launches = 2
         flops = 2 * 2 * B * Hkv * T * d * 32             # algorithmic: K and V, 2 FLOP per multiply-add
     else:
-        c = res["c"]
-        out_bytes = c.stored_bytes()
-        if w == "c1-pack":
-            in_bytes = 2 * 2 * B * Hkv * T * d + B * Hkv * T * d * 2   # K, V read for packing + K for energy
-            launches = 2 + 6
-        else:
-            in_bytes = 2 * B * Hkv * T * d * 2 + 2 * 2 * B * Hkv * 2176 * d   # K (score pass) + kept K / V
-            launches = 3 + 1 + 2
+        assert out_bytes == res["c"].stored_bytes()
+        launches = 2 + 6 if w == "c1-pack" else 3 + 1 + 2
         flops = 0
     for i in range(max(3, a.warmup)):
         step(i)
@@ -605,8 +753,7 @@ def compress_arm(a):
             "metric": f"{DESC[w]} GB/s (inputs read + packed output written)", "value": round(world * gbs, 2),
             "unit": "GB/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dt, "data": "synthetic",
-            "config": {"workload": DESC[w], "layers_cycled": L, "batch_per_gpu": B, "context": T, "Hq": Hq,
-                       "Hkv": Hkv, "d": d, "l2": "inputs larger than L2", "bytes_per_step": alg},
+            "config": compress_config(w, L, B, T, Hq, Hkv, alg),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_source": peak_kind, "kernel": "whole compress step",
                          "traffic": None},
@@ -624,9 +771,6 @@ def compress_arm(a):
 def main():
     a = args_()
     if a.impl == "reference":
-        if a.workload in COMPRESS:
-            print(json.dumps({"impl": "reference", "unavailable": "reference arm times the decode workloads only"}))
-            return
         return reference_arm(a)
     if a.workload in COMPRESS:
         return compress_arm(a)

@@ -164,10 +164,17 @@ kvb_status kvb_xchg_alloc(size_t bytes, void** region, unsigned char* handle /* 
 kvb_status kvb_xchg_open(const unsigned char* handle /* 64 bytes */, void** region);
 kvb_status kvb_xchg_close(void* peer_region);
 kvb_status kvb_xchg_free(void* region);
+/* Zero this rank's own region on `stream` (re-establishing the exchange after a timeout). */
+kvb_status kvb_xchg_zero(void* region, size_t bytes, void* stream);
 /* part (rows, d) float32 and lse (rows) float32: this rank's decode_lse output; regions: `world`
- * device pointers (this rank's own region at [rank], the mapped peers' elsewhere); out (rows, d). */
+ * device pointers (this rank's own region at [rank], the mapped peers' elsewhere); out (rows, d).
+ * timeout_ns bounds each wait for a peer's rows (0: 2 s).  A wait that runs out sets KVB_DEV_TIMEOUT
+ * in the device status word (site 0x40 in kvb_device_diag) and the slice is merged from what arrived.
+ * While the status word holds KVB_DEV_TIMEOUT no call does anything (site 0x41): re-establish the
+ * exchange first - on every rank clear the status (kvb_device_status with clear), synchronise the
+ * ranks, zero the whole region (its flags and call counters restart at 0), synchronise again. */
 kvb_status kvb_xchg_merge(const float* part, const float* lse, int64_t rows, int d, int rank, int world,
-                          void* const* regions, void* out, int out_dtype, void* stream);
+                          void* const* regions, void* out, int out_dtype, uint64_t timeout_ns, void* stream);
 
 /* ------------------------------------------------------------------------------------------ *
  * K5: per-vector row codes (token-like stored vectors and format variants).  Rows follow

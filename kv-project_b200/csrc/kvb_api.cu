@@ -468,13 +468,18 @@ kvb_status kvb_xchg_close(void* peer_region) {
     return cuda_check(cudaIpcCloseMemHandle(peer_region), "xchg_close");
 }
 
+kvb_status kvb_xchg_zero(void* region, size_t bytes, void* stream) {
+    if (!region || bytes == 0) return fail(KVB_EINVAL, "xchg_zero: arguments");
+    return cuda_check(cudaMemsetAsync(region, 0, bytes, static_cast<cudaStream_t>(stream)), "xchg_zero");
+}
+
 kvb_status kvb_xchg_free(void* region) {
     if (!region) return fail(KVB_EINVAL, "xchg_free: null");
     return cuda_check(cudaFree(region), "xchg_free");
 }
 
 kvb_status kvb_xchg_merge(const float* part, const float* lse, int64_t rows, int d, int rank, int world,
-                          void* const* regions, void* out, int out_dtype, void* stream) {
+                          void* const* regions, void* out, int out_dtype, uint64_t timeout_ns, void* stream) {
     if (!part || !lse || !regions || !out) return fail(KVB_EINVAL, "xchg_merge: null pointer");
     if (rows <= 0 || d <= 0 || d > 1024 || world <= 0 || world > kvb::XC_MAX_RANKS || rank < 0 || rank >= world)
         return fail(KVB_EINVAL, "xchg_merge: sizes (world <= %d)", kvb::XC_MAX_RANKS);
@@ -492,7 +497,7 @@ kvb_status kvb_xchg_merge(const float* part, const float* lse, int64_t rows, int
         p.region[r] = static_cast<float*>(regions[r]);
     }
     p.out = out;
-    p.timeout_ns = 2000000000ull;
+    p.timeout_ns = timeout_ns ? timeout_ns : 2000000000ull;
     kvb::xchg_merge_kernel<<<kvb::XC_SLICES, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
     return launch_check("xchg_merge_kernel");
 }

@@ -12,10 +12,7 @@
 #include "kvb_decode_tc.cuh"
 
 #ifndef KVB_TOKEN_COST
-#define KVB_TOKEN_COST 135    // fixed per-token decode work in byte-equivalents at d_code 128 (see build_plan)
-#endif
-#ifndef KVB_PLAN_HEAD_MAJOR
-#define KVB_PLAN_HEAD_MAJOR 0 // 1: deal chunks head by head (every CTA runs all widths of its heads)
+#define KVB_TOKEN_COST 60     // fixed per-token decode work in byte-equivalents at d_code 128 (see build_plan)
 #endif
 #ifndef KVB_PDL
 #define KVB_PDL 1             // programmatic dependent launch of the main kernel after the prologue
@@ -127,10 +124,10 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
         P.tok[s] = chunk_of(c, s);
         nch[s] = (st.n + P.tok[s] - 1) / P.tok[s];
         // work per token in byte-equivalents: its code bytes plus a fixed per-token cost (code
-        // extraction, MMAs, softmax).  One-width caches on B200 take 4.99 / 6.58 / 9.61 ns x SM per
-        // token-head at 2 / 4 / 8 bits (d_code 128, KIVI groups of 64: 80 / 144 / 272 bytes), a
-        // straight line of slope 1 through bytes + ~130, and with the stratum-major order below
-        // most CTAs run one width, as in those measurements.
+        // extraction, MMAs, softmax).  One-width caches alone take 4.99 / 6.58 / 9.61 ns x SM per
+        // token-head at 2 / 4 / 8 bits on B200 (80 / 144 / 272 bytes: bytes + ~130), but in a mixed
+        // cache the byte-heavy CTAs also compete for DRAM: a sweep of the constant on config 1 (main
+        // kernel 104.5 us at 8, 95.9 at 139, 92.3 at 60, 92.5 at 40) puts the best split near 60.
         const int64_t bpt = c->d_code * (st.kbits + st.vbits) / 8 + (KVB_TOKEN_COST * c->d_code + 64) / 128;
         wfull[s] = int64_t(P.tok[s]) * bpt;
         wlast[s] = (st.n - (nch[s] - 1) * P.tok[s]) * bpt;
@@ -143,9 +140,11 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
     int cur_cta = 0;
     int last_key_cta = -1, last_head = -1, last_s = -1;
     double cum = 0.0;
-    // Chunks are dealt to CTAs in order, contiguous runs of equal work.  Stratum-major order (every
-    // head's 8-bit chunks, then every head's 4-bit chunks, ...) gives most CTAs a single code width:
-    // one inner loop in the instruction cache, one ring geometry, no width switches mid-CTA.
+    // Chunks are dealt to CTAs in order, contiguous runs of equal work, head by head (every width of
+    // a head before the next head), so every SM streams a mix of memory-heavy (8-bit) and
+    // instruction-heavy (2-bit) chunks.  Measured on config 1: dealing stratum by stratum instead
+    // (most CTAs one width) is 107-118 us against 91 us: the ~24 SMs left with the 8-bit chunks
+    // cannot keep enough bytes in flight to stream them at their share of the bandwidth.
     auto visit = [&](int h, int s) {
         for (int64_t k = 0; k < nch[s]; ++k) {
             const double w = double(k + 1 == nch[s] ? wlast[s] : wfull[s]);
@@ -166,13 +165,8 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
             }
         }
     };
-#if KVB_PLAN_HEAD_MAJOR
     for (int h = 0; h < heads; ++h)
         for (int s = 0; s < c->n_strata; ++s) visit(h, s);
-#else
-    for (int s = 0; s < c->n_strata; ++s)
-        for (int h = 0; h < heads; ++h) visit(h, s);
-#endif
     while (cur_cta < n_ctas) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
     P.n_pieces = int(P.piece.size() / 4);
     // partial slots: pieces ordered by (head, stratum, first chunk), so a head's partials are

@@ -14,7 +14,8 @@
 // can be at most one call ahead (it needs this rank's flag of call k + 1 to finish call k + 1, which
 // this rank publishes only after finishing call k), so it never overwrites a region still being
 // read.  Flags only move forward; a wait accepts any epoch at or past its own.  Every wait is
-// bounded (timeout -> KVB_DEV_TIMEOUT, the slice is merged from whatever arrived).
+// bounded (timeout -> KVB_DEV_TIMEOUT, site 0x40 in the diagnostic word, the slice is merged from
+// whatever arrived), and no call starts while the status word holds a timeout (site 0x41).
 #pragma once
 
 #include "kvb_common.cuh"
@@ -45,6 +46,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 __global__ void __launch_bounds__(256) xchg_merge_kernel(const __grid_constant__ XchgParams p) {
     const int slice = blockIdx.x, tid = threadIdx.x;
+    // After a timed-out wait (this call's or an earlier one, on any kvb kernel of this device) the
+    // ranks' epochs may disagree: a new exchange could then write into a parity a slow peer is still
+    // reading.  So no call runs while the status word shows a timeout; the caller re-establishes the
+    // exchange (clear the status, barrier, zero every region) before the next one.
+    if (*reinterpret_cast<volatile unsigned*>(&g_status) & KVB_DEV_TIMEOUT) {
+        if (tid == 0) note_wait_timeout(0x41, slice);
+        return;
+    }
     const int64_t r0 = p.rows * slice / XC_SLICES, r1 = p.rows * (slice + 1) / XC_SLICES;
     const int64_t n = p.rows * (p.d + 1);                       // one rank's slot
     const int64_t data_floats = 2 * int64_t(p.world) * n;

@@ -70,7 +70,8 @@ SIGNATURES = {
     "kvb_xchg_open": (_i32, [_p, C.POINTER(C.c_void_p)]),
     "kvb_xchg_close": (_i32, [_p]),
     "kvb_xchg_free": (_i32, [_p]),
-    "kvb_xchg_merge": (_i32, [_p, _p, _i64, _i32, _i32, _i32, C.POINTER(C.c_void_p), _p, _i32, _p]),
+    "kvb_xchg_zero": (_i32, [_p, C.c_size_t, _p]),
+    "kvb_xchg_merge": (_i32, [_p, _p, _i64, _i32, _i32, _i32, C.POINTER(C.c_void_p), _p, _i32, C.c_uint64, _p]),
     "kvb_decode_workspace_size": (C.c_size_t, [C.POINTER(Cache), _i32, _i32, _i32]),
     "kvb_decode": (_i32, [C.POINTER(Cache), _p, _i32, _i32, _i32, _f32, C.POINTER(C.c_int64), _p, _i32, _i32,
                           _p, C.c_size_t, _p]),

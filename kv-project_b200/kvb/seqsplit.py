@@ -94,10 +94,11 @@ class P2PSeqSplitDecoder:
     (as they do for the collective version).  Ranks must share one node with peer access (NVLink /
     NVSwitch); call close() before destroying the process group."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, timeout_s: float = 2.0):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.timeout_ns = int(timeout_s * 1e9)
         self._state = {}
 
     def _setup(self, rows, d, device):
@@ -142,9 +143,29 @@ class P2PSeqSplitDecoder:
         elif tuple(out.shape) != (B, Tq, Hq, d) or not out.is_contiguous():
             raise ValueError("P2PSeqSplitDecoder: out must be contiguous (B, Tq, Hq, d)")
         L.check(L.lib().kvb_xchg_merge(ops._ptr(part), ops._ptr(lse), rows, d, self.rank, self.world, regions,
-                                        ops._ptr(out), ops.dtype_code(out), C.c_void_p(ops._stream(q.device))),
+                                        ops._ptr(out), ops.dtype_code(out), self.timeout_ns,
+                                        C.c_void_p(ops._stream(q.device))),
                 "kvb_xchg_merge")
         return out
+
+    def reset(self):
+        """Re-establish the exchange after a timed-out wait (KVB_DEV_TIMEOUT in the device status
+        word; kvb_xchg_merge does nothing until then): every rank clears its status word, the ranks
+        meet, every rank zeroes its whole region (flags and call counters restart at 0), and the ranks
+        meet again before the next attend().  Returns the status word that was cleared."""
+        torch.cuda.synchronize()
+        st = ops.device_status(clear=True)
+        dist.barrier(group=self.group)
+        lib = L.lib()
+        for (rows, d, device), (own, _, _, _, _) in self._state.items():
+            nbytes = lib.kvb_xchg_bytes(rows, d, self.world)
+            with torch.cuda.device(device):
+                torch.cuda.synchronize()
+                L.check(lib.kvb_xchg_zero(C.c_void_p(own), nbytes, C.c_void_p(ops._stream(device))),
+                        "kvb_xchg_zero")
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        return st
 
     def close(self):
         """Unmap the peers' regions and free this rank's (after a barrier: no peer may still write)."""

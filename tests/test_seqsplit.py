@@ -256,3 +256,60 @@ def test_seqsplit_p2p_two_ranks():
         assert sorted(ret.keys()) == [0, 1]
         for same, same_graph, err, status in ret.values():
             assert same and same_graph and err <= 1e-4 and status == 0
+
+
+@pytest.mark.gpu
+def test_xchg_wait_times_out_and_refuses(cuda_dev):
+    """Failure detection of the peer-memory exchange on one GPU, without any fault: world 2 with both
+    exchange regions on this GPU and a peer that never runs, so rank 0's bounded wait for the peer's
+    flag runs out (5 ms limit).  The kernel returns on its own, the status word carries the timeout
+    bit and the diagnostic word names the exchange wait (site 0x40).  While the timeout stands, the
+    next call does nothing (site 0x41, output untouched); after the status is cleared and the region
+    zeroed (the re-establishment kvb_xchg_merge documents), exchanges run again."""
+    import ctypes as C
+    import kvb
+    from kvb import _lib, ops
+    lib = _lib.lib()
+    kvb.device_status(clear=True)
+    ops.device_diag(clear=True)
+    rows, d, world = 16, 128, 2
+    nbytes = lib.kvb_xchg_bytes(rows, d, world)
+    regions = (C.c_void_p * world)()
+    owned = []
+    for r in range(world):
+        p, h = C.c_void_p(), (C.c_ubyte * 64)()
+        _lib.check(lib.kvb_xchg_alloc(nbytes, C.byref(p), h), "kvb_xchg_alloc")
+        regions[r] = p.value
+        owned.append(p)
+    part = torch.randn(rows, d, device=cuda_dev)
+    lse = torch.randn(rows, device=cuda_dev)
+    out = torch.full((rows, d), 7.0, device=cuda_dev)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def merge(w, regs, timeout_ns):
+        _lib.check(lib.kvb_xchg_merge(C.c_void_p(part.data_ptr()), C.c_void_p(lse.data_ptr()), rows, d, 0, w, regs,
+                                      C.c_void_p(out.data_ptr()), _lib.KVB_F32, timeout_ns, stream), "kvb_xchg_merge")
+        torch.cuda.synchronize()
+
+    try:
+        merge(world, regions, 5_000_000)                  # the peer's flag never arrives
+        assert kvb.device_status(clear=False) & 1         # KVB_DEV_TIMEOUT, read without clearing
+        diag = ops.device_diag(clear=True)
+        assert diag & 0x80000000 and (diag & 0xFF) == 0x40
+        out.fill_(7.0)
+        merge(world, regions, 5_000_000)                  # refused while the timeout stands
+        assert torch.all(out == 7.0)
+        assert (ops.device_diag(clear=True) & 0xFF) == 0x41
+        # re-establish: clear the status, zero the region; a one-rank exchange then merges normally
+        assert kvb.device_status(clear=True) & 1
+        one = (C.c_void_p * 1)(regions[0])
+        _lib.check(lib.kvb_xchg_zero(C.c_void_p(regions[0]), nbytes, stream), "kvb_xchg_zero")
+        merge(1, one, 5_000_000)
+        assert kvb.device_status() == 0
+        assert torch.equal(out, part)                     # one part: the merge returns it unchanged
+    finally:
+        torch.cuda.synchronize()
+        for p in owned:
+            lib.kvb_xchg_free(p)
+        kvb.device_status(clear=True)
+        ops.device_diag(clear=True)
