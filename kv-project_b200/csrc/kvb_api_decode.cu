@@ -18,6 +18,7 @@
 #define KVB_PDL 1             // programmatic dependent launch of the main kernel after the prologue
 #endif
 
+
 using kvbd::DecodeShape;
 using kvbd::Plan;
 using kvbd::launch_maybe_pdl;
@@ -169,6 +170,8 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
         for (int s = 0; s < c->n_strata; ++s) visit(h, s);
     while (cur_cta < n_ctas) P.cta_begin[++cur_cta] = int(P.piece.size() / 4);
     P.n_pieces = int(P.piece.size() / 4);
+    P.max_cta_pieces = 0;
+    for (int i = 0; i < n_ctas; ++i) P.max_cta_pieces = std::max(P.max_cta_pieces, P.cta_begin[i + 1] - P.cta_begin[i]);
     // partial slots: pieces ordered by (head, stratum, first chunk), so a head's partials are
     // contiguous for the merge kernel
     std::vector<int> order(P.n_pieces);
@@ -221,15 +224,17 @@ PlanKey plan_key(const kvb_cache* c, int n_ctas) {
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 struct WsLayout {
-    size_t qp, part, total;
+    size_t qp, cnt, part, total;
     int qp_stride;
 };
 
+// workspace: query prep per head, per-head counters of the fused merge, split-K partials
 WsLayout ws_layout(const kvb_cache* c, const DecodeShape& sh, int n_pieces) {
     WsLayout L;
     L.qp_stride = kvb::qp_size(sh.R, sh.D);
     L.qp = 256;
-    L.part = align256(L.qp + size_t(c->B) * c->Hkv * L.qp_stride * 4);
+    L.cnt = align256(L.qp + size_t(c->B) * c->Hkv * L.qp_stride * 4);
+    L.part = align256(L.cnt + size_t(c->B) * c->Hkv * 4);
     L.total = align256(L.part + size_t(n_pieces) * (2 * sh.R + sh.R * sh.D) * 4);
     return L;
 }
@@ -345,8 +350,7 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
     const int nct = resolve_decode_ctas(n_ctas);
     // programmatic dependent launch of the main kernel (its first cache copies overlap the prologue),
     // except when events bracket it (an event between two launches must see the first one complete).
-    // Measured on B200 at config 1: 1.3 % per step; the same for the merge kernel was 2.7 % slower,
-    // and merging in the main kernel's tail (the CTA completing a head) gained nothing.
+    // Measured on B200 at config 1: 1.3 % per step; the same for the merge kernel was 2.7 % slower.
     const bool pdl = KVB_PDL && !(ev_begin || ev_end);
     // The plan depends only on the cache's shape and the CTA count; consecutive calls on caches of
     // one shape (the layers of a model) reuse it, and the piece table already in the kernel
@@ -373,13 +377,51 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     float* qp = reinterpret_cast<float*>(ws + W.qp);
     float* part = reinterpret_cast<float*>(ws + W.part);
+    int* head_count = reinterpret_cast<int*>(ws + W.cnt);
     const int rep = Hq / c->Hkv;
+    const int Ra = rep * Tq;
+    // the merge arguments, for the fused merge inside the main kernel or the merge kernel
+    kvb::MergeArgs ma;
+    std::memset(&ma, 0, sizeof(ma));
+    ma.B = c->B;
+    ma.Hkv = c->Hkv;
+    ma.Hq = Hq;
+    ma.Tq = Tq;
+    ma.rep = rep;
+    ma.R_act = Ra;
+    ma.R = sh.R;
+    ma.d = c->d;
+    ma.d_code = c->d_code;
+    ma.out_dtype = out_dtype == KVB_F32 ? 0 : out_dtype == KVB_F16 ? 1 : 2;
+    ma.q_dtype = q_dtype;
+    ma.exact_dtype = c->exact_dtype;
+    ma.scaling = scaling;
+    ma.part = part;
+    ma.q = q;
+    ma.k_exact = c->k_exact;
+    ma.v_exact = c->v_exact;
+    ma.exact_cap = c->exact_cap;
+    ma.n_exact = c->n_exact;
+    ma.n0 = c->n0;
+    ma.pos0 = c->pos0;
+    for (int t = 0; t < Tq; ++t) ma.qpos[t] = qpos ? qpos[t] : 0;
+    ma.lift = c->lift;
+    ma.mu_v = c->mu_v;
+    ma.out = out;
+    ma.lse = lse;
+    // Fused merge: the main kernel's CTA that completes a head's last piece merges that head, saving
+    // the merge kernel's launch and its wait on the whole main grid (its shared memory is the
+    // end-of-piece merge buffer, free at that point).
+    const bool fuse = KVB_FUSE_MERGE && !uses_tc(c) && P.n_pieces > 0 && P.n_heads <= kvb::MERGE_SMALL_HEADS &&
+                      P.max_cta_pieces <= kvb::DEC_MAX_CTA_MERGES &&
+                      (kvb::merge_smem_floats(Ra, c->d, c->d_code, kvb::DEC_THREADS) + kvb::DEC_CWARPS) * 4 <=
+                          kvb::dec_red_bytes(sh.R, sh.D);
 
     // 1. prologue
     kvb::PrologueParams pp{q, q_dtype, c->B, c->Hkv, Hq, Tq, rep, rep * Tq, c->d, c->d_code,
                            c->code_kind == KVB_CODE_MIDRISE ? c->d_code
                                                             : (c->k_mode == KVB_K_PER_TOKEN ? c->k_group : c->d_code),
-                           scaling, c->qmap, c->mu_k, qp, W.qp_stride};
+                           scaling, c->qmap, c->mu_k, qp, W.qp_stride, fuse ? head_count : nullptr};
     const size_t psm = size_t(sh.R) * (c->d + c->d_code) * 4;
     const unsigned heads = unsigned(c->B * c->Hkv);
 #define KVB_PRO(T_)                                                                        \
@@ -411,6 +453,12 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
         dp.qp = qp;
         dp.part = part;
         dp.n_pieces = P.n_pieces;
+        dp.fuse_merge = fuse;
+        if (fuse) {
+            dp.head_count = head_count;
+            dp.merge = ma;
+            for (int h = 0; h <= P.n_heads; ++h) dp.head_begin[h] = P.head_begin[h];
+        }
         if (!same_plan) {
             for (int i = 0; i <= P.n_ctas; ++i) dp.cta_begin[i] = P.cta_begin[i];
             for (int i = 0; i < P.n_pieces; ++i)
@@ -435,38 +483,13 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
             return st;
     }
 
-    // 3. merge
-    const int Ra = rep * Tq;
-    const size_t msm = size_t(Ra) * (2 * c->d + c->d_code) * 4 + 3 * Ra * 4 + 256 * 4;
+    // 3. merge (unless fused into the main kernel)
+    if (fuse) return KVB_OK;
+    const size_t msm = size_t(kvb::merge_smem_floats(Ra, c->d, c->d_code, 256)) * 4;
     cudaError_t le;
     auto launch_merge = [&](auto& mp) -> cudaError_t {
         std::memset(&mp, 0, sizeof(mp));
-        mp.B = c->B;
-        mp.Hkv = c->Hkv;
-        mp.Hq = Hq;
-        mp.Tq = Tq;
-        mp.rep = rep;
-        mp.R_act = Ra;
-        mp.R = sh.R;
-        mp.d = c->d;
-        mp.d_code = c->d_code;
-        mp.out_dtype = out_dtype == KVB_F32 ? 0 : out_dtype == KVB_F16 ? 1 : 2;
-        mp.q_dtype = q_dtype;
-        mp.exact_dtype = c->exact_dtype;
-        mp.scaling = scaling;
-        mp.part = part;
-        mp.q = q;
-        mp.k_exact = c->k_exact;
-        mp.v_exact = c->v_exact;
-        mp.exact_cap = c->exact_cap;
-        mp.n_exact = c->n_exact;
-        mp.n0 = c->n0;
-        mp.pos0 = c->pos0;
-        for (int t = 0; t < Tq; ++t) mp.qpos[t] = qpos ? qpos[t] : 0;
-        mp.lift = c->lift;
-        mp.mu_v = c->mu_v;
-        mp.out = out;
-        mp.lse = lse;
+        static_cast<kvb::MergeArgs&>(mp) = ma;
         for (int h = 0; h <= P.n_heads; ++h) mp.head_begin[h] = P.head_begin[h];
         using MP = std::remove_reference_t<decltype(mp)>;
         constexpr int NH = sizeof(MP::head_begin) / sizeof(int) - 1;

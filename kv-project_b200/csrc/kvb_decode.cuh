@@ -34,10 +34,44 @@ constexpr int DEC_THREADS = DEC_CWARPS * 32;
 constexpr int DEC_MAX_STAGES = 4;
 constexpr int DEC_MAX_PIECES = 1536;
 constexpr int DEC_MAX_CTAS = 512;
-constexpr int DEC_SMEM_BUDGET = (DEC_CTAS_PER_SM == 1 ? 227 : 113) * 1024;
+// dynamic shared memory per CTA: the opt-in maximum less a reserve for the static shared variables
+constexpr int DEC_SMEM_BUDGET = (DEC_CTAS_PER_SM == 1 ? 227 : 113) * 1024 - 256;
+// Measured on B200, config 1 (one layer, main kernel / whole call): merging each head in the main
+// kernel (the CTA completing its last piece, after its own pieces) costs +8 us in the main kernel
+// and leaves the call time unchanged (the merge kernel it replaces takes about as long), so it is
+// off by default; taking one-tile-per-warp (8-bit) chunks two at a time slows an all-8-bit layer
+// from 136 to 150 us (fewer bytes in flight per SM), so it is off too.
+#ifndef KVB_FUSE_MERGE
+#define KVB_FUSE_MERGE 0      // 1: merge each head inside the main kernel (last CTA of the head)
+#endif
+#ifndef KVB_DEC_PAIR_MIN_STAGES
+#define KVB_DEC_PAIR_MIN_STAGES 99
+#endif
+// heads one CTA may complete (its pieces are the last of at most this many heads; the host checks)
+constexpr int DEC_MAX_CTA_MERGES = 32;
+// one-tile-per-warp chunks are taken two at a time when the CTA's ring has at least this many stages
+constexpr int DEC_PAIR_MIN_STAGES = KVB_DEC_PAIR_MIN_STAGES;
 // End-of-piece merge buffer: per-warp row maxima and sums, and DEC_RED_SLOTS slots of R x D partial
 // accumulators (with fewer slots than warps, the warps past the slots add into them in a second phase).
 __host__ __device__ constexpr int dec_red_bytes(int R, int D) { return (2 * DEC_CWARPS * R + DEC_RED_SLOTS * R * D) * 4; }
+
+constexpr int MERGE_MAX_HEADS = 4096;
+constexpr int MERGE_SMALL_HEADS = 256;
+struct MergeArgs {
+    int B, Hkv, Hq, Tq, rep, R_act, R, d, d_code, out_dtype, q_dtype, exact_dtype;
+    float scaling;
+    const float* part;
+    const void* q;
+    const void* k_exact;
+    const void* v_exact;
+    int64_t exact_cap, n_exact, n0, pos0;
+    int64_t qpos[16];
+    const float* lift;      // (Hkv, d_code, d) or null
+    const float* mu_v;      // (Hkv, d) or null
+    void* out;
+    float* lse;             // (B, Tq, Hq) natural-log sum of exp(scaled logits), or null
+};
+
 
 // ------------------------------------------------------------------------------------------
 // Parameters
@@ -59,6 +93,7 @@ struct PrologueParams {
     const float* mu_k;      // (Hkv, d) or null
     float* qp;              // output, per head qp_stride floats
     int qp_stride;
+    int* head_count;        // per head counters of the fused merge (zeroed here), or null
 };
 
 struct DecodeParams {
@@ -69,7 +104,13 @@ struct DecodeParams {
     float* part;            // per piece: m2[R] | l[R] | acc[R][D]
     int n_pieces;
     int cta_begin[DEC_MAX_CTAS + 1];
-    int2 piece[DEC_MAX_PIECES];            // packed (head, stratum | chunk_lo << 2 | chunk_hi << 17)
+    int2 piece[DEC_MAX_PIECES];            // packed (head | slot << 16, stratum | chunk_lo << 2 | chunk_hi << 17)
+    // fused merge (heads <= MERGE_SMALL_HEADS): the CTA that completes the last of a head's pieces
+    // merges the head (merge_head) right after its own end-of-piece merge
+    int fuse_merge;
+    int* head_count;                       // per head, zeroed by the prologue of the same call
+    int head_begin[MERGE_SMALL_HEADS + 1]; // slots of each head's partials
+    MergeArgs merge;
 };
 
 // A piece (head, stratum, chunk range [lo, hi)) and the slot of its split-K partial in 8 bytes: the
@@ -86,6 +127,195 @@ __host__ __device__ __forceinline__ int4 unpack_piece(int2 v) {
 __host__ __device__ __forceinline__ int piece_slot(int2 v) { return int(unsigned(v.x) >> 16); }
 
 // ------------------------------------------------------------------------------------------
+// 3. merge of one head: exact rows (fp32 on CUDA cores), log-sum-exp merge of the head's split-K
+//    partials (STRATA_KV.py:1784-1792), optional lift back to model space, output in q's dtype.
+//    Run by the last CTA of the main kernel to finish one of the head's pieces (up to
+//    MERGE_SMALL_HEADS heads), or by decode_merge (one CTA per head) otherwise.
+// ------------------------------------------------------------------------------------------
+// Shared memory of merge_head in floats: s_q, s_acc, s_out, row stats, s_p[nthreads].
+__host__ __device__ constexpr int merge_smem_floats(int Ra, int d, int dc, int nthreads) {
+    return Ra * (2 * d + dc) + 3 * Ra + nthreads;
+}
+
+// Head bh, partial slots [pb, pe); all `nthreads` threads of the CTA call it (it synchronises).
+// sm: merge_smem_floats(...) floats; s_w: nthreads / 32 floats.
+template <typename TQ, typename TE>
+__device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, int pe, float* sm, float* s_w, int tid,
+                                       int nthreads) {
+    const int b = bh / p.Hkv, h = bh % p.Hkv;
+    const int R = p.R, d = p.d, dc = p.d_code, Ra = p.R_act;
+    float* s_q = sm;                       // [Ra][d]
+    float* s_acc = s_q + Ra * d;           // [Ra][dc] coded accumulator (weighted)
+    float* s_out = s_acc + Ra * dc;        // [Ra][d]
+    float* s_rowM = s_out + Ra * d;        // [Ra]
+    float* s_rowL = s_rowM + Ra;           // [Ra] total mass
+    float* s_rowLc = s_rowL + Ra;          // [Ra] coded mass
+    float* s_p = s_rowLc + Ra;             // [nthreads] scratch probabilities
+    const TQ* q = static_cast<const TQ*>(p.q);
+    const int nwarps = nthreads >> 5;
+    for (int o = tid; o < Ra * d; o += nthreads) {
+        const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
+        s_q[o] = to_f32(q[((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * d + c]);
+    }
+    const int np = pe - pb;
+    const size_t pstride = size_t(2 * R + R * dc);
+    const float* part = p.part + size_t(pb) * pstride;
+    // coded partials.  The merge sits between two layers' main kernels, so its latency counts: when
+    // they fit, every piece's (max, mass) is fetched at once into shared memory (s_p, s_out as
+    // scratch) and the per-piece weights 2^(m - M) are kept there; each (row, channel) thread then
+    // issues its pieces' loads eight at a time.  Same arithmetic and order as one load at a time.
+    const bool staged = np * Ra <= nthreads && np * Ra <= Ra * d;
+    if (staged) {
+        for (int o = tid; o < np * Ra; o += nthreads) {
+            const int k = o / Ra, r = o - k * Ra;
+            s_p[o] = part[k * pstride + r];
+            s_out[o] = part[k * pstride + R + r];
+        }
+        __syncthreads();
+        if (tid < Ra) {
+            float M = -INFINITY;
+            for (int k = 0; k < np; ++k) M = fmaxf(M, s_p[k * Ra + tid]);
+            float L = 0.f;
+            for (int k = 0; k < np; ++k) {
+                const float m = s_p[k * Ra + tid];
+                const float w = (m == -INFINITY) ? 0.f : ex2(m - M);
+                L += (m == -INFINITY) ? 0.f : w * s_out[k * Ra + tid];
+                s_p[k * Ra + tid] = w;
+            }
+            s_rowM[tid] = M;
+            s_rowLc[tid] = L;
+        }
+    } else if (tid < Ra) {
+        float M = -INFINITY;
+        for (int k = 0; k < np; ++k) M = fmaxf(M, part[k * pstride + tid]);
+        float L = 0.f;
+        for (int k = 0; k < np; ++k) {
+            const float m = part[k * pstride + tid];
+            L += (m == -INFINITY) ? 0.f : ex2(m - M) * part[k * pstride + R + tid];
+        }
+        s_rowM[tid] = M;
+        s_rowLc[tid] = L;
+    }
+    __syncthreads();
+    for (int o = tid; o < Ra * dc; o += nthreads) {
+        const int r = o / dc, c = o % dc;
+        const float* src = part + 2 * R + r * dc + c;
+        float a = 0.f;
+        for (int k0 = 0; k0 < np; k0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = k0 + j < np ? src[(k0 + j) * pstride] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (k0 + j >= np) break;
+                if (staged) {
+                    const float w = s_p[(k0 + j) * Ra + r];
+                    if (w != 0.f) a += w * v[j];
+                } else {
+                    const float m = part[(k0 + j) * pstride + r];
+                    if (m != -INFINITY) a += ex2(m - s_rowM[r]) * v[j];
+                }
+            }
+        }
+        s_acc[o] = a;
+    }
+    __syncthreads();
+    // lift to model space (+ coded mass * mean value)
+    for (int o = tid; o < Ra * d; o += nthreads) {
+        const int r = o / d, c = o % d;
+        float v;
+        if (p.lift) {
+            const float* Lm = p.lift + size_t(h) * dc * d;
+            v = 0.f;
+            for (int k = 0; k < dc; ++k) v = fmaf(s_acc[r * dc + k], Lm[size_t(k) * d + c], v);
+        } else {
+            v = s_acc[r * dc + c];
+        }
+        if (p.mu_v) v = fmaf(s_rowLc[r], p.mu_v[size_t(h) * d + c], v);
+        s_out[o] = v;
+    }
+    if (tid < Ra) s_rowL[tid] = s_rowLc[tid];
+    __syncthreads();
+    // exact rows, fp32 on CUDA cores, merged online in blocks of 256 rows
+    if (p.n_exact > 0) {
+        const TE* Ke = static_cast<const TE*>(p.k_exact) + size_t(bh) * p.exact_cap * d;
+        const TE* Ve = static_cast<const TE*>(p.v_exact) + size_t(bh) * p.exact_cap * d;
+        const float lam = p.scaling * LOG2E;
+        for (int r = 0; r < Ra; ++r) {
+            const int tq = r % p.Tq;
+            for (int64_t j0 = 0; j0 < p.n_exact; j0 += nthreads) {
+                const int64_t j = j0 + tid;
+                float s = -INFINITY;
+                if (j < p.n_exact && (j < p.n0 || p.pos0 + (j - p.n0) <= p.qpos[tq])) {
+                    float a = 0.f;
+                    for (int c = 0; c < d; ++c) a = fmaf(s_q[r * d + c], to_f32(Ke[j * d + c]), a);
+                    s = a * lam;
+                }
+                float mx = warp_max(s);
+                if ((tid & 31) == 0) s_w[tid >> 5] = mx;
+                __syncthreads();
+                mx = s_w[0];
+                for (int w = 1; w < nwarps; ++w) mx = fmaxf(mx, s_w[w]);
+                const float Mold = s_rowM[r];
+                const float Mnew = fmaxf(Mold, mx);
+                const float pj = (s == -INFINITY) ? 0.f : ex2(s - Mnew);
+                s_p[tid] = pj;
+                float ps = warp_sum(pj);
+                __syncthreads();
+                if ((tid & 31) == 0) s_w[tid >> 5] = ps;
+                __syncthreads();
+                float tot = 0.f;
+                for (int w = 0; w < nwarps; ++w) tot += s_w[w];
+                const float alpha = (Mold == -INFINITY) ? 0.f : ex2(Mold - Mnew);
+                const int64_t nj = imin64(nthreads, p.n_exact - j0);
+                for (int c = tid; c < d; c += nthreads) {
+                    float a = s_out[r * d + c] * alpha;
+                    for (int64_t k = 0; k < nj; ++k) a = fmaf(s_p[k], to_f32(Ve[(j0 + k) * d + c]), a);
+                    s_out[r * d + c] = a;
+                }
+                __syncthreads();
+                if (tid == 0) {
+                    s_rowL[r] = s_rowL[r] * alpha + tot;
+                    s_rowM[r] = Mnew;
+                }
+                __syncthreads();
+            }
+        }
+    }
+    __syncthreads();
+    // a row with no readable token (possible in one part of a sequence split) gets 0 and lse -inf
+    for (int o = tid; o < Ra * d; o += nthreads) {
+        const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
+        const float v = s_rowL[r] > 0.f ? s_out[o] / s_rowL[r] : 0.f;
+        const size_t oi = ((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c;
+        if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
+        else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
+        else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
+    }
+    if (p.lse && tid < Ra) {
+        const int i = tid / p.Tq, t = tid % p.Tq;
+        const float L = s_rowL[tid];
+        p.lse[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
+            L > 0.f ? (s_rowM[tid] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+    }
+}
+
+// The per-head piece ranges ride in the kernel parameters; two capacities keep the parameter block
+// (copied on every launch) small for the usual head counts.  grid (B * Hkv), block 256.
+template <int NH>
+struct MergeParams : MergeArgs {
+    int head_begin[NH + 1];
+};
+
+template <typename TQ, typename TE, int NH>
+__global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ MergeParams<NH> p) {
+    extern __shared__ float sm[];
+    __shared__ float s_w[8];
+    const int bh = blockIdx.x;
+    merge_head<TQ, TE>(p, bh, p.head_begin[bh], p.head_begin[bh + 1], sm, s_w, threadIdx.x, blockDim.x);
+}
+
+// ------------------------------------------------------------------------------------------
 // 1. prologue: grid (B * Hkv), block 128
 // ------------------------------------------------------------------------------------------
 template <typename T, int R>
@@ -96,6 +326,7 @@ __global__ void __launch_bounds__(128) decode_prologue(const PrologueParams p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int bh = blockIdx.x, b = bh / p.Hkv, h = bh % p.Hkv;
     const int d = p.d, dc = p.d_code;
+    if (p.head_count && threadIdx.x == 0) p.head_count[bh] = 0;
     const T* q = static_cast<const T*>(p.q);
     float* out = p.qp + size_t(bh) * p.qp_stride;
     float* s_qc = s_q + R * d;
@@ -276,6 +507,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
     constexpr int red_bytes = dec_red_bytes(R, D);
     uint8_t* stages = smem + 128 + ((red_bytes + 127) / 128) * 128;
 
+    __shared__ int s_merge[DEC_MAX_CTA_MERGES], s_nmerge;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pc0 = p.cta_begin[blockIdx.x], pc1 = p.cta_begin[blockIdx.x + 1];
     // This CTA's ring: as many stages of its largest chunk as fit (a CTA whose pieces are all 8-bit
@@ -288,6 +520,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
             mbar_init(&full[s], 1);
             rel[s] = 0;
         }
+        s_nmerge = 0;
         fence_mbar_init();
     }
     __syncthreads();
@@ -387,62 +620,22 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
                 S.m[e] = -INFINITY;
                 S.l[e] = 0.f;
 #pragma unroll
-                for (int jv = 0; jv < C::NVT; ++jv) {
-                    S.sp[jv][e] = 0.f;
-                    S.z[jv][e] = 0.f;
-                }
+                for (int jv = 0; jv < C::NVT; ++jv) S.z[jv][e] = 0.f;
             }
+#pragma unroll
+            for (int jv = 0; jv < C::NVT; ++jv)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) S.spa[jv][e] = 0.f;
 #pragma unroll
             for (int jv = 0; jv < C::NVT; ++jv)
 #pragma unroll
                 for (int mt = 0; mt < C::MT; ++mt)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) S.acc[jv][mt][e] = 0.f;
-            for (int ch = pc.z; ch < pc.w; ++ch) {
-                const int s = it % nstage;
-                const uint32_t ph = (it / nstage) & 1;
-                // after a timeout, keep polling briefly (a fill may still land) but skip the compute
-                if (!mbar_wait(&full[s], ph, ok ? 2000000000ull : 1000000ull)) ok = false;
-                if constexpr (KMODE == KM_CHANNEL) {
-                    // all warps build this chunk's per-channel fragments, then meet before using them
-                    if (ok) {
-                        const int64_t tok0 = int64_t(ch) * sd.tok;
-                        const int ntok = int(imin64(sd.tok, sd.n - tok0));
-                        const int ng = (ntok + p.k_group - 1) / p.k_group;
-                        uint8_t* st = stages + s * sb;
-                        build_channel_frags<D, R, GK, GV, KMODE, CODE, KB>(st + L.km, st + L.kr, ng, red, warp, lane);
-                    }
-                    __syncthreads();
-                }
-                if (ok) {
-                    const int64_t tok0 = int64_t(ch) * sd.tok;
-                    const int ntok = int(imin64(sd.tok, sd.n - tok0));
-                    const int ntiles = (ntok + 15) >> 4;
-                    const uint8_t* st = stages + s * sb;
-                    auto cfp = [&](int tl) -> const uint8_t* {
-                        if constexpr (KMODE == KM_CHANNEL) return st + L.km + ((tl * 16) / p.k_group) * C::FRAG_BYTES;
-                        else return nullptr;
-                    };
-                    if (ntok == TOK && sd.tok == TOK) {
-                        // whole chunk: fixed tile count per warp, no masking
-                        if constexpr (PW == 1) {
-                            TL::template run<true, 1>(S, X, st, O, warp, -1, ntok, lane, cfp(warp), nullptr);
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < PW; i += 2) {
-                                const int t0 = warp + DEC_CWARPS * i, t1 = t0 + DEC_CWARPS;
-                                TL::template run<true, 2>(S, X, st, O, t0, t1, ntok, lane, cfp(t0), cfp(t1));
-                            }
-                        }
-                    } else {
-                        for (int tl = warp; tl < ntiles; tl += 2 * DEC_CWARPS) {
-                            const int tl1 = tl + DEC_CWARPS < ntiles ? tl + DEC_CWARPS : -1;
-                            TL::template run<false, 2>(S, X, st, O, tl, tl1, ntok, lane, cfp(tl), cfp(imax64(tl1, 0)));
-                        }
-                    }
-                }
-                // release the stage; the last of the 12 warps refills it (acq_rel counter in smem,
-                // then a proxy fence so the bulk copies are ordered after every warp's reads)
+            // release stage s of CTA chunk k; the last of the warps refills it with chunk k + nstage
+            // (acq_rel counter in shared memory, then a proxy fence so the bulk copies are ordered after
+            // every warp's reads)
+            auto release = [&](int s, uint32_t k) {
                 __syncwarp();
                 int last = 0;
                 if (lane == 0) {
@@ -455,10 +648,85 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
                     }
                 }
                 last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) fill(it + uint32_t(nstage));
+                if (last) fill(k + uint32_t(nstage));
+            };
+            for (int ch = pc.z; ch < pc.w;) {
+                const int s = it % nstage;
+                const uint32_t ph = (it / nstage) & 1;
+                // after a timeout, keep polling briefly (a fill may still land) but skip the compute
+                if (!mbar_wait(&full[s], ph, ok ? 2000000000ull : 1000000ull)) ok = false;
+                const int64_t tok0 = int64_t(ch) * sd.tok;
+                const int ntok = int(imin64(sd.tok, sd.n - tok0));
+                // Chunks of one tile per warp (8-bit codes): two whole chunks at once, so that every warp
+                // works two independent tiles (one per stage), as the narrower widths do within a chunk.
+                if constexpr (PW == 1 && KMODE == KM_TOKEN) {
+                    if (nstage >= DEC_PAIR_MIN_STAGES && ch + 1 < pc.w && ntok == TOK && sd.tok == TOK &&
+                        int64_t(ch + 2) * sd.tok <= sd.n) {
+                        const int s1 = (it + 1) % nstage;
+                        if (!mbar_wait(&full[s1], ((it + 1) / nstage) & 1, ok ? 2000000000ull : 1000000ull)) ok = false;
+                        if (ok)
+                            TL::template run<true, 2>(S, X, stages + s * sb, stages + s1 * sb, O, warp, warp, ntok, lane,
+                                                      nullptr, nullptr);
+                        release(s, it);
+                        release(s1, it + 1);
+                        it += 2;
+                        ch += 2;
+                        continue;
+                    }
+                }
+                if constexpr (KMODE == KM_CHANNEL) {
+                    // all warps build this chunk's per-channel fragments, then meet before using them
+                    if (ok) {
+                        const int ng = (ntok + p.k_group - 1) / p.k_group;
+                        uint8_t* st = stages + s * sb;
+                        build_channel_frags<D, R, GK, GV, KMODE, CODE, KB>(st + L.km, st + L.kr, ng, red, warp, lane);
+                    }
+                    __syncthreads();
+                }
+                if (ok) {
+                    const int ntiles = (ntok + 15) >> 4;
+                    const uint8_t* st = stages + s * sb;
+                    auto cfp = [&](int tl) -> const uint8_t* {
+                        if constexpr (KMODE == KM_CHANNEL) return st + L.km + ((tl * 16) / p.k_group) * C::FRAG_BYTES;
+                        else return nullptr;
+                    };
+                    if (ntok == TOK && sd.tok == TOK) {
+                        // whole chunk: fixed tile count per warp, no masking
+                        if constexpr (PW == 1) {
+                            TL::template run<true, 1>(S, X, st, st, O, warp, -1, ntok, lane, cfp(warp), nullptr);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < PW; i += 2) {
+                                const int t0 = warp + DEC_CWARPS * i, t1 = t0 + DEC_CWARPS;
+                                TL::template run<true, 2>(S, X, st, st, O, t0, t1, ntok, lane, cfp(t0), cfp(t1));
+                            }
+                        }
+                    } else {
+                        for (int tl = warp; tl < ntiles; tl += 2 * DEC_CWARPS) {
+                            const int tl1 = tl + DEC_CWARPS < ntiles ? tl + DEC_CWARPS : -1;
+                            TL::template run<false, 2>(S, X, st, st, O, tl, tl1, ntok, lane, cfp(tl),
+                                                       cfp(imax64(tl1, 0)));
+                        }
+                    }
+                }
+                release(s, it);
                 ++it;
+                ++ch;
             }
             TL::flush(S, red, part, warp, lane);
+#if KVB_FUSE_MERGE
+            if (p.fuse_merge) {
+                // is this CTA the one completing the head's last piece?  Then it merges the head once
+                // its own pieces are done (at the end of the kernel, where no loop state is live)
+                __threadfence();
+                __syncthreads();
+                const int head = pc.x;
+                if (threadIdx.x == 0) {
+                    const int np = p.head_begin[head + 1] - p.head_begin[head];
+                    if (atomicAdd(&p.head_count[head], 1) == np - 1) s_merge[s_nmerge++] = head;
+                }
+            }
+#endif
         };
         using I2 = std::integral_constant<int, 2>;
         using I4 = std::integral_constant<int, 4>;
@@ -477,197 +745,29 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
         }
         if (!done) raise_status(KVB_DEV_BOUNDS);
     }
+#if KVB_FUSE_MERGE
+    // the heads this CTA completed: merge them (their partials are read through L2, after the fences
+    // of the CTAs that wrote them)
+    __syncthreads();
+    for (int i = 0; i < s_nmerge; ++i) {
+        __threadfence();
+        const int head = s_merge[i];
+        const int pb = p.head_begin[head], pe = p.head_begin[head + 1];
+        float* sw = red + merge_smem_floats(p.merge.R_act, p.merge.d, p.merge.d_code, DEC_THREADS);
+        if (p.merge.q_dtype == 0)
+            merge_head<float, float>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+        else if (p.merge.q_dtype == 1)
+            merge_head<__half, __half>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+        else
+            merge_head<__nv_bfloat16, __nv_bfloat16>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+        __syncthreads();
+    }
+#endif
     // Every issued fill has been waited for above; if a wait gave up, give late copies a bounded
     // chance to land before the CTA's shared memory is released.
     if (threadIdx.x == 0 && it > 0) {
         const uint32_t first = it > uint32_t(nstage) ? it - nstage : 0;
         for (uint32_t k = first; k < it; ++k) mbar_wait(&full[k % nstage], (k / nstage) & 1, 10000000ull);
-    }
-}
-
-// ------------------------------------------------------------------------------------------
-// 3. merge: grid (B * Hkv), block 256
-// ------------------------------------------------------------------------------------------
-// The per-head piece ranges ride in the kernel parameters; two capacities keep the parameter block
-// (copied on every launch) small for the usual head counts.
-constexpr int MERGE_MAX_HEADS = 4096;
-constexpr int MERGE_SMALL_HEADS = 256;
-template <int NH>
-struct MergeParams {
-    int B, Hkv, Hq, Tq, rep, R_act, R, d, d_code, out_dtype, q_dtype, exact_dtype;
-    float scaling;
-    const float* part;
-    const void* q;
-    const void* k_exact;
-    const void* v_exact;
-    int64_t exact_cap, n_exact, n0, pos0;
-    int64_t qpos[16];
-    const float* lift;      // (Hkv, d_code, d) or null
-    const float* mu_v;      // (Hkv, d) or null
-    void* out;
-    float* lse;             // (B, Tq, Hq) natural-log sum of exp(scaled logits), or null
-    int head_begin[NH + 1];
-};
-
-template <typename TQ, typename TE, int NH>
-__global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ MergeParams<NH> p) {
-    extern __shared__ float sm[];
-    __shared__ float s_w[8];
-    const int bh = blockIdx.x, b = bh / p.Hkv, h = bh % p.Hkv;
-    const int R = p.R, d = p.d, dc = p.d_code, Ra = p.R_act;
-    float* s_q = sm;                       // [Ra][d]
-    float* s_acc = s_q + Ra * d;           // [Ra][dc] coded accumulator (weighted)
-    float* s_out = s_acc + Ra * dc;        // [Ra][d]
-    float* s_rowM = s_out + Ra * d;        // [Ra]
-    float* s_rowL = s_rowM + Ra;           // [Ra] total mass
-    float* s_rowLc = s_rowL + Ra;          // [Ra] coded mass
-    float* s_p = s_rowLc + Ra;             // [256] scratch probabilities
-    const TQ* q = static_cast<const TQ*>(p.q);
-    const int tid = threadIdx.x;
-    for (int o = tid; o < Ra * d; o += blockDim.x) {
-        const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
-        s_q[o] = to_f32(q[((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * d + c]);
-    }
-    const int pb = p.head_begin[bh], pe = p.head_begin[bh + 1], np = pe - pb;
-    const size_t pstride = size_t(2 * R + R * dc);
-    const float* part = p.part + size_t(pb) * pstride;
-    // coded partials.  The merge sits between two layers' main kernels, so its latency counts: when
-    // they fit, every piece's (max, mass) is fetched at once into shared memory (s_p, s_out as
-    // scratch) and the per-piece weights 2^(m - M) are kept there; each (row, channel) thread then
-    // issues its pieces' loads eight at a time.  Same arithmetic and order as one load at a time.
-    const bool staged = np * Ra <= 256 && np * Ra <= Ra * d;
-    if (staged) {
-        for (int o = tid; o < np * Ra; o += blockDim.x) {
-            const int k = o / Ra, r = o - k * Ra;
-            s_p[o] = part[k * pstride + r];
-            s_out[o] = part[k * pstride + R + r];
-        }
-        __syncthreads();
-        if (tid < Ra) {
-            float M = -INFINITY;
-            for (int k = 0; k < np; ++k) M = fmaxf(M, s_p[k * Ra + tid]);
-            float L = 0.f;
-            for (int k = 0; k < np; ++k) {
-                const float m = s_p[k * Ra + tid];
-                const float w = (m == -INFINITY) ? 0.f : ex2(m - M);
-                L += (m == -INFINITY) ? 0.f : w * s_out[k * Ra + tid];
-                s_p[k * Ra + tid] = w;
-            }
-            s_rowM[tid] = M;
-            s_rowLc[tid] = L;
-        }
-    } else if (tid < Ra) {
-        float M = -INFINITY;
-        for (int k = 0; k < np; ++k) M = fmaxf(M, part[k * pstride + tid]);
-        float L = 0.f;
-        for (int k = 0; k < np; ++k) {
-            const float m = part[k * pstride + tid];
-            L += (m == -INFINITY) ? 0.f : ex2(m - M) * part[k * pstride + R + tid];
-        }
-        s_rowM[tid] = M;
-        s_rowLc[tid] = L;
-    }
-    __syncthreads();
-    for (int o = tid; o < Ra * dc; o += blockDim.x) {
-        const int r = o / dc, c = o % dc;
-        const float* src = part + 2 * R + r * dc + c;
-        float a = 0.f;
-        for (int k0 = 0; k0 < np; k0 += 8) {
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = k0 + j < np ? src[(k0 + j) * pstride] : 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                if (k0 + j >= np) break;
-                if (staged) {
-                    const float w = s_p[(k0 + j) * Ra + r];
-                    if (w != 0.f) a += w * v[j];
-                } else {
-                    const float m = part[(k0 + j) * pstride + r];
-                    if (m != -INFINITY) a += ex2(m - s_rowM[r]) * v[j];
-                }
-            }
-        }
-        s_acc[o] = a;
-    }
-    __syncthreads();
-    // lift to model space (+ coded mass * mean value)
-    for (int o = tid; o < Ra * d; o += blockDim.x) {
-        const int r = o / d, c = o % d;
-        float v;
-        if (p.lift) {
-            const float* Lm = p.lift + size_t(h) * dc * d;
-            v = 0.f;
-            for (int k = 0; k < dc; ++k) v = fmaf(s_acc[r * dc + k], Lm[size_t(k) * d + c], v);
-        } else {
-            v = s_acc[r * dc + c];
-        }
-        if (p.mu_v) v = fmaf(s_rowLc[r], p.mu_v[size_t(h) * d + c], v);
-        s_out[o] = v;
-    }
-    if (tid < Ra) s_rowL[tid] = s_rowLc[tid];
-    __syncthreads();
-    // exact rows, fp32 on CUDA cores, merged online in blocks of 256 rows
-    if (p.n_exact > 0) {
-        const TE* Ke = static_cast<const TE*>(p.k_exact) + size_t(bh) * p.exact_cap * d;
-        const TE* Ve = static_cast<const TE*>(p.v_exact) + size_t(bh) * p.exact_cap * d;
-        const float lam = p.scaling * LOG2E;
-        for (int r = 0; r < Ra; ++r) {
-            const int tq = r % p.Tq;
-            for (int64_t j0 = 0; j0 < p.n_exact; j0 += blockDim.x) {
-                const int64_t j = j0 + tid;
-                float s = -INFINITY;
-                if (j < p.n_exact && (j < p.n0 || p.pos0 + (j - p.n0) <= p.qpos[tq])) {
-                    float a = 0.f;
-                    for (int c = 0; c < d; ++c) a = fmaf(s_q[r * d + c], to_f32(Ke[j * d + c]), a);
-                    s = a * lam;
-                }
-                float mx = warp_max(s);
-                if ((tid & 31) == 0) s_w[tid >> 5] = mx;
-                __syncthreads();
-                mx = s_w[0];
-                for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_w[w]);
-                const float Mold = s_rowM[r];
-                const float Mnew = fmaxf(Mold, mx);
-                const float pj = (s == -INFINITY) ? 0.f : ex2(s - Mnew);
-                s_p[tid] = pj;
-                float ps = warp_sum(pj);
-                __syncthreads();
-                if ((tid & 31) == 0) s_w[tid >> 5] = ps;
-                __syncthreads();
-                float tot = 0.f;
-                for (int w = 0; w < 8; ++w) tot += s_w[w];
-                const float alpha = (Mold == -INFINITY) ? 0.f : ex2(Mold - Mnew);
-                const int64_t nj = imin64(blockDim.x, p.n_exact - j0);
-                for (int c = tid; c < d; c += blockDim.x) {
-                    float a = s_out[r * d + c] * alpha;
-                    for (int64_t k = 0; k < nj; ++k) a = fmaf(s_p[k], to_f32(Ve[(j0 + k) * d + c]), a);
-                    s_out[r * d + c] = a;
-                }
-                __syncthreads();
-                if (tid == 0) {
-                    s_rowL[r] = s_rowL[r] * alpha + tot;
-                    s_rowM[r] = Mnew;
-                }
-                __syncthreads();
-            }
-        }
-    }
-    __syncthreads();
-    // a row with no readable token (possible in one part of a sequence split) gets 0 and lse -inf
-    for (int o = tid; o < Ra * d; o += blockDim.x) {
-        const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
-        const float v = s_rowL[r] > 0.f ? s_out[o] / s_rowL[r] : 0.f;
-        const size_t oi = ((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c;
-        if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
-        else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
-        else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
-    }
-    if (p.lse && tid < Ra) {
-        const int i = tid / p.Tq, t = tid % p.Tq;
-        const float L = s_rowL[tid];
-        p.lse[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
-            L > 0.f ? (s_rowM[tid] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
     }
 }
 

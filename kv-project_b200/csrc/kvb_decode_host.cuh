@@ -20,7 +20,7 @@ struct DecodeShape {
 // warps gets the same number of tiles), about 48 KB of codes, at most 768 tokens.
 
 struct Plan {
-    int n_ctas = 0, n_pieces = 0, n_heads = 0;
+    int n_ctas = 0, n_pieces = 0, n_heads = 0, max_cta_pieces = 0;
     std::vector<int> cta_begin, head_begin;
     std::vector<int> piece;   // 4 per piece (head, stratum, first chunk, end chunk), in CTA order
     std::vector<int> slot;    // per piece: index of its partial (head-major order; head_begin indexes slots)

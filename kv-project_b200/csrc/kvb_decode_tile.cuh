@@ -21,6 +21,9 @@ namespace kvb {
 #ifndef KVB_DEC_CTAS_PER_SM
 #define KVB_DEC_CTAS_PER_SM 1
 #endif
+#ifndef KVB_DEC_HOIST
+#define KVB_DEC_HOIST 0       // value codes before the softmax branch: 1 loaded + extracted, 2 loaded
+#endif
 #ifndef KVB_DEC_RED_SLOTS
 #define KVB_DEC_RED_SLOTS KVB_DEC_WARPS
 #endif
@@ -189,7 +192,10 @@ template <class C>
 struct WarpState {
     float m[2], l[2];                       // my two rows (log2 domain max, sum)
     float acc[C::NVT][C::MT][4];
-    float sp[C::NVT][2], z[C::NVT][2];      // sum of fp16 P', sum of p * zero point (my columns)
+    // sum over tokens of the fp16 P' per MMA column, as the accumulator of an MMA of a ones matrix
+    // with the P' fragments (every row equal: elements 0, 1 are my columns 2t, 2t + 1)
+    float spa[C::NVT][4];
+    float z[C::NVT][2];                     // sum of p * zero point (my columns, partial over lanes)
 };
 
 template <int D, int R, int GK, int GV, int KMODE, int CODE, int KB, int VB>
@@ -288,13 +294,15 @@ struct Tile {
     __device__ static void logits(float (&s2)[2][2], const Ctx& X, const uint8_t* stage, const Off& O, int tile,
                                   int lane, const uint8_t* cf) {
         const int t = lane & 3;
+        // per-token keys: chain 0 starts at -1024 * (fp16 query column sum), removing the offset of
+        // the 1024 pattern inside the MMA (partial sums stay near the signal's size)
         float acc[NKT][NCH][4];
 #pragma unroll
         for (int j = 0; j < NKT; ++j)
 #pragma unroll
             for (int c = 0; c < NCH; ++c)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) acc[j][c][e] = 0.f;
+                for (int e = 0; e < 4; ++e) acc[j][c][e] = (KMODE == KM_TOKEN && c == 0) ? -X.corr[j][e & 1] : 0.f;
         {
             const uint8_t* ka = stage + O.kA + tile * (16 * LK::RB);
             uint32_t wa[LK::KW], wb[LK::KW];
@@ -362,7 +370,7 @@ struct Tile {
                         sc = f.y;
                     }
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) part[e] += sc * (dot[j][2 * hh + e] - X.corr[j][e]) + lo * X.qs[j][e];
+                    for (int e = 0; e < 2; ++e) part[e] += sc * dot[j][2 * hh + e] + lo * X.qs[j][e];
                 }
 #pragma unroll
                 for (int e = 0; e < 2; ++e) s2[hh][e] = part[e];
@@ -380,12 +388,44 @@ struct Tile {
         }
     }
 
-    // Values of one tile: P' fragments from my probabilities, value codes as A, MMA into S.acc.
+    // Value codes of one tile as MMA A fragments: logical tokens (2t, 2t+1) and (2t+8, 2t+9) =
+    // physical rows t, t+4, t+8, t+12 (channels on M, tokens on K).  vload reads the code words of
+    // the token pairs (interleaved per 16-bit half), vext turns them into fp16 operands.  Neither
+    // depends on the softmax, so run() may issue them before the softmax branch.
+    __device__ static void vload(uint32_t (&cw)[2][LV::NCW], const uint8_t* stage, const Off& O, int tile) {
+#pragma unroll
+        for (int pair = 0; pair < 2; ++pair) {
+            const uint8_t* r0p = stage + O.vA + tile * (16 * LV::RB) + pair * (8 * LV::RB);
+            const uint8_t* r1p = r0p + 4 * LV::RB;
+            if constexpr (LV::U == 2) {
+                const uint32_t a = *reinterpret_cast<const uint16_t*>(r0p);
+                const uint32_t b = *reinterpret_cast<const uint16_t*>(r1p);
+                cw[pair][0] = __byte_perm(a, b, 0x5410);
+            } else {
+                uint32_t wa[LV::U / 4], wb[LV::U / 4];
+                lds_words<LV::U / 4>(r0p, wa);
+                lds_words<LV::U / 4>(r1p, wb);
+#pragma unroll
+                for (int i = 0; i < LV::U / 4; ++i) {
+                    cw[pair][2 * i] = __byte_perm(wa[i], wb[i], 0x5410);
+                    cw[pair][2 * i + 1] = __byte_perm(wa[i], wb[i], 0x7632);
+                }
+            }
+        }
+    }
+    __device__ static void vext(uint32_t (&va)[2][D / 8], const uint32_t (&cw)[2][LV::NCW]) {
+#pragma unroll
+        for (int pair = 0; pair < 2; ++pair)
+#pragma unroll
+            for (int c = 0; c < LV::NCW; ++c) Ext<VB>::run(cw[pair][c], va[pair] + c * LV::NE);
+    }
+
+    // Values of one tile: P' fragments from my probabilities, the value codes `va` as A, MMA into
+    // S.acc; the same P' against a ones matrix accumulates the column sums of P' (S.spa).
     // MASK: zero the scale / zero point of padding rows (a partial chunk may read rows past n).
     template <bool MASK>
-    __device__ static void values(WarpState<C>& S, const float (&pr)[2][2], const bool (&vld)[2],
-                                  const uint8_t* stage, const Off& O, int tile, int lane) {
-        const int g = lane >> 2, t = lane & 3;
+    __device__ static void vmma(WarpState<C>& S, const float (&pr)[2][2], const bool (&vld)[2],
+                                const uint32_t (&va)[2][D / 8], const uint8_t* stage, const Off& O, int tile) {
         uint32_t bv[NVT][2];
 #pragma unroll
         for (int jv = 0; jv < NVT; ++jv) {
@@ -407,37 +447,13 @@ struct Tile {
             }
             const uint32_t ra = pack_half2(pr[0][0] * sc[0], pr[0][1] * sc[0]);
             const uint32_t rb = pack_half2(pr[1][0] * sc[1], pr[1][1] * sc[1]);
-            const float2 fa = unpack_half2(ra), fb = unpack_half2(rb);
-            S.sp[jv][0] += fa.x + fb.x;
-            S.sp[jv][1] += fa.y + fb.y;
 #pragma unroll
             for (int e = 0; e < 2; ++e) S.z[jv][e] += pr[0][e] * lo[0] + pr[1][e] * lo[1];
             bv[jv][0] = movmatrix_trans(ra);
             bv[jv][1] = movmatrix_trans(rb);
-        }
-        // value codes of logical tokens (2t, 2t+1) and (2t+8, 2t+9) = physical t, t+4, t+8, t+12
-        uint32_t va[2][D / 8];
-#pragma unroll
-        for (int pair = 0; pair < 2; ++pair) {
-            const uint8_t* r0p = stage + O.vA + tile * (16 * LV::RB) + pair * (8 * LV::RB);
-            const uint8_t* r1p = r0p + 4 * LV::RB;
-            uint32_t cw[LV::NCW];
-            if constexpr (LV::U == 2) {
-                const uint32_t a = *reinterpret_cast<const uint16_t*>(r0p);
-                const uint32_t b = *reinterpret_cast<const uint16_t*>(r1p);
-                cw[0] = __byte_perm(a, b, 0x5410);
-            } else {
-                uint32_t wa[LV::U / 4], wb[LV::U / 4];
-                lds_words<LV::U / 4>(r0p, wa);
-                lds_words<LV::U / 4>(r1p, wb);
-#pragma unroll
-                for (int i = 0; i < LV::U / 4; ++i) {
-                    cw[2 * i] = __byte_perm(wa[i], wb[i], 0x5410);
-                    cw[2 * i + 1] = __byte_perm(wa[i], wb[i], 0x7632);
-                }
-            }
-#pragma unroll
-            for (int c = 0; c < LV::NCW; ++c) Ext<VB>::run(cw[c], va[pair] + c * LV::NE);
+            constexpr uint32_t kOnes = 0x3C003C00u;             // fp16 1.0 pairs
+            const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+            mma16816(S.spa[jv], ones, bv[jv][0], bv[jv][1]);
         }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
@@ -447,12 +463,14 @@ struct Tile {
         }
     }
 
-    // NT (1 or 2) tiles tl0, tl1.  FULL: every token of the tiles is valid (whole chunk), no masks.
-    // Otherwise tl1 < 0 means tile 1 is absent and tokens >= ntok are masked.  cf0 / cf1: per-channel
-    // key fragments of each tile's token group.
+    // NT (1 or 2) tiles: tile tl0 of stage st0 and tile tl1 of stage st1 (the same stage for two
+    // tiles of one chunk, two stages for the same tile slot of two chunks).  FULL: every token of the
+    // tiles is valid (whole chunks), no masks.  Otherwise tl1 < 0 means tile 1 is absent and tokens
+    // >= ntok are masked (single-stage use only).  cf0 / cf1: per-channel key fragments of each
+    // tile's token group.
     template <bool FULL, int NT>
-    __device__ static void run(WarpState<C>& S, const Ctx& X, const uint8_t* stage, const Off& O, int tl0,
-                               int tl1, int ntok, int lane, const uint8_t* cf0, const uint8_t* cf1) {
+    __device__ static void run(WarpState<C>& S, const Ctx& X, const uint8_t* st0, const uint8_t* st1, const Off& O,
+                               int tl0, int tl1, int ntok, int lane, const uint8_t* cf0, const uint8_t* cf1) {
         const int g = lane >> 2;
         const int tA = (g >> 1) + 4 * (g & 1);
         const bool two = NT == 2 && (FULL || tl1 >= 0);
@@ -466,10 +484,26 @@ struct Tile {
             vld[1][1] = two && tl1 * 16 + tA + 8 < ntok;
         }
         float s2[2][2][2];
-        logits(s2[0], X, stage, O, tl0, lane, cf0);
+        uint32_t va[NT][2][D / 8];
+        logits(s2[0], X, st0, O, tl0, lane, cf0);
         if constexpr (NT == 2) {
-            if (two) logits(s2[1], X, stage, O, tl1, lane, cf1);
+            if (two) logits(s2[1], X, st1, O, tl1, lane, cf1);
         }
+        // The value codes do not depend on the softmax: HOIST 2 reads their words here (the loads'
+        // latency hides under the key MMA chains), HOIST 1 also extracts the operands here.
+#if KVB_DEC_HOIST
+        uint32_t cw[NT][2][LV::NCW];
+        vload(cw[0], st0, O, tl0);
+        if constexpr (NT == 2) {
+            if (two) vload(cw[NT - 1], st1, O, tl1);
+        }
+#if KVB_DEC_HOIST == 1
+        vext(va[0], cw[0]);
+        if constexpr (NT == 2) {
+            if (two) vext(va[NT - 1], cw[NT - 1]);
+        }
+#endif
+#endif
         if constexpr (NT == 1 || !FULL) {
 #pragma unroll
             for (int u = 0; u < 2; ++u)
@@ -509,7 +543,7 @@ struct Tile {
                 S.l[e] *= alpha[e];
 #pragma unroll
                 for (int jv = 0; jv < NVT; ++jv) {
-                    S.sp[jv][e] *= alpha[e];
+                    S.spa[jv][e] *= alpha[e];
                     S.z[jv][e] *= alpha[e];
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
@@ -521,16 +555,35 @@ struct Tile {
         }
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const bool none = S.m[e] == -INFINITY;
+            // whole tiles always carry finite logits, so the reference is finite past the branch
+            const bool none = !FULL && S.m[e] == -INFINITY;
 #pragma unroll
             for (int u = 0; u < 2; ++u)
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) pr[u][hh][e] = none ? 0.f : ex2(s2[u][hh][e] - S.m[e]);
             S.l[e] += (pr[0][0][e] + pr[0][1][e]) + (pr[1][0][e] + pr[1][1][e]);
         }
-        values<!FULL>(S, pr[0], vld[0], stage, O, tl0, lane);
+#if !KVB_DEC_HOIST
+        {
+            uint32_t cw0[2][LV::NCW];
+            vload(cw0, st0, O, tl0);
+            vext(va[0], cw0);
+        }
+#elif KVB_DEC_HOIST == 2
+        vext(va[0], cw[0]);
+#endif
+        vmma<!FULL>(S, pr[0], vld[0], va[0], st0, O, tl0);
         if constexpr (NT == 2) {
-            if (two) values<!FULL>(S, pr[1], vld[1], stage, O, tl1, lane);
+            if (two) {
+#if !KVB_DEC_HOIST
+                uint32_t cw1[2][LV::NCW];
+                vload(cw1, st1, O, tl1);
+                vext(va[NT - 1], cw1);
+#elif KVB_DEC_HOIST == 2
+                vext(va[NT - 1], cw[NT - 1]);
+#endif
+                vmma<!FULL>(S, pr[1], vld[1], va[NT - 1], st1, O, tl1);
+            }
         }
     }
 
@@ -551,14 +604,10 @@ struct Tile {
             lt[e] = v;
 #pragma unroll
             for (int jv = 0; jv < NVT; ++jv) {
-                float a = S.sp[jv][e], b = S.z[jv][e];
-                a += __shfl_xor_sync(0xffffffffu, a, 4);
-                a += __shfl_xor_sync(0xffffffffu, a, 8);
-                a += __shfl_xor_sync(0xffffffffu, a, 16);
+                float b = S.z[jv][e];
                 b += __shfl_xor_sync(0xffffffffu, b, 4);
                 b += __shfl_xor_sync(0xffffffffu, b, 8);
                 b += __shfl_xor_sync(0xffffffffu, b, 16);
-                S.sp[jv][e] = a;
                 S.z[jv][e] = b;
             }
         }
@@ -591,7 +640,7 @@ struct Tile {
                         for (int e = 0; e < 2; ++e) {
                             const int c = 8 * jv + 2 * t + e;
                             if (C::VC::dup(c) || C::VC::grp(c) != ch / (D / GV)) continue;
-                            const float val = (S.acc[jv][mt][2 * hh + e] - 1024.f * S.sp[jv][e]) * (1.f / LV::vf(v)) +
+                            const float val = (S.acc[jv][mt][2 * hh + e] - 1024.f * S.spa[jv][e]) * (1.f / LV::vf(v)) +
                                               S.z[jv][e];
                             float* dst = &red_acc[(slot * R + C::VC::row(c)) * D + ch];
                             *dst = add ? *dst + beta[e] * val : beta[e] * val;
