@@ -23,6 +23,7 @@
 #include "kvb_quant.cuh"
 #include "kvb_select.cuh"
 #include "kvb_scores.cuh"
+#include "kvb_scores_tc.cuh"
 #include "kvb_decode.cuh"
 
 #define KVB_VERSION 101
@@ -82,8 +83,26 @@ EncodeTiledFn encode_tiled() {
 
 }  // namespace kvbh
 
-// Both score entry points (kvb_query_scores, kvb_snapkv_scores): two passes of scores_kernel + the
-// per-row log-sum-exp in between, optional pooling.
+#ifndef KVB_SCORES_TC
+#define KVB_SCORES_TC 1       // d = 128: the tcgen05 score passes (kvb_scores_tc.cuh); 0: mma.sync only
+#endif
+
+// 2D tensor map over `rows` rows of 128 16-bit channels (256-byte rows): box 64 x 128, 128-byte swizzle
+static kvb_status make_map_rows128(CUtensorMap* m, const void* base, int64_t rows, CUtensorMapDataType dt) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return fail(KVB_ECUDA, "query_scores: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {128, cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {256};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KVB_ECUDA, "query_scores: cuTensorMapEncodeTiled failed (%d)", int(r));
+    return KVB_OK;
+}
+
+// Both score entry points (kvb_query_scores, kvb_snapkv_scores): two score passes (tcgen05 for
+// d = 128, else mma.sync) with the per-row log-sum-exp in between, optional pooling.
 static kvb_status query_scores_impl(const void* q, const void* k, int dtype, int64_t B, int64_t Hq, int64_t Hkv,
                                     int64_t nq, int64_t T, int64_t d, float scaling, int64_t n_cand, int pool,
                                     float* out, void* workspace, size_t workspace_bytes, void* stream, int causal) {
@@ -118,6 +137,32 @@ static kvb_status query_scores_impl(const void* q, const void* k, int dtype, int
     p.out = pool > 1 ? tmp : out;
     p.causal = causal;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (KVB_SCORES_TC && d == 128) {
+        // tcgen05 passes (kvb_scores_tc.cuh): keys and query rows as 2D (128-channel rows) tensor maps
+        static thread_local kvb::ScoreTcParams tp;
+        std::memset(&tp, 0, sizeof(tp));
+        const CUtensorMapDataType dt = dtype == KVB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        kvb_status st = make_map_rows128(&tp.tm_q, q, B * Hq * nq, dt);
+        if (st) return st;
+        if ((st = make_map_rows128(&tp.tm_k, k, B * Hkv * T, dt))) return st;
+        const int64_t units = int64_t(heads) * kvb::SC_SPLIT;
+        const int ctas = int(std::min<int64_t>(resolve_ctas(0), units));
+        tp.units_per_cta = int((units + ctas - 1) / ctas);
+        tp.rows_pad = (p.rows + 31) / 32 * 32;
+        auto kern = dtype == KVB_BF16 ? kvb::scores_tc_kernel<__nv_bfloat16> : kvb::scores_tc_kernel<__half>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kvb::SCT_SMEM);
+        if (e != cudaSuccess) return cuda_check(e, "scores_tc smem attribute");
+        for (int pass = 1; pass <= 2; ++pass) {
+            p.pass = pass;
+            tp.s = p;
+            kern<<<ctas, kvb::SCT_THREADS, kvb::SCT_SMEM, s>>>(tp);
+            if ((st = launch_check("scores_tc_kernel"))) return st;
+            if (pass == 1) {
+                kvb::scores_lse_kernel<<<unsigned(heads), kvb::SC_ROWS, 0, s>>>(p);
+                if ((st = launch_check("scores_lse_kernel"))) return st;
+            }
+        }
+    } else {
     dim3 grid(kvb::SC_SPLIT, unsigned(heads));
     for (int pass = 1; pass <= 2; ++pass) {
         p.pass = pass;
@@ -138,6 +183,7 @@ static kvb_status query_scores_impl(const void* q, const void* k, int dtype, int
             kvb::scores_lse_kernel<<<unsigned(heads), kvb::SC_ROWS, 0, s>>>(p);
             if ((st = launch_check("scores_lse_kernel"))) return st;
         }
+    }
     }
     if (pool > 1) {
         const int64_t nthreads = int64_t(heads) * n_cand;
