@@ -52,6 +52,36 @@ __host__ __device__ constexpr uint32_t sct_idesc(int M, int N, int ab_bf16) {
 // 32 consecutive fp32 accumulator columns of this thread's TMEM lane
 __device__ __forceinline__ void sct_ld32(uint32_t taddr, float (&v)[32]) { tmem_ld32(taddr, v); }
 
+// 32 columns of this thread's TMEM lane, issued without waiting: the registers are valid only after
+// sct_wait() (tcgen05.wait::ld waits for every load the thread has issued)
+__device__ __forceinline__ void sct_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void sct_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// sum of 2^(v lam - sub) over a chunk, in 4 interleaved partial sums (short dependency chains)
+template <int I = 0>
+__device__ __forceinline__ void sct_sum_exp2(const float (&v)[32], float lam, float sub, float (&acc)[4]) {
+    if constexpr (I < 32) {
+        acc[I & 3] += ex2(__fmaf_rn(v[I], lam, -sub));
+        sct_sum_exp2<I + 1>(v, lam, sub, acc);
+    }
+}
+template <int I = 0>
+__device__ __forceinline__ void sct_sum_exp2_rows(const float (&v)[32], float lam, const float* lse, float (&acc)[4]) {
+    if constexpr (I < 32) {
+        acc[I & 3] += ex2(__fmaf_rn(v[I], lam, -lse[I]));
+        sct_sum_exp2_rows<I + 1>(v, lam, lse, acc);
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(SCT_THREADS, 1) scores_tc_kernel(const __grid_constant__ ScoreTcParams P) {
     const ScoreParams& p = P.s;
@@ -251,20 +281,31 @@ __global__ void __launch_bounds__(SCT_THREADS, 1) scores_tc_kernel(const __grid_
                     // keys kt + c for the 128 columns c: masked past the split's end / T and, for a
                     // causal window row, past its own position
                     const int lim = int(imax64(imin64(imin64(vis_end, k0 + per) - kt, SCT_KT), 0));
-#pragma unroll 1
-                    for (int c0 = 0; c0 < SCT_KT; c0 += 32) {
+                    // 32-column loads one round ahead of the arithmetic
+                    uint32_t raw[2][32];
+                    sct_ld32_async(lane_base + uint32_t(wg * SCT_KT), raw[0]);
+                    sct_wait();
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int c0 = 32 * c;
+                        if (c < 3) sct_ld32_async(lane_base + uint32_t(wg * SCT_KT + c0 + 32), raw[(c + 1) & 1]);
                         float v[32];
-                        sct_ld32(lane_base + uint32_t(wg * SCT_KT + c0), v);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[c & 1][i]);
                         if (c0 + 32 <= lim) {
-                            float mx = v[0];
+                            float mt[16];                   // max by a tree (depth 5, not a chain of 31)
 #pragma unroll
-                            for (int i = 1; i < 32; ++i) mx = fmaxf(mx, v[i]);
+                            for (int i = 0; i < 16; ++i) mt[i] = fmaxf(v[i], v[i + 16]);
+#pragma unroll
+                            for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+                                for (int i = 0; i < w; ++i) mt[i] = fmaxf(mt[i], mt[i + w]);
+                            const float mx = mt[0];
                             const float mn = fmaxf(m, mx * p.lam);
-                            float s = (m == -INFINITY) ? 0.f : l * ex2(m - mn);
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) s += ex2(__fmaf_rn(v[i], p.lam, -mn));
+                            float a4[4] = {(m == -INFINITY) ? 0.f : l * ex2(m - mn), 0.f, 0.f, 0.f};
+                            sct_sum_exp2(v, p.lam, mn, a4);
                             m = mn;
-                            l = s;
+                            l = (a4[0] + a4[1]) + (a4[2] + a4[3]);
                         } else if (c0 < lim) {
                             float mx = -INFINITY;
 #pragma unroll
@@ -276,17 +317,31 @@ __global__ void __launch_bounds__(SCT_THREADS, 1) scores_tc_kernel(const __grid_
                             m = mn;
                             l = s;
                         }
+                        sct_wait();
                     }
                 } else {
                     // this thread's key kt + lrow: sum over the rows of 2^(lam s - lse)
-                    float acc = 0.f;
+                    // 32-column loads one round ahead of the arithmetic
+                    float a4[4] = {0.f, 0.f, 0.f, 0.f};
+                    uint32_t raw[2][32];
+                    sct_ld32_async(lane_base, raw[0]);
+                    sct_wait();
 #pragma unroll 1
-                    for (int c0 = 0; c0 < P.rows_pad; c0 += 32) {
+                    for (int c0 = 0; c0 < P.rows_pad; c0 += 64) {
+                        if (c0 + 32 < P.rows_pad) sct_ld32_async(lane_base + uint32_t(c0 + 32), raw[1]);
                         float v[32];
-                        sct_ld32(lane_base + uint32_t(c0), v);
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) acc += ex2(__fmaf_rn(v[i], p.lam, -s_lse[c0 + i]));
+                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[0][i]);
+                        sct_sum_exp2_rows(v, p.lam, s_lse + c0, a4);
+                        sct_wait();
+                        if (c0 + 32 >= P.rows_pad) break;
+                        if (c0 + 64 < P.rows_pad) sct_ld32_async(lane_base + uint32_t(c0 + 64), raw[0]);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[1][i]);
+                        sct_sum_exp2_rows(v, p.lam, s_lse + c0 + 32, a4);
+                        sct_wait();
                     }
+                    const float acc = (a4[0] + a4[1]) + (a4[2] + a4[3]);
                     const int64_t j = kt + lrow;
                     if (j < imin64(p.n_cand, k0 + per) && j < p.T) p.out[head * p.n_cand + j] = acc / float(rows);
                 }
