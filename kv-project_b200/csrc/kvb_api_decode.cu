@@ -491,13 +491,19 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
         std::memset(&mp, 0, sizeof(mp));
         static_cast<kvb::MergeArgs&>(mp) = ma;
         for (int h = 0; h <= P.n_heads; ++h) mp.head_begin[h] = P.head_begin[h];
+        // few heads: blocks of >= 32 channels per CTA, so that the merge still spreads over the SMs
+        int nblk = 1;
+        if (!c->lift)
+            while (nblk < 4 && int(heads) * nblk * 2 <= 160 && c->d % (32 * nblk * 2) == 0) nblk *= 2;
+        mp.nblk = nblk;
+        const dim3 grid(heads * unsigned(nblk));
         using MP = std::remove_reference_t<decltype(mp)>;
         constexpr int NH = sizeof(MP::head_begin) / sizeof(int) - 1;
         if (q_dtype == KVB_F32)
-            return launch_maybe_pdl(kvb::decode_merge<float, float, NH>, dim3(heads), dim3(256), msm, s, false, mp);
+            return launch_maybe_pdl(kvb::decode_merge<float, float, NH>, grid, dim3(256), msm, s, false, mp);
         if (q_dtype == KVB_F16)
-            return launch_maybe_pdl(kvb::decode_merge<__half, __half, NH>, dim3(heads), dim3(256), msm, s, false, mp);
-        return launch_maybe_pdl(kvb::decode_merge<__nv_bfloat16, __nv_bfloat16, NH>, dim3(heads), dim3(256), msm, s,
+            return launch_maybe_pdl(kvb::decode_merge<__half, __half, NH>, grid, dim3(256), msm, s, false, mp);
+        return launch_maybe_pdl(kvb::decode_merge<__nv_bfloat16, __nv_bfloat16, NH>, grid, dim3(256), msm, s,
                                 false, mp);
     };
     if (P.n_heads <= kvb::MERGE_SMALL_HEADS) {

@@ -137,11 +137,13 @@ __host__ __device__ constexpr int merge_smem_floats(int Ra, int d, int dc, int n
     return Ra * (2 * d + dc) + 3 * Ra + nthreads;
 }
 
-// Head bh, partial slots [pb, pe); all `nthreads` threads of the CTA call it (it synchronises).
-// sm: merge_smem_floats(...) floats; s_w: nthreads / 32 floats.
+// Head bh, partial slots [pb, pe), output channels [c0, c1) (a block of channels when the head is
+// merged by several CTAs; the whole row when a lift mixes the coded channels); all `nthreads`
+// threads of the CTA call it (it synchronises).  sm: merge_smem_floats(...) floats; s_w:
+// nthreads / 32 floats.
 template <typename TQ, typename TE>
 __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, int pe, float* sm, float* s_w, int tid,
-                                       int nthreads) {
+                                           int nthreads, int c0 = 0, int c1 = -1) {
     const int b = bh / p.Hkv, h = bh % p.Hkv;
     const int R = p.R, d = p.d, dc = p.d_code, Ra = p.R_act;
     float* s_q = sm;                       // [Ra][d]
@@ -153,6 +155,11 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
     float* s_p = s_rowLc + Ra;             // [nthreads] scratch probabilities
     const TQ* q = static_cast<const TQ*>(p.q);
     const int nwarps = nthreads >> 5;
+    if (c1 < 0 || p.lift) {
+        c0 = 0;
+        c1 = d;
+    }
+    const int cw = c1 - c0;                // output channels of this CTA (coded channels too, without a lift)
     for (int o = tid; o < Ra * d; o += nthreads) {
         const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
         s_q[o] = to_f32(q[((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * d + c]);
@@ -197,8 +204,10 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
         s_rowLc[tid] = L;
     }
     __syncthreads();
-    for (int o = tid; o < Ra * dc; o += nthreads) {
-        const int r = o / dc, c = o % dc;
+    // coded channels needed: all of them under a lift, else this CTA's block
+    const int ac0 = p.lift ? 0 : c0, acw = p.lift ? dc : cw;
+    for (int o = tid; o < Ra * acw; o += nthreads) {
+        const int r = o / acw, c = ac0 + o % acw;
         const float* src = part + 2 * R + r * dc + c;
         float a = 0.f;
         for (int k0 = 0; k0 < np; k0 += 8) {
@@ -217,12 +226,12 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
                 }
             }
         }
-        s_acc[o] = a;
+        s_acc[r * dc + c] = a;
     }
     __syncthreads();
     // lift to model space (+ coded mass * mean value)
-    for (int o = tid; o < Ra * d; o += nthreads) {
-        const int r = o / d, c = o % d;
+    for (int o = tid; o < Ra * cw; o += nthreads) {
+        const int r = o / cw, c = c0 + o % cw;
         float v;
         if (p.lift) {
             const float* Lm = p.lift + size_t(h) * dc * d;
@@ -232,7 +241,7 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
             v = s_acc[r * dc + c];
         }
         if (p.mu_v) v = fmaf(s_rowLc[r], p.mu_v[size_t(h) * d + c], v);
-        s_out[o] = v;
+        s_out[r * d + c] = v;
     }
     if (tid < Ra) s_rowL[tid] = s_rowLc[tid];
     __syncthreads();
@@ -268,7 +277,7 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
                 for (int w = 0; w < nwarps; ++w) tot += s_w[w];
                 const float alpha = (Mold == -INFINITY) ? 0.f : ex2(Mold - Mnew);
                 const int64_t nj = imin64(nthreads, p.n_exact - j0);
-                for (int c = tid; c < d; c += nthreads) {
+                for (int c = c0 + tid; c < c1; c += nthreads) {
                     float a = s_out[r * d + c] * alpha;
                     for (int64_t k = 0; k < nj; ++k) a = fmaf(s_p[k], to_f32(Ve[(j0 + k) * d + c]), a);
                     s_out[r * d + c] = a;
@@ -284,15 +293,15 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
     }
     __syncthreads();
     // a row with no readable token (possible in one part of a sequence split) gets 0 and lse -inf
-    for (int o = tid; o < Ra * d; o += nthreads) {
-        const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
-        const float v = s_rowL[r] > 0.f ? s_out[o] / s_rowL[r] : 0.f;
+    for (int o = tid; o < Ra * cw; o += nthreads) {
+        const int r = o / cw, c = c0 + o % cw, i = r / p.Tq, t = r % p.Tq;
+        const float v = s_rowL[r] > 0.f ? s_out[r * d + c] / s_rowL[r] : 0.f;
         const size_t oi = ((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c;
         if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
         else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
         else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
     }
-    if (p.lse && tid < Ra) {
+    if (p.lse && c0 == 0 && tid < Ra) {
         const int i = tid / p.Tq, t = tid % p.Tq;
         const float L = s_rowL[tid];
         p.lse[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
@@ -304,15 +313,19 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
 // (copied on every launch) small for the usual head counts.  grid (B * Hkv), block 256.
 template <int NH>
 struct MergeParams : MergeArgs {
+    int nblk;                              // channel blocks per head (CTAs per head)
     int head_begin[NH + 1];
 };
 
+// grid (B * Hkv * nblk): CTA x merges head x / nblk, channel block x % nblk (nblk > 1 only without a
+// lift: few heads then still spread over many SMs).
 template <typename TQ, typename TE, int NH>
 __global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ MergeParams<NH> p) {
     extern __shared__ float sm[];
     __shared__ float s_w[8];
-    const int bh = blockIdx.x;
-    merge_head<TQ, TE>(p, bh, p.head_begin[bh], p.head_begin[bh + 1], sm, s_w, threadIdx.x, blockDim.x);
+    const int bh = blockIdx.x / p.nblk, blk = blockIdx.x % p.nblk;
+    merge_head<TQ, TE>(p, bh, p.head_begin[bh], p.head_begin[bh + 1], sm, s_w, threadIdx.x, blockDim.x,
+                       blk * p.d / p.nblk, (blk + 1) * p.d / p.nblk);
 }
 
 // ------------------------------------------------------------------------------------------
