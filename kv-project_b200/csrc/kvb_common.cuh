@@ -189,4 +189,62 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Float32 row sums in the order of torch's CPU reduction over a contiguous last axis, the order
+// the reference's Y.pow(2).mean(-1) takes on CPU (STRATA_KV.py:1166, HEDGE_KV.py:1119; PyTorch's
+// aten/src/ATen/native/cpu/SumKernel.cpp): the row as 8-lane vectors; vector j adds lanewise into
+// accumulator j % 4, from zero, in j order; the accumulators combine as ((a0 + a1) + a2) + a3; the 8
+// lanes then add one by one into zero.  For n = 32 m, element c sits in accumulator (c / 8) % 4,
+// lane c % 8, chain position c / 32.  Every add is an explicit __fadd_rn (nothing contracts).
+// ---------------------------------------------------------------------------------------------
+
+// n = 32, the whole row in one thread
+__device__ __forceinline__ float torch_sum32(const float (&x)[32]) {
+    float t = 0.f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l)
+        t = __fadd_rn(t, __fadd_rn(__fadd_rn(__fadd_rn(x[l], x[8 + l]), x[16 + l]), x[24 + l]));
+    return t;
+}
+
+// n = 32 M held as v[i] = x[lane + 32 i] by the 32 lanes of a warp: the lane's own elements are the
+// chain of accumulator lane / 8, lane lane % 8.  All 32 lanes call it; every lane gets the sum.
+template <int M>
+__device__ __forceinline__ float torch_sum_warp(const float (&v)[M]) {
+    float a = v[0];
+#pragma unroll
+    for (int i = 1; i < M; ++i) a = __fadd_rn(a, v[i]);
+    const float a1 = __shfl_down_sync(0xffffffffu, a, 8);
+    const float a2 = __shfl_down_sync(0xffffffffu, a, 16);
+    const float a3 = __shfl_down_sync(0xffffffffu, a, 24);
+    const float p = __fadd_rn(__fadd_rn(__fadd_rn(a, a1), a2), a3);     // lanes 0..7: the lane sums
+    float t = 0.f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) t = __fadd_rn(t, __shfl_sync(0xffffffffu, p, l));
+    return t;
+}
+
+// n = 128 held as v[t] = x[8 l16 + t] by the 16 lanes of each half-warp (l16 = lane % 16): lane l16
+// holds vector l16, i.e. accumulator l16 % 4 at chain position l16 / 4.  All 32 lanes call it;
+// every lane gets its own half-warp's sum.
+__device__ __forceinline__ float torch_sum128_half(const float (&v)[8]) {
+    float a[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) a[t] = v[t];
+#pragma unroll
+    for (int i = 1; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) a[t] = __fadd_rn(a[t], __shfl_down_sync(0xffffffffu, v[t], 4 * i, 16));
+    // lanes 0..3 of the half hold accumulators 0..3
+    float s = 0.f;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        float p = a[t];
+#pragma unroll
+        for (int k = 1; k < 4; ++k) p = __fadd_rn(p, __shfl_down_sync(0xffffffffu, a[t], k, 16));
+        s = __fadd_rn(s, p);
+    }
+    return __shfl_sync(0xffffffffu, s, 0, 16);
+}
+
 }  // namespace kvb

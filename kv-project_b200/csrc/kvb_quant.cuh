@@ -2,7 +2,8 @@
 //
 // Per-token mode (one warp per stored row): KIVI asymmetric groups of `group` channels
 // (kivi_quant along_tokens=False, STRATA_KV.py:846-852) or the STRATA mid-rise code with one
-// RMS scale per vector (strata_quantize, STRATA_KV.py:1158-1168).  Per-channel mode (one CTA per
+// RMS scale per vector (strata_quantize, STRATA_KV.py:1158-1168; the mean of squares in torch's CPU
+// summation order, see torch_sum_warp in kvb_common.cuh).  Per-channel mode (one CTA per
 // group of `group` stored rows): KIVI keys, min / max per channel over the group
 // (kivi_quant along_tokens=True, STRATA_KV.py:838-844).  Rows are gathered through an optional
 // index list, so one launch packs a stratum (StrataMethod.pack, STRATA_KV.py:1611-1627) or the
@@ -10,8 +11,8 @@
 //
 // Exactness: every float operation the reference performs is reproduced with the same IEEE
 // rounding (__fdiv_rn / __fmul_rn / __fadd_rn, rintf = round-half-even, __float2half_rn = the
-// fp16 cast), so codes and fp16 (lo, scale) pairs are bit-identical.  The mid-rise RMS sums the
-// float32 squares in float64 (order-independent; see oracle/codecs.py).
+// fp16 cast), so codes and fp16 (lo, scale) pairs are bit-identical.  The mid-rise RMS adds the
+// float32 squares in the order torch's CPU reduction takes (torch_sum_* in kvb_common.cuh).
 //
 // Output: packed rows are staged in shared memory and written with 16-byte stores; padding rows
 // [n, n_alloc) are zero-filled so a reader of whole 16-row tiles sees defined bytes.
@@ -90,13 +91,10 @@ __global__ void __launch_bounds__(128) quant_token_kernel(const QuantTokenParams
         uint8_t c[NCH];
         float lo_g[8], sc_g[8];
         if (p.midrise) {
-            double ss = 0.0;
+            float sq[NCH];
 #pragma unroll
-            for (int i = 0; i < NCH; ++i) ss += double(__fmul_rn(v[i], v[i]));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float mean = float(ss / double(D));
-            const float rms = sqrtf(mean);
+            for (int i = 0; i < NCH; ++i) sq[i] = __fmul_rn(v[i], v[i]);
+            const float rms = __fsqrt_rn(__fdiv_rn(torch_sum_warp<NCH>(sq), float(D)));
             const float s = fmaxf(as_stored(__fmul_rn(p.step, rms)), 5.9604644775390625e-8f);
             const float half = 0.5f * float(top);
 #pragma unroll
@@ -371,12 +369,10 @@ __device__ __forceinline__ void qrow_codes(const uint4 raw, bool valid, float st
     float v[8];
     unpack8<T>(raw, v);
     if constexpr (GROUP == 0) {
-        double ss = 0.0;
+        float sq[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss += double(__fmul_rn(v[i], v[i]));
-#pragma unroll
-        for (int m = 8; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-        const float rms = __fsqrt_rn(float(ss / 128.0));
+        for (int i = 0; i < 8; ++i) sq[i] = __fmul_rn(v[i], v[i]);
+        const float rms = __fsqrt_rn(__fdiv_rn(torch_sum128_half(sq), 128.f));
         sc = fmaxf(as_stored(__fmul_rn(step, rms)), 5.9604644775390625e-8f);
         lo = 0.f;
     } else {
@@ -510,16 +506,32 @@ __global__ void __launch_bounds__(256) quant_token128_kernel(const QuantFastPara
         const int r = r0 + 32 * ps;
         float lo[NGL], sc[NGL], y[NGL];
         if constexpr (GROUP == 0) {
-            double ss = 0.0;
+            // the row's squares through shared memory, then torch's CPU summation order: lane l8
+            // of the row's 8 lanes forms lane l8 of the 8-lane vectors (its four accumulators,
+            // combined), and the 8 lane sums add one by one
+            __shared__ float s_sq[8][4][136];             // [warp][row of the warp][channel], padded
+            float* const sq = s_sq[warp][lane >> 3];
 #pragma unroll
             for (int k = 0; k < P * WPP; ++k) {
                 const float a = half_lo<T>(w[ps][k]), c = half_hi<T>(w[ps][k]);
-                ss += double(__fmul_rn(a, a));
-                ss += double(__fmul_rn(c, c));
+                const int ch = (k / WPP) * PW + CPL * l8 + 2 * (k % WPP);
+                sq[ch] = __fmul_rn(a, a);
+                sq[ch + 1] = __fmul_rn(c, c);
             }
+            __syncwarp();
+            float pl8 = 0.f;
 #pragma unroll
-            for (int m = 4; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-            const float rms = __fsqrt_rn(float(ss / 128.0));
+            for (int k = 0; k < 4; ++k) {
+                float acc = sq[8 * k + l8];
+#pragma unroll
+                for (int i = 1; i < 4; ++i) acc = __fadd_rn(acc, sq[32 * i + 8 * k + l8]);
+                pl8 = k ? __fadd_rn(pl8, acc) : acc;
+            }
+            float tot = 0.f;
+#pragma unroll
+            for (int l = 0; l < 8; ++l) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, pl8, (lane & ~7) + l));
+            __syncwarp();                                 // the next pass reuses sq
+            const float rms = __fsqrt_rn(__fdiv_rn(tot, 128.f));
             sc[0] = fmaxf(as_stored(__fmul_rn(p.step, rms)), 5.9604644775390625e-8f);
             lo[0] = 0.f;
         } else {

@@ -203,7 +203,8 @@ __global__ void __launch_bounds__(256, 2) hedge_rows_kernel(const HedgeParams p)
     }
     __syncthreads();
 
-    // y[r][j] = sum_c x[r][c] R[j][c], rows 8w + i, columns lane + 32 q
+    // y[r][j] = sum_c x[r][c] R[j][c], rows 8w + i, columns lane + 32 q: one float32 FMA chain per
+    // output, c ascending from 0, the result the reference's CPU x @ R.T (MKL sgemm) gives
     float acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -236,12 +237,10 @@ __global__ void __launch_bounds__(256, 2) hedge_rows_kernel(const HedgeParams p)
             amax = warp_max(amax);
             s = fmaxf(as_stored(__fdiv_rn(amax, 127.f)), 5.9604644775390625e-8f);
         } else {
-            double ss = 0.0;
+            float sq[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) ss += double(__fmul_rn(acc[i][q], acc[i][q]));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            s = fmaxf(as_stored(__fsqrt_rn(float(ss / 128.0))), 5.9604644775390625e-8f);
+            for (int q = 0; q < 4; ++q) sq[q] = __fmul_rn(acc[i][q], acc[i][q]);
+            s = fmaxf(as_stored(__fsqrt_rn(__fdiv_rn(torch_sum_warp<4>(sq), 128.f))), 5.9604644775390625e-8f);
         }
         const float yr = __frcp_rn(s);
 #pragma unroll
@@ -277,7 +276,7 @@ __global__ void __launch_bounds__(256, 2) hedge_rows_kernel(const HedgeParams p)
     }
     if (!p.xhat) return;
 
-    // read-back xhat[r][c] = sum_j yhat[r][j] R[j][c] (+ mu)
+    // read-back xhat[r][c] = sum_j yhat[r][j] R[j][c] (+ mu), the same FMA chain order over j
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll

@@ -9,7 +9,7 @@
 //        (the basis split into two fp16 parts, so coefficients carry ~22 significant bits);
 //        four accumulators (128 TMEM columns) so the epilogues of four tiles overlap the next MMAs
 //   tcgen05.ld 32x32b.x32: thread = token row, its 32 fp32 coefficients in registers
-//   epilogue: RMS (float64 sum of float32 squares), fp16 scale, codes, planar pack, 16-byte stores.
+//   epilogue: RMS (torch's CPU float32 summation order), fp16 scale, codes, planar pack, 16-byte stores.
 //
 // Warp roles: warp 0 issues TMA loads, warp 1 allocates TMEM and issues the MMAs (one elected
 // lane), warps 2-17 run the epilogue in 4 groups of 4, group j on the tiles of accumulator j (warp w
@@ -113,17 +113,17 @@ __device__ __forceinline__ float div_rn_from_rcp(float a, float b, float y) {
     return __fmaf_rn(r, y, q0);
 }
 
-// Mid-rise code of one token's 32 coefficients (strata_quantize STRATA_KV.py:1158-1168 with the
-// RMS of rms_f32: float32 squares summed in float64, one rounding of the mean), planar-packed to
+// Mid-rise code of one token's 32 coefficients (strata_quantize STRATA_KV.py:1158-1168; the mean of
+// squares in torch's CPU summation order, torch_sum32), planar-packed to
 // 32 * BITS / 8 bytes (byte k holds coefficient pl * 32 / P + k in bits [pl * BITS, ...)).
 template <int BITS>
 __device__ __forceinline__ void midrise_code32(const float (&c)[32], float step, uint8_t* dst, __half* scale) {
     constexpr int TOP = (1 << BITS) - 1, P = 8 / BITS, RB = SP_R * BITS / 8;
     constexpr float HALF = 0.5f * float(TOP);
-    double ss = 0.0;
+    float sq[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) ss += double(__fmul_rn(c[i], c[i]));
-    const float rms = __fsqrt_rn(float(ss / 32.0));
+    for (int i = 0; i < 32; ++i) sq[i] = __fmul_rn(c[i], c[i]);
+    const float rms = __fsqrt_rn(__fdiv_rn(torch_sum32(sq), 32.f));
     const float sc = fmaxf(as_stored(__fmul_rn(step, rms)), 5.9604644775390625e-8f);
     const float y = __frcp_rn(sc);
     uint32_t code[32];

@@ -3,11 +3,21 @@ absmax code and the three bit-packing formats.  TEST INFRASTRUCTURE ONLY (see pa
 
 All arithmetic is float32 where the reference computes in float32, in the same operation order, so
 integer codes and fp16 scales are reproduced bit for bit (numpy and torch both use IEEE-754
-float32 division and round-half-to-even).  The one exception is the RMS of ``strata_quantize``:
-the reference sums squares in torch's vectorised float32 order, which no portable code can
-replay; here (and in the CUDA kernel) the float32 squares are summed in float64 and the mean is
-rounded once to float32.  The two agree except when torch's own rounding error crosses a float32
-boundary, which the golden tests measure and bound.
+float32 division and round-half-to-even).  Two results of the reference depend on the order of a
+float32 reduction inside a third-party library, PyTorch (2.11.0 CPU build, MKL 2024.2, the build the
+golden fixtures were made with; the reference pins no version):
+
+* ``Y.pow(2).mean(-1)`` (STRATA_KV.py:1166, HEDGE_KV.py:1119): torch's CPU float32 sum over a
+  contiguous last axis (``cascade_sum`` / ``vectorized_inner_sum`` / ``row_sum`` /
+  ``multi_row_sum`` in aten/src/ATen/native/cpu/SumKernel.cpp) followed by an IEEE division by n;
+  restated in :func:`mean_sq_f32`;
+* ``x @ R.T`` on CPU (HEDGE_KV.py:1113, :1121): MKL's sgemm, which for row counts of 7 and more
+  returns a float32 fused multiply-add chain over k in ascending order from 0 (checked bit for bit
+  against torch's CPU matmul; one to six rows take a gemv path with another order); restated in
+  :func:`matmul_fma`.
+
+The CUDA kernels take the same orders, so codes and scales match the reference's CPU results bit for
+bit.
 """
 
 from __future__ import annotations
@@ -113,13 +123,93 @@ def uniform_step(bits: int) -> tuple:
     return step, distortion(step)
 
 
-def rms_f32(Y: np.ndarray) -> np.ndarray:
-    """sqrt(mean(Y^2)) over the last axis: float32 squares, summed in float64, mean rounded once
-    to float32, float32 sqrt (the order-independent form the CUDA kernels use)."""
+def fma_f32(a, b, c) -> np.ndarray:
+    """Correctly rounded float32 fused multiply-add ``a * b + c`` (IEEE fmaf), elementwise.
+
+    ``a * b`` is exact in float64 (48-bit significand); the float64 sum rounds at most once, and its
+    exact error comes from Knuth's TwoSum.  Rounding the float64 sum to float32 is then wrong only when
+    the sum sits exactly halfway between two float32 values while the exact value does not; the
+    error's sign says which neighbour is right."""
+    f32, f64 = np.float32, np.float64
+    a = np.asarray(a, f32)
+    b = np.asarray(b, f32)
+    c = np.asarray(c, f32)
+    p = a.astype(f64) * b.astype(f64)
+    cd = c.astype(f64)
+    s = p + cd
+    bb = s - p
+    e = (p - (s - bb)) + (cd - bb)
+    r = s.astype(f32)
+    d = s - r.astype(f64)
+    with np.errstate(invalid="ignore", over="ignore"):
+        up = np.nextafter(r, f32(np.inf))
+        dn = np.nextafter(r, f32(-np.inf))
+        fix_up = (d == (up.astype(f64) - r.astype(f64)) / 2) & (e > 0)
+        fix_dn = (-d == (r.astype(f64) - dn.astype(f64)) / 2) & (e < 0)
+    return np.where(fix_up, up, np.where(fix_dn, dn, r)).astype(f32)
+
+
+def matmul_fma(x: np.ndarray, W: np.ndarray) -> np.ndarray:
+    """``x @ W.T`` in float32 as one fused multiply-add chain per output, k ascending from 0: the
+    result torch's CPU matmul (MKL sgemm) gives for 7 or more rows.  x (..., K), W (N, K)."""
+    x = np.asarray(x, np.float32)
+    W = np.asarray(W, np.float32)
+    y = np.zeros(x.shape[:-1] + (W.shape[0],), np.float32)
+    for k in range(x.shape[-1]):
+        y = fma_f32(x[..., k:k + 1], W[:, k], y)
+    return y
+
+
+def sum_f32_torch(x: np.ndarray) -> np.ndarray:
+    """Float32 sum over the last axis in the order of torch's CPU reduction of a contiguous row
+    (aten/src/ATen/native/cpu/SumKernel.cpp): the row as n // 8 vectors of 8 lanes; vector j adds into
+    accumulator j % 4 of the first n // 32 * 4 vectors (lanewise, in j order, from zero), the
+    remaining whole vectors into accumulator 0; the accumulators combine as ((a0 + a1) + a2) + a3;
+    the n % 8 scalar tail and then the 8 lanes add one by one, in order, into a zero.  Rows of fewer
+    than 8 elements take the same four-accumulator scheme on scalars.  Valid while n // 32 < 16 (no second cascade level), i.e. n < 512."""
+    f32 = np.float32
+    x = np.asarray(x, f32)
+    n = x.shape[-1]
+    lead = x.shape[:-1]
+    if n < 8:                                   # scalar path: the same four accumulators on scalars
+        acc = [np.zeros(lead, f32) for _ in range(4)]
+        for i in range(n // 4):
+            for k in range(4):
+                acc[k] = (acc[k] + x[..., 4 * i + k]).astype(f32)
+        for j in range(n // 4 * 4, n):
+            acc[0] = (acc[0] + x[..., j]).astype(f32)
+        return (((acc[0] + acc[1]).astype(f32) + acc[2]).astype(f32) + acc[3]).astype(f32)
+    nv = n // 8
+    assert nv // 4 < 16, "a second cascade level is not restated"
+    V = x[..., :nv * 8].reshape(*lead, nv, 8)
+    acc = [np.zeros(lead + (8,), f32) for _ in range(4)]
+    for i in range(nv // 4):
+        for k in range(4):
+            acc[k] = (acc[k] + V[..., 4 * i + k, :]).astype(f32)
+    for j in range(nv // 4 * 4, nv):
+        acc[0] = (acc[0] + V[..., j, :]).astype(f32)
+    p = acc[0]
+    for k in range(1, 4):
+        p = (p + acc[k]).astype(f32)
+    t = np.zeros(lead, f32)
+    for i in range(nv * 8, n):
+        t = (t + x[..., i]).astype(f32)
+    for lane in range(8):
+        t = (t + p[..., lane]).astype(f32)
+    return t
+
+
+def mean_sq_f32(Y: np.ndarray) -> np.ndarray:
+    """``Y.pow(2).mean(-1, keepdim=True)`` as torch computes it on CPU: float32 squares, the sum of
+    :func:`sum_f32_torch`, one IEEE float32 division by n."""
     Y = np.asarray(Y, np.float32)
-    sq = (Y * Y).astype(np.float64)
-    mean = (sq.sum(-1, keepdims=True) / Y.shape[-1]).astype(np.float32)
-    return np.sqrt(mean)
+    sq = (Y * Y).astype(np.float32)
+    return (sum_f32_torch(sq) / np.float32(Y.shape[-1])).astype(np.float32)[..., None]
+
+
+def rms_f32(Y: np.ndarray) -> np.ndarray:
+    """sqrt(mean(Y^2)) over the last axis (keepdim), float32, in the reference's order."""
+    return np.sqrt(mean_sq_f32(Y))
 
 
 def strata_quantize(Y: np.ndarray, bits: int):

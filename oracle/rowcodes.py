@@ -12,9 +12,10 @@ Restates the token-like stored vectors of the reference's chunk methods and its 
     each chunk key under the observed queries, top-m by share, kept positions ascending;
   * byte-LUT decode of MSB-first packed rows (``pack_rows`` / ``byte_lut`` QUASAR_KV.py:1185-1203).
 
-Order-dependent float32 reductions (the RMS of y, the share mean) are taken in float64 and rounded
-once, the order-free form the CUDA kernels use; the golden tests bound the difference to the
-reference's torch order.
+The rotation, its read-back and the RMS of y follow the reference's float32 CPU order
+(``codecs.matmul_fma``, ``codecs.rms_f32``), as the CUDA kernel does, so HEDGE codes, scales and
+reconstructions are bit-exact.  TILT's share (a float64 einsum here) is compared within tolerance;
+its top-m positions are exact.
 """
 
 from __future__ import annotations
@@ -23,7 +24,7 @@ from functools import lru_cache
 
 import numpy as np
 
-from .codecs import as_stored, pack_codes, _gauss_grid, _TINY
+from .codecs import as_stored, matmul_fma, pack_codes, rms_f32, _gauss_grid, _TINY
 
 
 def absmax_tilt(x: np.ndarray, bits: int):
@@ -58,13 +59,6 @@ def lloyd_max_gaussian(bits: int) -> np.ndarray:
     return c.astype(np.float32)
 
 
-def rms64(y: np.ndarray) -> np.ndarray:
-    """sqrt(mean(y^2)): float32 squares summed in float64, mean rounded once to float32, float32 sqrt."""
-    y = np.asarray(y, np.float32)
-    mean = ((y * y).astype(np.float64).sum(-1, keepdims=True) / y.shape[-1]).astype(np.float32)
-    return np.sqrt(mean)
-
-
 def hedge_codes_from_y(y: np.ndarray, bits: int, levels: np.ndarray = None):
     """The code step of ``hedge_quant`` (HEDGE_KV.py:1114-1121) applied to rotated rows y:
     returns (codes uint8, s (..., 1) float32, yhat = level * s float32)."""
@@ -74,7 +68,7 @@ def hedge_codes_from_y(y: np.ndarray, bits: int, levels: np.ndarray = None):
         c = np.clip(np.rint(y / s), -127, 127).astype(np.float32)
         return (c + 127).astype(np.uint8), s, c * s
     cb = lloyd_max_gaussian(bits) if levels is None else np.asarray(levels, np.float32)
-    s = np.maximum(as_stored(rms64(y)), _TINY)
+    s = np.maximum(as_stored(rms_f32(y)), _TINY)
     mids = ((cb[1:] + cb[:-1]) / np.float32(2)).astype(np.float32)
     c = np.searchsorted(mids, y / s, side="left")          # torch.bucketize(right=False)
     return c.astype(np.uint8), s, cb[c] * s
@@ -88,9 +82,9 @@ def hedge_quant(x: np.ndarray, R: np.ndarray, bits: int, mu: np.ndarray = None):
         return x, None, None, None
     xc = x if mu is None else x - np.asarray(mu, np.float32)
     R = np.asarray(R, np.float32)
-    y = xc @ R.T
+    y = matmul_fma(xc, R)
     c, s, yh = hedge_codes_from_y(y, bits)
-    xh = yh @ R
+    xh = matmul_fma(yh, R.T)
     return (xh if mu is None else xh + np.asarray(mu, np.float32)), c, s, y
 
 

@@ -311,12 +311,41 @@ def snapkv128():
     print("wrote snapkv128.npz", (HERE / "snapkv128.npz").stat().st_size)
 
 
+def midrise128():
+    """STRATA mid-rise codes at the kernels' head size (d = 128): the reference's strata_quantize
+    (STRATA_KV.py:1158-1168) on rotated vectors rounded to bf16 and to fp16 (the input dtypes of the
+    token-major and block-layout kernels), with outlier channels, tiny and zero rows, in
+    midrise128.npz (its own generator, so the other files are untouched).  Its float32 mean of squares
+    is torch's CPU summation order, which the oracle and the kernels restate."""
+    S, _ = load_reference()
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(1357)
+    R = S.rotation_matrix(128, "strata")
+    x = torch.randn(192, 128, generator=g) * (0.3 + 2.5 * torch.rand(1, 128, generator=g))
+    x[:, 11] *= 25.0
+    x[40:48] *= 1e-4                                   # tiny rows: subnormal fp16 scales
+    x[48] = 0.0                                        # a zero row: scale floored at 2^-24
+    y = x @ R.T
+    out = {}
+    for tag, dt in (("bf", torch.bfloat16), ("h", torch.float16)):
+        yd = y.to(dt).float()
+        out[f"{tag}_y"] = np32(yd)
+        for b in (2, 4, 8):
+            c, s, yh = S.strata_quantize(yd, b)
+            out[f"{tag}{b}_codes"], out[f"{tag}{b}_s"] = c.numpy(), np32(s)
+            if b == 2:
+                out[f"{tag}{b}_yhat"] = np32(yh)
+    np.savez_compressed(HERE / "midrise128.npz", **out)
+    print("wrote midrise128.npz", (HERE / "midrise128.npz").stat().st_size)
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["rowcodes"]:
         rowcodes()
     elif sys.argv[1:] == ["snapkv128"]:
         snapkv128()
+    elif sys.argv[1:] == ["midrise128"]:
+        midrise128()
     else:
         main()
-        rowcodes()
-        snapkv128()

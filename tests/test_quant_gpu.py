@@ -87,17 +87,38 @@ def test_midrise(cuda_dev, bits, d):
 
 
 def test_golden_strata_codes(golden, cuda_dev):
-    """Mid-rise codes of the golden rotated vectors: exact wherever the reference's float32 mean of
-    squares rounds like the float64 one (all but a measured sliver of rows)."""
+    """Mid-rise codes and scales of the reference's golden rotated 32-vectors, bit for bit (the RMS
+    takes torch's CPU summation order)."""
     import kvb
     g = golden("codecs")
     y = torch.from_numpy(g["sq_x"])[None, None].contiguous()
     for b in (2, 4, 8):
-        r = kvb.quant_pack(y.to(cuda_dev), b, 32, midrise=True)
-        s = r["meta"][0, 0, :y.shape[2]].float().cpu().numpy()
-        same = s == g[f"sq{b}_s"]
-        assert same.mean() >= 0.98
-        np.testing.assert_array_equal(unpack(r["codes"], b, y.shape[2])[0, 0][same], g[f"sq{b}_codes"][same])
+        r = kvb.quant_pack(y.to(cuda_dev), b, 32, midrise=True, want_xhat=True)
+        np.testing.assert_array_equal(r["meta"][0, 0, :y.shape[2]].float().cpu().numpy(), g[f"sq{b}_s"])
+        np.testing.assert_array_equal(unpack(r["codes"], b, y.shape[2])[0, 0], g[f"sq{b}_codes"])
+        np.testing.assert_array_equal(np32(r["xhat"])[0, 0], g[f"sq{b}_yhat"])
+
+
+@pytest.mark.parametrize("tag", ["bf", "h"])
+@pytest.mark.parametrize("src", ["float32", "native", "blocked"])
+def test_golden_midrise128(golden, cuda_dev, tag, src):
+    """d = 128 mid-rise codes and scales of the reference (midrise128.npz) from every kernel layout:
+    float32 rows (one row per warp), bf16 / fp16 rows (8 lanes per row, token-major) and the
+    128-token block layout (16 lanes per row), bit for bit."""
+    import kvb
+    g = golden("midrise128")
+    y = torch.from_numpy(g[f"{tag}_y"])[None, None].contiguous()
+    if src != "float32":
+        y = y.to(torch.bfloat16 if tag == "bf" else torch.float16)
+    n = y.shape[2]
+    for b in (2, 4, 8):
+        r = kvb.quant_pack(y.to(cuda_dev), b, 128, midrise=True, want_xhat=True, blocked=src == "blocked")
+        codes = kvb.ops.unblock_codes(r["codes"]) if src == "blocked" else r["codes"]
+        np.testing.assert_array_equal(r["meta"][0, 0, :n].float().cpu().numpy(), g[f"{tag}{b}_s"])
+        np.testing.assert_array_equal(unpack(codes, b, n)[0, 0], g[f"{tag}{b}_codes"])
+        if b == 2:
+            np.testing.assert_array_equal(np32(r["xhat"])[0, 0], g[f"{tag}{b}_yhat"])
+    assert kvb.device_status() == 0
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
