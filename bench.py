@@ -80,6 +80,9 @@ def args_():
     p.add_argument("--batch", type=int, default=None, help="batch per rank (default: the config's)")
     p.add_argument("--context", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-overlap", action="store_true",
+                   help="launch each layer's decode call only after the previous one completes (no programmatic "
+                        "dependent launch between consecutive calls)")
     p.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
                    help="c4s on N > 1 ranks: peer-memory exchange kernel (p2p) or NCCL all-gather + merge")
     p.add_argument("--strata", default="1,3",
@@ -270,7 +273,11 @@ def decode_config(a, w, world, L, B, T, Hq, Hkv, dt, bytes_step):
                                "peer-memory exchange + LSE merge kernel (kvb_xchg_merge) per layer"
                                if a.xchg == "p2p" else "NCCL all-gather + LSE merge per layer")
                            }.get(w, f"dp{world} (batch x kv-head shards, no collective)"),
-           "bytes_per_step_per_gpu": bytes_step}
+           "bytes_per_step_per_gpu": bytes_step,
+           "calls": {1: "one kernel per layer call (query prep and LSE merge inside the split-K kernel)",
+                     2: "query-map prologue + split-K kernel (LSE merge inside) per layer call",
+                     3: "prologue + split-K + merge kernels per layer call"}[launches_per_call(a, B, Hkv)]
+                    + ("" if a.no_overlap else "; consecutive calls overlap (programmatic dependent launch)")}
     if w == "c1":
         t8, t4 = (int(x) for x in a.strata.split(","))
         cfg["strata"] = (f"{10 * t8}% 8-bit / {10 * t4}% 4-bit / {100 - 10 * (t8 + t4)}% 2-bit, "
@@ -527,6 +534,15 @@ def barrier(world):
     torch.cuda.synchronize()
 
 
+def launches_per_call(a, B, Hkv):
+    """Kernels one kvb_decode call launches: the main kernel alone (query prep and merge inside it);
+    a prologue kernel too for a query map (config 3's spectral cache); a prologue and a merge kernel
+    for the tcgen05 decode or more than 256 (batch, KV head) pairs."""
+    if a.tc or B * Hkv > 256:
+        return 3
+    return 2 if a.workload == "c3" else 1
+
+
 def decode_arm(a):
     import torch
     import torch.distributed as dist
@@ -550,9 +566,14 @@ def decode_arm(a):
         else:
             kvb.decode(caches[layer], qq[layer], scaling, out=out[layer], events=events)
 
+    import contextlib
+    overlap = contextlib.nullcontext if a.no_overlap else kvb.overlap_previous
+
     def step():
-        for layer in range(L):
-            attend(layer, q)
+        # consecutive layers' calls may overlap: no kernel of the step writes a packed cache
+        with overlap():
+            for layer in range(L):
+                attend(layer, q)
 
     step()
     torch.cuda.synchronize()
@@ -616,8 +637,9 @@ def decode_arm(a):
 
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
-        for layer in range(L):
-            attend(layer, q_dev)
+        with overlap():
+            for layer in range(L):
+                attend(layer, q_dev)
         out_host.copy_(out, non_blocking=True)
 
     for _ in range(3):
@@ -660,7 +682,7 @@ def decode_arm(a):
             "e2e": {"value": round(world * bytes_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": q.numel() * esz,
                     "d2h_bytes_per_step": out.numel() * esz},
-            "gpu_launches": (3 + int(split)) * L * a.steps,
+            "gpu_launches": (launches_per_call(a, B, Hkv) + int(split)) * L * a.steps,
             "decode_kernel": "decode_tc (tcgen05)" if a.tc and w == "c1" else "decode_main (mma.sync)",
             "clocks": clk.summary(),
         }

@@ -48,7 +48,8 @@ const char* kvb_last_error(void);
 int kvb_version(void);
 
 /* Device status word (bit 0: a bounded wait timed out; bit 1: a bounds check failed; bit 2: a NaN
- * key reached kvb_rank_split, whose ranking is then undefined).  Synchronises
+ * key reached kvb_rank_split, whose ranking is then undefined; bit 3: a decode workspace was not
+ * zero-filled before its first use, so that call's merge may be wrong).  Synchronises
  * `stream`, copies the word to *out and clears it when `clear` is non-zero. */
 kvb_status kvb_device_status(unsigned* out, int clear, void* stream);
 
@@ -274,11 +275,25 @@ typedef struct kvb_cache {
     const float* mu_v;
 } kvb_cache;
 
+/* Options of the kvb_decode* calls made afterwards on the calling host thread; returns the previous
+ * options.  KVB_DECODE_OVERLAP: a call's main kernel may launch as a programmatic dependent of the
+ * kernel before it on the stream and start copying the packed cache while that kernel finishes (q,
+ * the workspace and the outputs are touched only after that kernel has completed).  Set it only when
+ * the kernel launched immediately before each call writes none of the packed strata the call reads;
+ * consecutive decode calls over a model's layers qualify.  Default: no options.  No counterpart in the
+ * reference (eager PyTorch launches). */
+#define KVB_DECODE_OVERLAP 1u
+unsigned kvb_set_decode_flags(unsigned flags);
+
 /* Number of split-K pieces and the plan / workspace sizes for a cache shape. */
 size_t kvb_decode_workspace_size(const kvb_cache* c, int Hq, int Tq, int n_ctas);
 /* q (B, Hq, Tq, d) dtype q_dtype dense; qpos (Tq) host array of query positions (used only for
  * appended exact rows); out (B, Tq, Hq, d) in out_dtype.  n_ctas: persistent CTAs (0 = one per
- * SM).  workspace: device buffer of kvb_decode_workspace_size bytes, 256-byte aligned. */
+ * SM).  workspace: device buffer of kvb_decode_workspace_size bytes, 256-byte aligned, zero-filled
+ * before its first use (e.g. one cudaMemsetAsync); every call leaves the part it needs zeroed again
+ * (per-head counters of the in-kernel merge; a counter found non-zero sets KVB_DEV_WORKSPACE).
+ * One kernel launch per call, except for the tcgen05 decode (block value layout) and caches of more
+ * than 256 (batch, KV head) pairs, which add a query-prep and / or a merge kernel. */
 kvb_status kvb_decode(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                       const int64_t* qpos, void* out, int out_dtype, int n_ctas,
                       void* workspace, size_t workspace_bytes, void* stream);

@@ -26,7 +26,7 @@
 #include "kvb_scores_tc.cuh"
 #include "kvb_decode.cuh"
 
-#define KVB_VERSION 101
+#define KVB_VERSION 102
 
 // The device status words (declared in kvb_common.cuh), one per device, shared by every kernel of the
 // library through the device link.

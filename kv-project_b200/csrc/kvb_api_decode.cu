@@ -1,6 +1,7 @@
 // kvb_api_decode.cu - the decode entry points of include/kvb.h (kvb_decode, kvb_decode_lse,
 // kvb_decode_events, kvb_decode_plan, kvb_decode_workspace_size, kvb_lse_merge, kvb_decode_noalloc):
-// validation, the split-K plan, the prologue / merge launches and dispatch to the main kernel.
+// validation, the split-K plan, dispatch to the main kernel (query prep and merge inside it; separate
+// prologue / merge kernels for the tcgen05 decode and for more than 256 heads).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -14,8 +15,23 @@
 #ifndef KVB_TOKEN_COST
 #define KVB_TOKEN_COST 60     // fixed per-token decode work in byte-equivalents at d_code 128 (see build_plan)
 #endif
+// Fixed costs in the plan, in byte-equivalents at d_code 128: the end-of-piece merge of every (head,
+// stratum) run a CTA holds, and at every head boundary the query prep of the new head plus the merge
+// of the previous head (which the CTA holding the boundary usually performs).  Both are doubled when
+// the CTAs hold fewer than 8 chunks on average (small batches), where they weigh most.  Measured on
+// B200, config 1, per layer (no fixed costs / these / doubled everywhere): batch 1 37.4 / 28.0 / 28.0
+// us, batch 2 44.7 / 36.8 / 36.8, batch 8 98.1 / 95.4 / 97.4.
+#ifndef KVB_PIECE_COST
+#define KVB_PIECE_COST 98304
+#endif
+#ifndef KVB_HEAD_COST
+#define KVB_HEAD_COST 131072
+#endif
+#ifndef KVB_FUSE_LIFT
+#define KVB_FUSE_LIFT 1       // 0: caches with a lift merge in the separate merge kernel
+#endif
 #ifndef KVB_PDL
-#define KVB_PDL 1             // programmatic dependent launch of the main kernel after the prologue
+#define KVB_PDL 1             // 0: never launch the main kernel as a programmatic dependent
 #endif
 
 
@@ -25,6 +41,9 @@ using kvbd::launch_maybe_pdl;
 using kvbd::dispatch_tc;
 
 namespace {
+
+// kvb_set_decode_flags: options of this host thread's decode calls
+thread_local unsigned g_decode_flags = 0;
 
 // CTAs of the main kernel: the caller's count, else every SM times the resident CTAs per SM.
 int resolve_decode_ctas(int n_ctas) {
@@ -134,6 +153,13 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
         wlast[s] = (st.n - (nch[s] - 1) * P.tok[s]) * bpt;
         W += double(nch[s] ? (nch[s] - 1) * wfull[s] + wlast[s] : 0) * heads;
     }
+    int64_t chunks = 0;
+    for (int s = 0; s < c->n_strata; ++s) chunks += nch[s] * heads;
+    const double fx = chunks < 8 * int64_t(n_ctas) ? 2.0 : 1.0;
+    // both scale with the accumulator a piece carries (R x d_code): measured on config 3 (d_code 32),
+    // 62.7 us per call against 65.2 with an unscaled head cost and 64.3 with none
+    const double seg_cost = fx * KVB_PIECE_COST * c->d_code / 128, head_cost = fx * KVB_HEAD_COST * c->d_code / 128;
+    W += (seg_cost * c->n_strata + head_cost) * heads;
     P.cta_begin.assign(n_ctas + 1, 0);
     P.head_begin.assign(heads + 1, 0);
     P.piece.clear();
@@ -147,6 +173,9 @@ kvb_status build_plan(const kvb_cache* c, int n_ctas, Plan& P) {
     // (most CTAs one width) is 107-118 us against 91 us: the ~24 SMs left with the 8-bit chunks
     // cannot keep enough bytes in flight to stream them at their share of the bandwidth.
     auto visit = [&](int h, int s) {
+        // the fixed costs sit before the segment's first chunk, so the CTA the boundary falls in
+        // (the one that gets the extra piece) takes correspondingly fewer chunks
+        cum += seg_cost + (s == 0 ? head_cost : 0.0);
         for (int64_t k = 0; k < nch[s]; ++k) {
             const double w = double(k + 1 == nch[s] ? wlast[s] : wfull[s]);
             int cta = W > 0 ? int((cum + 0.5 * w) * n_ctas / W) : 0;
@@ -228,13 +257,14 @@ struct WsLayout {
     int qp_stride;
 };
 
-// workspace: query prep per head, per-head counters of the fused merge, split-K partials
+// workspace: per-head counters of the in-kernel merge (at a fixed offset for every shape, zero
+// between calls), query prep per head (tcgen05 decode), split-K partials
 WsLayout ws_layout(const kvb_cache* c, const DecodeShape& sh, int n_pieces) {
     WsLayout L;
     L.qp_stride = kvb::qp_size(sh.R, sh.D);
-    L.qp = 256;
-    L.cnt = align256(L.qp + size_t(c->B) * c->Hkv * L.qp_stride * 4);
-    L.part = align256(L.cnt + size_t(c->B) * c->Hkv * 4);
+    L.cnt = 256;
+    L.qp = align256(L.cnt + size_t(kvb::MERGE_SMALL_HEADS) * 4);
+    L.part = align256(L.qp + size_t(c->B) * c->Hkv * L.qp_stride * 4);
     L.total = align256(L.part + size_t(n_pieces) * (2 * sh.R + sh.R * sh.D) * 4);
     return L;
 }
@@ -309,6 +339,12 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
 
 extern "C" {
 
+unsigned kvb_set_decode_flags(unsigned flags) {
+    const unsigned old = g_decode_flags;
+    g_decode_flags = flags & KVB_DECODE_OVERLAP;
+    return old;
+}
+
 kvb_status kvb_decode(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                       const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* workspace,
                       size_t workspace_bytes, void* stream) {
@@ -348,10 +384,12 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
     if (c->n_exact > 0 && c->exact_dtype != q_dtype) return fail(KVB_EINVAL, "decode: exact rows must have q's dtype");
     if (!aligned(workspace, 256)) return fail(KVB_EINVAL, "decode: workspace must be 256-byte aligned");
     const int nct = resolve_decode_ctas(n_ctas);
-    // programmatic dependent launch of the main kernel (its first cache copies overlap the prologue),
-    // except when events bracket it (an event between two launches must see the first one complete).
-    // Measured on B200 at config 1: 1.3 % per step; the same for the merge kernel was 2.7 % slower.
-    const bool pdl = KVB_PDL && !(ev_begin || ev_end);
+    // programmatic dependent launch of the main kernel, except when events bracket it (an event between
+    // two launches must see the first one complete): after a prologue kernel always (the main kernel's
+    // first cache copies overlap the prologue; 1.3 % per config-1 step); otherwise on the caller's
+    // opt-in (KVB_DECODE_OVERLAP), when the kernel before the call writes nothing the call's cache copies
+    // read.  The same for a separate merge kernel was 2.7 % slower.
+    const bool pdl = KVB_PDL && !(ev_begin || ev_end) && (uses_tc(c) || c->qmap || (g_decode_flags & KVB_DECODE_OVERLAP));
     // The plan depends only on the cache's shape and the CTA count; consecutive calls on caches of
     // one shape (the layers of a model) reuse it, and the piece table already in the kernel
     // parameters, instead of rebuilding both on the host every call.
@@ -409,29 +447,33 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
     ma.mu_v = c->mu_v;
     ma.out = out;
     ma.lse = lse;
-    // Fused merge: the main kernel's CTA that completes a head's last piece merges that head, saving
+    // In-kernel merge: the main kernel's CTA that completes a head's last piece merges that head, saving
     // the merge kernel's launch and its wait on the whole main grid (its shared memory is the
-    // end-of-piece merge buffer, free at that point).
-    const bool fuse = KVB_FUSE_MERGE && !uses_tc(c) && P.n_pieces > 0 && P.n_heads <= kvb::MERGE_SMALL_HEADS &&
+    // end-of-piece merge buffer, free at that point).  Its per-head counters sit at a fixed offset of
+    // the workspace; they start at zero and every call leaves them at zero.
+    const bool fuse = KVB_FUSE_MERGE && (KVB_FUSE_LIFT || !c->lift) && !uses_tc(c) && P.n_pieces > 0 &&
+                      P.n_heads <= kvb::MERGE_SMALL_HEADS &&
                       P.max_cta_pieces <= kvb::DEC_MAX_CTA_MERGES &&
                       (kvb::merge_smem_floats(Ra, c->d, c->d_code, kvb::DEC_THREADS) + kvb::DEC_CWARPS) * 4 <=
                           kvb::dec_red_bytes(sh.R, sh.D);
 
-    // 1. prologue
+    // 1. query prep: inside the main kernel (each CTA, for the heads of its pieces), except for caches
+    //    with a query map (its matrix product would sit on every CTA's critical path; measured on
+    //    config 3: 66.2 us per call in the main kernel against 61.6 with the prologue kernel) and the
+    //    tcgen05 decode: their prologue kernel writes it to the workspace, overlapping the main
+    //    kernel's first cache copies
     kvb::PrologueParams pp{q, q_dtype, c->B, c->Hkv, Hq, Tq, rep, rep * Tq, c->d, c->d_code,
                            c->code_kind == KVB_CODE_MIDRISE ? c->d_code
                                                             : (c->k_mode == KVB_K_PER_TOKEN ? c->k_group : c->d_code),
-                           scaling, c->qmap, c->mu_k, qp, W.qp_stride, fuse ? head_count : nullptr};
-    const size_t psm = size_t(sh.R) * (c->d + c->d_code) * 4;
+                           scaling, c->qmap, c->mu_k, qp, W.qp_stride};
     const unsigned heads = unsigned(c->B * c->Hkv);
-#define KVB_PRO(T_)                                                                        \
-    if (sh.R == 4) kvb::decode_prologue<T_, 4><<<heads, 128, psm, s>>>(pp);               \
-    else kvb::decode_prologue<T_, 8><<<heads, 128, psm, s>>>(pp);
-    if (q_dtype == KVB_F32) { KVB_PRO(float) }
-    else if (q_dtype == KVB_F16) { KVB_PRO(__half) }
-    else { KVB_PRO(__nv_bfloat16) }
-#undef KVB_PRO
-    if ((st = launch_check("decode_prologue"))) return st;
+    const bool qp_pre = uses_tc(c) || c->qmap != nullptr;
+    if (qp_pre && P.n_pieces > 0) {
+        const size_t psm = (size_t(sh.R) * (c->d + c->d_code) + 4) * 4;
+        if (sh.R == 4) kvb::decode_prologue<4><<<heads, 128, psm, s>>>(pp);
+        else kvb::decode_prologue<8><<<heads, 128, psm, s>>>(pp);
+        if ((st = launch_check("decode_prologue"))) return st;
+    }
 
     // 2. main
     if (P.n_pieces > 0) {
@@ -450,7 +492,9 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
             const kvb_stratum& sd = c->strata[i];
             dp.st[i] = kvb::StratumDev{sd.kbits, sd.vbits, P.tok[i], 0, sd.n, sd.n_alloc, sd.kc, sd.vc, sd.kmeta, sd.vmeta};
         }
+        dp.pro = pp;
         dp.qp = qp;
+        dp.qp_pre = qp_pre;
         dp.part = part;
         dp.n_pieces = P.n_pieces;
         dp.fuse_merge = fuse;

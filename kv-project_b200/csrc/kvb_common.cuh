@@ -16,6 +16,7 @@
 #define KVB_DEV_TIMEOUT 1u
 #define KVB_DEV_BOUNDS 2u
 #define KVB_DEV_NAN 4u
+#define KVB_DEV_WORKSPACE 8u   // a decode merge counter in the workspace was not zero at the call's start
 
 namespace kvb {
 

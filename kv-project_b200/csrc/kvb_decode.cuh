@@ -36,13 +36,14 @@ constexpr int DEC_MAX_PIECES = 1536;
 constexpr int DEC_MAX_CTAS = 512;
 // dynamic shared memory per CTA: the opt-in maximum less a reserve for the static shared variables
 constexpr int DEC_SMEM_BUDGET = (DEC_CTAS_PER_SM == 1 ? 227 : 113) * 1024 - 256;
-// Measured on B200, config 1 (one layer, main kernel / whole call): merging each head in the main
-// kernel (the CTA completing its last piece, after its own pieces) costs +8 us in the main kernel
-// and leaves the call time unchanged (the merge kernel it replaces takes about as long), so it is
-// off by default; taking one-tile-per-warp (8-bit) chunks two at a time slows an all-8-bit layer
-// from 136 to 150 us (fewer bytes in flight per SM), so it is off too.
+// Each head is merged inside the main kernel, by the CTA that completes its last piece (after its own
+// pieces), instead of by a separate merge kernel: one launch per call, which lets consecutive calls
+// overlap (programmatic dependent launch) and removes the merge kernel's launch gap.  Measured on
+// B200, config 1: the in-kernel merges cost +8 us in the main kernel at batch 8, about what the merge
+// kernel took, and save 20-30 % of the call at batch 1-2.  Taking one-tile-per-warp (8-bit) chunks two
+// at a time slows an all-8-bit layer from 136 to 150 us (fewer bytes in flight per SM): off.
 #ifndef KVB_FUSE_MERGE
-#define KVB_FUSE_MERGE 0      // 1: merge each head inside the main kernel (last CTA of the head)
+#define KVB_FUSE_MERGE 1      // 0: always merge in the separate merge kernel
 #endif
 #ifndef KVB_DEC_PAIR_MIN_STAGES
 #define KVB_DEC_PAIR_MIN_STAGES 99
@@ -54,6 +55,8 @@ constexpr int DEC_PAIR_MIN_STAGES = KVB_DEC_PAIR_MIN_STAGES;
 // End-of-piece merge buffer: per-warp row maxima and sums, and DEC_RED_SLOTS slots of R x D partial
 // accumulators (with fewer slots than warps, the warps past the slots add into them in a second phase).
 __host__ __device__ constexpr int dec_red_bytes(int R, int D) { return (2 * DEC_CWARPS * R + DEC_RED_SLOTS * R * D) * 4; }
+// shared memory of one head's query prep in the main kernel (qp_size floats, 128-byte multiple)
+__host__ __device__ constexpr int dec_qp_bytes(int R, int D) { return (qp_size(R, D) * 4 + 127) / 128 * 128; }
 
 constexpr int MERGE_MAX_HEADS = 4096;
 constexpr int MERGE_SMALL_HEADS = 256;
@@ -93,14 +96,15 @@ struct PrologueParams {
     const float* mu_k;      // (Hkv, d) or null
     float* qp;              // output, per head qp_stride floats
     int qp_stride;
-    int* head_count;        // per head counters of the fused merge (zeroed here), or null
 };
 
 struct DecodeParams {
     int B, Hkv, R_act, k_group, n_strata;
     int ring_bytes, qp_stride;             // ring_bytes: shared memory for the stage ring of every CTA
     StratumDev st[4];
-    const float* qp;
+    PrologueParams pro;                    // query prep (decode_main: each CTA, into shared memory)
+    const float* qp;                       // the prologue kernel's query prep, when qp_pre
+    int qp_pre;                            // 1: read qp (caches with a query map; the tcgen05 decode)
     float* part;            // per piece: m2[R] | l[R] | acc[R][D]
     int n_pieces;
     int cta_begin[DEC_MAX_CTAS + 1];
@@ -108,7 +112,7 @@ struct DecodeParams {
     // fused merge (heads <= MERGE_SMALL_HEADS): the CTA that completes the last of a head's pieces
     // merges the head (merge_head) right after its own end-of-piece merge
     int fuse_merge;
-    int* head_count;                       // per head, zeroed by the prologue of the same call
+    int* head_count;                       // per head; zero between calls (the merging CTA resets it)
     int head_begin[MERGE_SMALL_HEADS + 1]; // slots of each head's partials
     MergeArgs merge;
 };
@@ -141,7 +145,8 @@ __host__ __device__ constexpr int merge_smem_floats(int Ra, int d, int dc, int n
 // merged by several CTAs; the whole row when a lift mixes the coded channels); all `nthreads`
 // threads of the CTA call it (it synchronises).  sm: merge_smem_floats(...) floats; s_w:
 // nthreads / 32 floats.
-template <typename TQ, typename TE>
+// PSTRIDE: the partials' stride in floats when known at compile time (2 R + R d_code; 0: p.R, p.d_code).
+template <typename TQ, typename TE, int PSTRIDE = 0>
 __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, int pe, float* sm, float* s_w, int tid,
                                            int nthreads, int c0 = 0, int c1 = -1) {
     const int b = bh / p.Hkv, h = bh % p.Hkv;
@@ -160,13 +165,75 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
         c1 = d;
     }
     const int cw = c1 - c0;                // output channels of this CTA (coded channels too, without a lift)
-    for (int o = tid; o < Ra * d; o += nthreads) {
-        const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
-        s_q[o] = to_f32(q[((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * d + c]);
-    }
     const int np = pe - pb;
-    const size_t pstride = size_t(2 * R + R * dc);
+    const size_t pstride = PSTRIDE ? size_t(PSTRIDE) : size_t(2 * R + R * dc);
+    // partials are written by other CTAs of the same grid (in-kernel merge): read them through L2
     const float* part = p.part + size_t(pb) * pstride;
+    if (!p.lift && p.n_exact == 0 && np <= 32 && Ra <= nwarps && Ra * cw <= 2 * nthreads) {
+        // Fast path (the merge sits between two layers' kernels, so its latency counts): every thread
+        // issues the loads of its (at most two) outputs' partials first; meanwhile warp r < Ra weighs
+        // row r's pieces (lane = piece: max, 2^(m - M), coded mass); one barrier; then each output is
+        // summed in piece order and written.  Same arithmetic per output as the general path below,
+        // except that the row mass is a warp sum rather than a sequential one.
+        const int o0 = tid, o1 = tid + nthreads;
+        const bool h0 = o0 < Ra * cw, h1 = o1 < Ra * cw;
+        const int r0 = h0 ? o0 / cw : 0, r1 = h1 ? o1 / cw : 0;
+        const int ca = c0 + (h0 ? o0 % cw : 0), cb = c0 + (h1 ? o1 % cw : 0);
+        float v0[32], v1[32];
+        const float* src0 = part + 2 * R + r0 * dc + ca;     // piece k at src + k * pstride
+        const float* src1 = part + 2 * R + r1 * dc + cb;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+            v0[k] = h0 && k < np ? __ldcg(src0 + k * pstride) : 0.f;
+            v1[k] = h1 && k < np ? __ldcg(src1 + k * pstride) : 0.f;
+        }
+        const int warp = tid >> 5, lane = tid & 31;
+        if (warp < Ra) {
+            const float m = lane < np ? __ldcg(part + size_t(lane) * pstride + warp) : -INFINITY;
+            const float l = lane < np ? __ldcg(part + size_t(lane) * pstride + R + warp) : 0.f;
+            const float M = warp_max(m);
+            const float w = (m == -INFINITY) ? 0.f : ex2(m - M);
+            const float L = warp_sum(w * l);
+            if (lane < np) s_p[lane * Ra + warp] = w;
+            if (lane == 0) {
+                s_rowM[warp] = M;
+                s_rowLc[warp] = L;
+            }
+        }
+        __syncthreads();
+        auto finish = [&](const float (&v)[32], int r, int c) {
+            float w[32];                   // the row's piece weights, all loaded before the sum
+#pragma unroll
+            for (int k = 0; k < 32; ++k) w[k] = k < np ? s_p[k * Ra + r] : 0.f;
+            float a = 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+                if (w[k] != 0.f) a += w[k] * v[k];
+            const float L = s_rowLc[r];
+            if (p.mu_v) a = fmaf(L, p.mu_v[size_t(h) * d + c], a);
+            const float val = L > 0.f ? a / L : 0.f;
+            const int i = r / p.Tq, t = r % p.Tq;
+            const size_t oi = ((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c;
+            if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = val;
+            else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
+            else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(val);
+        };
+        if (h0) finish(v0, r0, ca);
+        if (h1) finish(v1, r1, cb);
+        if (p.lse && c0 == 0 && tid < Ra) {
+            const int i = tid / p.Tq, t = tid % p.Tq;
+            const float L = s_rowLc[tid];
+            p.lse[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
+                L > 0.f ? (s_rowM[tid] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+        }
+        __syncthreads();
+        return;
+    }
+    if (p.n_exact > 0)                     // the query rows serve only the exact rows
+        for (int o = tid; o < Ra * d; o += nthreads) {
+            const int r = o / d, c = o % d, i = r / p.Tq, t = r % p.Tq;
+            s_q[o] = to_f32(q[((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * d + c]);
+        }
     // coded partials.  The merge sits between two layers' main kernels, so its latency counts: when
     // they fit, every piece's (max, mass) is fetched at once into shared memory (s_p, s_out as
     // scratch) and the per-piece weights 2^(m - M) are kept there; each (row, channel) thread then
@@ -175,8 +242,8 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
     if (staged) {
         for (int o = tid; o < np * Ra; o += nthreads) {
             const int k = o / Ra, r = o - k * Ra;
-            s_p[o] = part[k * pstride + r];
-            s_out[o] = part[k * pstride + R + r];
+            s_p[o] = __ldcg(part + k * pstride + r);
+            s_out[o] = __ldcg(part + k * pstride + R + r);
         }
         __syncthreads();
         if (tid < Ra) {
@@ -194,11 +261,11 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
         }
     } else if (tid < Ra) {
         float M = -INFINITY;
-        for (int k = 0; k < np; ++k) M = fmaxf(M, part[k * pstride + tid]);
+        for (int k = 0; k < np; ++k) M = fmaxf(M, __ldcg(part + k * pstride + tid));
         float L = 0.f;
         for (int k = 0; k < np; ++k) {
-            const float m = part[k * pstride + tid];
-            L += (m == -INFINITY) ? 0.f : ex2(m - M) * part[k * pstride + R + tid];
+            const float m = __ldcg(part + k * pstride + tid);
+            L += (m == -INFINITY) ? 0.f : ex2(m - M) * __ldcg(part + k * pstride + R + tid);
         }
         s_rowM[tid] = M;
         s_rowLc[tid] = L;
@@ -206,27 +273,54 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
     __syncthreads();
     // coded channels needed: all of them under a lift, else this CTA's block
     const int ac0 = p.lift ? 0 : c0, acw = p.lift ? dc : cw;
-    for (int o = tid; o < Ra * acw; o += nthreads) {
-        const int r = o / acw, c = ac0 + o % acw;
-        const float* src = part + 2 * R + r * dc + c;
-        float a = 0.f;
-        for (int k0 = 0; k0 < np; k0 += 8) {
-            float v[8];
+    // Two outputs per thread and pass; the loads of the next 8 pieces are issued before the current
+    // 8 are consumed, so the L2 round trips overlap (the arithmetic and its order per output are those
+    // of one load at a time).
+    const int nout = Ra * acw;
+    for (int o0 = tid; o0 < nout; o0 += 2 * nthreads) {
+        const int o1 = o0 + nthreads;
+        const bool has1 = o1 < nout;
+        const int r0 = o0 / acw, r1 = has1 ? o1 / acw : r0;
+        const int ca = ac0 + o0 % acw, cb = has1 ? ac0 + o1 % acw : ca;
+        const float* src0 = part + 2 * R + r0 * dc + ca;
+        const float* src1 = part + 2 * R + r1 * dc + cb;
+        float a0 = 0.f, a1 = 0.f;
+        float v0[8], v1[8], n0[8], n1[8];
+        auto load8 = [&](float (&x0)[8], float (&x1)[8], int k0) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = k0 + j < np ? src[(k0 + j) * pstride] : 0.f;
+            for (int j = 0; j < 8; ++j) {
+                const bool in = k0 + j < np;
+                x0[j] = in ? __ldcg(src0 + size_t(k0 + j) * pstride) : 0.f;
+                x1[j] = in && has1 ? __ldcg(src1 + size_t(k0 + j) * pstride) : 0.f;
+            }
+        };
+        load8(v0, v1, 0);
+        for (int k0 = 0; k0 < np; k0 += 8) {
+            if (k0 + 8 < np) load8(n0, n1, k0 + 8);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 if (k0 + j >= np) break;
                 if (staged) {
-                    const float w = s_p[(k0 + j) * Ra + r];
-                    if (w != 0.f) a += w * v[j];
+                    const float w0 = s_p[(k0 + j) * Ra + r0], w1 = s_p[(k0 + j) * Ra + r1];
+                    if (w0 != 0.f) a0 += w0 * v0[j];
+                    if (w1 != 0.f) a1 += w1 * v1[j];
                 } else {
-                    const float m = part[(k0 + j) * pstride + r];
-                    if (m != -INFINITY) a += ex2(m - s_rowM[r]) * v[j];
+                    const float m0 = __ldcg(part + (k0 + j) * pstride + r0);
+                    const float m1 = __ldcg(part + (k0 + j) * pstride + r1);
+                    if (m0 != -INFINITY) a0 += ex2(m0 - s_rowM[r0]) * v0[j];
+                    if (m1 != -INFINITY) a1 += ex2(m1 - s_rowM[r1]) * v1[j];
+                }
+            }
+            if (k0 + 8 < np) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    v0[j] = n0[j];
+                    v1[j] = n1[j];
                 }
             }
         }
-        s_acc[r * dc + c] = a;
+        s_acc[r0 * dc + ca] = a0;
+        if (has1) s_acc[r1 * dc + cb] = a1;
     }
     __syncthreads();
     // lift to model space (+ coded mass * mean value)
@@ -234,9 +328,17 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
         const int r = o / cw, c = c0 + o % cw;
         float v;
         if (p.lift) {
-            const float* Lm = p.lift + size_t(h) * dc * d;
+            // the lift column's loads 16 at a time ahead of the (sequential) sum
+            const float* Lm = p.lift + size_t(h) * dc * d + c;
             v = 0.f;
-            for (int k = 0; k < dc; ++k) v = fmaf(s_acc[r * dc + k], Lm[size_t(k) * d + c], v);
+            for (int k0 = 0; k0 < dc; k0 += 16) {
+                float lv[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) lv[j] = k0 + j < dc ? __ldg(Lm + size_t(k0 + j) * d) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (k0 + j < dc) v = fmaf(s_acc[r * dc + k0 + j], lv[j], v);
+            }
         } else {
             v = s_acc[r * dc + c];
         }
@@ -329,33 +431,96 @@ __global__ void __launch_bounds__(256) decode_merge(const __grid_constant__ Merg
 }
 
 // ------------------------------------------------------------------------------------------
-// 1. prologue: grid (B * Hkv), block 128
+// 1. query prep of one head: done by each main-kernel CTA for the heads of its own pieces (into
+//    shared memory), or by decode_prologue (into the workspace) for the tcgen05 decode
 // ------------------------------------------------------------------------------------------
-template <typename T, int R>
-__global__ void __launch_bounds__(128) decode_prologue(const PrologueParams p) {
-    extern __shared__ float s_q[];          // [R][d] model-space query rows, then [R][d_code]
-    // the main kernel may launch now (programmatic dependent launch): it starts its cache copies and
-    // waits (griddepcontrol.wait) for this grid's results before using them
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int bh = blockIdx.x, b = bh / p.Hkv, h = bh % p.Hkv;
+__device__ __forceinline__ float load_q(const void* q, int dtype, size_t i) {
+    if (dtype == 0) return static_cast<const float*>(q)[i];
+    if (dtype == 1) return __half2float(static_cast<const __half*>(q)[i]);
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(q)[i]);
+}
+
+// Query prep of head bh into out (qp_size(R, d_code) floats, global or shared memory): the rows
+// r = i * Tq + t (HF repeat_kv order) of q in code space (q @ qmap[h], or q), a power-of-two prescale
+// putting max |q_code| in [2^7, 2^8) (exact; keeps the fp16 operands in range), the prescaled rows,
+// the per-(row, key group) sums, the logit bias scaling * log2(e) * (q . mu_k[h]) and
+// lam = scaling * log2(e) / prescale.  All `nthreads` threads of the CTA call it; it synchronises, and
+// `out` is complete on return.  scratch: R * (d + d_code) + nthreads / 32 floats of shared memory.
+// Without a query map and with d = 128 (every cache but the spectral one) one warp holds one row in
+// registers: one global round trip and two barriers, since the main kernel waits for it.
+template <int R>
+__device__ __forceinline__ void prep_query(const PrologueParams& p, int bh, float* out, float* scratch, int tid,
+                                           int nthreads) {
+    const int b = bh / p.Hkv, h = bh % p.Hkv;
     const int d = p.d, dc = p.d_code;
-    if (p.head_count && threadIdx.x == 0) p.head_count[bh] = 0;
-    const T* q = static_cast<const T*>(p.q);
-    float* out = p.qp + size_t(bh) * p.qp_stride;
-    float* s_qc = s_q + R * d;
-    __shared__ float s_red[4];
-    // rows r = i * Tq + t (i: query head inside the group, t: query token): HF repeat_kv order
-    for (int o = threadIdx.x; o < R * d; o += blockDim.x) {
+    const int nwarps = nthreads >> 5, warp = tid >> 5, lane = tid & 31;
+    if (!p.qmap && d == 128 && nwarps >= R) {
+        float* s_red = scratch;             // [R] row maxima
+        float v[4] = {0.f, 0.f, 0.f, 0.f};  // channels lane + 32 i of row `warp`
+        if (warp < R) {
+            if (warp < p.R_act) {
+                const int i = warp / p.Tq, t = warp % p.Tq;
+                const size_t base = ((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * 128 + lane;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = load_q(p.q, p.q_dtype, base + 32 * k);
+            }
+            float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+            am = warp_max(am);
+            if (lane == 0) s_red[warp] = am;
+        }
+        __syncthreads();
+        if (warp < R) {
+            float amax = s_red[0];
+#pragma unroll
+            for (int r = 1; r < R; ++r) amax = fmaxf(amax, s_red[r]);
+            int e = 0;
+            if (amax > 0.f) {
+                int ex;
+                frexpf(amax, &ex);          // amax = m * 2^ex, m in [0.5, 1)
+                e = 8 - ex;
+            }
+            const float sc = ldexpf(1.f, e);
+            const int r = warp;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) out[qp_qc(R) + r * 128 + lane + 32 * k] = v[k] * sc;
+            // per-group sums: this lane's channels of group g (ascending), then the warp's sum
+            const int kg = p.k_group, G = 128 / kg;
+            for (int g = 0; g < 8; ++g) {
+                float sg = 0.f;
+                if (g < G) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if ((lane + 32 * k) / kg == g) sg += v[k] * sc;
+                }
+                sg = warp_sum(sg);
+                if (lane == 0) out[qp_qsum(R, 128) + r * 8 + g] = sg;
+            }
+            float qb = 0.f;
+            if (p.mu_k) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) qb = fmaf(v[k], p.mu_k[size_t(h) * 128 + lane + 32 * k], qb);
+                qb = warp_sum(qb);
+            }
+            if (lane == 0) out[qp_qb(R, 128) + r] = qb * p.scaling * LOG2E;
+            if (r == 0 && lane == 0) out[qp_lam(R, 128)] = p.scaling * LOG2E * ldexpf(1.f, -e);
+        }
+        __syncthreads();
+        return;
+    }
+    float* s_q = scratch;                   // [R][d] model-space query rows
+    float* s_qc = s_q + R * d;              // [R][d_code]
+    float* s_red = s_qc + R * dc;           // [nwarps]
+    for (int o = tid; o < R * d; o += nthreads) {
         const int r = o / d, c = o % d;
         float v = 0.f;
         if (r < p.R_act) {
             const int i = r / p.Tq, t = r % p.Tq;
-            v = to_f32(q[((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * d + c]);
+            v = load_q(p.q, p.q_dtype, ((size_t(b) * p.Hq + h * p.rep + i) * p.Tq + t) * d + c);
         }
         s_q[o] = v;
     }
     __syncthreads();
-    for (int o = threadIdx.x; o < R * dc; o += blockDim.x) {
+    for (int o = tid; o < R * dc; o += nthreads) {
         const int r = o / dc, k = o % dc;
         float v;
         if (p.qmap) {
@@ -369,37 +534,49 @@ __global__ void __launch_bounds__(128) decode_prologue(const PrologueParams p) {
     }
     __syncthreads();
     float amax = 0.f;
-    for (int o = threadIdx.x; o < R * dc; o += blockDim.x) amax = fmaxf(amax, fabsf(s_qc[o]));
+    for (int o = tid; o < R * dc; o += nthreads) amax = fmaxf(amax, fabsf(s_qc[o]));
     amax = warp_max(amax);
-    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = amax;
+    if (lane == 0) s_red[warp] = amax;
     __syncthreads();
-    amax = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
-    // power-of-two prescale so that max |q| lies in [2^7, 2^8): exact, keeps fp16 operands in range
+    amax = s_red[0];
+    for (int w = 1; w < nwarps; ++w) amax = fmaxf(amax, s_red[w]);
     int e = 0;
     if (amax > 0.f) {
         int ex;
-        frexpf(amax, &ex);          // amax = m * 2^ex, m in [0.5, 1)
+        frexpf(amax, &ex);
         e = 8 - ex;
     }
     const float sc = ldexpf(1.f, e);
-    for (int o = threadIdx.x; o < R * dc; o += blockDim.x) out[qp_qc(R) + o] = s_qc[o] * sc;
+    for (int o = tid; o < R * dc; o += nthreads) out[qp_qc(R) + o] = s_qc[o] * sc;
     // per-group query sums, one warp per (row, group): lanes take channels lane, lane + 32, ...
     const int G = dc / p.k_group;
-    for (int o = threadIdx.x >> 5; o < R * 8; o += blockDim.x >> 5) {
+    for (int o = warp; o < R * 8; o += nwarps) {
         const int r = o / 8, g = o % 8;
         float s = 0.f;
         if (g < G)
-            for (int c = g * p.k_group + (threadIdx.x & 31); c < (g + 1) * p.k_group; c += 32) s += s_qc[r * dc + c] * sc;
+            for (int c = g * p.k_group + lane; c < (g + 1) * p.k_group; c += 32) s += s_qc[r * dc + c] * sc;
         s = warp_sum(s);
-        if ((threadIdx.x & 31) == 0) out[qp_qsum(R, dc) + o] = s;
+        if (lane == 0) out[qp_qsum(R, dc) + o] = s;
     }
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    for (int r = warp; r < R; r += nwarps) {
         float s = 0.f;
-        if (p.mu_k)
-            for (int c = 0; c < d; ++c) s = fmaf(s_q[r * d + c], p.mu_k[size_t(h) * d + c], s);
-        out[qp_qb(R, dc) + r] = s * p.scaling * LOG2E;
+        if (p.mu_k) {
+            for (int c = lane; c < d; c += 32) s = fmaf(s_q[r * d + c], p.mu_k[size_t(h) * d + c], s);
+            s = warp_sum(s);
+        }
+        if (lane == 0) out[qp_qb(R, dc) + r] = s * p.scaling * LOG2E;
     }
-    if (threadIdx.x == 0) out[qp_lam(R, dc)] = p.scaling * LOG2E * ldexpf(1.f, -e);
+    if (tid == 0) out[qp_lam(R, dc)] = p.scaling * LOG2E * ldexpf(1.f, -e);
+    __syncthreads();
+}
+
+// Prologue kernel of the tcgen05 decode: grid (B * Hkv), block 128; the query prep of every head into
+// the workspace.  The main kernel launches as its programmatic dependent.
+template <int R>
+__global__ void __launch_bounds__(128) decode_prologue(const PrologueParams p) {
+    extern __shared__ float s_scratch[];    // R * (d + d_code) + 4 floats
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    prep_query<R>(p, blockIdx.x, p.qp + size_t(blockIdx.x) * p.qp_stride, s_scratch, threadIdx.x, blockDim.x);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -518,7 +695,9 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
     int* rel = reinterpret_cast<int*>(full + DEC_MAX_STAGES);      // release counters per stage
     float* red = reinterpret_cast<float*>(smem + 128);
     constexpr int red_bytes = dec_red_bytes(R, D);
-    uint8_t* stages = smem + 128 + ((red_bytes + 127) / 128) * 128;
+    // the query prep of the piece's head (qp_size floats), after the end-of-piece merge buffer
+    float* sqp = reinterpret_cast<float*>(smem + 128 + ((red_bytes + 127) / 128) * 128);
+    uint8_t* stages = reinterpret_cast<uint8_t*>(sqp) + dec_qp_bytes(R, D);
 
     __shared__ int s_merge[DEC_MAX_CTA_MERGES], s_nmerge;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -555,7 +734,6 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
             const int ch = pc.z + int(k - base);
             const StratumDev& sd = p.st[pc.y];
             const int head = pc.x;
-            const float* qp = p.qp + size_t(head) * p.qp_stride;
             const StageLay L = stage_lay<D, R, GK, GV, KMODE, CODE>(sd.kbits, sd.vbits, sd.tok, p.k_group);
             const int rbk = D * sd.kbits / 8, rbv = D * sd.vbits / 8;
             const int s = k % nstage;
@@ -598,18 +776,28 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
     };
     if (warp == 0)
         for (int k = 0; k < nstage; ++k) fill(uint32_t(k));
-    // Programmatic dependent launch (when the host enables it): the first bulk copies above (the
-    // cache does not depend on the prologue) run while the prologue finishes; its query prep is
-    // read only after this wait (a no-op in a plain launch).
+    // Programmatic dependent launch.  This kernel lets the next kernel in the stream launch now: its
+    // CTAs take the SMs this grid's CTAs free and start their own cache copies there.  When this
+    // kernel was itself launched as a programmatic dependent (a caller's opt-in: the kernel before it
+    // writes nothing this call copies above), the copies above ran while that kernel finished; q,
+    // the workspace and the outputs are touched only after this wait, which returns once every
+    // earlier kernel of the stream has completed and its writes are visible (a no-op otherwise).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // Every warp consumes every chunk; the last warp to release a stage refills it with the chunk
     // nstage ahead, so no warp is reserved for copies and all 12 warps compute.
     uint32_t it = 0;
+    int prepped = -1;                      // head whose query prep sqp holds
     for (int pi = pc0; pi < pc1; ++pi) {
         const int4 pc = unpack_piece(p.piece[pi]);
         const StratumDev& sd = p.st[pc.y];
-        const float* qp = p.qp + size_t(pc.x) * p.qp_stride;
+        if (!p.qp_pre && pc.x != prepped) {
+            // the end-of-piece merge buffer is free here (the previous piece's merge synchronised)
+            prep_query<R>(p.pro, pc.x, sqp, red, threadIdx.x, DEC_THREADS);
+            prepped = pc.x;
+        }
+        const float* qp = p.qp_pre ? p.qp + size_t(pc.x) * p.qp_stride : sqp;
         float* part = p.part + size_t(piece_slot(p.piece[pi])) * (2 * R + R * D);
         bool ok = true;
         auto body = [&](auto kbc, auto vbc) {
@@ -736,7 +924,17 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
                 const int head = pc.x;
                 if (threadIdx.x == 0) {
                     const int np = p.head_begin[head + 1] - p.head_begin[head];
-                    if (atomicAdd(&p.head_count[head], 1) == np - 1) s_merge[s_nmerge++] = head;
+                    const int done_before = atomicAdd(&p.head_count[head], 1);
+                    if (done_before == np - 1) {
+                        // every other piece of the head has counted: reset for the next call; the
+                        // fence orders the other CTAs' partials (published before their counts)
+                        // before this CTA's reads of them, which follow a CTA barrier
+                        __threadfence();
+                        p.head_count[head] = 0;
+                        s_merge[s_nmerge++] = head;
+                    } else if (done_before < 0 || done_before >= np) {
+                        raise_status(KVB_DEV_WORKSPACE);
+                    }
                 }
             }
 #endif
@@ -763,16 +961,16 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
     // of the CTAs that wrote them)
     __syncthreads();
     for (int i = 0; i < s_nmerge; ++i) {
-        __threadfence();
         const int head = s_merge[i];
         const int pb = p.head_begin[head], pe = p.head_begin[head + 1];
         float* sw = red + merge_smem_floats(p.merge.R_act, p.merge.d, p.merge.d_code, DEC_THREADS);
+        constexpr int PS = 2 * R + R * D;
         if (p.merge.q_dtype == 0)
-            merge_head<float, float>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+            merge_head<float, float, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
         else if (p.merge.q_dtype == 1)
-            merge_head<__half, __half>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+            merge_head<__half, __half, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
         else
-            merge_head<__nv_bfloat16, __nv_bfloat16>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+            merge_head<__nv_bfloat16, __nv_bfloat16, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
         __syncthreads();
     }
 #endif

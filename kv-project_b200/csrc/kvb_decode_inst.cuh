@@ -25,7 +25,7 @@ kvb_status run_main(const kvb_cache* c, const Plan& P, kvb::DecodeParams& p, cud
         p.st[i].stage_bytes = std::max(128, (L.end + 127) / 128 * 128);
         mx = std::max(mx, p.st[i].stage_bytes);
     }
-    const int fixed = 128 + (kvb::dec_red_bytes(R, D) + 127) / 128 * 128;
+    const int fixed = 128 + (kvb::dec_red_bytes(R, D) + 127) / 128 * 128 + kvb::dec_qp_bytes(R, D);
     const int ring = std::min((kvb::DEC_SMEM_BUDGET - fixed) / 128 * 128, kvb::DEC_MAX_STAGES * mx);
     if (ring < 2 * mx) return fail(KVB_EUNSUPPORTED, "decode: stage of %d bytes does not fit twice in shared memory", mx);
     p.ring_bytes = ring;

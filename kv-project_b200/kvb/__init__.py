@@ -9,9 +9,9 @@ strata assignment (K2), fused split-K flash decoding over packed codes (K3), the
 
 from . import _lib, ops, cache, workloads, state, seqsplit, codebooks   # noqa: F401
 from .ops import (PackedCache, quant_pack, key_energy, rank_split, query_scores, snapkv_scores, decode, decode_plan,  # noqa: F401
-                  device_status, UNIFORM_STEP)
+                  device_status, overlap_previous, UNIFORM_STEP)
 from .state import KvbStrataState, KvbCodedState, tier_as_kvb  # noqa: F401
 
 __all__ = ["ops", "cache", "workloads", "state", "seqsplit", "codebooks", "PackedCache", "quant_pack", "key_energy", "rank_split",
-           "query_scores", "snapkv_scores", "decode", "decode_plan", "device_status", "UNIFORM_STEP",
+           "query_scores", "snapkv_scores", "decode", "decode_plan", "device_status", "overlap_previous", "UNIFORM_STEP",
            "KvbStrataState", "KvbCodedState", "tier_as_kvb"]

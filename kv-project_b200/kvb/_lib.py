@@ -44,6 +44,7 @@ SIGNATURES = {
     "kvb_version": (C.c_int, []),
     "kvb_device_status": (_i32, [C.POINTER(C.c_uint), _i32, _p]),
     "kvb_device_diag": (_i32, [C.POINTER(C.c_uint), _i32, _p]),
+    "kvb_set_decode_flags": (C.c_uint, [C.c_uint]),
     "kvb_quant_pack": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                               _i32, _i32, _i32, _i32, _f32, _p, _p, _p, _p]),
     "kvb_quant_pack_blocked": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,

@@ -336,8 +336,24 @@ class PackedCache:
             if size == 0:
                 L.check(L.KVB_EINVAL, "kvb_decode_workspace_size")
             dev = self.strata[0]["kc"].device if self.strata else self.k_exact.device
-            self._ws[key] = torch.empty(size, dtype=torch.uint8, device=dev)
+            # zero-filled once: the in-kernel merge's counters start at zero and every call leaves them so
+            self._ws[key] = torch.zeros(size, dtype=torch.uint8, device=dev)
         return self._ws[key]
+
+
+class overlap_previous:
+    """Context manager: decode calls inside it may start copying their packed cache while the kernel
+    launched before them on the stream finishes (kvb_set_decode_flags(KVB_DECODE_OVERLAP)).  Use it
+    only where no kernel right before a decode call writes that call's packed strata, e.g. around the
+    decode calls of consecutive layers."""
+
+    def __enter__(self):
+        self._old = L.lib().kvb_set_decode_flags(1)
+        return self
+
+    def __exit__(self, *exc):
+        L.lib().kvb_set_decode_flags(self._old)
+        return False
 
 
 def decode(cache: PackedCache, q: torch.Tensor, scaling: float, qpos=None, out=None, out_dtype=None,

@@ -87,16 +87,24 @@ def test_plan_covers_every_chunk_once(B, H, T, n_ctas):
         ps = by_slot[head_begin[h]:head_begin[h + 1]]
         assert len(ps) and np.all(ps[:, 0] == h)
         assert [tuple(x) for x in ps[:, 1:3]] == sorted(tuple(x) for x in ps[:, 1:3])
-    # balance: no CTA gets more than (average + one chunk) of work (code bytes + 60 per token)
+    # balance: no CTA gets more than (average + one chunk + one segment's fixed costs) of work: code
+    # bytes + 60 per token, plus 98304 byte-equivalents per (head, stratum) segment start (its
+    # end-of-piece merge) and 131072 per head start (query prep and the previous head's merge),
+    # charged to the CTA holding the start, both doubled below 8 chunks per CTA
     bpt = {s: 128 * (bits[s][0] + bits[s][1]) // 8 + 60 for s in range(3)}
+    n_chunks = B * H * sum(-(-counts[s] // TOK[bits[s]]) for s in range(3))
+    fx = 2 if n_chunks < 8 * n_ctas else 1
+    seg, head = 98304 * fx, 131072 * fx
     w = np.zeros(n_ctas)
     for cta in range(n_ctas):
         for h, s, lo, hi in pieces[cta_begin[cta]:cta_begin[cta + 1]]:
             tok = TOK[bits[s]]
+            if lo == 0:
+                w[cta] += seg + (head if s == 0 else 0)
             for k in range(lo, hi):
                 w[cta] += min(tok, counts[s] - k * tok) * bpt[s]
     max_chunk = max(TOK[bits[s]] * bpt[s] for s in range(3))
-    assert w.max() <= w.sum() / n_ctas + max_chunk + 1
+    assert w.max() <= w.sum() / n_ctas + max_chunk + seg + head + 1
 
 
 def test_decode_rejects_bad_requests():
