@@ -659,7 +659,13 @@ def decode_arm(a):
     if rank == 0:
         peak, peak_kind = peaks()
         gbs = world * bytes_step / (ms * 1e-3) / 1e9
-        achieved = (sum(bytes_layer) / L) / (main_ms_avg * 1e-3) / 1e9
+        # When the timed region holds nothing but the main kernel's launches (one per layer call, back
+        # to back), its average launch duration is the region's time over its launches; consecutive
+        # launches overlap there, so events between them cannot bracket one.  Otherwise the duration
+        # comes from events around each main kernel, launched alone (no overlap).
+        alone = launches_per_call(a, B, Hkv) == 1 and not split and L >= 8
+        launch_ms = ms / L if alone else main_ms_avg
+        achieved = (sum(bytes_layer) / L) / (launch_ms * 1e-3) / 1e9
         traffic = None
         rec = TRAFFIC.get(a.workload)
         if rec and (a.layers, a.batch, a.context, a.tc, a.strata, world) == (None, None, None, False, "1,3", 1) \
@@ -677,7 +683,10 @@ def decode_arm(a):
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "kernel": "decode_tc" if a.tc and w == "c1" else "decode_main",
                          "bytes_per_launch": sum(bytes_layer) // L,
-                         "us_per_launch": round(main_ms_avg * 1000, 2),
+                         "us_per_launch": round(launch_ms * 1000, 2),
+                         "timing": (f"timed region / its {L} decode_main launches per step (back to back)" if alone
+                                    else "CUDA events around each decode_main launch, launched alone"),
+                         "us_per_launch_alone": round(main_ms_avg * 1000, 2),
                          "traffic": None if traffic is None else round(traffic)},
             "e2e": {"value": round(world * bytes_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": q.numel() * esz,
