@@ -330,9 +330,10 @@ kvb_status kvb_lse_merge(const float* parts, int64_t part_stride, const float* l
  * library keeps until process exit.  Requests needing more scratch return KVB_EINVAL (the message
  * gives the size needed; use kvb_decode with your own workspace for those).  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress, with that device current); make
- * that first call before any stream capture.  All calls share the one array and nothing in it needs
- * to start at zero, but calls that overlap on the GPU (concurrent streams, or several host threads)
- * race on it: serialise them.  The current device must be the device of `stream` (KVB_EINVAL
+ * that first call before any stream capture.  All calls share the one array.  Its per-head merge
+ * counters must be zero when a call starts: the array is zero when the library loads and every call
+ * leaves them at zero again (a non-zero counter sets KVB_DEV_WORKSPACE).  Calls that overlap on the GPU
+ * (concurrent streams, or several host threads) race on it: serialise them.  The current device must be the device of `stream` (KVB_EINVAL
  * otherwise). */
 #define KVB_NOALLOC_SCRATCH_BYTES (8u << 20)
 kvb_status kvb_decode_noalloc(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
