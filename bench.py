@@ -20,8 +20,9 @@ Other workloads (--workload), each printing the same JSON line for its own confi
   c4          config 4: 70B shape, B 32 sharded over ranks (strong scaling), 131072 tokens, 4-bit g128;
               the layers that fit in HBM are resident and timed (config.layers)
   c4s         config 4 with batch 4: the 131072-token context split over ranks (strong scaling); per
-              layer the ranks' (output, lse) parts meet in one peer-memory exchange + merge kernel
-              (--xchg p2p, default) or an NCCL all-gather + kvb_lse_merge (--xchg nccl)
+              layer the ranks' (output, lse) parts meet over peer memory inside the decode kernel
+              (--xchg p2p, default), in a second kernel (--xchg p2p2), or through an NCCL all-gather +
+              kvb_lse_merge (--xchg nccl)
   c1-pack     compress side of config 1 (key energy, rank split, 6 quantise+pack calls per layer)
   c2-evict    compress side of config 2 (accumulated scores of 64 queries, top-k, 2 packs per layer)
   c3-project  compress side of config 3 (tcgen05 basis projection + mid-rise code of K and V)
@@ -83,8 +84,9 @@ def args_():
     p.add_argument("--no-overlap", action="store_true",
                    help="launch each layer's decode call only after the previous one completes (no programmatic "
                         "dependent launch between consecutive calls)")
-    p.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
-                   help="c4s on N > 1 ranks: peer-memory exchange kernel (p2p) or NCCL all-gather + merge")
+    p.add_argument("--xchg", choices=["p2p", "p2p2", "nccl"], default="p2p",
+                   help="c4s on N > 1 ranks: exchange inside the decode kernel (p2p), a second exchange kernel "
+                        "(p2p2) or NCCL all-gather + merge")
     p.add_argument("--strata", default="1,3",
                    help="config 1: tenths of the tokens at 8 and 4 bits (the rest 2-bit); e.g. 0,0 = all 2-bit")
     p.add_argument("--tc", action="store_true",
@@ -270,8 +272,11 @@ def decode_config(a, w, world, L, B, T, Hq, Hkv, dt, bytes_step):
                                  f"per rank), no collective",
                            "c4": f"batch split over {world} ranks, no collective",
                            "c4s": f"context split over {world} ranks, " + (
-                               "peer-memory exchange + LSE merge kernel (kvb_xchg_merge) per layer"
-                               if a.xchg == "p2p" else "NCCL all-gather + LSE merge per layer")
+                               {"p2p": "peer-memory exchange + LSE merge inside the decode kernel "
+                                       "(kvb_decode_xchg), one kernel per layer",
+                                "p2p2": "decode kernel + peer-memory exchange / LSE merge kernel (kvb_xchg_merge) "
+                                        "per layer",
+                                "nccl": "NCCL all-gather + LSE merge per layer"}[a.xchg])
                            }.get(w, f"dp{world} (batch x kv-head shards, no collective)"),
            "bytes_per_step_per_gpu": bytes_step,
            "calls": {1: "one kernel per layer call (query prep and LSE merge inside the split-K kernel)",
@@ -558,7 +563,8 @@ def decode_arm(a):
     split = a.workload == "c4s" and world > 1
     dec = None
     if split:
-        dec = kvb.seqsplit.P2PSeqSplitDecoder() if a.xchg == "p2p" else kvb.seqsplit.SeqSplitDecoder()
+        dec = (kvb.seqsplit.SeqSplitDecoder() if a.xchg == "nccl" else
+               kvb.seqsplit.P2PSeqSplitDecoder(fused=a.xchg == "p2p"))
 
     def attend(layer, qq, events=None):
         if split:
@@ -691,7 +697,7 @@ def decode_arm(a):
             "e2e": {"value": round(world * bytes_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": q.numel() * esz,
                     "d2h_bytes_per_step": out.numel() * esz},
-            "gpu_launches": (launches_per_call(a, B, Hkv) + int(split)) * L * a.steps,
+            "gpu_launches": (launches_per_call(a, B, Hkv) + int(split and a.xchg != "p2p")) * L * a.steps,
             "decode_kernel": "decode_tc (tcgen05)" if a.tc and w == "c1" else "decode_main (mma.sync)",
             "clocks": clk.summary(),
         }

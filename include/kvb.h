@@ -313,6 +313,25 @@ kvb_status kvb_decode_lse(const kvb_cache* c, const void* q, int q_dtype, int Hq
                           const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* Sequence-split decode with the cross-rank merge in the same kernel.  Each of `world` ranks (one GPU
+ * each, peer access over NVLink / NVSwitch) holds a contiguous token range of every (batch, KV head)
+ * in its cache c and calls this with the same q, shapes and order as the others; out (B, Tq, Hq, d)
+ * receives attention over all ranks' tokens on every rank.  regions[r]: rank r's exchange region of
+ * kvb_decode_xchg_bytes bytes (kvb_xchg_alloc on rank r, kvb_xchg_open of its handle elsewhere; zeroed
+ * at allocation).  The CTA that merges a head writes this rank's normalised rows and lse into slot
+ * `rank` of every region, publishes a flag per (rank, head), waits (bounded by timeout_ns, 0: 2 s) for
+ * every rank's flag of the head and merges the parts with the arithmetic of kvb_lse_merge: one kernel
+ * per call instead of kvb_decode_lse + kvb_xchg_merge.  A wait that runs out sets KVB_DEV_TIMEOUT
+ * (site 0x42) and merges what arrived; while the status word holds it, calls write no output (site
+ * 0x43) until the exchange is re-established as for kvb_xchg_merge (kvb_xchg_zero on every rank).
+ * KVB_EUNSUPPORTED where the merge cannot run inside the main kernel (more than 256 (batch, KV head)
+ * pairs, the tcgen05 value layout, an empty token range): use kvb_decode_lse + kvb_xchg_merge. */
+size_t kvb_decode_xchg_bytes(const kvb_cache* c, int Hq, int Tq, int world);
+kvb_status kvb_decode_xchg(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                           const int64_t* qpos, void* out, int out_dtype, int rank, int world,
+                           void* const* regions, uint64_t timeout_ns, int n_ctas, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Merge of n_parts attention parts over disjoint token sets: part k's rows at parts + k * part_stride
  * ((rows, d) float32, each row normalised) with lse at lse + k * lse_stride ((rows) float32, natural
  * log).  out (rows, d) in out_dtype = sum_k exp(lse_k - M) o_k / sum_k exp(lse_k - M) (the exact LSE

@@ -270,11 +270,26 @@ WsLayout ws_layout(const kvb_cache* c, const DecodeShape& sh, int n_pieces) {
 }
 
 kvb_status dispatch_main(const DecodeShape& sh, const kvb_cache* c, const Plan& P, kvb::DecodeParams& p,
-                         cudaStream_t s, bool pdl) {
+                         cudaStream_t s, bool pdl, bool xc) {
     using namespace kvb;
+#define KVB_XCASE(D_, R_, GK_, GV_, KM_, CK_)                                                          \
+    if (sh.D == D_ && sh.R == R_ && sh.GK == GK_ && sh.GV == GV_ && sh.kmode == KM_ && sh.code == CK_) \
+        return kvbd::run_main<D_, R_, GK_, GV_, KM_, CK_, true>(c, P, p, s, pdl);
+    if (xc) {
+        KVB_XCASE(128, 4, 1, 1, KM_CHANNEL, KV_ASYM)
+        KVB_XCASE(128, 8, 1, 1, KM_CHANNEL, KV_ASYM)
+        KVB_XCASE(128, 4, 2, 2, KM_TOKEN, KV_ASYM)
+        KVB_XCASE(128, 8, 2, 2, KM_TOKEN, KV_ASYM)
+        KVB_XCASE(128, 4, 1, 1, KM_TOKEN, KV_ASYM)
+        KVB_XCASE(128, 8, 1, 1, KM_TOKEN, KV_ASYM)
+        return fail(KVB_EUNSUPPORTED, "decode_xchg: no sequence-split kernel for d_code=%d rows=%d key groups=%d "
+                    "value groups=%d mode=%d code=%d (use kvb_decode_lse + kvb_xchg_merge)",
+                    sh.D, sh.R, sh.GK, sh.GV, sh.kmode, sh.code);
+    }
+#undef KVB_XCASE
 #define KVB_CASE(D_, R_, GK_, GV_, KM_, CK_)                                                           \
     if (sh.D == D_ && sh.R == R_ && sh.GK == GK_ && sh.GV == GV_ && sh.kmode == KM_ && sh.code == CK_) \
-        return kvbd::run_main<D_, R_, GK_, GV_, KM_, CK_>(c, P, p, s, pdl);
+        return kvbd::run_main<D_, R_, GK_, GV_, KM_, CK_, false>(c, P, p, s, pdl);
     // KIVI per-token keys (mixed-precision strata, config 1)
     KVB_CASE(128, 4, 2, 2, KM_TOKEN, KV_ASYM)
     KVB_CASE(128, 8, 2, 2, KM_TOKEN, KV_ASYM)
@@ -332,9 +347,16 @@ size_t kvb_decode_workspace_size(const kvb_cache* c, int Hq, int Tq, int n_ctas)
 }  // extern "C"
 
 namespace {
+// the sequence-split exchange of kvb_decode_xchg (world 0: none)
+struct XchgArgs {
+    int rank = 0, world = 0;
+    void* const* regions = nullptr;
+    uint64_t timeout_ns = 0;
+};
 kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                        const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas, void* workspace,
-                       size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end);
+                       size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end,
+                       const XchgArgs& xa = XchgArgs());
 }  // namespace
 
 extern "C" {
@@ -368,12 +390,36 @@ kvb_status kvb_decode_lse(const kvb_cache* c, const void* q, int q_dtype, int Hq
                        workspace_bytes, stream, nullptr, nullptr);
 }
 
+size_t kvb_decode_xchg_bytes(const kvb_cache* c, int Hq, int Tq, int world) {
+    DecodeShape sh{};
+    if (validate_cache(c, sh, Hq, Tq) || world < 2 || world > kvb::XC_MAX_RANKS) return 0;
+    const size_t rows = size_t(c->B) * Tq * Hq, heads = size_t(c->B) * c->Hkv;
+    return (2 * size_t(world) * rows * (c->d + 1)) * 4 + (size_t(world) + 1) * heads * 4;
+}
+
+kvb_status kvb_decode_xchg(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
+                           const int64_t* qpos, void* out, int out_dtype, int rank, int world,
+                           void* const* regions, uint64_t timeout_ns, int n_ctas, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+    if (world < 2 || world > kvb::XC_MAX_RANKS || rank < 0 || rank >= world || !regions)
+        return fail(KVB_EINVAL, "decode_xchg: rank / world (2 <= world <= %d) / regions", kvb::XC_MAX_RANKS);
+    for (int r = 0; r < world; ++r)
+        if (!regions[r] || !aligned(regions[r], 16)) return fail(KVB_EINVAL, "decode_xchg: region %d", r);
+    XchgArgs xa;
+    xa.rank = rank;
+    xa.world = world;
+    xa.regions = regions;
+    xa.timeout_ns = timeout_ns;
+    return decode_impl(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, nullptr, n_ctas, workspace,
+                       workspace_bytes, stream, nullptr, nullptr, xa);
+}
+
 }  // extern "C"
 
 namespace {
 kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                        const int64_t* qpos, void* out, int out_dtype, float* lse, int n_ctas, void* workspace,
-                       size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end) {
+                       size_t workspace_bytes, void* stream, void* ev_begin, void* ev_end, const XchgArgs& xa) {
     DecodeShape sh{};
     kvb_status st = validate_cache(c, sh, Hq, Tq);
     if (st) return st;
@@ -447,6 +493,13 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
     ma.mu_v = c->mu_v;
     ma.out = out;
     ma.lse = lse;
+    if (xa.world > 1) {
+        ma.xrank = xa.rank;
+        ma.xworld = xa.world;
+        ma.xheads = c->B * c->Hkv;
+        ma.xtimeout_ns = xa.timeout_ns ? xa.timeout_ns : 2000000000ull;
+        for (int r = 0; r < xa.world; ++r) ma.xregion[r] = static_cast<float*>(xa.regions[r]);
+    }
     // In-kernel merge: the main kernel's CTA that completes a head's last piece merges that head, saving
     // the merge kernel's launch and its wait on the whole main grid (its shared memory is the
     // end-of-piece merge buffer, free at that point).  Its per-head counters sit at a fixed offset of
@@ -456,6 +509,11 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
                       P.max_cta_pieces <= kvb::DEC_MAX_CTA_MERGES &&
                       (kvb::merge_smem_floats(Ra, c->d, c->d_code, kvb::DEC_THREADS) + kvb::DEC_CWARPS) * 4 <=
                           kvb::dec_red_bytes(sh.R, sh.D);
+
+    if (xa.world > 1 && !fuse)
+        return fail(KVB_EUNSUPPORTED, "decode_xchg: needs the in-kernel merge (at most %d heads, no tcgen05 "
+                    "value layout, at most %d pieces per CTA, a non-empty token range)", kvb::MERGE_SMALL_HEADS,
+                    kvb::DEC_MAX_CTA_MERGES);
 
     // 1. query prep: inside the main kernel (each CTA, for the heads of its pieces), except for caches
     //    with a query map (its matrix product would sit on every CTA's critical path; measured on
@@ -521,7 +579,8 @@ kvb_status decode_impl(const kvb_cache* c, const void* q, int q_dtype, int Hq, i
         if (ev_begin && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_begin), s, ev_flags),
                                          "record event")))
             return st;
-        if ((st = uses_tc(c) ? dispatch_tc(sh, c, P, dp, s) : dispatch_main(sh, c, P, dp, s, pdl))) return st;
+        if ((st = uses_tc(c) ? dispatch_tc(sh, c, P, dp, s) : dispatch_main(sh, c, P, dp, s, pdl, xa.world > 1)))
+            return st;
         if (ev_end && (st = cuda_check(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev_end), s, ev_flags),
                                        "record event")))
             return st;

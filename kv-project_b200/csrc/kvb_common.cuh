@@ -33,6 +33,19 @@ __device__ __forceinline__ void note_wait_timeout(unsigned site, unsigned counte
     atomicCAS(&g_diag, 0u, 0x80000000u | (site & 0xFFu) | ((blockIdx.x & 0xFFu) << 8) | ((counter & 0x7FFFu) << 16));
 }
 
+// ranks of a sequence split over peer memory (kvb_xchg_merge, kvb_decode_xchg)
+constexpr int XC_MAX_RANKS = 8;
+
+// flag store / load of the peer-memory exchanges: release / acquire at system scope
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

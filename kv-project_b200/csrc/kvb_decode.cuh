@@ -35,7 +35,7 @@ constexpr int DEC_MAX_STAGES = 4;
 constexpr int DEC_MAX_PIECES = 1536;
 constexpr int DEC_MAX_CTAS = 512;
 // dynamic shared memory per CTA: the opt-in maximum less a reserve for the static shared variables
-constexpr int DEC_SMEM_BUDGET = (DEC_CTAS_PER_SM == 1 ? 227 : 113) * 1024 - 256;
+constexpr int DEC_SMEM_BUDGET = (DEC_CTAS_PER_SM == 1 ? 227 : 113) * 1024 - 512;
 // Each head is merged inside the main kernel, by the CTA that completes its last piece (after its own
 // pieces), instead of by a separate merge kernel: one launch per call, which lets consecutive calls
 // overlap (programmatic dependent launch) and removes the merge kernel's launch gap.  Measured on
@@ -73,6 +73,11 @@ struct MergeArgs {
     const float* mu_v;      // (Hkv, d) or null
     void* out;
     float* lse;             // (B, Tq, Hq) natural-log sum of exp(scaled logits), or null
+    // sequence split over peer memory (xworld > 1; in-kernel merge only): each head's normalised rows
+    // and lse go to slot xrank of every rank's region, then the ranks' parts are merged into out
+    int xrank, xworld, xheads;
+    uint64_t xtimeout_ns;
+    float* xregion[XC_MAX_RANKS];
 };
 
 
@@ -146,9 +151,19 @@ __host__ __device__ constexpr int merge_smem_floats(int Ra, int d, int dc, int n
 // threads of the CTA call it (it synchronises).  sm: merge_smem_floats(...) floats; s_w:
 // nthreads / 32 floats.
 // PSTRIDE: the partials' stride in floats when known at compile time (2 R + R d_code; 0: p.R, p.d_code).
+// xout / xlse (optional): write the head's rows as float32 to xout and its lse to xlse (indexed as
+// out and lse) instead of out / lse (the local part of a sequence-split exchange).
 template <typename TQ, typename TE, int PSTRIDE = 0>
 __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, int pe, float* sm, float* s_w, int tid,
-                                           int nthreads, int c0 = 0, int c1 = -1) {
+                                           int nthreads, int c0 = 0, int c1 = -1, float* xout = nullptr,
+                                           float* xlse = nullptr) {
+    float* const lse_dst = xout ? xlse : p.lse;
+    auto emit = [&](size_t oi, float v) {
+        if (xout) xout[oi] = v;
+        else if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
+        else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
+        else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
+    };
     const int b = bh / p.Hkv, h = bh % p.Hkv;
     const int R = p.R, d = p.d, dc = p.d_code, Ra = p.R_act;
     float* s_q = sm;                       // [Ra][d]
@@ -213,17 +228,14 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
             if (p.mu_v) a = fmaf(L, p.mu_v[size_t(h) * d + c], a);
             const float val = L > 0.f ? a / L : 0.f;
             const int i = r / p.Tq, t = r % p.Tq;
-            const size_t oi = ((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c;
-            if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = val;
-            else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
-            else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(val);
+            emit(((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c, val);
         };
         if (h0) finish(v0, r0, ca);
         if (h1) finish(v1, r1, cb);
-        if (p.lse && c0 == 0 && tid < Ra) {
+        if (lse_dst && c0 == 0 && tid < Ra) {
             const int i = tid / p.Tq, t = tid % p.Tq;
             const float L = s_rowLc[tid];
-            p.lse[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
+            lse_dst[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
                 L > 0.f ? (s_rowM[tid] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
         }
         __syncthreads();
@@ -398,17 +410,115 @@ __device__ __forceinline__ void merge_head(const MergeArgs& p, int bh, int pb, i
     for (int o = tid; o < Ra * cw; o += nthreads) {
         const int r = o / cw, c = c0 + o % cw, i = r / p.Tq, t = r % p.Tq;
         const float v = s_rowL[r] > 0.f ? s_out[r * d + c] / s_rowL[r] : 0.f;
-        const size_t oi = ((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c;
+        emit(((size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i) * d + c, v);
+    }
+    if (lse_dst && c0 == 0 && tid < Ra) {
+        const int i = tid / p.Tq, t = tid % p.Tq;
+        const float L = s_rowL[tid];
+        lse_dst[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
+            L > 0.f ? (s_rowM[tid] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Sequence split over peer memory, fused into the main kernel (kvb_decode_xchg).  Every rank decodes
+// its own token range; the CTA that merges head bh writes the head's normalised rows and lse into
+// slot `xrank` of its own region (merge_head with xout / xlse), copies them into the same slot of every
+// peer's region (plain peer stores; no TMA, no multicast) and publishes a flag per (rank, head) with a
+// system-scope release (xchg_publish); then it waits (bounded) for every rank's flag of the head and
+// merges the ranks' rows: out = sum_r e^(lse_r - M) o_r / sum_r e^(lse_r - M), the arithmetic of
+// kvb_xchg_merge / kvb_lse_merge (the merge of StrataState.attend, STRATA_KV.py:1784-1792, across
+// ranks; xchg_finish).  A CTA publishes every head it merges before it waits for any, so no wait can
+// stand between two ranks' publications.  Region of one rank: [2 parities][world][rows * (d + 1)]
+// floats, then flags [world][heads] and per-head call counters [heads] (uint32, zero at allocation).
+// Call k of a head (counted on the device, so graph replays advance it) uses parity k & 1: a peer is
+// at most one call ahead, as in kvb_xchg_merge.  A wait that runs out raises KVB_DEV_TIMEOUT (site
+// 0x42) and merges what arrived; while the status word holds a timeout no exchange runs (site 0x43;
+// the head's output is not written) until the caller re-establishes the exchange.
+// ------------------------------------------------------------------------------------------
+__host__ __device__ inline int64_t dx_rows(const MergeArgs& p) { return int64_t(p.B) * p.Tq * p.Hq; }
+__host__ __device__ inline int64_t dx_slot(const MergeArgs& p) { return dx_rows(p) * (p.d + 1); }
+__host__ __device__ inline uint32_t* dx_flags(const MergeArgs& p, float* region) {
+    return reinterpret_cast<uint32_t*>(region + 2 * int64_t(p.xworld) * dx_slot(p));
+}
+
+// this rank's slot of head call `epoch` in its own region
+__device__ __forceinline__ float* dx_own_slot(const MergeArgs& p, uint32_t epoch) {
+    return p.xregion[p.xrank] + (int64_t(epoch & 1u) * p.xworld + p.xrank) * dx_slot(p);
+}
+
+// row index (in out's (B, Tq, Hq) order) of row r of head bh
+__device__ __forceinline__ int64_t dx_row(const MergeArgs& p, int bh, int r) {
+    const int b = bh / p.Hkv, h = bh % p.Hkv, i = r / p.Tq, t = r % p.Tq;
+    return (int64_t(b) * p.Tq + t) * p.Hq + h * p.rep + i;
+}
+
+__device__ __forceinline__ void xchg_publish(const MergeArgs& p, int bh, uint32_t epoch, int tid, int nthreads) {
+    const int d = p.d;
+    const int64_t rows = dx_rows(p), n = dx_slot(p);
+    const int64_t par = int64_t(epoch & 1u) * p.xworld * n;
+    const float* mine = p.xregion[p.xrank] + par + int64_t(p.xrank) * n;
+    for (int k = 1; k < p.xworld; ++k) {
+        const int peer = (p.xrank + k) % p.xworld;
+        float* dst = p.xregion[peer] + par + int64_t(p.xrank) * n;
+        for (int o = tid; o < p.R_act * (d + 1); o += nthreads) {
+            const int r = o / (d + 1), c = o % (d + 1);
+            const int64_t row = dx_row(p, bh, r);
+            const int64_t off = c < d ? row * d + c : rows * d + row;
+            dst[off] = mine[off];
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid < p.xworld) st_release_sys(dx_flags(p, p.xregion[tid]) + p.xrank * p.xheads + bh, epoch);
+}
+
+__device__ __forceinline__ void xchg_finish(const MergeArgs& p, int bh, uint32_t epoch, int tid, int nthreads) {
+    const int d = p.d;
+    const int64_t rows = dx_rows(p), n = dx_slot(p);
+    const int64_t par = int64_t(epoch & 1u) * p.xworld * n;
+    if (tid == 0) {
+        uint32_t* my_flags = dx_flags(p, p.xregion[p.xrank]);
+        const uint64_t t0 = global_timer_ns();
+        bool ok = true;
+        for (int r = 0; r < p.xworld && ok; ++r) {
+            for (uint32_t it = 0; int(ld_acquire_sys(my_flags + r * p.xheads + bh) - epoch) < 0; ++it) {
+                if ((it & 15u) == 15u && global_timer_ns() - t0 > p.xtimeout_ns) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        if (!ok) {
+            raise_status(KVB_DEV_TIMEOUT);
+            note_wait_timeout(0x42, epoch);
+        }
+        my_flags[p.xworld * p.xheads + bh] = epoch;
+    }
+    __syncthreads();
+    // merge the ranks' rows of the head (L1 bypassed: peers wrote these lines)
+    const float* g = p.xregion[p.xrank] + par;
+    for (int o = tid; o < p.R_act * d; o += nthreads) {
+        const int r = o / d, c = o % d;
+        const int64_t row = dx_row(p, bh, r);
+        float M = -INFINITY;
+        for (int k = 0; k < p.xworld; ++k) M = fmaxf(M, __ldcg(g + k * n + rows * d + row));
+        float acc = 0.f, ws = 0.f;
+        for (int k = 0; k < p.xworld; ++k) {
+            const float l = __ldcg(g + k * n + rows * d + row);
+            if (l == -INFINITY) continue;
+            const float w = __expf(l - M);
+            ws += w;
+            acc = fmaf(w, __ldcg(g + k * n + row * d + c), acc);
+        }
+        const float v = ws > 0.f ? acc / ws : 0.f;
+        const size_t oi = size_t(row) * d + c;
         if (p.out_dtype == 0) static_cast<float*>(p.out)[oi] = v;
         else if (p.out_dtype == 1) static_cast<__half*>(p.out)[oi] = __float2half_rn(v);
         else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(v);
     }
-    if (p.lse && c0 == 0 && tid < Ra) {
-        const int i = tid / p.Tq, t = tid % p.Tq;
-        const float L = s_rowL[tid];
-        p.lse[(size_t(b) * p.Tq + t) * p.Hq + h * p.rep + i] =
-            L > 0.f ? (s_rowM[tid] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
-    }
+    __syncthreads();
 }
 
 // The per-head piece ranges ride in the kernel parameters; two capacities keep the parameter block
@@ -687,7 +797,9 @@ __device__ __forceinline__ void build_channel_frags(uint8_t* km, const uint8_t* 
     }
 }
 
-template <int D, int R, int GK, int GV, int KMODE, int CODE>
+// XC: the sequence-split variant (kvb_decode_xchg), whose in-kernel merges exchange each head's part
+// with the other ranks; a separate instantiation, so plain calls carry none of its code.
+template <int D, int R, int GK, int GV, int KMODE, int CODE, bool XC = false>
 __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(const __grid_constant__ DecodeParams p) {
     using C = DecCfg<D, R, GK, GV, KMODE, CODE>;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -960,18 +1072,52 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CTAS_PER_SM) decode_main(cons
     // the heads this CTA completed: merge them (their partials are read through L2, after the fences
     // of the CTAs that wrote them)
     __syncthreads();
-    for (int i = 0; i < s_nmerge; ++i) {
-        const int head = s_merge[i];
-        const int pb = p.head_begin[head], pe = p.head_begin[head + 1];
-        float* sw = red + merge_smem_floats(p.merge.R_act, p.merge.d, p.merge.d_code, DEC_THREADS);
-        constexpr int PS = 2 * R + R * D;
-        if (p.merge.q_dtype == 0)
-            merge_head<float, float, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
-        else if (p.merge.q_dtype == 1)
-            merge_head<__half, __half, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
-        else
-            merge_head<__nv_bfloat16, __nv_bfloat16, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
-        __syncthreads();
+    if constexpr (!XC) {
+        for (int i = 0; i < s_nmerge; ++i) {
+            const int head = s_merge[i];
+            const int pb = p.head_begin[head], pe = p.head_begin[head + 1];
+            float* sw = red + merge_smem_floats(p.merge.R_act, p.merge.d, p.merge.d_code, DEC_THREADS);
+            constexpr int PS = 2 * R + R * D;
+            if (p.merge.q_dtype == 0)
+                merge_head<float, float, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+            else if (p.merge.q_dtype == 1)
+                merge_head<__half, __half, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+            else
+                merge_head<__nv_bfloat16, __nv_bfloat16, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS);
+            __syncthreads();
+        }
+    } else {
+        // sequence split: each head's part goes to this rank's own slot, then to every peer
+        // (xchg_publish); only after every head of this CTA is published does it wait (xchg_finish)
+        __shared__ uint32_t s_xepoch[DEC_MAX_CTA_MERGES];   // exchange call of each head (0: refused)
+        for (int i = 0; i < s_nmerge; ++i) {
+            const int head = s_merge[i];
+            const int pb = p.head_begin[head], pe = p.head_begin[head + 1];
+            float* sw = red + merge_smem_floats(p.merge.R_act, p.merge.d, p.merge.d_code, DEC_THREADS);
+            if (threadIdx.x == 0) {
+                uint32_t e = 0;
+                if (*reinterpret_cast<volatile unsigned*>(&g_status) & KVB_DEV_TIMEOUT) note_wait_timeout(0x43, head);
+                else e = dx_flags(p.merge, p.merge.xregion[p.merge.xrank])[p.merge.xworld * p.merge.xheads + head] + 1u;
+                s_xepoch[i] = e;
+            }
+            __syncthreads();
+            const uint32_t epoch = s_xepoch[i];
+            if (epoch == 0) continue;
+            float* xo = dx_own_slot(p.merge, epoch);
+            float* xl = xo + dx_rows(p.merge) * p.merge.d;
+            constexpr int PS = 2 * R + R * D;
+            if (p.merge.q_dtype == 0)
+                merge_head<float, float, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS, 0, -1, xo, xl);
+            else if (p.merge.q_dtype == 1)
+                merge_head<__half, __half, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS, 0, -1, xo, xl);
+            else
+                merge_head<__nv_bfloat16, __nv_bfloat16, PS>(p.merge, head, pb, pe, red, sw, threadIdx.x, DEC_THREADS,
+                                                            0, -1, xo, xl);
+            __syncthreads();
+            xchg_publish(p.merge, head, epoch, threadIdx.x, DEC_THREADS);
+        }
+        for (int i = 0; i < s_nmerge; ++i)
+            if (s_xepoch[i]) xchg_finish(p.merge, s_merge[i], s_xepoch[i], threadIdx.x, DEC_THREADS);
     }
 #endif
     // Every issued fill has been waited for above; if a wait gave up, give late copies a bounded

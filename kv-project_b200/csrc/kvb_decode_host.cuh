@@ -47,8 +47,9 @@ cudaError_t launch_maybe_pdl(void (*fn)(P), dim3 grid, dim3 block, size_t smem, 
     return cudaLaunchKernelEx(&cfg, fn, arg);
 }
 
-// decode_main<D, R, GK, GV, KM, CK> with the stage ring sized for the cache (kvb_decode_main_*.cu)
-template <int D, int R, int GK, int GV, int KM, int CK>
+// decode_main<D, R, GK, GV, KM, CK, XC> with the stage ring sized for the cache (kvb_decode_main_*.cu;
+// the sequence-split variants XC in kvb_decode_main_xchg.cu)
+template <int D, int R, int GK, int GV, int KM, int CK, bool XC>
 kvb_status run_main(const kvb_cache* c, const Plan& P, kvb::DecodeParams& p, cudaStream_t s, bool pdl);
 
 // decode_tc for a cache in the 128-token block value layout (kvb_decode_tc.cu)

@@ -22,7 +22,6 @@
 
 namespace kvb {
 
-constexpr int XC_MAX_RANKS = 8;
 constexpr int XC_SLICES = 64;            // grid size: one CTA per row slice, all co-resident
 
 struct XchgParams {
@@ -34,15 +33,6 @@ struct XchgParams {
     void* out;                           // (rows, d)
     uint64_t timeout_ns;
 };
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 __global__ void __launch_bounds__(256) xchg_merge_kernel(const __grid_constant__ XchgParams p) {
     const int slice = blockIdx.x, tid = threadIdx.x;

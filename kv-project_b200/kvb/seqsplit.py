@@ -7,9 +7,10 @@ StrataState.attend, STRATA_KV.py:1784-1792, across ranks instead of across strat
 
   SeqSplitDecoder     one exchange buffer per rank, a single all-gather (NCCL over NVLink on the
                       GPUs; any torch.distributed backend works), then ``kvb_lse_merge``;
-  P2PSeqSplitDecoder  ``kvb_xchg_merge``: one kernel stores this rank's rows straight into every
-                      peer's exchange region over NVLink (CUDA IPC mappings, plain peer stores),
-                      flags each row slice, waits for the other ranks' flags and merges.
+  P2PSeqSplitDecoder  peer memory (CUDA IPC mappings, plain peer stores over NVLink): by default ONE
+                      kernel per call (``kvb_decode_xchg``: each head's in-kernel merge publishes
+                      this rank's part to every peer, waits for theirs and merges); or
+                      ``kvb_decode_lse`` + ``kvb_xchg_merge`` (fused=False).
 
 Exact rows (sinks, appended tokens) belong to one rank, the owner of the last range.
 """
@@ -87,29 +88,30 @@ class SeqSplitDecoder:
 
 
 class P2PSeqSplitDecoder:
-    """Sequence-split decode whose cross-rank step runs over peer memory: per (B, Tq, Hq, d) shape
-    each rank allocates an exchange region in libkvb (zeroed), the 64-byte CUDA IPC handles are
-    all-gathered once over the process group, and every attend() is decode_lse + one
-    ``kvb_xchg_merge`` kernel.  All ranks must call attend() with the same shapes in the same order
-    (as they do for the collective version).  Ranks must share one node with peer access (NVLink /
-    NVSwitch); call close() before destroying the process group."""
+    """Sequence-split decode whose cross-rank step runs over peer memory.  Per shape each rank allocates
+    an exchange region in libkvb (zeroed) and the 64-byte CUDA IPC handles are all-gathered once over
+    the process group.  fused=True (default): every attend() is ONE ``kvb_decode_xchg`` kernel, whose
+    in-kernel head merges publish this rank's part to every peer, wait for theirs and merge; fused=False:
+    ``kvb_decode_lse`` + one ``kvb_xchg_merge`` kernel.  All ranks must use the same setting and call
+    attend() with the same shapes in the same order, each holding at least one token (as for the
+    collective version).  Ranks must share one node with peer access (NVLink / NVSwitch); call close()
+    before destroying the process group."""
 
-    def __init__(self, group=None, timeout_s: float = 2.0):
+    def __init__(self, group=None, timeout_s: float = 2.0, fused: bool = True):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.timeout_ns = int(timeout_s * 1e9)
+        self.fused = fused
         self._state = {}
 
-    def _setup(self, rows, d, device):
-        key = (rows, d, device)
+    def _setup(self, key, nbytes, rows, d, device):
         if key in self._state:
             return self._state[key]
         lib = L.lib()
         with torch.cuda.device(device):
-            nbytes = lib.kvb_xchg_bytes(rows, d, self.world)
             if nbytes == 0:
-                raise ValueError(f"P2PSeqSplitDecoder: unsupported world size {self.world}")
+                raise ValueError(f"P2PSeqSplitDecoder: unsupported shape or world size {self.world}")
             own = C.c_void_p()
             handle = (C.c_ubyte * 64)()
             L.check(lib.kvb_xchg_alloc(nbytes, C.byref(own), handle), "kvb_xchg_alloc")
@@ -126,39 +128,55 @@ class P2PSeqSplitDecoder:
                 L.check(lib.kvb_xchg_open(hb, C.byref(ptr)), "kvb_xchg_open")
                 regions[r] = ptr.value
                 opened.append(ptr.value)
-        part = torch.empty((rows, d), dtype=torch.float32, device=device)
-        lse = torch.empty((rows,), dtype=torch.float32, device=device)
-        self._state[key] = (own.value, opened, regions, part, lse)
+        part = lse = None
+        if not self.fused:
+            part = torch.empty((rows, d), dtype=torch.float32, device=device)
+            lse = torch.empty((rows,), dtype=torch.float32, device=device)
+        self._state[key] = (own.value, opened, regions, part, lse, nbytes, device)
         return self._state[key]
 
     def attend(self, cache: "ops.PackedCache", q: torch.Tensor, scaling: float, qpos=None, out=None,
                out_dtype=None) -> torch.Tensor:
         B, Hq, Tq, d = q.shape
         rows = B * Tq * Hq
-        _, _, regions, part, lse = self._setup(rows, d, q.device)
-        ops.decode_lse(cache, q, scaling, part.view(B, Tq, Hq, d), lse.view(B, Tq, Hq), qpos=qpos)
         odt = out_dtype or q.dtype
         if out is None:
             out = torch.empty((B, Tq, Hq, d), dtype=odt, device=q.device)
         elif tuple(out.shape) != (B, Tq, Hq, d) or not out.is_contiguous():
             raise ValueError("P2PSeqSplitDecoder: out must be contiguous (B, Tq, Hq, d)")
-        L.check(L.lib().kvb_xchg_merge(ops._ptr(part), ops._ptr(lse), rows, d, self.rank, self.world, regions,
-                                        ops._ptr(out), ops.dtype_code(out), self.timeout_ns,
-                                        C.c_void_p(ops._stream(q.device))),
-                "kvb_xchg_merge")
+        lib = L.lib()
+        if self.fused:
+            ops._cuda(q, out)
+            q = q.contiguous()
+            c = cache.struct()
+            nbytes = lib.kvb_decode_xchg_bytes(C.byref(c), Hq, Tq, self.world)
+            _, _, regions, _, _, _, _ = self._setup(("fused", B, Tq, Hq, cache.Hkv, d, q.device), nbytes, rows, d,
+                                                    q.device)
+            ws = cache.workspace(Hq, Tq)
+            qp = None if qpos is None else (C.c_int64 * Tq)(*[int(v) for v in qpos])
+            L.check(lib.kvb_decode_xchg(C.byref(c), ops._ptr(q), ops.dtype_code(q), Hq, Tq, C.c_float(scaling), qp,
+                                        ops._ptr(out), ops.dtype_code(out), self.rank, self.world, regions,
+                                        self.timeout_ns, 0, ops._ptr(ws), ws.numel(),
+                                        C.c_void_p(ops._stream(q.device))), "kvb_decode_xchg")
+            return out
+        nbytes = lib.kvb_xchg_bytes(rows, d, self.world)
+        _, _, regions, part, lse, _, _ = self._setup(("two-kernel", rows, d, q.device), nbytes, rows, d, q.device)
+        ops.decode_lse(cache, q, scaling, part.view(B, Tq, Hq, d), lse.view(B, Tq, Hq), qpos=qpos)
+        L.check(lib.kvb_xchg_merge(ops._ptr(part), ops._ptr(lse), rows, d, self.rank, self.world, regions,
+                                   ops._ptr(out), ops.dtype_code(out), self.timeout_ns,
+                                   C.c_void_p(ops._stream(q.device))), "kvb_xchg_merge")
         return out
 
     def reset(self):
         """Re-establish the exchange after a timed-out wait (KVB_DEV_TIMEOUT in the device status
-        word; kvb_xchg_merge does nothing until then): every rank clears its status word, the ranks
-        meet, every rank zeroes its whole region (flags and call counters restart at 0), and the ranks
-        meet again before the next attend().  Returns the status word that was cleared."""
+        word; no exchange runs until then): every rank clears its status word, the ranks meet, every
+        rank zeroes its whole region (flags and call counters restart at 0), and the ranks meet again
+        before the next attend().  Returns the status word that was cleared."""
         torch.cuda.synchronize()
         st = ops.device_status(clear=True)
         dist.barrier(group=self.group)
         lib = L.lib()
-        for (rows, d, device), (own, _, _, _, _) in self._state.items():
-            nbytes = lib.kvb_xchg_bytes(rows, d, self.world)
+        for own, _, _, _, _, nbytes, device in self._state.values():
             with torch.cuda.device(device):
                 torch.cuda.synchronize()
                 L.check(lib.kvb_xchg_zero(C.c_void_p(own), nbytes, C.c_void_p(ops._stream(device))),
@@ -172,11 +190,11 @@ class P2PSeqSplitDecoder:
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
         lib = L.lib()
-        for own, opened, _, _, _ in self._state.values():
+        for own, opened, _, _, _, _, _ in self._state.values():
             for ptr in opened:
                 L.check(lib.kvb_xchg_close(C.c_void_p(ptr)), "kvb_xchg_close")
         dist.barrier(group=self.group)
-        for own, _, _, _, _ in self._state.values():
+        for own, _, _, _, _, _, _ in self._state.values():
             L.check(lib.kvb_xchg_free(C.c_void_p(own)), "kvb_xchg_free")
         self._state.clear()
 

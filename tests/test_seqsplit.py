@@ -199,7 +199,7 @@ def _p2p_rank_main(rank, world, port, ret):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
-    p2p = None
+    decs = []
     try:
         B, Hkv, rep, Tq, T, d = 2, 2, 8, 1, 3000, 128
         K, V = kvb.workloads.outlier_kv(B, Hkv, T, d, torch.bfloat16, seed=17)
@@ -208,36 +208,40 @@ def _p2p_rank_main(rank, world, port, ret):
         build = lambda k, v: kvb.cache.build_kivi(k, v, 4, 4, 128, 128)
         cache = SS.shard_cache(build, K, V, rank, world)
         ref = SS.SeqSplitDecoder().attend(cache, q, d ** -0.5, out_dtype=torch.float32)
-        p2p = SS.P2PSeqSplitDecoder()
-        outs = [p2p.attend(cache, q, d ** -0.5, out_dtype=torch.float32) for _ in range(3)]
-        # inside a CUDA graph: the call count lives on the device, so replays keep exchanging
-        out_g = torch.empty_like(outs[0])
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            p2p.attend(cache, q, d ** -0.5, out=out_g)
-        torch.cuda.current_stream().wait_stream(s)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            p2p.attend(cache, q, d ** -0.5, out=out_g)
-        for _ in range(3):
-            out_g.zero_()
-            g.replay()
-        torch.cuda.synchronize()
         full = kvb.decode(build(K, V), q, d ** -0.5, out_dtype=torch.float32)
-        torch.cuda.synchronize()
-        ret[rank] = (all(torch.equal(o, ref) for o in outs), bool(torch.equal(out_g, ref)),
-                     float((outs[0] - full).abs().max()), kvb.device_status())
-        del g
+        res = {}
+        for fused in (True, False):
+            p2p = SS.P2PSeqSplitDecoder(fused=fused)
+            decs.append(p2p)
+            outs = [p2p.attend(cache, q, d ** -0.5, out_dtype=torch.float32) for _ in range(3)]
+            # inside a CUDA graph: the call count lives on the device, so replays keep exchanging
+            out_g = torch.empty_like(outs[0])
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                p2p.attend(cache, q, d ** -0.5, out=out_g)
+            torch.cuda.current_stream().wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                p2p.attend(cache, q, d ** -0.5, out=out_g)
+            for _ in range(3):
+                out_g.zero_()
+                g.replay()
+            torch.cuda.synchronize()
+            res[fused] = (all(torch.equal(o, ref) for o in outs), bool(torch.equal(out_g, ref)),
+                          float((outs[0] - full).abs().max()), kvb.device_status())
+            del g
+        ret[rank] = res
     finally:
-        if p2p is not None:
+        for p2p in decs:
             p2p.close()
         dist.destroy_process_group()
 
 
 @pytest.mark.gpu
 def test_seqsplit_p2p_two_ranks():
-    """The peer-memory exchange (kvb_xchg_merge) on 2 GPUs: bit-identical to the NCCL all-gather +
+    """The peer-memory exchange on 2 GPUs, fused into the decode kernel (kvb_decode_xchg) and as a
+    second kernel (kvb_decode_lse + kvb_xchg_merge): bit-identical to the NCCL all-gather +
     kvb_lse_merge path, repeatable (parity / epoch advance), correct under CUDA-graph replay, and equal
     to the one-GPU decode of the whole context."""
     if torch.cuda.device_count() < 2:
@@ -254,8 +258,10 @@ def test_seqsplit_p2p_two_ranks():
             p.join(300)
             assert p.exitcode == 0
         assert sorted(ret.keys()) == [0, 1]
-        for same, same_graph, err, status in ret.values():
-            assert same and same_graph and err <= 1e-4 and status == 0
+        for res in ret.values():
+            assert sorted(res.keys()) == [False, True]
+            for same, same_graph, err, status in res.values():
+                assert same and same_graph and err <= 1e-4 and status == 0
 
 
 @pytest.mark.gpu
@@ -307,6 +313,67 @@ def test_xchg_wait_times_out_and_refuses(cuda_dev):
         merge(1, one, 5_000_000)
         assert kvb.device_status() == 0
         assert torch.equal(out, part)                     # one part: the merge returns it unchanged
+    finally:
+        torch.cuda.synchronize()
+        for p in owned:
+            lib.kvb_xchg_free(p)
+        kvb.device_status(clear=True)
+        ops.device_diag(clear=True)
+
+
+@pytest.mark.gpu
+def test_fused_xchg_wait_times_out_and_refuses(cuda_dev):
+    """Failure detection of the exchange fused into the decode kernel (kvb_decode_xchg), on one GPU and
+    without any fault: world 2 with both regions on this GPU and a peer that never runs, so the
+    merging CTAs' bounded waits for the peer's flags run out (5 ms limit).  The kernel returns on its
+    own, the status word carries the timeout bit and the diagnostic word names the fused exchange wait
+    (site 0x42).  While the timeout stands, the next call writes no output (site 0x43); once the status
+    is cleared, plain decode calls run as before."""
+    import ctypes as C
+    import kvb
+    from kvb import _lib, ops
+    lib = _lib.lib()
+    kvb.device_status(clear=True)
+    ops.device_diag(clear=True)
+    B, Hkv, rep, T, d = 1, 2, 8, 1024, 128
+    K, V = kvb.workloads.outlier_kv(B, Hkv, T, d, torch.bfloat16, seed=19)
+    q = kvb.workloads.queries(B, Hkv * rep, 1, d, torch.bfloat16, seed=19).to(cuda_dev)
+    cache = kvb.cache.build_kivi(K.to(cuda_dev), V.to(cuda_dev), 4, 4, 128, 128)
+    c = cache.struct()
+    world = 2
+    nbytes = lib.kvb_decode_xchg_bytes(C.byref(c), Hkv * rep, 1, world)
+    assert nbytes > 0
+    regions = (C.c_void_p * world)()
+    owned = []
+    for r in range(world):
+        p, h = C.c_void_p(), (C.c_ubyte * 64)()
+        _lib.check(lib.kvb_xchg_alloc(nbytes, C.byref(p), h), "kvb_xchg_alloc")
+        regions[r] = p.value
+        owned.append(p)
+    out = torch.full((B, 1, Hkv * rep, d), 7.0, device=cuda_dev)
+    ws = cache.workspace(Hkv * rep, 1)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def call():
+        _lib.check(lib.kvb_decode_xchg(C.byref(c), C.c_void_p(q.data_ptr()), ops.dtype_code(q), Hkv * rep, 1,
+                                       C.c_float(d ** -0.5), None, C.c_void_p(out.data_ptr()), _lib.KVB_F32, 0,
+                                       world, regions, 5_000_000, 0, C.c_void_p(ws.data_ptr()), ws.numel(),
+                                       stream), "kvb_decode_xchg")
+        torch.cuda.synchronize()
+
+    try:
+        call()                                            # the peer's flags never arrive
+        assert kvb.device_status(clear=False) & 1         # KVB_DEV_TIMEOUT, read without clearing
+        diag = ops.device_diag(clear=True)
+        assert diag & 0x80000000 and (diag & 0xFF) == 0x42
+        out.fill_(7.0)
+        call()                                            # refused while the timeout stands
+        assert torch.all(out == 7.0)
+        assert (ops.device_diag(clear=True) & 0xFF) == 0x43
+        assert kvb.device_status(clear=True) & 1
+        ref = kvb.decode(cache, q, d ** -0.5, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        assert kvb.device_status() == 0 and torch.isfinite(ref).all()
     finally:
         torch.cuda.synchronize()
         for p in owned:
