@@ -21,6 +21,7 @@ from .codecs import (FP16_MAX, as_stored, kivi_quant, kivi_dequant, uniform_step
 from .attention import chunked_attention, strata_attend, tier_reference, lse_merge
 from .select import snapkv_scores, query_scores, topk_kept, l2_importance, mixed_strata, strata_counts
 from .spectral import seeded_qr_basis, rotation_matrix, spectral_encode, spectral_attend
+from .alloc import head_sync_allocate
 
 __all__ = [
     "FP16_MAX", "as_stored", "kivi_quant", "kivi_dequant", "uniform_step", "strata_quantize",
@@ -28,4 +29,5 @@ __all__ = [
     "chunked_attention", "strata_attend", "tier_reference", "lse_merge",
     "snapkv_scores", "query_scores", "topk_kept", "l2_importance", "mixed_strata", "strata_counts",
     "seeded_qr_basis", "rotation_matrix", "spectral_encode", "spectral_attend",
+    "head_sync_allocate",
 ]

@@ -340,11 +340,51 @@ def midrise128():
     print("wrote midrise128.npz", (HERE / "midrise128.npz").stat().st_size)
 
 
+def alloc():
+    """STRATA's head-synchronous rate allocation: the reference's head_sync_allocate
+    (STRATA_KV.py:1308-1351, CPU) on seeded distortion tables shaped like compress_layer's
+    (:1562-1575: columns drop | 2 / 4 / 8 bits | exact, costs in bits summed over 8 KV heads, fixed bits
+    of the basis and histogram), at several budgets, in alloc.npz (its own generator)."""
+    S, _ = load_reference()
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(97531)
+    out = {}
+    cases = [("a", 600, (2, 4, 8), 0.30), ("b", 600, (2, 4, 8), 0.0005), ("c", 600, (2, 4, 8), 2.0),
+             ("d", 400, (), 0.25), ("e", 3000, (2, 4), 0.15), ("f", 1000, (2, 4, 8), 0.08)]
+    Hkv, d = 8, 128
+    for name, n, bits, keep in cases:
+        nb = len(bits)
+        imp = torch.sort(torch.exp(1.5 * torch.randn(n, generator=g)), descending=True).values
+        cols = [imp * (2.0 + torch.rand(n, generator=g))]                          # drop
+        for b in bits:
+            cols.append(imp * 4.0 ** (-b) * (0.5 + torch.rand(n, generator=g)))    # coded at b bits
+        cols.append(torch.zeros(n))                                                # exact
+        D = torch.stack(cols, 1).float()
+        cost_tok = [0.0] + [2.0 * (b * d + 16) for b in bits] + [2.0 * d * 16]
+        hist_bits = (nb + 2) * 32.0
+        fixed = [hist_bits + (Hkv * 2 * d * 16.0 if i > 0 else 0.0) for i in range(nb + 1)]
+        cost = torch.tensor(cost_tok, dtype=torch.float32) * Hkv
+        fixed = torch.tensor(fixed, dtype=torch.float32)
+        budget = keep * n * Hkv * 2 * d * 16.0
+        r = S.head_sync_allocate(D, cost, fixed, budget)
+        out[f"{name}_D"], out[f"{name}_cost"], out[f"{name}_fixed"] = np32(D), np32(cost), np32(fixed)
+        out[f"{name}_budget"] = np.array(budget, np.float64)
+        out[f"{name}_choice"] = r["choice"].numpy()
+        out[f"{name}_cap"] = np.array(int(r["cap"]))
+        out[f"{name}_bits"] = np.array(float(r["bits"]), np.float64)
+    out["linspace32"] = torch.linspace(0.0, 1.0, 32).numpy()
+    np.savez_compressed(HERE / "alloc.npz", **out)
+    print("wrote alloc.npz", (HERE / "alloc.npz").stat().st_size)
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["rowcodes"]:
         rowcodes()
     elif sys.argv[1:] == ["snapkv128"]:
         snapkv128()
+    elif sys.argv[1:] == ["alloc"]:
+        alloc()
     elif sys.argv[1:] == ["midrise128"]:
         midrise128()
     else:
