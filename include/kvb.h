@@ -358,6 +358,22 @@ kvb_status kvb_lse_merge(const float* parts, int64_t part_stride, const float* l
 kvb_status kvb_decode_noalloc(const kvb_cache* c, const void* q, int q_dtype, int Hq, int Tq, float scaling,
                               const int64_t* qpos, void* out, int out_dtype, int n_ctas, void* stream);
 
+/* STRATA's head-synchronous rate allocation (head_sync_allocate, STRATA_KV.py:1308-1351) on the device.
+ * Dsort (n, nlev) float32 row-major, device: the distortion (summed over KV heads) of giving rank
+ * position j option l, columns drop | coded level 1 .. nlev - 2 | exact; cost (nlev) and fixed
+ * (nlev - 1) host arrays: bits of option l over the heads, and the layer's fixed bits when the deepest
+ * coded level used is c (0: none).  Minimises sum_j Dsort[j, l_j] subject to sum_j cost[l_j] +
+ * fixed[c] <= budget by Lagrangian relaxation: `rounds` rounds (4 in the reference) of `grid` (32)
+ * multipliers on a log scale over [e^-80, e^25], then the allocation at the smallest feasible one.
+ * Outputs (device): choice (n) int32, cap (1) int32, bits (1) float64.  workspace: device buffer of
+ * kvb_head_sync_allocate_workspace() bytes, 16-byte aligned (its round counter is reset by every
+ * call).  No host synchronisation: rounds are launched back to back.  Choices equal the reference's
+ * except where two layer totals agree to float32 rounding (totals are summed in float64 here). */
+size_t kvb_head_sync_allocate_workspace(void);
+kvb_status kvb_head_sync_allocate(const float* Dsort, int64_t n, int nlev, const float* cost, const float* fixed,
+                                  double budget, int rounds, int grid, int32_t* choice, int32_t* cap, double* bits,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* Build the split-K plan (pure host computation, no CUDA calls) for n_ctas CTAs.  plan_out receives
  * [n_ctas, n_pieces, n_heads, cta_begin[n_ctas + 1], n_pieces x (head, stratum, first chunk, end
  * chunk, slot), head_begin[n_heads + 1]]: pieces in CTA order, each with the slot of its partial;

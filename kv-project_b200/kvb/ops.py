@@ -647,3 +647,37 @@ def spectral_encode(x: torch.Tensor, basis_hilo: torch.Tensor, bits: int = 4, wa
                                         C.c_void_p(_stream(x.device))), "kvb_spectral_encode")
     return {"codes": codes, "meta": scales, "n": T, "n_alloc": n_alloc, "bits": bits, "group": SPECTRAL_R,
             "coef": coef}
+
+
+# ------------------------------------------------------------------------------------------------
+# STRATA rate allocation (head_sync_allocate, STRATA_KV.py:1308-1351)
+# ------------------------------------------------------------------------------------------------
+def head_sync_allocate(Dsort: torch.Tensor, cost, fixed, budget: float, rounds: int = 4, grid: int = 32):
+    """Device allocation of rank positions to options (drop | coded levels | exact) under a bit budget.
+    Dsort (n, nlev) float32 CUDA; cost (nlev) and fixed (nlev - 1) sequences of floats.  Returns
+    {"choice": (n,) int32, "cap": () int32, "bits": () float64} on Dsort's device (no synchronisation)."""
+    _cuda(Dsort)
+    if Dsort.dtype != torch.float32 or Dsort.dim() != 2:
+        raise ValueError("head_sync_allocate: Dsort (n, nlev) float32")
+    Dsort = Dsort.contiguous()
+    n, nlev = Dsort.shape
+    cost = [float(x) for x in cost]
+    fixed = [float(x) for x in fixed]
+    if len(cost) != nlev or len(fixed) != nlev - 1:
+        raise ValueError("head_sync_allocate: cost has nlev entries, fixed nlev - 1")
+    lib = L.lib()
+    dev = Dsort.device
+    key = ("alloc_ws", dev)
+    ws = _ALLOC_WS.get(key)
+    if ws is None:
+        ws = _ALLOC_WS[key] = torch.zeros(lib.kvb_head_sync_allocate_workspace(), dtype=torch.uint8, device=dev)
+    choice = torch.empty(n, dtype=torch.int32, device=dev)
+    cap = torch.empty((), dtype=torch.int32, device=dev)
+    bits = torch.empty((), dtype=torch.float64, device=dev)
+    L.check(lib.kvb_head_sync_allocate(_ptr(Dsort), n, nlev, (C.c_float * nlev)(*cost), (C.c_float * (nlev - 1))(*fixed),
+                                       C.c_double(budget), rounds, grid, _ptr(choice), _ptr(cap), _ptr(bits), _ptr(ws),
+                                       ws.numel(), C.c_void_p(_stream(dev))), "kvb_head_sync_allocate")
+    return {"choice": choice, "cap": cap, "bits": bits}
+
+
+_ALLOC_WS = {}
