@@ -28,12 +28,6 @@
 
 #define KVB_VERSION 102
 
-// The device status words (declared in kvb_common.cuh), one per device, shared by every kernel of the
-// library through the device link.
-namespace kvb {
-__device__ unsigned g_status;
-__device__ unsigned g_diag;
-}  // namespace kvb
 
 namespace {
 thread_local std::string g_last_error;
@@ -200,41 +194,31 @@ extern "C" {
 const char* kvb_last_error(void) { return g_last_error.c_str(); }
 int kvb_version(void) { return KVB_VERSION; }
 
-kvb_status kvb_device_status(unsigned* out, int clear, void* stream) {
+// Read (and optionally clear) the status or the diagnostic words of every .cu file of the library;
+// the status words are OR-ed, the first non-zero diagnostic word is reported.
+static kvb_status read_words(bool diag, unsigned* out, int clear, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    unsigned v = 0;
-    kvb_status st = cuda_check(cudaMemcpyFromSymbolAsync(&v, kvb::g_status, sizeof(v), 0, cudaMemcpyDeviceToHost, s),
-                               "read status");
-    if (st) return st;
+    int n = 0;
+    const kvbh::StatusWordsFn* fns = kvbh::status_word_files(&n);
+    unsigned v[16] = {};
+    kvb_status st;
+    for (int i = 0; i < n; ++i)
+        if ((st = fns[i](diag ? nullptr : &v[i], diag ? &v[i] : nullptr, 0, 0, s))) return st;
     if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
-    if (out) *out = v;
+    unsigned r = 0;
+    for (int i = 0; i < n; ++i) r = diag ? (r ? r : v[i]) : (r | v[i]);
+    if (out) *out = r;
     if (clear) {
-        const unsigned z = 0;
-        if ((st = cuda_check(cudaMemcpyToSymbolAsync(kvb::g_status, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s),
-                             "clear status")))
-            return st;
+        for (int i = 0; i < n; ++i)
+            if ((st = fns[i](nullptr, nullptr, diag ? 0 : 1, diag ? 1 : 0, s))) return st;
         if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
     }
     return KVB_OK;
 }
 
-kvb_status kvb_device_diag(unsigned* out, int clear, void* stream) {
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    unsigned v = 0;
-    kvb_status st = cuda_check(cudaMemcpyFromSymbolAsync(&v, kvb::g_diag, sizeof(v), 0, cudaMemcpyDeviceToHost, s),
-                               "read diag");
-    if (st) return st;
-    if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
-    if (out) *out = v;
-    if (clear) {
-        const unsigned z = 0;
-        if ((st = cuda_check(cudaMemcpyToSymbolAsync(kvb::g_diag, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s),
-                             "clear diag")))
-            return st;
-        if ((st = cuda_check(cudaStreamSynchronize(s), "synchronise"))) return st;
-    }
-    return KVB_OK;
-}
+kvb_status kvb_device_status(unsigned* out, int clear, void* stream) { return read_words(false, out, clear, stream); }
+
+kvb_status kvb_device_diag(unsigned* out, int clear, void* stream) { return read_words(true, out, clear, stream); }
 
 // =============================================================================================
 // K1
@@ -689,3 +673,5 @@ kvb_status kvb_chunk_select(const void* k, int k_dtype, int64_t U, int64_t H, in
 }
 
 }  // extern "C"
+
+KVB_STATUS_WORDS(status_words_api)

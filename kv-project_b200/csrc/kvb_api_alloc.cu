@@ -58,3 +58,5 @@ kvb_status kvb_head_sync_allocate(const float* Dsort, int64_t n, int nlev, const
 }
 
 }  // extern "C"
+
+KVB_STATUS_WORDS(status_words_alloc)

@@ -702,3 +702,5 @@ extern "C" kvb_status kvb_decode_noalloc(const kvb_cache* c, const void* q, int 
     return kvb_decode_events(c, q, q_dtype, Hq, Tq, scaling, qpos, out, out_dtype, n_ctas, scratch,
                              size_t(KVB_NOALLOC_SCRATCH_BYTES), stream, nullptr, nullptr);
 }
+
+KVB_STATUS_WORDS(status_words_decode)

@@ -86,3 +86,5 @@ extern "C" kvb_status kvb_spectral_encode(const void* x, int64_t B, int64_t H, i
 
 // =============================================================================================
 // K3 host side: validation, plan, dispatch
+
+KVB_STATUS_WORDS(status_words_spectral)

@@ -20,15 +20,17 @@
 
 namespace kvb {
 
-// One status word per device and library instance; read (and cleared) by kvb_device_status().
-// Defined once in kvb_api.cu; every translation unit's kernels reach it through the device link.
-extern __device__ unsigned g_status;
+// The device status word.  Every .cu file of the library is its own device module (built without
+// relocatable device code, which costs the kernels registers), so each holds its own copy of this word
+// and of g_diag; kvb_device_status / kvb_device_diag read (and clear) all copies together
+// (KVB_STATUS_WORDS in kvb_host.h).
+static __device__ unsigned g_status;
 
 __device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status, bits); }
 
 // Where the first bounded wait gave up: site code (bits 0-7), CTA (bits 8-15), a counter of the
 // waiting role (bits 16-30), bit 31 set.  Read with kvb_device_diag(); 0 when nothing timed out.
-extern __device__ unsigned g_diag;
+static __device__ unsigned g_diag;
 __device__ __forceinline__ void note_wait_timeout(unsigned site, unsigned counter) {
     atomicCAS(&g_diag, 0u, 0x80000000u | (site & 0xFFu) | ((blockIdx.x & 0xFFu) << 8) | ((counter & 0x7FFFu) << 16));
 }

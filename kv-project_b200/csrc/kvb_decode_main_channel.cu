@@ -6,3 +6,5 @@ KVB_INSTANTIATE_MAIN(128, 4, 1, 2, kvb::KM_CHANNEL, kvb::KV_ASYM)
 KVB_INSTANTIATE_MAIN(128, 4, 1, 1, kvb::KM_CHANNEL, kvb::KV_ASYM)
 KVB_INSTANTIATE_MAIN(128, 8, 1, 1, kvb::KM_CHANNEL, kvb::KV_ASYM)
 KVB_INSTANTIATE_MAIN(128, 8, 1, 2, kvb::KM_CHANNEL, kvb::KV_ASYM)
+
+KVB_STATUS_WORDS(status_words_main_channel)

@@ -6,3 +6,5 @@ KVB_INSTANTIATE_MAIN(128, 8, 1, 1, kvb::KM_TOKEN, kvb::KV_MIDRISE)
 KVB_INSTANTIATE_MAIN(64, 4, 1, 1, kvb::KM_TOKEN, kvb::KV_MIDRISE)
 KVB_INSTANTIATE_MAIN(32, 4, 1, 1, kvb::KM_TOKEN, kvb::KV_MIDRISE)
 KVB_INSTANTIATE_MAIN(32, 8, 1, 1, kvb::KM_TOKEN, kvb::KV_MIDRISE)
+
+KVB_STATUS_WORDS(status_words_main_midrise)

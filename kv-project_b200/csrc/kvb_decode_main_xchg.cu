@@ -8,3 +8,5 @@ KVB_INSTANTIATE_MAIN_XC(128, 4, 2, 2, kvb::KM_TOKEN, kvb::KV_ASYM)
 KVB_INSTANTIATE_MAIN_XC(128, 8, 2, 2, kvb::KM_TOKEN, kvb::KV_ASYM)
 KVB_INSTANTIATE_MAIN_XC(128, 4, 1, 1, kvb::KM_TOKEN, kvb::KV_ASYM)
 KVB_INSTANTIATE_MAIN_XC(128, 8, 1, 1, kvb::KM_TOKEN, kvb::KV_ASYM)
+
+KVB_STATUS_WORDS(status_words_main_xchg)

@@ -77,3 +77,5 @@ kvb_status dispatch_tc(const DecodeShape& sh, const kvb_cache* c, const Plan& P,
 }
 
 }  // namespace kvbd
+
+KVB_STATUS_WORDS(status_words_decode_tc)
