@@ -378,6 +378,49 @@ def alloc():
     print("wrote alloc.npz", (HERE / "alloc.npz").stat().st_size)
 
 
+def quasar():
+    """QUASAR's coded decode over embedded stage codes: the reference's QuasarState.coded_scores and
+    coded_values (QUASAR_KV.py:1918-1940, the eager path that its Triton kernels are checked
+    against) on seeded step tables with stages (2, 2, 4), in quasar.npz (its own generator).  Each
+    step owns a token prefix and a band of coefficients at one stage; its codes are MSB-first packed
+    rows (pack_rows, QUASAR_KV.py:1185)."""
+    _, Q = load_reference()
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(24680)
+    out = {}
+    stages = (2, 2, 4)
+    for name, (Hkv, rows, n_c, R) in {"a": (2, 4, 300, 64), "b": (3, 8, 600, 128)}.items():
+        bands = [(0, R // 4), (R // 4, R // 2), (R // 2, R)]
+        steps = []
+        for side in (0, 1):
+            for bi, (a, b) in enumerate(bands):
+                for t in range(len(stages)):
+                    if t > 2 - bi:                       # later bands keep fewer stages
+                        continue
+                    n = max(1, int(n_c * (1.0 - 0.25 * (bi + t))))
+                    codes = torch.randint(0, 2 ** stages[t], (Hkv, n, b - a), generator=g)
+                    steps.append({"side": side, "stage": t, "a": a, "b": b, "n": n,
+                                  "codes": Q.pack_rows(codes, stages[t])})
+        Ke = torch.zeros(1, Hkv, 1, 16)
+        packed = {"n_c": n_c, "steps": steps, "T_v": torch.zeros(Hkv, 16, R)}
+        st = Q.QuasarState(Ke, Ke.clone(), packed, stages, 0, 1)
+        qt = torch.randn(1, Hkv, rows, R, generator=g)
+        pv = torch.softmax(torch.randn(1, Hkv, rows, n_c, generator=g), -1)
+        sc = st.coded_scores(qt)
+        va = st.coded_values(pv)
+        for s in (0, 1):
+            side = st.sides[s]
+            out[f"{name}_flat{s}"] = side["flat"].numpy()
+            out[f"{name}_table{s}"] = side["table"].numpy()
+        out[f"{name}_levels"] = np32(st.sides[0]["levels"])
+        out[f"{name}_shape"] = np.array([Hkv, rows, n_c, R])
+        out[f"{name}_qt"], out[f"{name}_pv"] = np32(qt[0]), np32(pv[0])
+        out[f"{name}_scores"], out[f"{name}_values"] = np32(sc[0]), np32(va[0])
+    np.savez_compressed(HERE / "quasar.npz", **out)
+    print("wrote quasar.npz", (HERE / "quasar.npz").stat().st_size)
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["rowcodes"]:
         rowcodes()
@@ -385,6 +428,8 @@ if __name__ == "__main__":
         snapkv128()
     elif sys.argv[1:] == ["alloc"]:
         alloc()
+    elif sys.argv[1:] == ["quasar"]:
+        quasar()
     elif sys.argv[1:] == ["midrise128"]:
         midrise128()
     else:
