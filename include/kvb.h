@@ -374,6 +374,23 @@ kvb_status kvb_head_sync_allocate(const float* Dsort, int64_t n, int nlev, const
                                   double budget, int rounds, int grid, int32_t* choice, int32_t* cap, double* bits,
                                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* QUASAR's coded decode over embedded stage codes: the sums of QuasarState.coded_scores / coded_values
+ * (QUASAR_KV.py:1918-1940; its Triton kernels :1498-1556 compute the same).  flat (flat_bytes, device):
+ * every step's (Hkv, n_s, bytes) block of MSB-first packed codes; table (n_steps x 7 int32, HOST):
+ * offset, n_s, bytes per row, band start a, band width w, bits b, level offset; levels (n_levels
+ * float32, HOST): the stage level tables, concatenated.  Step s owns tokens [0, n_s) and coefficients
+ * [a, a + w).  scores (Hkv, rows, n_c) = sum over owning steps of qt[band] . level[codes], from qt
+ * (Hkv, rows, R); values (Hkv, rows, R) = sum_j pv[j] level[codes] per band, from pv (Hkv, rows, n_c),
+ * without atomics (token splits added in a fixed order; workspace of kvb_quasar_values_workspace
+ * bytes).  rows <= 32, R <= 256, n_steps <= 32, n_levels <= 64; float32 device tensors, dense. */
+kvb_status kvb_quasar_scores(const float* qt, int Hkv, int rows, int R, const uint8_t* flat, size_t flat_bytes,
+                             const int32_t* table, int n_steps, const float* levels, int n_levels, int64_t n_c,
+                             float* scores, void* stream);
+size_t kvb_quasar_values_workspace(int Hkv, int rows, int64_t n_c, int R);
+kvb_status kvb_quasar_values(const float* pv, int Hkv, int rows, int64_t n_c, const uint8_t* flat, size_t flat_bytes,
+                             const int32_t* table, int n_steps, const float* levels, int n_levels, int R,
+                             float* values, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Build the split-K plan (pure host computation, no CUDA calls) for n_ctas CTAs.  plan_out receives
  * [n_ctas, n_pieces, n_heads, cta_begin[n_ctas + 1], n_pieces x (head, stratum, first chunk, end
  * chunk, slot), head_begin[n_heads + 1]]: pieces in CTA order, each with the slot of its partial;

@@ -75,6 +75,9 @@ SIGNATURES = {
     "kvb_xchg_merge": (_i32, [_p, _p, _i64, _i32, _i32, _i32, C.POINTER(C.c_void_p), _p, _i32, C.c_uint64, _p]),
     "kvb_decode_workspace_size": (C.c_size_t, [C.POINTER(Cache), _i32, _i32, _i32]),
     "kvb_head_sync_allocate_workspace": (C.c_size_t, []),
+    "kvb_quasar_scores": (_i32, [_p, _i32, _i32, _i32, _p, C.c_size_t, _p, _i32, _p, _i32, _i64, _p, _p]),
+    "kvb_quasar_values_workspace": (C.c_size_t, [_i32, _i32, _i64, _i32]),
+    "kvb_quasar_values": (_i32, [_p, _i32, _i32, _i64, _p, C.c_size_t, _p, _i32, _p, _i32, _i32, _p, _p, C.c_size_t, _p]),
     "kvb_head_sync_allocate": (_i32, [_p, _i64, _i32, C.POINTER(C.c_float), C.POINTER(C.c_float), C.c_double, _i32,
                                       _i32, _p, _p, _p, _p, C.c_size_t, _p]),
     "kvb_decode_xchg_bytes": (C.c_size_t, [C.POINTER(Cache), _i32, _i32, _i32]),

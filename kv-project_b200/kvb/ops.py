@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import numpy as np
 
 import torch
 
@@ -681,3 +682,41 @@ def head_sync_allocate(Dsort: torch.Tensor, cost, fixed, budget: float, rounds: 
 
 
 _ALLOC_WS = {}
+
+
+# ------------------------------------------------------------------------------------------------
+# QUASAR coded decode over embedded stage codes (coded_scores / coded_values, QUASAR_KV.py:1918-1940)
+# ------------------------------------------------------------------------------------------------
+def _quasar_tables(table, levels):
+    t = np.ascontiguousarray(np.asarray(table, np.int32).reshape(-1, 7))
+    lv = np.ascontiguousarray(np.asarray(levels, np.float32).reshape(-1))
+    return t, lv
+
+
+def quasar_scores(qt: torch.Tensor, flat: torch.Tensor, table, levels, n_c: int) -> torch.Tensor:
+    """qt (Hkv, rows, R) float32 CUDA, flat uint8 CUDA, table (n_steps, 7) and levels on the host ->
+    scores (Hkv, rows, n_c) float32."""
+    _cuda(qt, flat)
+    qt = qt.float().contiguous()
+    Hkv, rows, R = qt.shape
+    t, lv = _quasar_tables(table, levels)
+    out = torch.empty((Hkv, rows, n_c), dtype=torch.float32, device=qt.device)
+    L.check(L.lib().kvb_quasar_scores(_ptr(qt), Hkv, rows, R, _ptr(flat), flat.numel(), t.ctypes.data, len(t),
+                                      lv.ctypes.data, len(lv), n_c, _ptr(out), C.c_void_p(_stream(qt.device))),
+            "kvb_quasar_scores")
+    return out
+
+
+def quasar_values(pv: torch.Tensor, flat: torch.Tensor, table, levels, R: int) -> torch.Tensor:
+    """pv (Hkv, rows, n_c) float32 CUDA -> values (Hkv, rows, R) float32."""
+    _cuda(pv, flat)
+    pv = pv.float().contiguous()
+    Hkv, rows, n_c = pv.shape
+    t, lv = _quasar_tables(table, levels)
+    lib = L.lib()
+    ws = torch.empty(max(16, lib.kvb_quasar_values_workspace(Hkv, rows, n_c, R)), dtype=torch.uint8, device=pv.device)
+    out = torch.empty((Hkv, rows, R), dtype=torch.float32, device=pv.device)
+    L.check(lib.kvb_quasar_values(_ptr(pv), Hkv, rows, n_c, _ptr(flat), flat.numel(), t.ctypes.data, len(t),
+                                  lv.ctypes.data, len(lv), R, _ptr(out), _ptr(ws), ws.numel(),
+                                  C.c_void_p(_stream(pv.device))), "kvb_quasar_values")
+    return out
