@@ -58,7 +58,7 @@ COMPRESS = ("c1-pack", "c2-evict", "c3-project")
 # DRAM bytes (read + write) of one decode_main launch from an ncu capture of this bench's workload
 # (profiles/decode_main_config1.md), with the hash of the decode sources the capture ran on: the
 # figure is reported only while those sources are unchanged (else roofline.traffic is null).
-TRAFFIC = {"c1": (253.80e6, "d81f25ab756ed052")}
+TRAFFIC = {"c1": (253.19e6, "9482263baa11c21b")}
 TRAFFIC_SOURCES = ("kvb_common.cuh", "kvb_decode.cuh", "kvb_decode_tile.cuh", "kvb_decode_inst.cuh")
 
 
