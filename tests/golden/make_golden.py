@@ -421,6 +421,48 @@ def quasar():
     print("wrote quasar.npz", (HERE / "quasar.npz").stat().st_size)
 
 
+def atoms():
+    """TILT's moment-atom read: the reference's atom_read (TILT_KV.py:673-714) on one set of seeded
+    atoms (key means and log-masses, rank-r covariance factors U / lam / diag, ball radii, value tilt
+    factors A / Bk, one disabled atom with log-mass -inf) under every combination of order, tilt,
+    projection and the phase correction, in atoms.npz (its own generator)."""
+    load_reference()
+    import TILT_KV as T              # noqa: E402  (reference module, read-only)
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(11235)
+    out = {}
+    B, H, rep, c, NA, d, r = 2, 2, 4, 5, 3, 128, 4
+    base = {
+        "mu_k": 0.3 * torch.randn(B, H, NA, d, generator=g),
+        "logn": torch.log(torch.randint(8, 400, (B, H, NA), generator=g).float()),
+        "U": torch.randn(B, H, NA, d, r, generator=g) / d ** 0.5,
+        "lam": 3.0 * torch.rand(B, H, NA, r, generator=g),
+        "diag": 0.05 * torch.rand(B, H, NA, d, generator=g),
+        "R": 2.0 + 3.0 * torch.rand(B, H, NA, generator=g),
+        "A": torch.randn(B, H, NA, d, r, generator=g) / d ** 0.5,
+        "Bk": torch.randn(B, H, NA, d, r, generator=g) / d ** 0.5,
+        "Rv": 0.2 + torch.rand(B, H, NA, generator=g),
+    }
+    base["logn"][0, 1, 2] = float("-inf")                          # a disabled atom
+    for k, v in base.items():
+        out[k] = np32(v)
+    qs = torch.randn(B, H * rep, c, d, generator=g) * (0.5 + 2.0 * torch.rand(1, 1, c, 1, generator=g))
+    out["qs"] = np32(qs)
+    cases = {"a": (2, True, True, True), "b": (2, False, False, False), "c": (2, True, False, True),
+             "d": (1, True, True, True), "e": (2, False, True, False)}
+    for name, (order, tilt, project, phase) in cases.items():
+        mom = dict(base)
+        mom.update({"order": order, "tilt": tilt, "project": project, "phase": phase})
+        logit, cfac, tB = T.atom_read(qs, mom, rep)
+        out[f"{name}_flags"] = np.array([order, int(tilt), int(project), int(phase), rep])
+        out[f"{name}_logit"], out[f"{name}_cfac"] = np32(logit), np32(cfac)
+        if tB is not None:
+            out[f"{name}_tB"] = np32(tB)
+    np.savez_compressed(HERE / "atoms.npz", **out)
+    print("wrote atoms.npz", (HERE / "atoms.npz").stat().st_size)
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["rowcodes"]:
         rowcodes()
@@ -430,6 +472,8 @@ if __name__ == "__main__":
         alloc()
     elif sys.argv[1:] == ["quasar"]:
         quasar()
+    elif sys.argv[1:] == ["atoms"]:
+        atoms()
     elif sys.argv[1:] == ["midrise128"]:
         midrise128()
     else:
