@@ -391,6 +391,30 @@ kvb_status kvb_quasar_values(const float* pv, int Hkv, int rows, int64_t n_c, co
                              const int32_t* table, int n_steps, const float* levels, int n_levels, int R,
                              float* values, void* workspace, size_t workspace_bytes, void* stream);
 
+/* TILT's moment atoms of a chunk's bulk (moment_atoms, TILT_KV.py:622-670, built by the caller), float32
+ * device tensors, dense: mu_k (B, Hkv, NA, d), logn (B, Hkv, NA), U (B, Hkv, NA, d, r), lam (B, Hkv, NA, r),
+ * diag (B, Hkv, NA, d), R (B, Hkv, NA), A (B, Hkv, NA, d, r), Bk (B, Hkv, NA, d, r), Rv (B, Hkv, NA);
+ * the tensors the flags do not use may be null. */
+typedef struct kvb_atoms {
+    const float* mu_k;
+    const float* logn;
+    const float* U;
+    const float* lam;
+    const float* diag;
+    const float* R;
+    const float* A;
+    const float* Bk;
+    const float* Rv;
+    int B, Hkv, NA, d, r;     /* d <= 256, 1 <= r <= 8 */
+    int order, tilt, project, phase;
+} kvb_atoms;
+
+/* atom_read (TILT_KV.py:673-714): for scaled queries qs (B, Hq, c, d) float32, the logit and value
+ * factor of every (query, atom) pair, logit / cfac (B, Hq, c, NA), and with tilt the coordinates tB
+ * (B, Hq, c, NA, r); KV head h serves query heads h * rep .. (HF repeat_kv order). */
+kvb_status kvb_atom_read(const kvb_atoms* m, const float* qs, int Hq, int c, float* logit, float* cfac, float* tB,
+                         void* stream);
+
 /* Build the split-K plan (pure host computation, no CUDA calls) for n_ctas CTAs.  plan_out receives
  * [n_ctas, n_pieces, n_heads, cta_begin[n_ctas + 1], n_pieces x (head, stratum, first chunk, end
  * chunk, slot), head_begin[n_heads + 1]]: pieces in CTA order, each with the slot of its partial;

@@ -39,6 +39,12 @@ class Cache(C.Structure):
                 ("qmap", C.c_void_p), ("lift", C.c_void_p), ("mu_k", C.c_void_p), ("mu_v", C.c_void_p)]
 
 
+class Atoms(C.Structure):
+    """kvb_atoms of include/kvb.h: TILT moment atoms (device float32 pointers) and their flags."""
+    _fields_ = [(n, C.c_void_p) for n in ("mu_k", "logn", "U", "lam", "diag", "R", "A", "Bk", "Rv")] + \
+               [(n, C.c_int) for n in ("B", "Hkv", "NA", "d", "r", "order", "tilt", "project", "phase")]
+
+
 SIGNATURES = {
     "kvb_last_error": (C.c_char_p, []),
     "kvb_version": (C.c_int, []),
@@ -75,6 +81,7 @@ SIGNATURES = {
     "kvb_xchg_merge": (_i32, [_p, _p, _i64, _i32, _i32, _i32, C.POINTER(C.c_void_p), _p, _i32, C.c_uint64, _p]),
     "kvb_decode_workspace_size": (C.c_size_t, [C.POINTER(Cache), _i32, _i32, _i32]),
     "kvb_head_sync_allocate_workspace": (C.c_size_t, []),
+    "kvb_atom_read": (_i32, [C.POINTER(Atoms), _p, _i32, _i32, _p, _p, _p, _p]),
     "kvb_quasar_scores": (_i32, [_p, _i32, _i32, _i32, _p, C.c_size_t, _p, _i32, _p, _i32, _i64, _p, _p]),
     "kvb_quasar_values_workspace": (C.c_size_t, [_i32, _i32, _i64, _i32]),
     "kvb_quasar_values": (_i32, [_p, _i32, _i32, _i64, _p, C.c_size_t, _p, _i32, _p, _i32, _i32, _p, _p, C.c_size_t, _p]),

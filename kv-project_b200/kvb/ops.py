@@ -720,3 +720,40 @@ def quasar_values(pv: torch.Tensor, flat: torch.Tensor, table, levels, R: int) -
                                   lv.ctypes.data, len(lv), R, _ptr(out), _ptr(ws), ws.numel(),
                                   C.c_void_p(_stream(pv.device))), "kvb_quasar_values")
     return out
+
+
+# ------------------------------------------------------------------------------------------------
+# TILT moment-atom read (atom_read, TILT_KV.py:673-714)
+# ------------------------------------------------------------------------------------------------
+def atom_read(qs: torch.Tensor, mom: dict, rep: int):
+    """qs (B, Hq, c, d) float32 CUDA; mom: the atoms' float32 CUDA tensors (mu_k, logn, U, lam, diag,
+    R, A, Bk, Rv; those the flags leave unused may be missing) and the flags order, tilt, project,
+    phase.  Returns (logit, cfac, tB or None) like the reference's atom_read."""
+    _cuda(qs)
+    qs = qs.float().contiguous()
+    B, Hq, c, d = qs.shape
+    mu = mom["mu_k"]
+    Bm, Hkv, NA, dm = mu.shape
+    if Bm != B or dm != d or Hq != Hkv * rep:
+        raise ValueError("atom_read: qs does not match the atoms")
+    order, tilt = int(mom["order"]), bool(mom["tilt"])
+    r = mom["U"].shape[-1] if order == 2 else (mom["Bk"].shape[-1] if tilt else 1)
+    keep = []
+
+    def ptr(name):
+        t = mom.get(name)
+        if t is None:
+            return None
+        t = t.float().contiguous()
+        keep.append(t)
+        return _ptr(t)
+
+    m = L.Atoms(*(ptr(n) for n in ("mu_k", "logn", "U", "lam", "diag", "R", "A", "Bk", "Rv")),
+                B, Hkv, NA, d, r, order, int(tilt), int(bool(mom["project"])), int(bool(mom.get("phase", True))))
+    logit = torch.empty((B, Hq, c, NA), dtype=torch.float32, device=qs.device)
+    cfac = torch.empty_like(logit)
+    tB = torch.empty((B, Hq, c, NA, r), dtype=torch.float32, device=qs.device) if tilt else None
+    L.check(L.lib().kvb_atom_read(C.byref(m), _ptr(qs), Hq, c, _ptr(logit), _ptr(cfac),
+                                  _ptr(tB) if tB is not None else None, C.c_void_p(_stream(qs.device))),
+            "kvb_atom_read")
+    return logit, cfac, tB
