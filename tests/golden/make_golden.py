@@ -463,8 +463,61 @@ def atoms():
     print("wrote atoms.npz", (HERE / "atoms.npz").stat().st_size)
 
 
+def coverage():
+    """STRATA's coverage statistics: the reference's coverage_groups / coverage_stats
+    (STRATA_KV.py:1206-1298, CPU, float32) on seeded bf16 queries, keys and values, with output
+    metrics M_a = W_aᵀ W_a (:1519-1526), in coverage.npz.  Case a uses the reference's own test
+    configuration (:1964: segments of 64, 8 queries, local 16), case b the same inputs with only the
+    window group, case c the default configuration at 8 query heads per KV head and d 128, case d
+    segments of 256 whose last one holds 10 positions (fewer than its 16 queries)."""
+    S, _ = load_reference()
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(24680)
+    base = S.Config()
+    cases = [("a", 2, 4, 64, 600, dict(STRATA_SEGMENT=64, STRATA_QUERIES=8, STRATA_LOCAL=16), False),
+             ("b", 2, 4, 64, 600, dict(STRATA_SEGMENT=64, STRATA_QUERIES=8, STRATA_LOCAL=16), True),
+             ("c", 1, 8, 128, 700, {}, False),
+             ("d", 2, 2, 64, 878, dict(STRATA_SEGMENT=256, STRATA_QUERIES=16, STRATA_LOCAL=64), False)]
+    out = {}
+    for name, Hkv, rep, d, H, over, wonly in cases:
+        cfg = replace(base, **over)
+        spec = torch.exp(-torch.arange(d) / (d / 5.0))
+        q = (torch.randn(1, Hkv * rep, H, d, generator=g) * spec.sqrt() * 3).bfloat16()
+        k = (torch.randn(1, Hkv, H, d, generator=g) * spec.sqrt() * 3 + 1.0).bfloat16()
+        v = torch.randn(1, Hkv, H, d, generator=g).bfloat16()
+        Wa = torch.randn(Hkv * rep, 3 * d // 2, d, generator=g) / d ** 0.5
+        M = (Wa.transpose(-1, -2) @ Wa).float()
+        scaling = d ** -0.5
+        rs, re = cfg.N_SINK, H - cfg.WINDOW
+        groups = S.coverage_groups(H, cfg)
+        if wonly:
+            groups = groups[-1:]
+        st = S.coverage_stats(q, k, v, scaling, H, rs, re, M, cfg, wonly)
+        pos = np.concatenate([np.asarray(p, np.int64) for p in groups])
+        upos = np.unique(pos)
+        # bf16 bit patterns; queries only at the observation positions (the only rows read)
+        out[f"{name}_qpos"] = upos
+        out[f"{name}_q"] = q[0][:, torch.as_tensor(upos)].view(torch.int16).numpy().view(np.uint16)
+        out[f"{name}_k"] = k[0].view(torch.int16).numpy().view(np.uint16)
+        out[f"{name}_v"] = v[0].view(torch.int16).numpy().view(np.uint16)
+        out[f"{name}_M"] = np32(M)
+        out[f"{name}_shape"] = np.array([Hkv, rep, d, H, rs, re, cfg.STRATA_LOCAL, int(wonly),
+                                         cfg.N_SINK, cfg.W_OBS, cfg.STRATA_SEGMENT, cfg.STRATA_QUERIES])
+        out[f"{name}_scaling"] = np.array(scaling, np.float64)
+        out[f"{name}_floor"] = np.array(cfg.STRATA_FLOOR, np.float64)
+        out[f"{name}_pos"] = pos
+        out[f"{name}_goff"] = np.cumsum([0] + [len(p) for p in groups]).astype(np.int64)
+        for key in ("A", "W", "DD", "S", "Mbar"):
+            out[f"{name}_{key}"] = np32(st[key])
+    np.savez_compressed(HERE / "coverage.npz", **out)
+    print("wrote coverage.npz", (HERE / "coverage.npz").stat().st_size)
+
+
 if __name__ == "__main__":
-    if sys.argv[1:] == ["rowcodes"]:
+    if sys.argv[1:] == ["coverage"]:
+        coverage()
+    elif sys.argv[1:] == ["rowcodes"]:
         rowcodes()
     elif sys.argv[1:] == ["snapkv128"]:
         snapkv128()

@@ -1,0 +1,78 @@
+"""STRATA's coverage statistics (coverage_groups / coverage_stats, STRATA_KV.py:1206-1298) in the oracle
+against the reference's own outputs (coverage.npz): the sampled observation positions exactly, and
+A, W, DD, S, Mbar within float32 round-off of the reference (the oracle computes in float64).  CPU
+only."""
+
+import numpy as np
+import pytest
+
+from oracle.coverage import coverage_groups, coverage_stats
+
+
+def bf16(bits):
+    return (np.asarray(bits, np.uint32) << 16).view(np.float32)
+
+
+def case(g, name):
+    Hkv, rep, d, H, rs, re, local, wonly, n_sink, w_obs, seg, nqs = (int(x) for x in g[f"{name}_shape"])
+    qpos = g[f"{name}_qpos"]
+    q = np.zeros((Hkv * rep, H, d), np.float32)
+    q[:, qpos] = bf16(g[f"{name}_q"])
+    pos, off = g[f"{name}_pos"], g[f"{name}_goff"]
+    groups = [pos[off[i]:off[i + 1]] for i in range(len(off) - 1)]
+    return dict(q=q, k=bf16(g[f"{name}_k"]), v=bf16(g[f"{name}_v"]), M=g[f"{name}_M"], H=H, rs=rs, re=re,
+                local=local, wonly=bool(wonly), n_sink=n_sink, w_obs=w_obs, segment=seg, queries=nqs,
+                groups=groups, scaling=float(g[f"{name}_scaling"]), floor=float(g[f"{name}_floor"]))
+
+
+@pytest.mark.parametrize("name", list("abcd"))
+def test_coverage_groups_golden(golden, name):
+    c = case(golden("coverage"), name)
+    got = coverage_groups(c["H"], c["n_sink"], c["local"], c["w_obs"], c["segment"], c["queries"])
+    if c["wonly"]:
+        got = got[-1:]
+    assert len(got) == len(c["groups"])
+    for a, b in zip(got, c["groups"]):
+        np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("name", list("abcd"))
+def test_coverage_stats_golden(golden, name):
+    g = golden("coverage")
+    c = case(g, name)
+    st = coverage_stats(c["q"], c["k"], c["v"], c["scaling"], c["rs"], c["re"], c["M"], c["groups"],
+                        c["local"], c["floor"])
+    for key in ("A", "W", "DD", "S", "Mbar"):
+        check_close(st[key], g[f"{name}_{key}"], key)
+
+
+# Tolerances against a float32 computation of the same sums.  DD carries (pR / (1 - pR))^2, which
+# float32 resolves to ~1e-4 where one key holds nearly all of a query's probability (1 - pR loses its
+# digits); every group's weight 1 / N inherits that through N = sum DD, so A, W and S move together by
+# N's relative error (~6e-5 in case b).
+SCALE_TOL = {"A": 3e-4, "W": 3e-4, "DD": 5e-3, "S": 3e-4, "Mbar": 3e-4}
+
+
+def check_close(x, ref, key):
+    x, ref = np.asarray(x, np.float64), np.asarray(ref, np.float64)
+    assert x.shape == ref.shape, key
+    assert np.all(np.isfinite(x)), key
+    scale = np.abs(ref).max()
+    err = np.abs(x - ref)
+    assert err.max() <= SCALE_TOL[key] * scale, (key, err.max() / scale)
+    assert np.median(err / np.maximum(np.abs(ref), 1e-30)) <= 1e-4, key
+
+
+def test_coverage_groups_edges():
+    # no position can see a compressible key at long range: no group at all
+    assert coverage_groups(50) == []
+    # too short for a segment: the window group alone, starting at n_sink + local
+    gs = coverage_groups(90)
+    assert len(gs) == 1
+    np.testing.assert_array_equal(gs[0], np.arange(68, 90))
+    # segments: sorted, unique, inside their segment, at most `queries` each
+    gs = coverage_groups(5000)
+    for s, grp in zip(range(68, 5000 - 32, 512), gs[:-1]):
+        assert np.all(np.diff(grp) > 0) and grp[0] >= s and grp[-1] < min(s + 512, 5000 - 32)
+        assert len(grp) == min(16, min(s + 512, 5000 - 32) - s)
+    np.testing.assert_array_equal(gs[-1], np.arange(5000 - 32, 5000))
