@@ -415,6 +415,33 @@ typedef struct kvb_atoms {
 kvb_status kvb_atom_read(const kvb_atoms* m, const float* qs, int Hq, int c, float* logit, float* cfac, float* tB,
                          void* stream);
 
+/* STRATA's coverage statistics of one layer (coverage_stats, STRATA_KV.py:1226-1298; replaces the
+ * reference's eager torch code called from StrataMethod.compress_layer, :1537).  q (Hq, H, d) (only the
+ * rows at the groups' positions are read), k and v (Hkv, H, d), all three of `dtype` with d contiguous
+ * and the element strides below (multiples of 16 bytes); M (Hq, d, d) float32 dense, M_a = W_O,aᵀ W_O,a
+ * (:1519-1526).  The observation groups (coverage_groups, :1206-1222, computed by the caller; pass the
+ * last alone for window_only) are the host arrays pos[group_off[g] .. group_off[g + 1]); the last group
+ * counts reads at any distance >= 1, the others at distance >= local.  Outputs, float32 device
+ * tensors: A, W, DD (Hkv, re - rs), S and Mbar (Hkv, d, d).  d in {64, 128}; Hq / Hkv <= 8. */
+typedef struct kvb_coverage {
+    const void* q;
+    const void* k;
+    const void* v;
+    int dtype;                          /* KVB_F32 / KVB_F16 / KVB_BF16 for q, k and v */
+    int64_t q_head_stride, q_pos_stride, kv_head_stride, kv_pos_stride;
+    const float* M;
+    int Hq, Hkv, d;
+    int64_t H, rs, re;                  /* context length; coded tokens [rs, re) */
+    float scaling;                      /* query scale */
+    float floor;                        /* STRATA_FLOOR */
+    int local;                          /* STRATA_LOCAL */
+} kvb_coverage;
+/* Device workspace bytes of kvb_coverage_stats for these groups (0 for invalid arguments). */
+size_t kvb_coverage_workspace_size(const kvb_coverage* c, const int64_t* pos, const int64_t* group_off, int n_groups);
+kvb_status kvb_coverage_stats(const kvb_coverage* c, const int64_t* pos, const int64_t* group_off, int n_groups,
+                              float* A, float* W, float* DD, float* S, float* Mbar, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* Build the split-K plan (pure host computation, no CUDA calls) for n_ctas CTAs.  plan_out receives
  * [n_ctas, n_pieces, n_heads, cta_begin[n_ctas + 1], n_pieces x (head, stratum, first chunk, end
  * chunk, slot), head_begin[n_heads + 1]]: pieces in CTA order, each with the slot of its partial;

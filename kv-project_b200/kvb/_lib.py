@@ -45,6 +45,16 @@ class Atoms(C.Structure):
                [(n, C.c_int) for n in ("B", "Hkv", "NA", "d", "r", "order", "tilt", "project", "phase")]
 
 
+class Coverage(C.Structure):
+    """kvb_coverage of include/kvb.h: one layer's queries, keys, values and output metrics for STRATA's
+    coverage statistics."""
+    _fields_ = [("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("dtype", C.c_int),
+                ("q_head_stride", C.c_int64), ("q_pos_stride", C.c_int64), ("kv_head_stride", C.c_int64),
+                ("kv_pos_stride", C.c_int64), ("M", C.c_void_p), ("Hq", C.c_int), ("Hkv", C.c_int), ("d", C.c_int),
+                ("H", C.c_int64), ("rs", C.c_int64), ("re", C.c_int64), ("scaling", C.c_float), ("floor", C.c_float),
+                ("local", C.c_int)]
+
+
 SIGNATURES = {
     "kvb_last_error": (C.c_char_p, []),
     "kvb_version": (C.c_int, []),
@@ -82,6 +92,8 @@ SIGNATURES = {
     "kvb_decode_workspace_size": (C.c_size_t, [C.POINTER(Cache), _i32, _i32, _i32]),
     "kvb_head_sync_allocate_workspace": (C.c_size_t, []),
     "kvb_atom_read": (_i32, [C.POINTER(Atoms), _p, _i32, _i32, _p, _p, _p, _p]),
+    "kvb_coverage_workspace_size": (C.c_size_t, [C.POINTER(Coverage), _p, _p, _i32]),
+    "kvb_coverage_stats": (_i32, [C.POINTER(Coverage), _p, _p, _i32, _p, _p, _p, _p, _p, _p, C.c_size_t, _p]),
     "kvb_quasar_scores": (_i32, [_p, _i32, _i32, _i32, _p, C.c_size_t, _p, _i32, _p, _i32, _i64, _p, _p]),
     "kvb_quasar_values_workspace": (C.c_size_t, [_i32, _i32, _i64, _i32]),
     "kvb_quasar_values": (_i32, [_p, _i32, _i32, _i64, _p, C.c_size_t, _p, _i32, _p, _i32, _i32, _p, _p, C.c_size_t, _p]),

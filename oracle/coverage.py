@@ -68,7 +68,7 @@ def coverage_stats(q, k, v, scaling: float, rs: int, re: int, M, groups, local: 
     live = 0.0
     Mg = M.reshape(Hkv, rep, d, d)
     VR = v[:, rs:re]
-    vMv = np.stack([np.einsum("hnd,hde,hne->hn", VR, Mg[:, r], VR) for r in range(rep)], 1)
+    vMv = np.stack([((VR @ Mg[:, r]) * VR).sum(-1) for r in range(rep)], 1)
     for gi, P in enumerate(groups):
         P = np.asarray(P, np.int64)
         nq, mmax = len(P), int(P.max()) + 1
@@ -77,17 +77,17 @@ def coverage_stats(q, k, v, scaling: float, rs: int, re: int, M, groups, local: 
             continue
         nt = te - rs
         qa = q[:, P].reshape(Hkv, rep, nq, d) * scaling
-        sc = np.einsum("hrqd,hjd->hrqj", qa, k[:, :mmax])
+        sc = qa @ k[:, None, :mmax].swapaxes(-1, -2)
         sc = np.where(np.arange(mmax)[None, None, None, :] > P[None, None, :, None], -np.inf, sc)
         mx = sc.max(-1, keepdims=True)
         e = np.exp(sc - mx)
         p = e / e.sum(-1, keepdims=True)
-        o = np.einsum("hrqj,hjd->hrqd", p, v[:, :mmax])
+        o = p @ v[:, None, :mmax]
         loc = 1 if gi == len(groups) - 1 else local
         far = np.arange(rs, te)[None, :] <= (P[:, None] - loc)
         pR = p[..., rs:te] * far
-        oM = np.einsum("hrqd,hrde->hrqe", o, Mg)
-        u2 = np.maximum(vMv[:, :, None, :nt] - 2 * np.einsum("hrqd,hjd->hrqj", oM, VR[:, :nt])
+        oM = o @ Mg
+        u2 = np.maximum(vMv[:, :, None, :nt] - 2 * (oM @ VR[:, None, :nt].swapaxes(-1, -2))
                         + (oM * o).sum(-1)[..., None], 0.0)
         dd = ((pR / np.maximum(1 - pR, 1e-6)) ** 2 * u2).sum((1, 2)) / nq
         a = pR ** 2 * u2
@@ -97,7 +97,8 @@ def coverage_stats(q, k, v, scaling: float, rs: int, re: int, M, groups, local: 
         DD[:, :nt] += dd * wgt
         WVa[:, :, :nt] += (pR ** 2).sum(2) / nq * wgt
         alpha = a.sum(-1) / nq
-        S += np.einsum("hrq,hrqd,hrqe->hde", alpha, qa, qa) * wgt
+        qw = (alpha[..., None] * qa).reshape(Hkv, rep * nq, d)
+        S += (qw.swapaxes(-1, -2) @ qa.reshape(Hkv, rep * nq, d)) * wgt
         live += float(N > 0)
     live = max(live, 1.0)
     A, DD, WVa, S = A / live, DD / live, WVa / live, S / live

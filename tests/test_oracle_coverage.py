@@ -46,11 +46,15 @@ def test_coverage_stats_golden(golden, name):
         check_close(st[key], g[f"{name}_{key}"], key)
 
 
-# Tolerances against a float32 computation of the same sums.  DD carries (pR / (1 - pR))^2, which
-# float32 resolves to ~1e-4 where one key holds nearly all of a query's probability (1 - pR loses its
-# digits); every group's weight 1 / N inherits that through N = sum DD, so A, W and S move together by
-# N's relative error (~6e-5 in case b).
-SCALE_TOL = {"A": 3e-4, "W": 3e-4, "DD": 5e-3, "S": 3e-4, "Mbar": 3e-4}
+# Tolerances of a float32 computation of the same sums, relative to each array's largest entry.  DD
+# carries (pR / (1 - pR))^2: where one key holds nearly all of a query's probability, float32 keeps
+# few digits of 1 - pR (one unit in the last place of 1.0 is 6e-8, so 1 - pR = 1e-5 is known to
+# ~1e-2 and its square to ~2e-2), in the reference as here.  Those few entries get the loose maximum;
+# 99.9 % of DD's entries and every entry of the other arrays are held tightly.  Every group's weight
+# 1 / N inherits DD's error through N = sum DD, so A, W and S move together by N's relative error
+# (~6e-5 in case b).
+SCALE_TOL = {"A": 3e-4, "W": 3e-4, "DD": 3e-2, "S": 3e-4, "Mbar": 3e-4}
+Q999_TOL = 1e-3
 
 
 def check_close(x, ref, key):
@@ -60,6 +64,7 @@ def check_close(x, ref, key):
     scale = np.abs(ref).max()
     err = np.abs(x - ref)
     assert err.max() <= SCALE_TOL[key] * scale, (key, err.max() / scale)
+    assert np.quantile(err, 0.999) <= Q999_TOL * scale, (key, np.quantile(err, 0.999) / scale)
     assert np.median(err / np.maximum(np.abs(ref), 1e-30)) <= 1e-4, key
 
 
