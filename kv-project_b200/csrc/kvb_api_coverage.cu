@@ -23,11 +23,12 @@ struct CovPlan {
     std::vector<CovGroup> grp;
     std::vector<int> pos;
     std::vector<int4> it1, it2;
-    int64_t rows = 0, parts = 0, T_all = 0, alps = 0;
+    int64_t rows = 0, parts = 0, T_all = 0, alps = 0, nparts = 0;
+    int n_ablk = 0;
     // byte offsets in the workspace
     size_t o_grp = 0, o_pos = 0, o_it1 = 0, o_it2 = 0, host_bytes = 0;
     size_t o_vmv = 0, o_part = 0, o_rowinfo = 0, o_oM = 0, o_alpha = 0, o_dd = 0, o_a = 0, o_w = 0, o_alp = 0,
-           o_gw = 0, o_wva = 0, o_hsum = 0, total = 0;
+           o_npart = 0, o_gw = 0, o_wva = 0, o_apart = 0, o_hsum = 0, total = 0;
 };
 
 kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* goff, int n_groups, CovPlan& P) {
@@ -70,11 +71,13 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
         G.part_base = P.parts;
         G.tok_base = P.T_all;
         G.alp_base = P.alps;
+        G.n_base = P.nparts;
         const int64_t grows = int64_t(c->Hq) * G.nq;
         P.rows += grows;
         P.parts += grows * G.ns;
         P.T_all += G.nt;
         P.alps += grows * G.nit;
+        P.nparts += int64_t(c->Hkv) * G.nit;
         const int gi = int(P.grp.size());
         const int nrb = (rep * G.nq + kvb::CV_ROWS - 1) / kvb::CV_ROWS;
         for (int h = 0; h < c->Hkv; ++h) {
@@ -101,8 +104,11 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
     P.o_a = o;       o += up(size_t(c->Hkv) * P.T_all * 4);
     P.o_w = o;       o += up(size_t(c->Hq) * P.T_all * 4);
     P.o_alp = o;     o += up(size_t(P.alps) * 4);
+    P.o_npart = o;   o += up(size_t(P.nparts) * 4);
     P.o_gw = o;      o += up(P.grp.size() * 8);
     P.o_wva = o;     o += up(size_t(c->Hq) * n * 4);
+    P.n_ablk = int((n + kvb::CV_THREADS - 1) / kvb::CV_THREADS);
+    P.o_apart = o;   o += up(size_t(c->Hkv) * P.n_ablk * kvb::CV_APART * 4);
     P.o_hsum = o;    o += up(size_t(c->Hkv) * 16);
     P.total = o;
     return KVB_OK;
@@ -142,14 +148,13 @@ kvb_status cov_launch(const kvb_coverage* c, const CovPlan& P, kvb::CovParams& p
         cov_norm_kernel<<<unsigned(ng), CV_THREADS, 0, s>>>(p);
         if ((st = launch_check("coverage norm"))) return st;
     }
-    const unsigned nb = unsigned((int64_t(c->Hkv) * n + CV_THREADS - 1) / CV_THREADS);
-    cov_accum_kernel<<<nb, CV_THREADS, 0, s>>>(p);
+    cov_accum_kernel<<<dim3(unsigned(P.n_ablk), unsigned(c->Hkv)), CV_THREADS, 0, s>>>(p);
     if ((st = launch_check("coverage accum"))) return st;
     cov_gram_kernel<D, T><<<dim3(D / 32, D / 32, unsigned(c->Hkv)), CV_THREADS, 0, s>>>(p);
     if ((st = launch_check("coverage gram"))) return st;
     cov_finish_kernel<D><<<unsigned(c->Hkv), CV_THREADS, 0, s>>>(p);
     if ((st = launch_check("coverage finish"))) return st;
-    cov_floor_kernel<<<nb, CV_THREADS, 0, s>>>(p);
+    cov_floor_kernel<<<unsigned((int64_t(c->Hkv) * n + CV_THREADS - 1) / CV_THREADS), CV_THREADS, 0, s>>>(p);
     return launch_check("coverage floor");
 }
 
@@ -219,7 +224,10 @@ kvb_status kvb_coverage_stats(const kvb_coverage* c, const int64_t* pos, const i
     p.a_raw = reinterpret_cast<float*>(ws + P.o_a);
     p.w_raw = reinterpret_cast<float*>(ws + P.o_w);
     p.alp = reinterpret_cast<float*>(ws + P.o_alp);
+    p.npart = reinterpret_cast<float*>(ws + P.o_npart);
     p.gw = reinterpret_cast<float*>(ws + P.o_gw);
+    p.apart = reinterpret_cast<float*>(ws + P.o_apart);
+    p.n_ablk = P.n_ablk;
     p.wva = reinterpret_cast<float*>(ws + P.o_wva);
     p.hsum = reinterpret_cast<float*>(ws + P.o_hsum);
     p.A = A;

@@ -48,6 +48,7 @@ struct CovGroup {
     int64_t part_base;  // attention partials: part_base + (a nq + i) ns + split
     int64_t tok_base;   // token columns of the group in the per-group token sums
     int64_t alp_base;   // alpha partials: alp_base + (a nq + i) nit + item
+    int64_t n_base;     // partial sums of dd: n_base + h nit + item
 };
 
 struct CovParams {
@@ -70,7 +71,10 @@ struct CovParams {
     float* a_raw;                    // (Hkv, T_all)
     float* w_raw;                    // (Hq, T_all)
     float* alp;                      // alpha partials
+    float* npart;                    // partial sums of dd per (group, head, item)
     float* gw;                       // per group: weight, N > 0
+    float* apart;                    // per (head, accumulation block): sums of A, W, DD, WVa[r]
+    int n_ablk;                      // accumulation blocks per head
     float* wva;                      // (Hq, n)
     float* hsum;                     // per head: sum A, sum W, sum DD, sum omega
     float* A;                        // (Hkv, n)
@@ -106,6 +110,30 @@ template <> __device__ __forceinline__ void cv_load8<__half>(const __half* p, fl
         f[2 * e] = x.x;
         f[2 * e + 1] = x.y;
     }
+}
+
+// 8 elements of a 16-byte word as float32.
+template <typename T> __device__ __forceinline__ void cv_unpack8(const uint4& u, float (&f)[8]);
+template <> __device__ __forceinline__ void cv_unpack8<__nv_bfloat16>(const uint4& u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        f[2 * e] = __uint_as_float(w[e] << 16);
+        f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+    }
+}
+template <> __device__ __forceinline__ void cv_unpack8<__half>(const uint4& u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+        f[2 * e] = x.x;
+        f[2 * e + 1] = x.y;
+    }
+}
+template <> __device__ __forceinline__ void cv_unpack8<float>(const uint4&, float (&f)[8]) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = 0.f;
 }
 
 // Rows 0..63 of a tile into Xt[D][64] (transposed: element (row r, dim e) at e * 64 + r), times `scale`;
@@ -410,13 +438,58 @@ __global__ void __launch_bounds__(D) cov_merge_kernel(CovParams p) {
 
 template <int D>
 constexpr int cov_sense_smem() {
-    return (4 * D * 64 + 3 * 64 * 64 + (2 + CV_MAX_REP) * CV_TOKS + CV_MAX_REP * 64) * 4;
+    return (4 * D * 64 + 64 * 64 + 2 * 8 * 64 + (2 + CV_MAX_REP) * CV_TOKS + CV_MAX_REP * 64) * 4;
 }
 
+// The next tile's key and value rows held in registers while the current tile computes (16-bit inputs;
+// float32 inputs load at the store point instead).  Chunk w = threadIdx.x + CV_THREADS x: row w & 63,
+// 8 elements from (w >> 6) x 8: the layout of cv_rows_t.
+template <int D, typename T>
+struct CvNext {
+    static constexpr bool REG = sizeof(T) == 2;
+    static constexpr int N = REG ? 64 * (D / 8) / CV_THREADS : 1;
+    uint4 k[N], v[N];
+    __device__ __forceinline__ void load(const T* kb, const T* vb, int64_t stride, int tt, int nk) {
+        if constexpr (REG) {
+#pragma unroll
+            for (int x = 0; x < N; ++x) {
+                const int w = threadIdx.x + CV_THREADS * x, r = w & 63, c = w >> 6;
+                if (r < nk) {
+                    k[x] = __ldg(reinterpret_cast<const uint4*>(kb + int64_t(tt + r) * stride + c * 8));
+                    v[x] = __ldg(reinterpret_cast<const uint4*>(vb + int64_t(tt + r) * stride + c * 8));
+                } else {
+                    k[x] = v[x] = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+        }
+    }
+    __device__ __forceinline__ void store(float* Kt, float* Vt, const T* kb, const T* vb, int64_t stride, int tt,
+                                          int nk) {
+        if constexpr (REG) {
+#pragma unroll
+            for (int x = 0; x < N; ++x) {
+                const int w = threadIdx.x + CV_THREADS * x, r = w & 63, c = w >> 6;
+                float fk[8], fv[8];
+                cv_unpack8<T>(k[x], fk);
+                cv_unpack8<T>(v[x], fv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    Kt[(c * 8 + e) * 64 + r] = fk[e];
+                    Vt[(c * 8 + e) * 64 + r] = fv[e];
+                }
+            }
+        } else {
+            cv_rows_t<D, T>(Kt, [&](int r) -> const T* { return r < nk ? kb + int64_t(tt + r) * stride : nullptr; }, 1.f);
+            cv_rows_t<D, T>(Vt, [&](int r) -> const T* { return r < nk ? vb + int64_t(tt + r) * stride : nullptr; }, 1.f);
+        }
+    }
+};
+
 // One CTA per (group, KV head, CV_TOKS coded tokens).  Per block of 64 rows: the scaled queries and oM
-// rows once; per tile of 64 tokens the scores s and t = oM . v (two FMA tiles), the elementwise terms,
-// their sums over rows per token (one thread per token and statistic, rows in order) and over tokens
-// per row (butterflies over the row's 16 lanes, tiles in order).
+// rows once; per tile of 64 tokens the scores s and t = oM . v (two FMA tiles, the next tile's rows
+// loading meanwhile), the elementwise terms and their sums: over rows per token (a thread's 4 rows,
+// the two row groups of a warp, then the 8 warps in order; pR^2 per r from a staged tile, rows in
+// order) and over tokens per row (butterflies over the row's 16 lanes, tiles in order).
 template <int D, typename T>
 __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, const int4* items) {
     extern __shared__ float4 cv_smem[];
@@ -424,10 +497,10 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
     float* Ot = Qt + D * 64;                              // [D][64]
     float* Kt = Ot + D * 64;                              // [D][64]
     float* Vt = Kt + D * 64;                              // [D][64]
-    float* Edd = Vt + D * 64;                             // [64 rows][64 tokens]
-    float* Ea = Edd + 64 * 64;
-    float* Ew = Ea + 64 * 64;
-    float* tdd = Ew + 64 * 64;                            // [CV_TOKS]
+    float* Ew = Vt + D * 64;                              // [64 rows][64 tokens]: pR^2
+    float* red_dd = Ew + 64 * 64;                         // [8 warps][64 tokens]
+    float* red_a = red_dd + 8 * 64;
+    float* tdd = red_a + 8 * 64;                          // [CV_TOKS]
     float* ta = tdd + CV_TOKS;                            // [CV_TOKS]
     float* tw = ta + CV_TOKS;                             // [CV_MAX_REP][CV_TOKS]
     float* svmv = tw + CV_MAX_REP * CV_TOKS;              // [CV_MAX_REP][64]
@@ -439,10 +512,17 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
     const int R = p.rep * G.nq;
     const int t0 = item * CV_TOKS, t1 = min(t0 + CV_TOKS, G.nt);
     for (int x = threadIdx.x; x < (2 + CV_MAX_REP) * CV_TOKS; x += CV_THREADS) tdd[x] = 0.f;
-    const int rg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+    const int rg = threadIdx.x >> 4, cg = threadIdx.x & 15, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const T* kb = static_cast<const T*>(p.k) + h * p.khs + p.rs * p.kps;
     const T* vb = static_cast<const T*>(p.v) + h * p.khs + p.rs * p.kps;
     const int64_t hrow = G.row_base + int64_t(h) * R;    // the head's first row
+    auto load_vmv = [&](int tt, int nk) {
+        for (int x = threadIdx.x; x < p.rep * 64; x += CV_THREADS) {
+            const int r = x >> 6, j = x & 63;
+            svmv[x] = j < nk ? p.vmv[size_t(h * p.rep + r) * p.n + tt + j] : 0.f;
+        }
+    };
+    CvNext<D, T> nx;
     for (int row0 = 0; row0 < R; row0 += CV_ROWS) {
         const int nrows = min(CV_ROWS, R - row0);
         __syncthreads();
@@ -460,25 +540,29 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
             return cv_qrow<T>(p, h * p.rep + rr / G.nq, p.pos[G.off + rr % G.nq]);
         }, p.scaling);
         cv_rows_t<D, float>(Ot, [&](int r) -> const float* { return r < nrows ? p.oM + (hrow + row0 + r) * D : nullptr; }, 1.f);
+        {
+            const int nk = min(CV_TILE, t1 - t0);
+            nx.load(kb, vb, p.kps, t0, nk);
+            nx.store(Kt, Vt, kb, vb, p.kps, t0, nk);
+            load_vmv(t0, nk);
+        }
+        const int r_first = row0 / G.nq, n_r = (row0 + nrows - 1) / G.nq - r_first + 1;
         float alpha[4] = {0.f, 0.f, 0.f, 0.f};
+        __syncthreads();
         for (int tt = t0; tt < t1; tt += CV_TILE) {
             const int nk = min(CV_TILE, t1 - tt);
-            cv_rows_t<D, T>(Kt, [&](int r) -> const T* { return r < nk ? kb + int64_t(tt + r) * p.kps : nullptr; }, 1.f);
-            cv_rows_t<D, T>(Vt, [&](int r) -> const T* { return r < nk ? vb + int64_t(tt + r) * p.kps : nullptr; }, 1.f);
-            for (int x = threadIdx.x; x < p.rep * 64; x += CV_THREADS) {
-                const int r = x >> 6, j = x & 63;
-                svmv[x] = j < nk ? p.vmv[size_t(h * p.rep + r) * p.n + tt + j] : 0.f;
-            }
-            __syncthreads();
+            const int tn = tt + CV_TILE, nkn = min(CV_TILE, t1 - tn);
+            if (tn < t1) nx.load(kb, vb, p.kps, tn, nkn);
             float s[4][4] = {}, tv[4][4] = {};
             cv_tile<D>(s, Qt, Kt, rg, cg);
             cv_tile<D>(tv, Ot, Vt, rg, cg);
+            float dsum[4] = {0.f, 0.f, 0.f, 0.f}, asum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int row = rg * 4 + i;
                 const int pos = s_pos[row], r = s_r[row];
                 const float lse = s_lse[row], c = s_c[row];
-                float dd4[4], a4[4], w4[4];
+                float w4[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int kk = cg * 4 + j;
@@ -493,43 +577,47 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
                         wv = pr * pr;
                         av = wv * u2;
                     }
-                    dd4[j] = ddv;
-                    a4[j] = av;
+                    dsum[j] += ddv;
+                    asum[j] += av;
                     w4[j] = wv;
                     alpha[i] += av;
                 }
-                *reinterpret_cast<float4*>(Edd + row * 64 + cg * 4) = make_float4(dd4[0], dd4[1], dd4[2], dd4[3]);
-                *reinterpret_cast<float4*>(Ea + row * 64 + cg * 4) = make_float4(a4[0], a4[1], a4[2], a4[3]);
                 *reinterpret_cast<float4*>(Ew + row * 64 + cg * 4) = make_float4(w4[0], w4[1], w4[2], w4[3]);
             }
+            // the warp's two row groups, then one slot per warp
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                dsum[j] += __shfl_xor_sync(0xffffffffu, dsum[j], 16);
+                asum[j] += __shfl_xor_sync(0xffffffffu, asum[j], 16);
+            }
+            if (lane < 16) {
+                *reinterpret_cast<float4*>(red_dd + warp * 64 + cg * 4) = make_float4(dsum[0], dsum[1], dsum[2], dsum[3]);
+                *reinterpret_cast<float4*>(red_a + warp * 64 + cg * 4) = make_float4(asum[0], asum[1], asum[2], asum[3]);
+            }
             __syncthreads();
-            // per token: sums over this block's rows, in row order (threads 0-63 dd, 64-127 a, 128-191 w by r)
-            {
-                const int t = threadIdx.x & 63, stat = threadIdx.x >> 6;
-                if (stat < 3 && t < nk) {
-                    const int col = tt - t0 + t;
-                    if (stat == 0) {
-                        float acc = 0.f;
-                        for (int row = 0; row < nrows; ++row) acc += Edd[row * 64 + t];
-                        tdd[col] += acc;
-                    } else if (stat == 1) {
-                        float acc = 0.f;
-                        for (int row = 0; row < nrows; ++row) acc += Ea[row * 64 + t];
-                        ta[col] += acc;
-                    } else {
-                        int rc = s_r[0];
-                        float acc = 0.f;
-                        for (int row = 0; row < nrows; ++row) {
-                            if (s_r[row] != rc) {
-                                tw[rc * CV_TOKS + col] += acc;
-                                acc = 0.f;
-                                rc = s_r[row];
-                            }
-                            acc += Ew[row * 64 + t];
-                        }
-                        tw[rc * CV_TOKS + col] += acc;
-                    }
+            // per token: the 8 warps in order (dd: threads 0-63, a: 64-127); pR^2 per (r, token) pair,
+            // the r's rows of this block in order (all threads)
+            if (threadIdx.x < 128) {
+                const int t = threadIdx.x & 63;
+                if (t < nk) {
+                    const float* src = threadIdx.x < 64 ? red_dd : red_a;
+                    float acc = 0.f;
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) acc += src[w * 64 + t];
+                    (threadIdx.x < 64 ? tdd : ta)[tt - t0 + t] += acc;
                 }
+            }
+            for (int x = threadIdx.x; x < 64 * n_r; x += CV_THREADS) {
+                const int t = x & 63, r = r_first + (x >> 6);
+                if (t >= nk) continue;
+                const int lo = max(r * G.nq, row0) - row0, hi = min((r + 1) * G.nq, row0 + nrows) - row0;
+                float acc = 0.f;
+                for (int row = lo; row < hi; ++row) acc += Ew[row * 64 + t];
+                tw[r * CV_TOKS + tt - t0 + t] += acc;
+            }
+            if (tn < t1) {
+                nx.store(Kt, Vt, kb, vb, p.kps, tn, nkn);
+                load_vmv(tn, nkn);
             }
             __syncthreads();
         }
@@ -542,6 +630,13 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
         }
     }
     __syncthreads();
+    {
+        // this item's share of N = sum dd (dd = the row sum / nq), a fixed-order block sum
+        float ns = 0.f;
+        for (int x = threadIdx.x; x < t1 - t0; x += CV_THREADS) ns += tdd[x] / float(G.nq);
+        ns = cv_block_sum(ns, red_dd);
+        if (threadIdx.x == 0) p.npart[G.n_base + int64_t(h) * G.nit + item] = ns;
+    }
     for (int x = threadIdx.x; x < t1 - t0; x += CV_THREADS) {
         const int64_t col = G.tok_base + t0 + x;
         p.dd_raw[h * p.T_all + col] = tdd[x];
@@ -557,11 +652,7 @@ __global__ void __launch_bounds__(CV_THREADS) cov_norm_kernel(CovParams p) {
     const CovGroup G = p.grp[blockIdx.x];
     const float nq = float(G.nq);
     float s = 0.f;
-    for (int64_t x = threadIdx.x; x < int64_t(p.Hkv) * G.nt; x += CV_THREADS) {
-        const int h = int(x / G.nt);
-        const int64_t t = x % G.nt;
-        s += p.dd_raw[h * p.T_all + G.tok_base + t] / nq;        // dd = sum_(r,i) ... / nq
-    }
+    for (int x = threadIdx.x; x < p.Hkv * G.nit; x += CV_THREADS) s += p.npart[G.n_base + x];
     const float N = cv_block_sum(s, red);
     if (threadIdx.x == 0) {
         p.gw[2 * blockIdx.x] = N > 0.f ? 1.f / fmaxf(N, 1e-30f) : 0.f;
@@ -577,18 +668,22 @@ __global__ void __launch_bounds__(CV_THREADS) cov_norm_kernel(CovParams p) {
 
 // ---- per (head, token): A, DD, WVa over the groups in order; W; over live --------------------------
 
+// Grid (accumulation blocks, KV heads); each block also leaves its sums of A, W, DD and WVa[r] for the
+// head totals.
+constexpr int CV_APART = 3 + CV_MAX_REP;
+
 __global__ void __launch_bounds__(CV_THREADS) cov_accum_kernel(CovParams p) {
-    const int64_t x = int64_t(blockIdx.x) * CV_THREADS + threadIdx.x;
-    if (x >= int64_t(p.Hkv) * p.n) return;
-    const int h = int(x / p.n);
-    const int64_t t = x % p.n;
+    __shared__ float red[CV_THREADS / 32];
+    const int h = blockIdx.y;
+    const int64_t t = int64_t(blockIdx.x) * CV_THREADS + threadIdx.x;
+    const bool ok = t < p.n;
     float A = 0.f, DD = 0.f, live = 0.f, w[CV_MAX_REP];
 #pragma unroll
     for (int r = 0; r < CV_MAX_REP; ++r) w[r] = 0.f;
     for (int g = 0; g < p.n_groups; ++g) {
         const CovGroup& G = p.grp[g];
         live += p.gw[2 * g + 1];
-        if (t >= G.nt) continue;
+        if (!ok || t >= G.nt) continue;
         const float wgt = p.gw[2 * g], nq = float(G.nq);
         const int64_t col = G.tok_base + t;
         A += p.a_raw[h * p.T_all + col] / nq * wgt;
@@ -600,15 +695,33 @@ __global__ void __launch_bounds__(CV_THREADS) cov_accum_kernel(CovParams p) {
     live = fmaxf(live, 1.f);
     float W = 0.f;
 #pragma unroll
-    for (int r = 0; r < CV_MAX_REP; ++r)
+    for (int r = 0; r < CV_MAX_REP; ++r) {
+        w[r] /= live;
         if (r < p.rep) {
-            const float wr = w[r] / live;
-            p.wva[(h * p.rep + r) * p.n + t] = wr;
-            W += wr;
+            if (ok) p.wva[(h * p.rep + r) * p.n + t] = w[r];
+            W += w[r];
         }
-    p.A[x] = A / live;
-    p.DD[x] = DD / live;
-    p.W[x] = W;
+    }
+    A /= live;
+    DD /= live;
+    if (ok) {
+        p.A[h * p.n + t] = A;
+        p.DD[h * p.n + t] = DD;
+        p.W[h * p.n + t] = W;
+    }
+    float* dst = p.apart + (int64_t(h) * p.n_ablk + blockIdx.x) * CV_APART;
+    const float sa = cv_block_sum(ok ? A : 0.f, red);
+    const float sw = cv_block_sum(ok ? W : 0.f, red);
+    const float sd = cv_block_sum(ok ? DD : 0.f, red);
+    if (threadIdx.x == 0) {
+        dst[0] = sa;
+        dst[1] = sw;
+        dst[2] = sd;
+    }
+    for (int r = 0; r < p.rep; ++r) {
+        const float so = cv_block_sum(ok ? w[r] : 0.f, red);
+        if (threadIdx.x == 0) dst[3 + r] = so;
+    }
 }
 
 // ---- S[h] = sum_g wgt_g sum_rows alpha qa qaᵀ, over live --------------------------------------------
@@ -662,38 +775,24 @@ __global__ void __launch_bounds__(CV_THREADS) cov_gram_kernel(CovParams p) {
 
 template <int D>
 __global__ void __launch_bounds__(CV_THREADS) cov_finish_kernel(CovParams p) {
-    __shared__ float red[CV_THREADS / 32];
-    __shared__ float s_om[CV_MAX_REP];
+    __shared__ float s_sum[CV_APART];
     const int h = blockIdx.x;
-    float sa = 0.f, sw = 0.f, sd = 0.f;
-    for (int64_t t = threadIdx.x; t < p.n; t += CV_THREADS) {
-        sa += p.A[h * p.n + t];
-        sw += p.W[h * p.n + t];
-        sd += p.DD[h * p.n + t];
-    }
-    const float sumA = cv_block_sum(sa, red);
-    const float sumW = cv_block_sum(sw, red);
-    const float sumDD = cv_block_sum(sd, red);
-    for (int r = 0; r < p.rep; ++r) {
-        float so = 0.f;
-        for (int64_t t = threadIdx.x; t < p.n; t += CV_THREADS) so += p.wva[(h * p.rep + r) * p.n + t];
-        const float om = cv_block_sum(so, red);
-        if (threadIdx.x == 0) s_om[r] = om;
-    }
-    if (threadIdx.x == 0) {
-        p.hsum[4 * h] = sumA;
-        p.hsum[4 * h + 1] = sumW;
-        p.hsum[4 * h + 2] = sumDD;
+    if (threadIdx.x < 3 + p.rep) {
+        float acc = 0.f;
+        for (int b = 0; b < p.n_ablk; ++b) acc += p.apart[(int64_t(h) * p.n_ablk + b) * CV_APART + threadIdx.x];
+        s_sum[threadIdx.x] = acc;
     }
     __syncthreads();
+    if (threadIdx.x < 3) p.hsum[4 * h + threadIdx.x] = s_sum[threadIdx.x];
+    const float sumA = s_sum[0];
     float osum = 0.f;
-    for (int r = 0; r < p.rep; ++r) osum += s_om[r];
+    for (int r = 0; r < p.rep; ++r) osum += s_sum[3 + r];
     const float inv = fmaxf(sumA, 1e-30f);
     for (int e = threadIdx.x; e < D * D; e += CV_THREADS) {
         p.S[size_t(h) * D * D + e] /= inv;
         float mb = 0.f;
         if (osum > 0.f) {
-            for (int r = 0; r < p.rep; ++r) mb += s_om[r] * p.M[size_t(h * p.rep + r) * D * D + e];
+            for (int r = 0; r < p.rep; ++r) mb += s_sum[3 + r] * p.M[size_t(h * p.rep + r) * D * D + e];
             mb /= fmaxf(osum, 1e-30f);
         } else {
             for (int r = 0; r < p.rep; ++r) mb += p.M[size_t(h * p.rep + r) * D * D + e];

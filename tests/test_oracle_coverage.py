@@ -65,7 +65,8 @@ def check_close(x, ref, key):
     err = np.abs(x - ref)
     assert err.max() <= SCALE_TOL[key] * scale, (key, err.max() / scale)
     assert np.quantile(err, 0.999) <= Q999_TOL * scale, (key, np.quantile(err, 0.999) / scale)
-    assert np.median(err / np.maximum(np.abs(ref), 1e-30)) <= 1e-4, key
+    if key != "S":      # S's small off-diagonal entries are sums that cancel: no relative bound
+        assert np.median(err / np.maximum(np.abs(ref), 1e-30)) <= 1e-4, key
 
 
 def test_coverage_groups_edges():
