@@ -26,6 +26,8 @@ Other workloads (--workload), each printing the same JSON line for its own confi
   c1-pack     compress side of config 1 (key energy, rank split, 6 quantise+pack calls per layer)
   c2-evict    compress side of config 2 (accumulated scores of 64 queries, top-k, 2 packs per layer)
   c3-project  compress side of config 3 (tcgen05 basis projection + mid-rise code of K and V)
+  c1-cover    STRATA's coverage statistics of one config-1 layer (batch row 1, 32768 positions, 65
+              observation groups): exact per-group softmax sensitivities A, W, DD, S, Mbar (FP32 FMA)
 
   python bench.py [--gpus N --steps K --warmup W] [--workload W]   # kvb (CUDA) arm
   python bench.py --strata 0,0                                      # config 1 with every token at 2 bits
@@ -54,6 +56,10 @@ METRIC = "packed-KV decode attn µs/step and HBM GB/s (% of peak) at 1/2/4/8 B20
 FALLBACK_HBM_GBS = 6650.0
 DECODE = ("c1", "c0", "c2", "c3", "c4", "c4s")
 COMPRESS = ("c1-pack", "c2-evict", "c3-project")
+COVER = ("c1-cover",)
+# nominal FP32 FMA rate of a B200 (148 SMs x 128 lanes x 2 FLOP x 1965 MHz): the coverage kernels'
+# roofline (MEASURED_PEAKS.json holds the copy and tensor-core rates only)
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 # DRAM bytes (read + write) of one decode_main launch from an ncu capture of this bench's workload
 # (profiles/decode_main_config1.md), with the hash of the decode sources the capture ran on: the
@@ -76,7 +82,7 @@ def args_():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["kvb", "reference"], default="kvb")
-    p.add_argument("--workload", choices=DECODE + COMPRESS, default="c1")
+    p.add_argument("--workload", choices=DECODE + COMPRESS + COVER, default="c1")
     p.add_argument("--layers", type=int, default=None, help="layers per rank (default: the config's)")
     p.add_argument("--batch", type=int, default=None, help="batch per rank (default: the config's)")
     p.add_argument("--context", type=int, default=None)
@@ -168,6 +174,8 @@ def shape(a, world):
         L = min(L, int(110e9 // per_layer))         # layers resident on one GPU (all 80 from 4 GPUs up)
     if a.workload in COMPRESS:
         L = min(L, 4)                               # distinct layer inputs cycled through (each > L2)
+    if a.workload in COVER:
+        L, B = 2, 1                                 # one batch row (the reference's coverage is per row)
     L = a.layers or L
     B = a.batch or B
     T = a.context or T
@@ -184,6 +192,7 @@ DESC = {
     "c1-pack": "config1-compress-mixed-strata",
     "c2-evict": "config2-compress-scores-topk-pack",
     "c3-project": "config3-compress-tcgen05-projection",
+    "c1-cover": "config1-strata-coverage-stats",
 }
 
 
@@ -465,6 +474,8 @@ def reference_arm(a):
     w = a.workload
     world = int(os.environ.get("WORLD_SIZE", "1"))
     L, B, T, Hq, Hkv, dt = shape(a, world)
+    if w in COVER:
+        return cover_reference(a, T, Hq, Hkv)
     run, nbytes, desc = cpu_sample(w, context=a.context)
     threads = _threads()
     for _ in range(a.warmup):
@@ -500,6 +511,30 @@ def reference_arm(a):
             "cpu_baseline_1thread": {"value": round(gbs1, 4), "unit": "GB/s", "cores": 1, "kind": "port",
                                      "ms_per_sample": round(sec1 * 1e3, 3)},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cover_reference(a, T, Hq, Hkv):
+    """Reference arm of c1-cover: the numpy port of coverage_stats on 1/8 of the layer (one KV head),
+    --steps timed samples after --warmup; value = the sample's algorithmic FLOPs / its time."""
+    run, flops, desc = cover_cpu_sample(T)
+    threads = _threads()
+    for _ in range(a.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        run()
+    sec = (time.perf_counter() - t0) / a.steps
+    tf = flops / sec / 1e12
+    line = {"metric": f"{DESC[a.workload]} TFLOP/s (algorithmic FP32 of the reference's coverage_stats)",
+            "value": round(tf, 5), "unit": "TFLOP/s", "impl": "reference", "n_gpus": a.gpus, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": DESC[a.workload], "layers_cycled": 2, "batch_per_gpu": 1, "context": T, "Hq": Hq,
+                       "Hkv": Hkv, "d": 128},
+            "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": f"{desc}; one step = this sample"},
+            "e2e": {"value": round(tf, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -805,12 +840,141 @@ def compress_arm(a):
         dist.destroy_process_group()
 
 
+def cover_flops(groups, Hq, Hkv, d, rs, re):
+    """(algorithmic FLOPs of the reference's coverage_stats, FLOPs the kvb kernels execute) for one
+    layer: per processed group of rows = Hq nq query rows, keys [0, mmax), coded tokens nt: scores and
+    p v over mmax keys, o M_a, (o M_a) v_j over nt tokens and the S update (2 FLOP per multiply-add),
+    plus vMv over the coded tokens once; the kernels also recompute the scores over nt tokens."""
+    alg = 2 * Hq * (re - rs) * d * d
+    extra = 0
+    for P in groups:
+        mmax = int(max(P)) + 1
+        nt = min(re, mmax) - rs
+        if nt <= 0:
+            continue
+        rows = Hq * len(P)
+        alg += rows * (2 * 2 * mmax * d + 2 * d * d + 2 * nt * d + 2 * d * d)
+        extra += rows * 2 * nt * d
+    return alg, alg + extra
+
+
+def cover_arm(a):
+    """STRATA's coverage statistics of a config-1 layer (batch row 1): one step = kvb.coverage_stats of
+    one layer (2 layers cycled: each layer's keys and values, 128 MiB, exceed L2 together with the
+    other's).  value = the reference's algorithmic FP32 FLOPs / step time."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import kvb
+    from kvb import workloads as W
+    world, rank, local, dev = setup_dist()
+    w = a.workload
+    L, B, T, Hq, Hkv, dt = shape(a, world)
+    d = 128
+    rs, re = 4, T - 32
+    layers = [W.coverage_layer(Hq, Hkv, T, d, torch.bfloat16, device=dev, seed=60 + 1000 * rank + i) for i in range(L)]
+    res = {}
+
+    def step(i):
+        q, k, v, M = layers[i % L]
+        res["st"] = kvb.coverage_stats(q, k, v, d ** -0.5, T, rs, re, M)
+
+    step(0)
+    torch.cuda.synchronize()
+    groups = res["st"]["groups"]
+    alg, executed = cover_flops(groups, Hq, Hkv, d, rs, re)
+    launches = 9
+    for i in range(max(3, a.warmup)):
+        step(i)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for i in range(a.steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps, world, dev)
+    # end to end through the public call: the layer's q, k, v from pinned host memory, the five outputs back
+    hq, hk, hv, hM = (t.cpu().pin_memory() for t in layers[0])
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hM))
+    for i in range(2):
+        kvb.coverage_stats(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True),
+                           d ** -0.5, T, rs, re, hM.to(dev, non_blocking=True))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_steps = max(1, min(a.steps, 5))
+    d2h = 0
+    for i in range(e2e_steps):
+        st = kvb.coverage_stats(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True),
+                                hv.to(dev, non_blocking=True), d ** -0.5, T, rs, re, hM.to(dev, non_blocking=True))
+        outs = [st[x].cpu() for x in ("A", "W", "DD", "S", "Mbar")]
+        d2h = sum(o.numel() * o.element_size() for o in outs)
+    e2e_ms = (time.perf_counter() - t0) / e2e_steps * 1e3
+    if kvb.device_status():
+        raise RuntimeError("device status word set after the timed region")
+    if rank == 0:
+        tflops = alg / (ms * 1e-3) / 1e12
+        line = {
+            "metric": f"{DESC[w]} TFLOP/s (algorithmic FP32 of the reference's coverage_stats)",
+            "value": round(world * tflops, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": DESC[w], "layers_cycled": L, "batch_per_gpu": 1, "context": T, "Hq": Hq,
+                       "Hkv": Hkv, "d": d, "inputs": dt, "groups": len(groups), "rs": rs, "re": re,
+                       "l2": "two layers cycled, keys + values 256 MiB", "flops_per_step": alg,
+                       "flops_executed_per_step": executed},
+            "roofline": {"bound": "fp32", "achieved": round(tflops, 2), "peak": round(FP32_NOMINAL_TFLOPS, 1),
+                         "unit": "TFLOP/s", "frac": round(tflops / FP32_NOMINAL_TFLOPS, 4),
+                         "peak_source": "nominal (148 SMs x 128 FP32 lanes x 2 x 1965 MHz)",
+                         "kernel": "whole coverage call (9 kernels; cov_sense + cov_attend ~90 %)", "traffic": None},
+            "e2e": {"value": round(world * alg / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
+            "gpu_launches": launches * a.steps,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not a.no_cpu_baseline:
+            run, sflops, desc = cover_cpu_sample(T)
+            threads = _threads()
+            run()
+            t0 = time.perf_counter()
+            run()
+            sec = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": round(sflops / sec / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
+                                    "kind": "port", "sample": desc}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cover_cpu_sample(T=32768, seed=60):
+    """The reference's coverage_stats restated in numpy (oracle/coverage.py) on one KV head (4 query
+    heads) of the config-1 layer, every group: (run, its algorithmic FLOPs, description)."""
+    import torch
+    import oracle.coverage as OC
+    from kvb import workloads as W
+    Hq, Hkv, d = 4, 1, 128
+    q, k, v, M = W.coverage_layer(Hq, Hkv, T, d, torch.bfloat16, seed=seed)
+    qf, kf, vf, Mf = q[0].float().numpy(), k[0].float().numpy(), v[0].float().numpy(), M.numpy()
+    groups = OC.coverage_groups(T)
+    rs, re = 4, T - 32
+
+    def run():
+        OC.coverage_stats(qf, kf, vf, d ** -0.5, rs, re, Mf, groups, 64, 1e-3)
+    alg, _ = cover_flops(groups, Hq, Hkv, d, rs, re)
+    return run, alg, (f"coverage_stats (numpy port, float64) of 1 KV head x 4 query heads x {T} positions, "
+                      f"{len(groups)} groups: 1/8 of the layer")
+
+
 def main():
     a = args_()
     if a.impl == "reference":
         return reference_arm(a)
     if a.workload in COMPRESS:
         return compress_arm(a)
+    if a.workload in COVER:
+        return cover_arm(a)
     return decode_arm(a)
 
 

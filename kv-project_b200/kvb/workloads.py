@@ -89,3 +89,18 @@ def qr_bases(Hkv: int, d: int, seed: int = SEED + 3) -> torch.Tensor:
         Q, R = np.linalg.qr(rng.standard_normal((d, d)))
         out[h] = Q * np.sign(np.diag(R))[None, :]
     return torch.from_numpy(out)
+
+
+def coverage_layer(Hq, Hkv, T, d, dtype, device="cpu", seed=SEED + 1, o_dim=None):
+    """One layer's prefill for STRATA's coverage statistics (config 1's shape, batch row 1): queries and
+    keys with a decaying per-channel spectrum (keys offset by 1, as the reference's own self-test draws
+    them, STRATA_KV.py:1963-1967), values N(0, 1), and output metrics M_a = W_aᵀ W_a from seeded
+    Gaussian output projections W_a ((3/2) d x d, scaled 1 / sqrt(d))."""
+    g = gen(device, seed)
+    spec = torch.exp(-torch.arange(d, device=device) / (d / 5.0)).sqrt()
+    q = (torch.randn(1, Hq, T, d, generator=g, device=device) * spec * 3).to(dtype)
+    k = (torch.randn(1, Hkv, T, d, generator=g, device=device) * spec * 3 + 1.0).to(dtype)
+    v = torch.randn(1, Hkv, T, d, generator=g, device=device).to(dtype)
+    Wa = torch.randn(Hq, o_dim or (3 * d // 2), d, generator=g, device=device) / d ** 0.5
+    M = (Wa.transpose(-1, -2) @ Wa).float().contiguous()
+    return q, k, v, M
