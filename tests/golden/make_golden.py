@@ -6,7 +6,7 @@ box never runs this):
     KVB_REFERENCE=/path/to/KV-Project python tests/golden/make_golden.py
 
 It imports the reference modules read-only (``STRATA_KV.py``, ``QUASAR_KV.py``, ``HEDGE_KV.py``,
-``TILT_KV.py``), calls their own
+``TILT_KV.py``, ``LCTC_KV.py``), calls their own
 functions on seeded inputs and stores inputs and outputs as small ``.npz`` files beside this
 script.  ``tests/test_oracle_golden.py`` checks the numpy oracle against every array here.
 """
@@ -514,8 +514,46 @@ def coverage():
     print("wrote coverage.npz", (HERE / "coverage.npz").stat().st_size)
 
 
+def lctc():
+    """LCTC's clipped uniform quantiser and its rate-distortion table: the reference's uq_codes,
+    uq_values and operational_rd (LCTC_KV.py:443-481, CPU, float32) on seeded heavy-tailed columns, in
+    lctc.npz: codes and values for per-column widths 1-8 and clips (including values outside the
+    clip), and the RD table (D, clips) for the default widths (0, 1, 2, 3, 4, 5, 6, 8) at 24 and 12
+    clip multipliers."""
+    load_reference()
+    import LCTC_KV as LC             # noqa: E402  (reference module, read-only)
+    import torch
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(13579)
+    out = {}
+    N, n = 300, 48
+    t = torch.distributions.StudentT(torch.tensor(3.0))
+    torch.manual_seed(13579)
+    a = (t.sample((N, n)) * torch.exp(torch.randn(n, generator=g))).float()
+    bits = torch.randint(1, 9, (n,), generator=g).float()
+    bits[:8] = torch.arange(1, 9).float()
+    clip = (a.abs().max(0).values * (0.2 + 0.9 * torch.rand(n, generator=g))).float()
+    idx = LC.uq_codes(a, bits, clip)
+    out["uq_a"], out["uq_bits"], out["uq_clip"] = np32(a), np32(bits), np32(clip)
+    out["uq_idx"] = idx.numpy().astype(np.uint8)
+    out["uq_values"] = np32(LC.uq_values(idx, bits, clip))
+    base = LC.Config()
+    for name, N, n, mults in (("rd24", 2048, 64, base.CLIP_MULTS), ("rd12", 700, 40, 12)):
+        A = (t.sample((N, n)) * torch.exp(0.8 * torch.randn(n, generator=g))).float()
+        A[:, :4] = torch.randn(N, 4, generator=g)                 # light-tailed columns too
+        A[:, 4] = 0.0                                             # a dead column (rms floor)
+        D, C = LC.operational_rd(A, base.BITS, mults)
+        out[f"{name}_A"], out[f"{name}_D"], out[f"{name}_C"] = np32(A), D.numpy(), np32(C)
+        out[f"{name}_bits"] = np.array(base.BITS, np.int64)
+        out[f"{name}_mults"] = np32(torch.logspace(np.log10(0.5), np.log10(8.0), mults))
+    np.savez_compressed(HERE / "lctc.npz", **out)
+    print("wrote lctc.npz", (HERE / "lctc.npz").stat().st_size)
+
+
 if __name__ == "__main__":
-    if sys.argv[1:] == ["coverage"]:
+    if sys.argv[1:] == ["lctc"]:
+        lctc()
+    elif sys.argv[1:] == ["coverage"]:
         coverage()
     elif sys.argv[1:] == ["rowcodes"]:
         rowcodes()
