@@ -442,6 +442,24 @@ kvb_status kvb_coverage_stats(const kvb_coverage* c, const int64_t* pos, const i
                               float* A, float* W, float* DD, float* S, float* Mbar, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* LCTC's clipped uniform quantiser (uq_codes / uq_values, LCTC_KV.py:443-455): per column k a width
+ * bits[k] (integral, 1..8) and a clip; code = min(max(floor((a + clip) / step), 0), 2^bits - 1) with
+ * step = 2 clip / 2^bits, value = -clip + (code + 0.5) step, each operation rounded as float32 (codes and
+ * values bit-identical to the reference).  a (rows, n) float32 with row stride lda; codes (rows, n) uint8
+ * and values (rows, n) float32 dense (values may be null). */
+kvb_status kvb_uq_codes(const float* a, int64_t rows, int64_t n, int64_t lda, const float* bits, const float* clip,
+                        uint8_t* codes, float* values, void* stream);
+kvb_status kvb_uq_values(const uint8_t* codes, int64_t rows, int64_t n, int64_t ldc, const float* bits,
+                         const float* clip, float* values, void* stream);
+/* operational_rd (LCTC_KV.py:458-481): per column of A (rows = calibration tokens) D[k][0] = mean a^2 and,
+ * per width bits_set[j] (host array, bits_set[0] = 0, the others 1..8, nb <= 16), the least mean squared
+ * quantisation error over the clips mults[m] x rms (mults: n_mults float32 on the device, the reference's
+ * logspace(0.5, 8)), the first on ties, and that clip: D (n, nb) float64, C (n, nb) float32. */
+size_t kvb_operational_rd_workspace(int64_t n, int nb, int n_mults);
+kvb_status kvb_operational_rd(const float* A, int64_t rows, int64_t n, int64_t lda, const int32_t* bits_set, int nb,
+                              const float* mults, int n_mults, double* D, float* C, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* Build the split-K plan (pure host computation, no CUDA calls) for n_ctas CTAs.  plan_out receives
  * [n_ctas, n_pieces, n_heads, cta_begin[n_ctas + 1], n_pieces x (head, stratum, first chunk, end
  * chunk, slot), head_begin[n_heads + 1]]: pieces in CTA order, each with the slot of its partial;

@@ -51,11 +51,13 @@ kvb_status status_words_alloc(unsigned*, unsigned*, int, int, cudaStream_t);
 kvb_status status_words_quasar(unsigned*, unsigned*, int, int, cudaStream_t);
 kvb_status status_words_atoms(unsigned*, unsigned*, int, int, cudaStream_t);
 kvb_status status_words_coverage(unsigned*, unsigned*, int, int, cudaStream_t);
+kvb_status status_words_lctc(unsigned*, unsigned*, int, int, cudaStream_t);
 inline const StatusWordsFn* status_word_files(int* n) {
     static const StatusWordsFn fns[] = {status_words_api,          status_words_spectral,     status_words_decode,
                                         status_words_main_token,   status_words_main_channel, status_words_main_midrise,
                                         status_words_main_xchg,    status_words_decode_tc,    status_words_alloc,
-                                        status_words_quasar,       status_words_atoms,        status_words_coverage};
+                                        status_words_quasar,       status_words_atoms,        status_words_coverage,
+                                        status_words_lctc};
     *n = int(sizeof(fns) / sizeof(fns[0]));
     return fns;
 }

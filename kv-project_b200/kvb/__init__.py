@@ -7,7 +7,7 @@ strata assignment (K2), fused split-K flash decoding over packed codes (K3), the
 ``include/kvb.h``); this package only moves tensors and builds descriptors.
 """
 
-from . import _lib, ops, cache, workloads, state, seqsplit, codebooks, coverage   # noqa: F401
+from . import _lib, ops, cache, workloads, state, seqsplit, codebooks, coverage, lctc   # noqa: F401
 from .ops import (PackedCache, quant_pack, key_energy, rank_split, query_scores, snapkv_scores, decode, decode_plan,  # noqa: F401
                   device_status, overlap_previous, UNIFORM_STEP)
 from .state import KvbStrataState, KvbCodedState, tier_as_kvb  # noqa: F401
@@ -15,4 +15,4 @@ from .coverage import coverage_groups, coverage_stats  # noqa: F401
 
 __all__ = ["ops", "cache", "workloads", "state", "seqsplit", "codebooks", "PackedCache", "quant_pack", "key_energy", "rank_split",
            "query_scores", "snapkv_scores", "decode", "decode_plan", "device_status", "overlap_previous", "UNIFORM_STEP",
-           "KvbStrataState", "KvbCodedState", "tier_as_kvb", "coverage", "coverage_groups", "coverage_stats"]
+           "KvbStrataState", "KvbCodedState", "tier_as_kvb", "coverage", "coverage_groups", "coverage_stats", "lctc"]

@@ -94,6 +94,10 @@ SIGNATURES = {
     "kvb_atom_read": (_i32, [C.POINTER(Atoms), _p, _i32, _i32, _p, _p, _p, _p]),
     "kvb_coverage_workspace_size": (C.c_size_t, [C.POINTER(Coverage), _p, _p, _i32]),
     "kvb_coverage_stats": (_i32, [C.POINTER(Coverage), _p, _p, _i32, _p, _p, _p, _p, _p, _p, C.c_size_t, _p]),
+    "kvb_uq_codes": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
+    "kvb_uq_values": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "kvb_operational_rd_workspace": (C.c_size_t, [_i64, _i32, _i32]),
+    "kvb_operational_rd": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p, _i32, _p, _p, _p, C.c_size_t, _p]),
     "kvb_quasar_scores": (_i32, [_p, _i32, _i32, _i32, _p, C.c_size_t, _p, _i32, _p, _i32, _i64, _p, _p]),
     "kvb_quasar_values_workspace": (C.c_size_t, [_i32, _i32, _i64, _i32]),
     "kvb_quasar_values": (_i32, [_p, _i32, _i32, _i64, _p, C.c_size_t, _p, _i32, _p, _i32, _i32, _p, _p, C.c_size_t, _p]),
