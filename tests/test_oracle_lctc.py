@@ -18,11 +18,12 @@ def test_uq_codes_values_golden(golden):
 
 
 def check_rd(D, C, errs, ref_D, ref_C):
-    """D within 2e-6 relative (float32 means against float64 sums); clips within 1e-6 relative (the
-    column rms from a float32 mean there, a float64 one here: an ulp apart at most) except at near-ties,
-    where a different multiplier (12 % apart at 24 multipliers) may win."""
+    """D within 2e-5 relative (the reference's float32 means over a few hundred to a few thousand rows
+    carry ~1e-6 to 1e-5 of round-off; float64 sums here); clips within 1e-6 relative (the column rms
+    from a float32 mean there, a float64 one here: an ulp apart at most) except at near-ties, where a
+    different multiplier (12 % apart at 24 multipliers) may win."""
     # (a dead column's errors are float32 subnormals there, ~1e-42: compared absolutely)
-    np.testing.assert_allclose(D, ref_D, rtol=2e-6, atol=1e-35)
+    np.testing.assert_allclose(D, ref_D, rtol=2e-5, atol=1e-35)
     same = np.isclose(C, ref_C, rtol=1e-6, atol=0)
     if not same.all():
         # every differing choice is a near-tie: the reference's pick is within round-off of the best
@@ -30,7 +31,7 @@ def check_rd(D, C, errs, ref_D, ref_C):
         assert (j > 0).all()
         e = errs[k, j - 1]
         srt = np.sort(e, axis=-1)
-        assert np.all(srt[:, 1] - srt[:, 0] <= 4e-6 * srt[:, 0]), (k, j)
+        assert np.all(srt[:, 1] - srt[:, 0] <= 4e-5 * srt[:, 0]), (k, j)
     return int((~same).sum())
 
 
