@@ -841,10 +841,11 @@ def compress_arm(a):
 
 
 def cover_flops(groups, Hq, Hkv, d, rs, re):
-    """(algorithmic FLOPs of the reference's coverage_stats, FLOPs the kvb kernels execute) for one
-    layer: per processed group of rows = Hq nq query rows, keys [0, mmax), coded tokens nt: scores and
-    p v over mmax keys, o M_a, (o M_a) v_j over nt tokens and the S update (2 FLOP per multiply-add),
-    plus vMv over the coded tokens once; the kernels also recompute the scores over nt tokens."""
+    """(algorithmic FLOPs of the reference's coverage_stats, FLOPs the kvb kernels execute: the same,
+    the scores of the coded tokens are stored between the two passes) for one layer: per processed
+    group of rows = Hq nq query rows, keys [0, mmax), coded tokens nt: scores and p v over mmax keys,
+    o M_a, (o M_a) v_j over nt tokens and the S update (2 FLOP per multiply-add), plus vMv over the
+    coded tokens once."""
     alg = 2 * Hq * (re - rs) * d * d
     extra = 0
     for P in groups:
@@ -854,7 +855,6 @@ def cover_flops(groups, Hq, Hkv, d, rs, re):
             continue
         rows = Hq * len(P)
         alg += rows * (2 * 2 * mmax * d + 2 * d * d + 2 * nt * d + 2 * d * d)
-        extra += rows * 2 * nt * d
     return alg, alg + extra
 
 
@@ -927,7 +927,7 @@ def cover_arm(a):
             "roofline": {"bound": "fp32", "achieved": round(tflops, 2), "peak": round(FP32_NOMINAL_TFLOPS, 1),
                          "unit": "TFLOP/s", "frac": round(tflops / FP32_NOMINAL_TFLOPS, 4),
                          "peak_source": "nominal (148 SMs x 128 FP32 lanes x 2 x 1965 MHz)",
-                         "kernel": "whole coverage call (9 kernels; cov_sense + cov_attend ~90 %)", "traffic": None},
+                         "kernel": "whole coverage call (9 kernels; cov_attend + cov_sense ~85 %)", "traffic": None},
             "e2e": {"value": round(world * alg / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
             "gpu_launches": launches * a.steps,

@@ -18,9 +18,18 @@ using kvb::CovGroup;
 constexpr size_t ALIGN = 256;
 size_t up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
 
+// Groups [g0, g1) with attention items [a0, a1) and sensitivity items [s0, s1): one pass of both
+// kernels over a score buffer of at most CV_SCORE_CAP bytes.
+struct CovBatch {
+    int g0, g1;
+    int64_t a0, a1, s0, s1;
+};
+
 // Host tables and the workspace layout of one call.
 struct CovPlan {
     std::vector<CovGroup> grp;
+    std::vector<CovBatch> batches;
+    int64_t score_floats = 0;        // the largest batch's scores
     std::vector<int> pos;
     std::vector<int4> it1, it2;
     int64_t rows = 0, parts = 0, T_all = 0, alps = 0, nparts = 0;
@@ -28,7 +37,7 @@ struct CovPlan {
     // byte offsets in the workspace
     size_t o_grp = 0, o_pos = 0, o_it1 = 0, o_it2 = 0, host_bytes = 0;
     size_t o_vmv = 0, o_part = 0, o_rowinfo = 0, o_oM = 0, o_alpha = 0, o_dd = 0, o_a = 0, o_w = 0, o_alp = 0,
-           o_npart = 0, o_gw = 0, o_wva = 0, o_apart = 0, o_hsum = 0, total = 0;
+           o_npart = 0, o_gw = 0, o_wva = 0, o_apart = 0, o_hsum = 0, o_sbuf = 0, total = 0;
 };
 
 kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* goff, int n_groups, CovPlan& P) {
@@ -52,6 +61,7 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
         if (pos[i] < 0 || pos[i] >= c->H) return fail(KVB_EINVAL, "coverage: position %lld outside [0, H)", (long long)pos[i]);
         P.pos[size_t(i)] = int(pos[i]);
     }
+    int64_t batch_floats = 0;
     for (int g = 0; g < n_groups; ++g) {
         const int64_t b = goff[g], e = goff[g + 1];
         if (e <= b || e > npos) return fail(KVB_EINVAL, "coverage: group %d is empty or out of order", g);
@@ -67,6 +77,7 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
         G.local = g == n_groups - 1 ? 1 : c->local;             // the last group is the window group
         G.ns = int((mmax + kvb::CV_SPLIT - 1) / kvb::CV_SPLIT);
         G.nit = (G.nt + kvb::CV_TOKS - 1) / kvb::CV_TOKS;
+        G.ld = (G.nt + 3) & ~3;
         G.row_base = P.rows;
         G.part_base = P.parts;
         G.tok_base = P.T_all;
@@ -80,12 +91,25 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
         P.nparts += int64_t(c->Hkv) * G.nit;
         const int gi = int(P.grp.size());
         const int nrb = (rep * G.nq + kvb::CV_ROWS - 1) / kvb::CV_ROWS;
+        const int64_t sfl = grows * G.ld;                       // this group's stored scores
+        if (P.batches.empty() || (batch_floats > 0 && (batch_floats + sfl) * 4 > kvb::CV_SCORE_CAP)) {
+            const int64_t a = int64_t(P.it1.size()), b = int64_t(P.it2.size());
+            P.batches.push_back(CovBatch{gi, gi, a, a, b, b});
+            batch_floats = 0;
+        }
+        G.s_base = batch_floats;
+        batch_floats += sfl;
+        P.score_floats = std::max(P.score_floats, batch_floats);
         for (int h = 0; h < c->Hkv; ++h) {
             for (int rb = 0; rb < nrb; ++rb)
                 for (int s = 0; s < G.ns; ++s) P.it1.push_back(make_int4(gi, h, rb, s));
             for (int it = 0; it < G.nit; ++it) P.it2.push_back(make_int4(gi, h, it, 0));
         }
         P.grp.push_back(G);
+        CovBatch& B = P.batches.back();
+        B.g1 = gi + 1;
+        B.a1 = int64_t(P.it1.size());
+        B.s1 = int64_t(P.it2.size());
     }
     const int D = c->d;
     const int64_t n = c->re - c->rs;
@@ -110,6 +134,7 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
     P.n_ablk = int((n + kvb::CV_THREADS - 1) / kvb::CV_THREADS);
     P.o_apart = o;   o += up(size_t(c->Hkv) * P.n_ablk * kvb::CV_APART * 4);
     P.o_hsum = o;    o += up(size_t(c->Hkv) * 16);
+    P.o_sbuf = o;    o += up(size_t(P.score_floats) * 4);
     P.total = o;
     return KVB_OK;
 }
@@ -133,18 +158,20 @@ kvb_status cov_launch(const kvb_coverage* c, const CovPlan& P, kvb::CovParams& p
         if ((st = cuda_check(cudaFuncSetAttribute(cov_attend_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1),
                              "coverage attend smem")))
             return st;
-        cov_attend_kernel<D, T><<<unsigned(P.it1.size()), CV_THREADS, smem1, s>>>(
-            p, reinterpret_cast<const int4*>(ws + P.o_it1));
-        if ((st = launch_check("coverage attend"))) return st;
-        cov_merge_kernel<D><<<dim3(unsigned(ng), unsigned(c->Hq)), D, 0, s>>>(p);
-        if ((st = launch_check("coverage merge"))) return st;
         const int smem2 = cov_sense_smem<D>();
         if ((st = cuda_check(cudaFuncSetAttribute(cov_sense_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2),
                              "coverage sense smem")))
             return st;
-        cov_sense_kernel<D, T><<<unsigned(P.it2.size()), CV_THREADS, smem2, s>>>(
-            p, reinterpret_cast<const int4*>(ws + P.o_it2));
-        if ((st = launch_check("coverage sense"))) return st;
+        const int4* it1 = reinterpret_cast<const int4*>(ws + P.o_it1);
+        const int4* it2 = reinterpret_cast<const int4*>(ws + P.o_it2);
+        for (const CovBatch& B : P.batches) {
+            cov_attend_kernel<D, T><<<unsigned(B.a1 - B.a0), CV_THREADS, smem1, s>>>(p, it1 + B.a0);
+            if ((st = launch_check("coverage attend"))) return st;
+            cov_merge_kernel<D><<<dim3(unsigned(B.g1 - B.g0), unsigned(c->Hq)), D, 0, s>>>(p, B.g0);
+            if ((st = launch_check("coverage merge"))) return st;
+            cov_sense_kernel<D, T><<<unsigned(B.s1 - B.s0), CV_THREADS, smem2, s>>>(p, it2 + B.s0);
+            if ((st = launch_check("coverage sense"))) return st;
+        }
         cov_norm_kernel<<<unsigned(ng), CV_THREADS, 0, s>>>(p);
         if ((st = launch_check("coverage norm"))) return st;
     }
@@ -230,6 +257,7 @@ kvb_status kvb_coverage_stats(const kvb_coverage* c, const int64_t* pos, const i
     p.n_ablk = P.n_ablk;
     p.wva = reinterpret_cast<float*>(ws + P.o_wva);
     p.hsum = reinterpret_cast<float*>(ws + P.o_hsum);
+    p.sbuf = reinterpret_cast<float*>(ws + P.o_sbuf);
     p.A = A;
     p.W = W;
     p.DD = DD;

@@ -9,7 +9,8 @@
 //   cov_attend   exact causal softmax of each row over its keys, split into key ranges: per split the
 //                running max, sum and unnormalised output (flash-attention form, float32 FMA tiles)
 //   cov_merge    per row: lse = m + log l over the splits, o, oM = o M_a and c = oM . o
-//   cov_sense    per (group, head, token range): p = exp(s - lse) recomputed, pR = p on the long-range
+//   cov_sense    per (group, head, token range): p = exp(s - lse) from the scores the attention pass
+//                stored for the coded tokens, pR = p on the long-range
 //                reads, u2 = max(vMv - 2 oM . v + c, 0); per token the sums over rows of
 //                (pR / max(1 - pR, 1e-6))^2 u2, pR^2 u2 and (per r) pR^2; per row the sum of pR^2 u2
 //   cov_norm     per group: N = sum dd, the weight 1 / N (0 when N = 0), the rows' alpha
@@ -33,6 +34,9 @@ constexpr int CV_SPLIT = 2048;    // keys per attention item
 constexpr int CV_TOKS = 512;      // coded tokens per sensitivity item
 constexpr int CV_MAX_REP = 8;
 constexpr int CV_MERGE_ROWS = 16;
+// Scores of the coded tokens held between the two passes, per batch of consecutive groups: at most
+// this many bytes (a group larger than that forms a batch of its own).
+constexpr int64_t CV_SCORE_CAP = int64_t(4) << 30;
 
 // One observation group on the device (groups the reference skips, te <= rs, are left out).
 struct CovGroup {
@@ -43,12 +47,13 @@ struct CovGroup {
     int local;      // reads at distance < local do not count (1 for the window group)
     int ns;         // attention splits: ceil(mmax / CV_SPLIT)
     int nit;        // sensitivity items per head: ceil(nt / CV_TOKS)
-    int pad;
+    int ld;         // row stride of the group's stored scores: nt rounded up to 4
     int64_t row_base;   // rows (a, i) of the group at row_base + a nq + i in the row tables
     int64_t part_base;  // attention partials: part_base + (a nq + i) ns + split
     int64_t tok_base;   // token columns of the group in the per-group token sums
     int64_t alp_base;   // alpha partials: alp_base + (a nq + i) nit + item
     int64_t n_base;     // partial sums of dd: n_base + h nit + item
+    int64_t s_base;     // the scores of the coded tokens: s_base + (a nq + i) ld + t, in this group's batch
 };
 
 struct CovParams {
@@ -63,6 +68,7 @@ struct CovParams {
     int64_t rs, n, T_all;            // coded tokens [rs, rs + n); token columns of all groups
     float scaling, floor;
     float* vmv;                      // (Hq, n)
+    float* sbuf;                     // scores of the coded tokens of the groups of one batch
     float* part;                     // (m, l, o[D]) per row and split
     float* rowinfo;                  // (lse, c) per row
     float* oM;                       // D per row
@@ -313,6 +319,20 @@ __global__ void __launch_bounds__(CV_THREADS, 2) cov_attend_kernel(CovParams p, 
         __syncthreads();
         float s[4][4] = {};
         cv_tile<D>(s, Qt, Kt, rg, cg);
+        if (kt + CV_TILE > p.rs && kt < p.rs + G.nt) {
+            // the coded tokens' raw scores, for the sensitivity pass (row-major per row, token t = key - rs)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = rg * 4 + i;
+                if (r >= nrows) continue;
+                float* dst = p.sbuf + G.s_base + int64_t(h * R + row0 + r) * G.ld;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t key = kt + cg * 4 + j;
+                    if (cg * 4 + j < nk && key >= p.rs && key < p.rs + G.nt) dst[key - p.rs] = s[i][j];
+                }
+            }
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             float tmax = -INFINITY;
@@ -379,11 +399,11 @@ __global__ void __launch_bounds__(CV_THREADS, 2) cov_attend_kernel(CovParams p, 
 // One CTA of D threads per (group, query head a): rows of CV_MERGE_ROWS positions at a time, merged over
 // the key splits (thread = dimension), then oM[e] = sum_d o[d] M_a[d][e] (thread = column e) and c.
 template <int D>
-__global__ void __launch_bounds__(D) cov_merge_kernel(CovParams p) {
+__global__ void __launch_bounds__(D) cov_merge_kernel(CovParams p, int g0) {
     __shared__ float s_o[CV_MERGE_ROWS][D];
     __shared__ float s_red[CV_MERGE_ROWS][D / 32];
     __shared__ float s_lse[CV_MERGE_ROWS];
-    const CovGroup G = p.grp[blockIdx.x];
+    const CovGroup G = p.grp[g0 + blockIdx.x];
     const int a = blockIdx.y, e = threadIdx.x;
     const float* Ma = p.M + size_t(a) * D * D;
     for (int i0 = 0; i0 < G.nq; i0 += CV_MERGE_ROWS) {
@@ -438,65 +458,54 @@ __global__ void __launch_bounds__(D) cov_merge_kernel(CovParams p) {
 
 template <int D>
 constexpr int cov_sense_smem() {
-    return (4 * D * 64 + 64 * 64 + 2 * 8 * 64 + (2 + CV_MAX_REP) * CV_TOKS + CV_MAX_REP * 64) * 4;
+    return (2 * D * 64 + 64 * 64 + 2 * 8 * 64 + (2 + CV_MAX_REP) * CV_TOKS + CV_MAX_REP * 64) * 4;
 }
 
-// The next tile's key and value rows held in registers while the current tile computes (16-bit inputs;
-// float32 inputs load at the store point instead).  Chunk w = threadIdx.x + CV_THREADS x: row w & 63,
-// 8 elements from (w >> 6) x 8: the layout of cv_rows_t.
+// The next tile's value rows held in registers while the current tile computes (16-bit inputs; float32
+// inputs load at the store point instead).  Chunk w = threadIdx.x + CV_THREADS x: row w & 63, 8 elements
+// from (w >> 6) x 8: the layout of cv_rows_t.
 template <int D, typename T>
 struct CvNext {
     static constexpr bool REG = sizeof(T) == 2;
     static constexpr int N = REG ? 64 * (D / 8) / CV_THREADS : 1;
-    uint4 k[N], v[N];
-    __device__ __forceinline__ void load(const T* kb, const T* vb, int64_t stride, int tt, int nk) {
+    uint4 v[N];
+    __device__ __forceinline__ void load(const T* vb, int64_t stride, int tt, int nk) {
         if constexpr (REG) {
 #pragma unroll
             for (int x = 0; x < N; ++x) {
                 const int w = threadIdx.x + CV_THREADS * x, r = w & 63, c = w >> 6;
-                if (r < nk) {
-                    k[x] = __ldg(reinterpret_cast<const uint4*>(kb + int64_t(tt + r) * stride + c * 8));
-                    v[x] = __ldg(reinterpret_cast<const uint4*>(vb + int64_t(tt + r) * stride + c * 8));
-                } else {
-                    k[x] = v[x] = make_uint4(0u, 0u, 0u, 0u);
-                }
+                v[x] = r < nk ? __ldg(reinterpret_cast<const uint4*>(vb + int64_t(tt + r) * stride + c * 8))
+                              : make_uint4(0u, 0u, 0u, 0u);
             }
         }
     }
-    __device__ __forceinline__ void store(float* Kt, float* Vt, const T* kb, const T* vb, int64_t stride, int tt,
-                                          int nk) {
+    __device__ __forceinline__ void store(float* Vt, const T* vb, int64_t stride, int tt, int nk) {
         if constexpr (REG) {
 #pragma unroll
             for (int x = 0; x < N; ++x) {
                 const int w = threadIdx.x + CV_THREADS * x, r = w & 63, c = w >> 6;
-                float fk[8], fv[8];
-                cv_unpack8<T>(k[x], fk);
+                float fv[8];
                 cv_unpack8<T>(v[x], fv);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    Kt[(c * 8 + e) * 64 + r] = fk[e];
-                    Vt[(c * 8 + e) * 64 + r] = fv[e];
-                }
+                for (int e = 0; e < 8; ++e) Vt[(c * 8 + e) * 64 + r] = fv[e];
             }
         } else {
-            cv_rows_t<D, T>(Kt, [&](int r) -> const T* { return r < nk ? kb + int64_t(tt + r) * stride : nullptr; }, 1.f);
             cv_rows_t<D, T>(Vt, [&](int r) -> const T* { return r < nk ? vb + int64_t(tt + r) * stride : nullptr; }, 1.f);
         }
     }
 };
 
-// One CTA per (group, KV head, CV_TOKS coded tokens).  Per block of 64 rows: the scaled queries and oM
-// rows once; per tile of 64 tokens the scores s and t = oM . v (two FMA tiles, the next tile's rows
-// loading meanwhile), the elementwise terms and their sums: over rows per token (a thread's 4 rows,
-// the two row groups of a warp, then the 8 warps in order; pR^2 per r from a staged tile, rows in
-// order) and over tokens per row (butterflies over the row's 16 lanes, tiles in order).
+// One CTA per (group, KV head, CV_TOKS coded tokens), two per SM.  Per block of 64 rows: the oM rows
+// once; per tile of 64 tokens t = oM . v (an FMA tile, the next tile's values loading meanwhile) and
+// the rows' scores s from the attention pass, then the elementwise terms and their sums: over rows per
+// token (a thread's 4 rows, the two row groups of a warp, then the 8 warps in order; pR^2 per r from a
+// staged tile, rows in order) and over tokens per row (butterflies over the row's 16 lanes, tiles in
+// order).
 template <int D, typename T>
-__global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, const int4* items) {
+__global__ void __launch_bounds__(CV_THREADS, 2) cov_sense_kernel(CovParams p, const int4* items) {
     extern __shared__ float4 cv_smem[];
-    float* Qt = reinterpret_cast<float*>(cv_smem);       // [D][64]
-    float* Ot = Qt + D * 64;                              // [D][64]
-    float* Kt = Ot + D * 64;                              // [D][64]
-    float* Vt = Kt + D * 64;                              // [D][64]
+    float* Ot = reinterpret_cast<float*>(cv_smem);       // [D][64]
+    float* Vt = Ot + D * 64;                              // [D][64]
     float* Ew = Vt + D * 64;                              // [64 rows][64 tokens]: pR^2
     float* red_dd = Ew + 64 * 64;                         // [8 warps][64 tokens]
     float* red_a = red_dd + 8 * 64;
@@ -513,9 +522,9 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
     const int t0 = item * CV_TOKS, t1 = min(t0 + CV_TOKS, G.nt);
     for (int x = threadIdx.x; x < (2 + CV_MAX_REP) * CV_TOKS; x += CV_THREADS) tdd[x] = 0.f;
     const int rg = threadIdx.x >> 4, cg = threadIdx.x & 15, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const T* kb = static_cast<const T*>(p.k) + h * p.khs + p.rs * p.kps;
     const T* vb = static_cast<const T*>(p.v) + h * p.khs + p.rs * p.kps;
     const int64_t hrow = G.row_base + int64_t(h) * R;    // the head's first row
+    const float* sb = p.sbuf + G.s_base + int64_t(h) * R * G.ld;
     auto load_vmv = [&](int tt, int nk) {
         for (int x = threadIdx.x; x < p.rep * 64; x += CV_THREADS) {
             const int r = x >> 6, j = x & 63;
@@ -534,16 +543,11 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
             s_lse[r] = ok ? p.rowinfo[2 * (hrow + rr)] : 0.f;
             s_c[r] = ok ? p.rowinfo[2 * (hrow + rr) + 1] : 0.f;
         }
-        cv_rows_t<D, T>(Qt, [&](int r) -> const T* {
-            if (r >= nrows) return nullptr;
-            const int rr = row0 + r;
-            return cv_qrow<T>(p, h * p.rep + rr / G.nq, p.pos[G.off + rr % G.nq]);
-        }, p.scaling);
         cv_rows_t<D, float>(Ot, [&](int r) -> const float* { return r < nrows ? p.oM + (hrow + row0 + r) * D : nullptr; }, 1.f);
         {
             const int nk = min(CV_TILE, t1 - t0);
-            nx.load(kb, vb, p.kps, t0, nk);
-            nx.store(Kt, Vt, kb, vb, p.kps, t0, nk);
+            nx.load(vb, p.kps, t0, nk);
+            nx.store(Vt, vb, p.kps, t0, nk);
             load_vmv(t0, nk);
         }
         const int r_first = row0 / G.nq, n_r = (row0 + nrows - 1) / G.nq - r_first + 1;
@@ -552,9 +556,8 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
         for (int tt = t0; tt < t1; tt += CV_TILE) {
             const int nk = min(CV_TILE, t1 - tt);
             const int tn = tt + CV_TILE, nkn = min(CV_TILE, t1 - tn);
-            if (tn < t1) nx.load(kb, vb, p.kps, tn, nkn);
-            float s[4][4] = {}, tv[4][4] = {};
-            cv_tile<D>(s, Qt, Kt, rg, cg);
+            if (tn < t1) nx.load(vb, p.kps, tn, nkn);
+            float tv[4][4] = {};
             cv_tile<D>(tv, Ot, Vt, rg, cg);
             float dsum[4] = {0.f, 0.f, 0.f, 0.f}, asum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -562,6 +565,7 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
                 const int row = rg * 4 + i;
                 const int pos = s_pos[row], r = s_r[row];
                 const float lse = s_lse[row], c = s_c[row];
+                const float* srow = sb + int64_t(row0 + row) * G.ld + tt;
                 float w4[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -570,7 +574,7 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
                     float ddv = 0.f, av = 0.f, wv = 0.f;
                     if (row < nrows && kk < nk && key <= pos - G.local) {
                         // p at a long-range read (key <= pos - local < pos: never masked)
-                        const float pr = expf(s[i][j] - lse);
+                        const float pr = expf(srow[kk] - lse);
                         const float u2 = fmaxf((svmv[r * 64 + kk] - 2.f * tv[i][j]) + c, 0.f);
                         const float x = pr / fmaxf(1.f - pr, 1e-6f);
                         ddv = x * x * u2;
@@ -596,7 +600,7 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
             }
             __syncthreads();
             // per token: the 8 warps in order (dd: threads 0-63, a: 64-127); pR^2 per (r, token) pair,
-            // the r's rows of this block in order (all threads)
+            // the r's rows of this block in order (all threads); the next tile's values and vMv
             if (threadIdx.x < 128) {
                 const int t = threadIdx.x & 63;
                 if (t < nk) {
@@ -616,7 +620,7 @@ __global__ void __launch_bounds__(CV_THREADS, 1) cov_sense_kernel(CovParams p, c
                 tw[r * CV_TOKS + tt - t0 + t] += acc;
             }
             if (tn < t1) {
-                nx.store(Kt, Vt, kb, vb, p.kps, tn, nkn);
+                nx.store(Vt, vb, p.kps, tn, nkn);
                 load_vmv(tn, nkn);
             }
             __syncthreads();
