@@ -435,6 +435,7 @@ typedef struct kvb_coverage {
     float scaling;                      /* query scale */
     float floor;                        /* STRATA_FLOOR */
     int local;                          /* STRATA_LOCAL */
+    int64_t score_cap;                  /* bytes of stored scores per pass over a batch of groups; 0: 4 GiB */
 } kvb_coverage;
 /* Device workspace bytes of kvb_coverage_stats for these groups (0 for invalid arguments). */
 size_t kvb_coverage_workspace_size(const kvb_coverage* c, const int64_t* pos, const int64_t* group_off, int n_groups);

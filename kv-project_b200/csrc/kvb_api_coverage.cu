@@ -62,6 +62,7 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
         P.pos[size_t(i)] = int(pos[i]);
     }
     int64_t batch_floats = 0;
+    const int64_t cap = c->score_cap > 0 ? c->score_cap : kvb::CV_SCORE_CAP;
     for (int g = 0; g < n_groups; ++g) {
         const int64_t b = goff[g], e = goff[g + 1];
         if (e <= b || e > npos) return fail(KVB_EINVAL, "coverage: group %d is empty or out of order", g);
@@ -92,7 +93,7 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
         const int gi = int(P.grp.size());
         const int nrb = (rep * G.nq + kvb::CV_ROWS - 1) / kvb::CV_ROWS;
         const int64_t sfl = grows * G.ld;                       // this group's stored scores
-        if (P.batches.empty() || (batch_floats > 0 && (batch_floats + sfl) * 4 > kvb::CV_SCORE_CAP)) {
+        if (P.batches.empty() || (batch_floats > 0 && (batch_floats + sfl) * 4 > cap)) {
             const int64_t a = int64_t(P.it1.size()), b = int64_t(P.it2.size());
             P.batches.push_back(CovBatch{gi, gi, a, a, b, b});
             batch_floats = 0;

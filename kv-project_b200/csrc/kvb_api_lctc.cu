@@ -10,8 +10,11 @@
 
 namespace {
 
-unsigned lc_grid(int64_t total) {
-    return unsigned(std::max<int64_t>(1, std::min<int64_t>((total + kvb::LC_THREADS - 1) / kvb::LC_THREADS, 148 * 16)));
+// (row blocks, column blocks): about 8 CTAs of 256 threads per SM in all, at most one row block per row.
+dim3 lc_grid(int64_t rows, int64_t n) {
+    const int64_t cb = (n + kvb::LC_THREADS - 1) / kvb::LC_THREADS;
+    const int64_t rb = std::max<int64_t>(1, std::min<int64_t>(rows, (148 * 8 + cb - 1) / cb));
+    return dim3(unsigned(rb), unsigned(cb));
 }
 
 size_t errs_offset(int64_t n) { return size_t((n * 4 + 255) / 256 * 256); }
@@ -23,9 +26,9 @@ extern "C" {
 kvb_status kvb_uq_codes(const float* a, int64_t rows, int64_t n, int64_t lda, const float* bits, const float* clip,
                         uint8_t* codes, float* values, void* stream) {
     if (!a || !bits || !clip || !codes) return fail(KVB_EINVAL, "uq_codes: null argument");
-    if (rows < 0 || n <= 0 || lda < n) return fail(KVB_EINVAL, "uq_codes: shapes (n > 0, lda >= n)");
+    if (rows < 0 || n <= 0 || lda < n || n > int64_t(65535) * kvb::LC_THREADS) return fail(KVB_EINVAL, "uq_codes: shapes (0 < n <= 65535 x 256, lda >= n)");
     if (rows == 0) return KVB_OK;
-    kvb::uq_codes_kernel<<<lc_grid(rows * n), kvb::LC_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+    kvb::uq_codes_kernel<<<lc_grid(rows, n), kvb::LC_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
         a, rows, n, lda, bits, clip, codes, values);
     return launch_check("uq_codes");
 }
@@ -33,9 +36,9 @@ kvb_status kvb_uq_codes(const float* a, int64_t rows, int64_t n, int64_t lda, co
 kvb_status kvb_uq_values(const uint8_t* codes, int64_t rows, int64_t n, int64_t ldc, const float* bits,
                          const float* clip, float* values, void* stream) {
     if (!codes || !bits || !clip || !values) return fail(KVB_EINVAL, "uq_values: null argument");
-    if (rows < 0 || n <= 0 || ldc < n) return fail(KVB_EINVAL, "uq_values: shapes (n > 0, ldc >= n)");
+    if (rows < 0 || n <= 0 || ldc < n || n > int64_t(65535) * kvb::LC_THREADS) return fail(KVB_EINVAL, "uq_values: shapes (0 < n <= 65535 x 256, ldc >= n)");
     if (rows == 0) return KVB_OK;
-    kvb::uq_values_kernel<<<lc_grid(rows * n), kvb::LC_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+    kvb::uq_values_kernel<<<lc_grid(rows, n), kvb::LC_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
         codes, rows, n, ldc, bits, clip, values);
     return launch_check("uq_values");
 }

@@ -35,7 +35,7 @@ constexpr int CV_TOKS = 512;      // coded tokens per sensitivity item
 constexpr int CV_MAX_REP = 8;
 constexpr int CV_MERGE_ROWS = 16;
 // Scores of the coded tokens held between the two passes, per batch of consecutive groups: at most
-// this many bytes (a group larger than that forms a batch of its own).
+// this many bytes by default (a group larger than the cap forms a batch of its own).
 constexpr int64_t CV_SCORE_CAP = int64_t(4) << 30;
 
 // One observation group on the device (groups the reference skips, te <= rs, are left out).

@@ -40,35 +40,36 @@ __device__ __forceinline__ float lc_value(float q, float clip, float step) {
     return __fadd_rn(-clip, __fmul_rn(__fadd_rn(q, 0.5f), step));
 }
 
+// Grid (row blocks, column blocks of LC_THREADS): each thread one column, its width and step computed
+// once, rows strided by the row blocks (coalesced along the row).
 __global__ void __launch_bounds__(LC_THREADS) uq_codes_kernel(const float* __restrict__ a, int64_t rows, int64_t n,
                                                               int64_t lda, const float* __restrict__ bits,
                                                               const float* __restrict__ clip, uint8_t* codes,
                                                               float* values) {
-    const int64_t total = rows * n;
-    for (int64_t x = int64_t(blockIdx.x) * LC_THREADS + threadIdx.x; x < total; x += int64_t(gridDim.x) * LC_THREADS) {
-        const int64_t r = x / n, k = x % n;
-        const float levels = lc_levels(bits[k]);
-        if (levels == 0.f) continue;
-        const float c = clip[k];
-        const float step = __fdiv_rn(__fmul_rn(2.f, c), levels);
-        const float q = lc_code(a[r * lda + k], c, levels, step);
-        codes[x] = uint8_t(q);
-        if (values) values[x] = lc_value(q, c, step);
+    const int64_t k = int64_t(blockIdx.y) * LC_THREADS + threadIdx.x;
+    if (k >= n) return;
+    const float levels = lc_levels(bits[k]);
+    if (levels == 0.f) return;
+    const float c = clip[k];
+    const float step = __fdiv_rn(__fmul_rn(2.f, c), levels);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float q = lc_code(__ldg(a + r * lda + k), c, levels, step);
+        codes[r * n + k] = uint8_t(q);
+        if (values) values[r * n + k] = lc_value(q, c, step);
     }
 }
 
 __global__ void __launch_bounds__(LC_THREADS) uq_values_kernel(const uint8_t* __restrict__ codes, int64_t rows,
                                                                int64_t n, int64_t ldc, const float* __restrict__ bits,
                                                                const float* __restrict__ clip, float* values) {
-    const int64_t total = rows * n;
-    for (int64_t x = int64_t(blockIdx.x) * LC_THREADS + threadIdx.x; x < total; x += int64_t(gridDim.x) * LC_THREADS) {
-        const int64_t r = x / n, k = x % n;
-        const float levels = lc_levels(bits[k]);
-        if (levels == 0.f) continue;
-        const float c = clip[k];
-        const float step = __fdiv_rn(__fmul_rn(2.f, c), levels);
-        values[x] = lc_value(float(codes[r * ldc + k]), c, step);
-    }
+    const int64_t k = int64_t(blockIdx.y) * LC_THREADS + threadIdx.x;
+    if (k >= n) return;
+    const float levels = lc_levels(bits[k]);
+    if (levels == 0.f) return;
+    const float c = clip[k];
+    const float step = __fdiv_rn(__fmul_rn(2.f, c), levels);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
+        values[r * n + k] = lc_value(float(__ldg(codes + r * ldc + k)), c, step);
 }
 
 // Per column: mean a^2 (float64) into D[k][0], rms = max(sqrt(mean), 1e-20) and C[k][0] = 0.

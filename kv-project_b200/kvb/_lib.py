@@ -52,7 +52,7 @@ class Coverage(C.Structure):
                 ("q_head_stride", C.c_int64), ("q_pos_stride", C.c_int64), ("kv_head_stride", C.c_int64),
                 ("kv_pos_stride", C.c_int64), ("M", C.c_void_p), ("Hq", C.c_int), ("Hkv", C.c_int), ("d", C.c_int),
                 ("H", C.c_int64), ("rs", C.c_int64), ("re", C.c_int64), ("scaling", C.c_float), ("floor", C.c_float),
-                ("local", C.c_int)]
+                ("local", C.c_int), ("score_cap", C.c_int64)]
 
 
 SIGNATURES = {

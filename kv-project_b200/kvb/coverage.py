@@ -67,10 +67,11 @@ def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
 
 
 def coverage_stats(q, k, v, scaling, H: int, rs: int, re: int, M: torch.Tensor, cfg=None,
-                   window_only: bool = False) -> dict:
+                   window_only: bool = False, score_cap: int = 0) -> dict:
     """q (1, Hq, T, d), k and v (1, Hkv, T, d) CUDA tensors of one dtype (f32 / f16 / bf16, d contiguous,
     d in {64, 128}); M (Hq, d, d) the output metrics W_O,aᵀ W_O,a.  Returns {"A", "W", "DD" (Hkv, re - rs),
-    "S", "Mbar" (Hkv, d, d), "groups"} as the reference's coverage_stats does."""
+    "S", "Mbar" (Hkv, d, d), "groups"} as the reference's coverage_stats does.  score_cap: bytes of
+    scores held between the two passes over a batch of groups (0: the library's 4 GiB)."""
     cfg = cfg or CoverageConfig()
     for t in (q, k, v, M):
         if not isinstance(t, torch.Tensor) or not t.is_cuda:
@@ -90,7 +91,7 @@ def coverage_stats(q, k, v, scaling, H: int, rs: int, re: int, M: torch.Tensor, 
     Mc = M.float().contiguous()
     desc = L.Coverage(_ptr(q), _ptr(k), _ptr(v), _DT[k.dtype], q.stride(1), q.stride(2), k.stride(1), k.stride(2),
                       _ptr(Mc), Hq, Hkv, d, int(H), int(rs), int(re), float(scaling), float(cfg.STRATA_FLOOR),
-                      int(cfg.STRATA_LOCAL))
+                      int(cfg.STRATA_LOCAL), int(score_cap))
     lib = L.lib()
     pp, gp = pos.ctypes.data_as(C.c_void_p), goff.ctypes.data_as(C.c_void_p)
     need = lib.kvb_coverage_workspace_size(C.byref(desc), pp, gp, len(groups))

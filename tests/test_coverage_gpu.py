@@ -96,6 +96,18 @@ def test_coverage_32k_every_group_deterministic(cuda_dev):
     assert kvb.device_status() == 0
 
 
+def test_coverage_batches_of_groups_bit_identical(cuda_dev):
+    """A score cap of 1 MiB splits the 17 groups of an 8192-position layer into many passes (one group
+    per pass for most): the same results, bit for bit, as one pass."""
+    import kvb
+    H = 8192
+    q, k, v, M = (t.to(cuda_dev) for t in layer(H, 21, cuda_dev))
+    one = kvb.coverage_stats(q, k, v, 128 ** -0.5, H, 4, H - 32, M)
+    many = kvb.coverage_stats(q, k, v, 128 ** -0.5, H, 4, H - 32, M, score_cap=1 << 20)
+    for key in KEYS:
+        assert torch.equal(one[key], many[key]), key
+
+
 def test_coverage_rejects_bad_arguments(cuda_dev):
     import kvb
     q, k, v, M = (t.to(cuda_dev) for t in layer(256, 3, cuda_dev))
