@@ -1,7 +1,10 @@
 """kvb_coverage_stats (STRATA's coverage statistics, STRATA_KV.py:1226-1298) on the GPU:
 
-* the reference's own outputs (coverage.npz, its coverage_stats in float32 on CPU) for four cases, in the
-  three input dtypes, with the tolerances of the oracle's own pin (tests/test_oracle_coverage.py);
+* for four cases in the three input dtypes: the float64 oracle on the same inputs with the tolerances
+  of the oracle's own pin (tests/test_oracle_coverage.py), and the reference's own float32 outputs
+  (coverage.npz) with the median bound doubled: the reference's result is itself up to 6e-5 (median,
+  case b) from the float64 value, and the kernels' float32 sums (FMA for float32 inputs, split-TF32
+  tensor-core tiles for 16-bit ones) round in another order than its sequential ones;
 * the float64 oracle at config 1's layer shape (32 query heads, 8 KV heads, d 128): the window group
   alone at 32768 positions, and every group at 8192;
 * at 32768 positions with every group (65): two calls bit-identical, finite and non-negative sums.
@@ -40,8 +43,11 @@ def test_coverage_matches_reference(golden, cuda_dev, name, dtype):
     assert len(st["groups"]) == len(c["groups"])
     for a, b in zip(st["groups"], c["groups"]):
         np.testing.assert_array_equal(a, b)
+    ref = oracle_stats(c["q"], c["k"], c["v"], c["scaling"], c["rs"], c["re"], c["M"], c["groups"], c["local"],
+                       c["floor"])
     for key in KEYS:
-        check_close(st[key].cpu().numpy(), g[f"{name}_{key}"], key)
+        check_close(st[key].cpu().numpy(), ref[key], key)
+        check_close(st[key].cpu().numpy(), g[f"{name}_{key}"], key, median_tol=2e-4)
 
 
 def layer(H, seed, dev):
