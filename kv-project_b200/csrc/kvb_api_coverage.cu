@@ -37,7 +37,7 @@ struct CovPlan {
     // byte offsets in the workspace
     size_t o_grp = 0, o_pos = 0, o_it1 = 0, o_it2 = 0, host_bytes = 0;
     size_t o_vmv = 0, o_part = 0, o_rowinfo = 0, o_oM = 0, o_alpha = 0, o_dd = 0, o_a = 0, o_w = 0, o_alp = 0,
-           o_npart = 0, o_gw = 0, o_wva = 0, o_apart = 0, o_hsum = 0, o_sbuf = 0, total = 0;
+           o_npart = 0, o_gw = 0, o_wva = 0, o_apart = 0, o_hsum = 0, o_sbuf = 0, o_spart = 0, total = 0;
 };
 
 kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* goff, int n_groups, CovPlan& P) {
@@ -136,6 +136,7 @@ kvb_status cov_plan(const kvb_coverage* c, const int64_t* pos, const int64_t* go
     P.o_apart = o;   o += up(size_t(c->Hkv) * P.n_ablk * kvb::CV_APART * 4);
     P.o_hsum = o;    o += up(size_t(c->Hkv) * 16);
     P.o_sbuf = o;    o += up(size_t(P.score_floats) * 4);
+    P.o_spart = o;   o += up(size_t(kvb::CV_GRAM_CHUNKS) * c->Hkv * D * D * 4);
     P.total = o;
     return KVB_OK;
 }
@@ -178,7 +179,7 @@ kvb_status cov_launch(const kvb_coverage* c, const CovPlan& P, kvb::CovParams& p
     }
     cov_accum_kernel<<<dim3(unsigned(P.n_ablk), unsigned(c->Hkv)), CV_THREADS, 0, s>>>(p);
     if ((st = launch_check("coverage accum"))) return st;
-    cov_gram_kernel<D, T><<<dim3(D / 32, D / 32, unsigned(c->Hkv)), CV_THREADS, 0, s>>>(p);
+    cov_gram_kernel<D, T><<<dim3(D / 32, D / 32, unsigned(c->Hkv * CV_GRAM_CHUNKS)), CV_THREADS, 0, s>>>(p);
     if ((st = launch_check("coverage gram"))) return st;
     cov_finish_kernel<D><<<unsigned(c->Hkv), CV_THREADS, 0, s>>>(p);
     if ((st = launch_check("coverage finish"))) return st;
@@ -259,6 +260,7 @@ kvb_status kvb_coverage_stats(const kvb_coverage* c, const int64_t* pos, const i
     p.wva = reinterpret_cast<float*>(ws + P.o_wva);
     p.hsum = reinterpret_cast<float*>(ws + P.o_hsum);
     p.sbuf = reinterpret_cast<float*>(ws + P.o_sbuf);
+    p.spart = reinterpret_cast<float*>(ws + P.o_spart);
     p.A = A;
     p.W = W;
     p.DD = DD;

@@ -15,8 +15,8 @@
 //                (pR / max(1 - pR, 1e-6))^2 u2, pR^2 u2 and (per r) pR^2; per row the sum of pR^2 u2
 //   cov_norm     per group: N = sum dd, the weight 1 / N (0 when N = 0), the rows' alpha
 //   cov_accum    per (head, token): A, DD, WVa summed over the groups in the reference's order, over live
-//   cov_gram     S[h] = sum_g wgt_g sum_rows alpha qa qaᵀ, over live
-//   cov_finish   per head: S / sum A, omega, Mbar, the head sums of A, W, DD
+//   cov_gram     S[h] = sum_g wgt_g sum_rows alpha qa qaᵀ per chunk of groups
+//   cov_finish   per head: S over live and sum A, omega, Mbar, the head sums of A, W, DD
 //   cov_floor    A, W, DD plus floor x their means
 // The contractions are float32 FMA tiles of 64 rows x 64 keys over d (the reference computes in float32;
 // bf16 operands would not hold p or oM).  Every reduction has a fixed order: no atomics, the results do
@@ -34,6 +34,7 @@ constexpr int CV_SPLIT = 2048;    // keys per attention item
 constexpr int CV_TOKS = 512;      // coded tokens per sensitivity item
 constexpr int CV_MAX_REP = 8;
 constexpr int CV_MERGE_ROWS = 16;
+constexpr int CV_GRAM_CHUNKS = 8;       // the groups of the S update in this many chunks of CTAs
 // Scores of the coded tokens held between the two passes, per batch of consecutive groups: at most
 // this many bytes by default (a group larger than the cap forms a batch of its own).
 constexpr int64_t CV_SCORE_CAP = int64_t(4) << 30;
@@ -80,6 +81,7 @@ struct CovParams {
     float* npart;                    // partial sums of dd per (group, head, item)
     float* gw;                       // per group: weight, N > 0
     float* apart;                    // per (head, accumulation block): sums of A, W, DD, WVa[r]
+    float* spart;                    // (CV_GRAM_CHUNKS, Hkv, D, D): S summed over a chunk of groups
     int n_ablk;                      // accumulation blocks per head
     float* wva;                      // (Hq, n)
     float* hsum;                     // per head: sum A, sum W, sum DD, sum omega
@@ -730,16 +732,18 @@ __global__ void __launch_bounds__(CV_THREADS) cov_accum_kernel(CovParams p) {
 
 // ---- S[h] = sum_g wgt_g sum_rows alpha qa qaᵀ, over live --------------------------------------------
 
-// One CTA per (32 x 32 block of S, KV head); the group's rows 64 at a time in shared memory.
+// One CTA per (32 x 32 block of S, KV head, chunk of consecutive groups); the group's rows 64 at a time
+// in shared memory.  The chunks' sums are added in chunk order by cov_finish.
 template <int D, typename T>
 __global__ void __launch_bounds__(CV_THREADS) cov_gram_kernel(CovParams p) {
     __shared__ float s_q1[64][33], s_q2[64][33], s_al[64];
-    const int h = blockIdx.z, d1b = blockIdx.y * 32, d2b = blockIdx.x * 32;
+    const int h = blockIdx.z / CV_GRAM_CHUNKS, chunk = blockIdx.z % CV_GRAM_CHUNKS;
+    const int d1b = blockIdx.y * 32, d2b = blockIdx.x * 32;
     const int ty = threadIdx.x >> 3, tx = threadIdx.x & 7;
-    float S[4] = {0.f, 0.f, 0.f, 0.f}, live = 0.f;
-    for (int g = 0; g < p.n_groups; ++g) {
+    const int g_lo = chunk * p.n_groups / CV_GRAM_CHUNKS, g_hi = (chunk + 1) * p.n_groups / CV_GRAM_CHUNKS;
+    float S[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int g = g_lo; g < g_hi; ++g) {
         const CovGroup G = p.grp[g];
-        live += p.gw[2 * g + 1];
         const int R = p.rep * G.nq;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int row0 = 0; row0 < R; row0 += 64) {
@@ -769,10 +773,9 @@ __global__ void __launch_bounds__(CV_THREADS) cov_gram_kernel(CovParams p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) S[j] += acc[j] * wgt;
     }
-    live = fmaxf(live, 1.f);
-    float* dst = p.S + (size_t(h) * D + d1b + ty) * D + d2b + tx * 4;
+    float* dst = p.spart + ((size_t(chunk) * p.Hkv + h) * D + d1b + ty) * D + d2b + tx * 4;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = S[j] / live;
+    for (int j = 0; j < 4; ++j) dst[j] = S[j];
 }
 
 // ---- per head: S / sum A, omega, Mbar, the head sums for the floors -------------------------------
@@ -792,8 +795,14 @@ __global__ void __launch_bounds__(CV_THREADS) cov_finish_kernel(CovParams p) {
     float osum = 0.f;
     for (int r = 0; r < p.rep; ++r) osum += s_sum[3 + r];
     const float inv = fmaxf(sumA, 1e-30f);
+    float live = 0.f;
+    for (int g = 0; g < p.n_groups; ++g) live += p.gw[2 * g + 1];
+    live = fmaxf(live, 1.f);
     for (int e = threadIdx.x; e < D * D; e += CV_THREADS) {
-        p.S[size_t(h) * D * D + e] /= inv;
+        float sv = 0.f;
+#pragma unroll
+        for (int c = 0; c < CV_GRAM_CHUNKS; ++c) sv += p.spart[(size_t(c) * p.Hkv + h) * D * D + e];
+        p.S[size_t(h) * D * D + e] = sv / live / inv;
         float mb = 0.f;
         if (osum > 0.f) {
             for (int r = 0; r < p.rep; ++r) mb += s_sum[3 + r] * p.M[size_t(h * p.rep + r) * D * D + e];
