@@ -28,6 +28,8 @@ Other workloads (--workload), each printing the same JSON line for its own confi
   c3-project  compress side of config 3 (tcgen05 basis projection + mid-rise code of K and V)
   c1-cover    STRATA's coverage statistics of one config-1 layer (batch row 1, 32768 positions, 65
               observation groups): exact per-group softmax sensitivities A, W, DD, S, Mbar (FP32 FMA)
+  lctc        LCTC's clipped uniform quantiser over 1 GiB of float32 coefficients (codes + values), and
+              its RD table at the calibration shape (8192 rows x 1024 coefficients, 7 widths, 24 clips)
 
   python bench.py [--gpus N --steps K --warmup W] [--workload W]   # kvb (CUDA) arm
   python bench.py --strata 0,0                                      # config 1 with every token at 2 bits
@@ -56,7 +58,7 @@ METRIC = "packed-KV decode attn µs/step and HBM GB/s (% of peak) at 1/2/4/8 B20
 FALLBACK_HBM_GBS = 6650.0
 DECODE = ("c1", "c0", "c2", "c3", "c4", "c4s")
 COMPRESS = ("c1-pack", "c2-evict", "c3-project")
-COVER = ("c1-cover",)
+COVER = ("c1-cover", "lctc")
 # nominal FP32 FMA rate of a B200 (148 SMs x 128 lanes x 2 FLOP x 1965 MHz): the coverage kernels'
 # roofline (MEASURED_PEAKS.json holds the copy and tensor-core rates only)
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
@@ -161,7 +163,8 @@ def shape(a, world):
     w = a.workload.split("-")[0]
     base = {"c0": (1, 1, 4096, 32, 8, "f16"), "c1": (32, 8, 32768, 32, 8, "bf16"),
             "c2": (32, 4, 32768, 32, 8, "bf16"), "c3": (1, 16, 16384, 32, 8, "f16"),
-            "c4": (80, 32, 131072, 64, 8, "bf16"), "c4s": (80, 4, 131072, 64, 8, "bf16")}[w]
+            "c4": (80, 32, 131072, 64, 8, "bf16"), "c4s": (80, 4, 131072, 64, 8, "bf16"),
+            "lctc": (1, 1, 262144, 0, 0, "f32")}[w]
     L, B, T, Hq, Hkv, dt = base
     if w in ("c1", "c4") and a.workload not in COMPRESS:
         # strong scaling: the (batch, KV head) units of one job are split over the ranks by batch row
@@ -193,6 +196,7 @@ DESC = {
     "c2-evict": "config2-compress-scores-topk-pack",
     "c3-project": "config3-compress-tcgen05-projection",
     "c1-cover": "config1-strata-coverage-stats",
+    "lctc": "lctc-uniform-quantiser",
 }
 
 
@@ -474,6 +478,8 @@ def reference_arm(a):
     w = a.workload
     world = int(os.environ.get("WORLD_SIZE", "1"))
     L, B, T, Hq, Hkv, dt = shape(a, world)
+    if w == "lctc":
+        return lctc_reference(a)
     if w in COVER:
         return cover_reference(a, T, Hq, Hkv)
     run, nbytes, desc = cpu_sample(w, context=a.context)
@@ -510,6 +516,37 @@ def reference_arm(a):
                              "sample": sample},
             "cpu_baseline_1thread": {"value": round(gbs1, 4), "unit": "GB/s", "cores": 1, "kind": "port",
                                      "ms_per_sample": round(sec1 * 1e3, 3)},
+            "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def lctc_reference(a):
+    """Reference arm of lctc: the numpy port of uq_codes + uq_values (LCTC_KV.py:443-455) on 16384 rows x
+    1024 coefficients per step; value = the sample's bytes read and written / its time."""
+    import numpy as np
+    import oracle.lctc as OL
+    rng = np.random.default_rng(70)
+    rows, n = 16384, 1024
+    x = rng.standard_normal((rows, n), dtype=np.float32)
+    bits = rng.integers(1, 9, n).astype(np.float32)
+    clip = (rng.random(n, dtype=np.float32) * 3 + 0.5).astype(np.float32)
+
+    def run():
+        OL.uq_values(OL.uq_codes(x, bits, clip), bits, clip)
+    for _ in range(a.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        run()
+    sec = (time.perf_counter() - t0) / a.steps
+    gbs = rows * n * 9 / sec / 1e9
+    sample = f"uq_codes + uq_values (numpy port) of {rows} x {n} float32 coefficients; one step = this sample"
+    line = {"metric": f"{DESC['lctc']} GB/s (coefficients read + codes and values written)", "value": round(gbs, 4),
+            "unit": "GB/s", "impl": "reference", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": DESC["lctc"], "rows": rows, "coefficients": n, "widths": "1-8 per column"},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -948,6 +985,81 @@ def cover_arm(a):
         dist.destroy_process_group()
 
 
+def lctc_arm(a):
+    """LCTC's quantiser (uq_codes + uq_values, LCTC_KV.py:443-455): one step = quantising 262144 rows x
+    1024 float32 coefficients at per-column widths 1-8 (codes uint8 + values float32); value = bytes read
+    and written / step time.  The RD table (operational_rd, :458-481) at the calibration shape is timed
+    beside it (rd_ms)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from kvb import lctc
+    world, rank, local, dev = setup_dist()
+    rows, n = 262144, 1024
+    g = torch.Generator(device=dev).manual_seed(70 + rank)
+    X = [torch.randn(rows, n, device=dev, generator=g) for _ in range(2)]       # 2 x 1 GiB, cycled
+    bits = torch.randint(1, 9, (n,), device=dev, generator=g).float()
+    clip = torch.rand(n, device=dev, generator=g) * 3 + 0.5
+    for i in range(max(3, a.warmup)):
+        lctc.uq_quantize(X[i % 2], bits, clip)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for i in range(a.steps):
+            lctc.uq_quantize(X[i % 2], bits, clip)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps, world, dev)
+    A = torch.randn(8192, 1024, device=dev, generator=g)
+    lctc.operational_rd(A, [0, 1, 2, 3, 4, 5, 6, 8], 24)
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record()
+    for _ in range(3):
+        lctc.operational_rd(A, [0, 1, 2, 3, 4, 5, 6, 8], 24)
+    r1.record()
+    torch.cuda.synchronize()
+    rd_ms = r0.elapsed_time(r1) / 3
+    # end to end: coefficients from pinned host memory, codes back
+    hx = X[0][:65536].cpu().pin_memory()
+    t0 = time.perf_counter()
+    for _ in range(3):
+        codes, _v = lctc.uq_quantize(hx.to(dev, non_blocking=True), bits, clip)
+        codes.cpu()
+    e2e_ms = (time.perf_counter() - t0) / 3 * 1e3
+    if rank == 0:
+        peak, peak_kind = peaks()
+        nbytes = rows * n * (4 + 1 + 4)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        line = {"metric": f"{DESC['lctc']} GB/s (coefficients read + codes and values written)",
+                "value": round(world * gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic",
+                "config": {"workload": DESC["lctc"], "rows": rows, "coefficients": n, "widths": "1-8 per column",
+                           "l2": "inputs larger than L2 (2 x 1 GiB cycled)", "bytes_per_step": nbytes},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(gbs / peak, 4), "peak_source": peak_kind, "kernel": "uq_codes_kernel",
+                             "traffic": None},
+                "rd_ms": round(rd_ms, 3), "rd_shape": "8192 rows x 1024 coefficients x 7 widths x 24 clips",
+                "e2e": {"value": round(65536 * n * 5 / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                        "h2d_bytes_per_step": 65536 * n * 4, "d2h_bytes_per_step": 65536 * n, "rows": 65536},
+                "gpu_launches": a.steps, "clocks": clk.summary()}
+        if world == 1 and not a.no_cpu_baseline:
+            import oracle.lctc as OL
+            xs = X[0][:8192].cpu().numpy()
+            b_, c_ = bits.cpu().numpy(), clip.cpu().numpy()
+            t0 = time.perf_counter()
+            OL.uq_values(OL.uq_codes(xs, b_, c_), b_, c_)
+            sec = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": round(8192 * n * 9 / sec / 1e9, 4), "unit": "GB/s", "cores": 1,
+                                    "kind": "port", "sample": f"uq_codes + uq_values (numpy port) of 8192 x {n} coefficients"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def cover_cpu_sample(T=32768, seed=60):
     """The reference's coverage_stats restated in numpy (oracle/coverage.py) on one KV head (4 query
     heads) of the config-1 layer, every group: (run, its algorithmic FLOPs, description)."""
@@ -973,6 +1085,8 @@ def main():
         return reference_arm(a)
     if a.workload in COMPRESS:
         return compress_arm(a)
+    if a.workload == "lctc":
+        return lctc_arm(a)
     if a.workload in COVER:
         return cover_arm(a)
     return decode_arm(a)
