@@ -82,3 +82,23 @@ def test_coverage_groups_edges():
         assert np.all(np.diff(grp) > 0) and grp[0] >= s and grp[-1] < min(s + 512, 5000 - 32)
         assert len(grp) == min(16, min(s + 512, 5000 - 32) - s)
     np.testing.assert_array_equal(gs[-1], np.arange(5000 - 32, 5000))
+
+
+def test_coverage_stats_edges():
+    """Every group skipped (no group reads a coded token: te <= rs): zero sensitivities, Mbar the plain
+    mean of the head's metrics (STRATA_KV.py:1293-1294); a context with only the window group."""
+    rng = np.random.default_rng(3)
+    Hkv, rep, d, H = 2, 2, 16, 200
+    q = rng.standard_normal((Hkv * rep, H, d)).astype(np.float32)
+    k = rng.standard_normal((Hkv, H, d)).astype(np.float32)
+    v = rng.standard_normal((Hkv, H, d)).astype(np.float32)
+    Wa = rng.standard_normal((Hkv * rep, 24, d)).astype(np.float32)
+    M = np.einsum("axd,axe->ade", Wa, Wa)
+    st = coverage_stats(q, k, v, 0.25, 150, 190, M, [np.arange(100, 120)], 4, 1e-3)
+    for key in ("A", "W", "DD", "S"):
+        np.testing.assert_array_equal(st[key], 0.0)
+    np.testing.assert_allclose(st["Mbar"], M.astype(np.float64).reshape(Hkv, rep, d, d).mean(1), rtol=1e-12)
+    gs = coverage_groups(H, w_obs=32)
+    assert len(gs) == 1 and gs[0][0] == H - 32
+    st = coverage_stats(q, k, v, 0.25, 4, H - 32, M, gs, 64, 1e-3)
+    assert np.all(st["A"] > 0) and np.all(np.isfinite(st["S"]))
