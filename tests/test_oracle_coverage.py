@@ -98,7 +98,7 @@ def test_coverage_stats_edges():
     for key in ("A", "W", "DD", "S"):
         np.testing.assert_array_equal(st[key], 0.0)
     np.testing.assert_allclose(st["Mbar"], M.astype(np.float64).reshape(Hkv, rep, d, d).mean(1), rtol=1e-12)
-    gs = coverage_groups(H, w_obs=32)
-    assert len(gs) == 1 and gs[0][0] == H - 32
-    st = coverage_stats(q, k, v, 0.25, 4, H - 32, M, gs, 64, 1e-3)
+    gs = coverage_groups(90, w_obs=32)                 # 90 < n_sink + local + w_obs: no segment group
+    assert len(gs) == 1 and gs[0][0] == 68
+    st = coverage_stats(q, k, v, 0.25, 4, 90 - 32, M, gs, 64, 1e-3)
     assert np.all(st["A"] > 0) and np.all(np.isfinite(st["S"]))
