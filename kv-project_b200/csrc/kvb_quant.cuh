@@ -243,8 +243,10 @@ __global__ void __launch_bounds__(D) quant_channel_kernel(const QuantTokenParams
 // =============================================================================================
 
 // a / b rounded to nearest even from y = RN(1 / b) (P. Markstein, IBM J. Res. Dev. 34(1), 1990):
-// q0 = RN(a y), r = a - q0 b exactly (FMA), RN(q0 + r y) = RN(a / b) for normal b and quotients
-// that neither overflow nor underflow (b >= 2^-24 here; |a / b| is bounded by the code range).
+// q0 = RN(a y), r = a - q0 b exactly (FMA), RN(q0 + r y) = RN(a / b) for normal b and y and quotients
+// that neither overflow nor underflow.  Here b is a stored scale, clamped into [2^-24, 65504] (fp16
+// storage), so y = RN(1 / b) is normal too, whatever the input's range (bf16 up to 3.4e38: the
+// quotient stays below 2^113 and the codes are clamped after it).
 __device__ __forceinline__ float div_rn_markstein(float a, float b, float y) {
     const float q0 = __fmul_rn(a, y);
     const float r = __fmaf_rn(-q0, b, a);
